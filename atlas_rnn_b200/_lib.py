@@ -1,0 +1,93 @@
+"""ctypes binding of the C ABI in include/atlas_mem.h (libatlas_mem.so).
+
+The shared library is built in-tree (``atlas_rnn_b200/build.py``) and loaded
+from this package directory. There is no fallback: if the library is missing
+or fails to load, every entry point raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libatlas_mem.so")
+
+FMAP = {"off": 0, "elementwise": 1, "tensor": 2}
+GATE_NONE, GATE_TOKEN, GATE_WINDOW = 0, 1, 2
+F32, BF16 = 0, 1
+
+
+class Shape(ctypes.Structure):
+    _fields_ = [("N", ctypes.c_int64), ("T", ctypes.c_int64), ("d_k", ctypes.c_int32),
+                ("d_phi", ctypes.c_int32), ("d_v", ctypes.c_int32), ("window", ctypes.c_int32),
+                ("fmap_mode", ctypes.c_int32), ("fmap_degree", ctypes.c_int32),
+                ("gate_mode", ctypes.c_int32), ("momentum", ctypes.c_int32),
+                ("dtype_io", ctypes.c_int32), ("chunk", ctypes.c_int32)]
+
+
+_vp = ctypes.c_void_p
+
+
+class Fwd(ctypes.Structure):
+    _fields_ = [(n, _vp) for n in ("k", "q", "v", "lr", "decay", "beta", "gate", "S_ref", "S0", "Z0",
+                                   "buf_in", "proj", "y", "S_end", "Z_end", "buf_out")]
+
+
+class Bwd(ctypes.Structure):
+    _fields_ = [(n, _vp) for n in ("dy", "dS_end", "dZ_end", "dbuf_out", "dk", "dq", "dv", "dlr",
+                                   "ddecay", "dbeta", "dgate", "dS_ref", "dS0", "dZ0", "dbuf_in")]
+
+
+_lib = None
+
+
+def lib():
+    """Load the library once; raise with the path if it is absent."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(
+                f"atlas_rnn_b200: native library not built ({LIB_PATH}); run "
+                "`python -m atlas_rnn_b200.build` (there is no non-CUDA fallback)")
+        L = ctypes.CDLL(LIB_PATH)
+        P = ctypes.POINTER
+        sz = P(ctypes.c_size_t)
+        L.atlas_mem_abi_version.restype = ctypes.c_int
+        L.atlas_mem_error_string.restype = ctypes.c_char_p
+        L.atlas_mem_error_string.argtypes = [ctypes.c_int]
+        L.atlas_mem_workspace_size.argtypes = [P(Shape), sz, sz, sz]
+        L.atlas_mem_forward.argtypes = [P(Shape), P(Fwd), _vp, ctypes.c_size_t, _vp, ctypes.c_size_t, _vp]
+        L.atlas_mem_backward.argtypes = [P(Shape), P(Fwd), P(Bwd), _vp, ctypes.c_size_t, _vp,
+                                         ctypes.c_size_t, _vp]
+        L.atlas_mem_forward_local.argtypes = [P(Shape), P(Fwd), _vp, ctypes.c_size_t, _vp, ctypes.c_size_t,
+                                              _vp, _vp, _vp, _vp]
+        L.atlas_mem_forward_finish.argtypes = [P(Shape), P(Fwd), _vp, ctypes.c_size_t, _vp, ctypes.c_size_t,
+                                               _vp]
+        L.atlas_mem_backward_local.argtypes = [P(Shape), P(Fwd), P(Bwd), _vp, ctypes.c_size_t, _vp,
+                                               ctypes.c_size_t, _vp, _vp, _vp, _vp]
+        L.atlas_mem_backward_finish.argtypes = [P(Shape), P(Fwd), P(Bwd), _vp, ctypes.c_size_t, _vp,
+                                                ctypes.c_size_t, ctypes.c_int, _vp]
+        for name in ("atlas_mem_workspace_size", "atlas_mem_forward", "atlas_mem_backward",
+                     "atlas_mem_forward_local", "atlas_mem_forward_finish", "atlas_mem_backward_local",
+                     "atlas_mem_backward_finish"):
+            getattr(L, name).restype = ctypes.c_int
+        _lib = L
+    return _lib
+
+
+def check(code: int, what: str):
+    if code != 0:
+        msg = lib().atlas_mem_error_string(code).decode()
+        raise RuntimeError(f"atlas_rnn_b200: {what} failed: {msg} (code {code})")
+
+
+def ptr(t):
+    """Device pointer of a tensor (or None)."""
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def workspace_sizes(shape: Shape):
+    s, f, b = ctypes.c_size_t(), ctypes.c_size_t(), ctypes.c_size_t()
+    check(lib().atlas_mem_workspace_size(ctypes.byref(shape), ctypes.byref(s), ctypes.byref(f),
+                                         ctypes.byref(b)), "workspace_size")
+    return s.value, f.value, b.value

@@ -1,0 +1,454 @@
+// C ABI of libatlas_mem.so: argument checks, workspace layout and the launch
+// sequences of the forward and backward passes. Declarations and the reference
+// interfaces they replace are in include/atlas_mem.h.
+#include <mutex>
+
+#include "chunk_kernels.cuh"
+
+using namespace atlas;
+
+namespace {
+
+constexpr size_t kAlign = 256;
+inline size_t align_up(size_t x) { return (x + kAlign - 1) & ~(kAlign - 1); }
+inline int r4(int n) { return (n + 3) & ~3; }
+
+int chunk_of(const AtlasMemShape* s) {
+  if (s->chunk > 0) return s->chunk;
+  return s->window - 1 > 32 ? s->window - 1 : 32;
+}
+
+struct Layout {
+  int C, nch;
+  size_t saved, fwd, bwd;
+  size_t st, delta, ST, cs, phik, phiq;                        // in saved
+  size_t adj, acs, dpsi, ddel, dphiR, hdd, hdp, du, hdu;       // in bwd scratch
+};
+
+Layout make_layout(const AtlasMemShape* s) {
+  Layout L{};
+  L.C = chunk_of(s);
+  L.nch = (int)((s->T + L.C - 1) / L.C);
+  const size_t N = (size_t)s->N, T = (size_t)s->T, nch = (size_t)L.nch;
+  const size_t D2 = (size_t)s->d_v * s->d_phi, e1 = (size_t)(s->window - 1);
+  const bool tens = s->fmap_mode == ATLAS_FMAP_TENSOR;
+  size_t o = 0;
+  auto put = [&](size_t bytes) { const size_t at = o; o = align_up(o + bytes); return at; };
+  L.st = put(N * nch * 2 * D2 * 4);
+  L.delta = put(N * T * s->d_v * 4);
+  L.ST = put(N * D2 * 4);
+  L.cs = put(N * nch * 4 * 4);
+  L.phik = tens ? put(N * T * s->d_phi * 4) : 0;
+  L.phiq = tens ? put(N * T * s->d_phi * 4) : 0;
+  L.saved = o;
+  L.fwd = 0;
+  o = 0;
+  L.adj = put(N * nch * 2 * D2 * 4);
+  L.acs = put(N * nch * 4 * 4);
+  L.dpsi = put(N * T * s->d_phi * 4);
+  L.ddel = put(N * T * s->d_v * 4);
+  L.dphiR = put(N * T * s->d_phi * 4);
+  L.hdd = put(N * nch * (e1 ? e1 : 1) * s->d_v * 4);
+  L.hdp = put(N * nch * (e1 ? e1 : 1) * s->d_phi * 4);
+  L.du = put(N * T * 4);
+  L.hdu = put(N * nch * (e1 ? e1 : 1) * 4);
+  L.bwd = o;
+  return L;
+}
+
+// Dynamic shared memory of each kernel; mirrors the SmemAlloc::take sequences.
+struct Smem {
+  size_t f1, f3, b1, b3, fin, dsref, bufout, fmf, fmb;
+};
+Smem smem_sizes(const AtlasMemShape* s, int C) {
+  const int e = s->window, L = C, K = C + e - 1, dphi = s->d_phi, dv = s->d_v, dk = s->d_k;
+  const int ctx = r4(C) * 3 + r4(C + e) + r4(C * e);
+  const int coefF = 2 * r4((L + 1) * K) + 3 * r4(L + 1);
+  const int coefA = 3 * r4(L + 1) + 2 * r4((L + 1) * L);
+  Smem m{};
+  m.f1 = 4 * (size_t)(ctx + r4(K * dphi) + r4(K * dv) + coefF + kStageFloats);
+  m.f3 = 4 * (size_t)(ctx + r4(K * dphi) + r4(K * dv) + r4(L * dphi) + r4(L * K) + coefF + kStageFloats);
+  m.b1 = 4 * (size_t)(ctx + r4(L * dphi) + r4(L * dv) + coefA + kStageFloats);
+  m.b3 = 4 * (size_t)(ctx + r4(K * dphi) + 2 * r4(K * dv) + r4(L * dphi) + r4(L * dv) + 2 * r4(L * K) +
+                      r4((L + 2) * (K + 2)) + coefF + coefA + 2 * r4(K) + r4(K * L) + r4(3 * L) + r4(K) + 32 +
+                      kStageFloats);
+  m.fin = 4 * (size_t)(r4(kFinTile * dv) + kStageFloats);
+  m.dsref = 4 * (size_t)kStageFloats;
+  m.bufout = 4 * (size_t)(dphi + dv + 32);
+  m.fmf = 4 * (size_t)(r4(kFmTile * dk) + kStageFloats);
+  m.fmb = 4 * (size_t)(2 * r4(kFmTile * dk) + r4(kFmTile * dphi) + kStageFloats);
+  return m;
+}
+
+int max_smem_optin() {
+  int dev = 0, v = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  if (cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess) return 0;
+  return v;
+}
+
+// Raise the dynamic shared-memory cap of every kernel once per device.
+std::mutex g_attr_mu;
+bool g_attr_done[64];
+int ensure_attrs() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return ATLAS_ERR_LAUNCH;
+  std::lock_guard<std::mutex> lk(g_attr_mu);
+  if (dev < 64 && g_attr_done[dev]) return ATLAS_OK;
+  const int mx = max_smem_optin();
+  const void* ks[] = {(const void*)k_fwd_chunk,   (const void*)k_fwd_out,      (const void*)k_bwd_chunk,
+                      (const void*)k_bwd_grads,   (const void*)k_bwd_finalize, (const void*)k_bwd_dsref,
+                      (const void*)k_bwd_bufout,  (const void*)k_fmap_tensor_fwd, (const void*)k_fmap_tensor_bwd};
+  for (const void* k : ks)
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, mx) != cudaSuccess)
+      return ATLAS_ERR_LAUNCH;
+  if (dev < 64) g_attr_done[dev] = true;
+  return ATLAS_OK;
+}
+
+int validate_shape(const AtlasMemShape* s) {
+  if (!s) return ATLAS_ERR_INVALID_ARG;
+  if (s->N < 1 || s->T < 1 || s->d_k < 1 || s->d_phi < 1 || s->d_v < 1 || s->window < 1)
+    return ATLAS_ERR_INVALID_ARG;
+  if (s->fmap_mode < 0 || s->fmap_mode > 2 || s->gate_mode < 0 || s->gate_mode > 2) return ATLAS_ERR_INVALID_ARG;
+  if (s->dtype_io != ATLAS_F32 && s->dtype_io != ATLAS_BF16) return ATLAS_ERR_INVALID_ARG;
+  if (s->momentum != 0 && s->momentum != 1) return ATLAS_ERR_INVALID_ARG;
+  if (s->fmap_mode != ATLAS_FMAP_TENSOR && s->d_phi != s->d_k) return ATLAS_ERR_INVALID_ARG;
+  if (s->fmap_mode == ATLAS_FMAP_TENSOR && s->fmap_degree <= 1) return ATLAS_ERR_INVALID_ARG;
+  if (s->d_phi > 256 || s->d_v > 256 || s->d_k > 256) return ATLAS_ERR_UNSUPPORTED;
+  if (s->N > 65535 || s->T > (int64_t)1 << 30) return ATLAS_ERR_UNSUPPORTED;
+  const int C = chunk_of(s);
+  if (C < 1 || C > 64 || C < s->window - 1 || C + s->window > 127) return ATLAS_ERR_UNSUPPORTED;
+  if ((int64_t)s->N * s->T * (s->d_v > s->d_phi ? s->d_v : s->d_phi) > ((int64_t)1 << 40)) return ATLAS_ERR_UNSUPPORTED;
+  const Smem m = smem_sizes(s, C);
+  const size_t mx = (size_t)max_smem_optin();
+  if (mx == 0) return ATLAS_ERR_LAUNCH;
+  const size_t big[] = {m.f1, m.f3, m.b1, m.b3, m.fin, m.fmf, m.fmb};
+  for (size_t b : big)
+    if (b > mx) return ATLAS_ERR_UNSUPPORTED;
+  return ATLAS_OK;
+}
+
+int validate_fwd(const AtlasMemShape* s, const AtlasMemFwd* f, bool need_outputs) {
+  if (!f) return ATLAS_ERR_INVALID_ARG;
+  if (!f->k || !f->q || !f->v || !f->lr || !f->decay || !f->S_ref || !f->S0) return ATLAS_ERR_INVALID_ARG;
+  if (s->momentum && !f->beta) return ATLAS_ERR_INVALID_ARG;
+  if (s->gate_mode != ATLAS_GATE_NONE && !f->gate) return ATLAS_ERR_INVALID_ARG;
+  if (s->fmap_mode == ATLAS_FMAP_TENSOR && !f->proj) return ATLAS_ERR_INVALID_ARG;
+  if (need_outputs && (!f->y || !f->S_end)) return ATLAS_ERR_INVALID_ARG;
+  return ATLAS_OK;
+}
+
+Params make_params(const AtlasMemShape* s, const Layout& L, const AtlasMemFwd* f, const AtlasMemBwd* b,
+                   const void* saved, void* scratch) {
+  Params P{};
+  P.N = (int)s->N; P.T = (int)s->T; P.dk = s->d_k; P.dphi = s->d_phi; P.dv = s->d_v; P.e = s->window;
+  P.fmode = s->fmap_mode; P.fdeg = s->fmap_degree; P.gmode = s->gate_mode; P.mom = s->momentum;
+  P.bf = s->dtype_io == ATLAS_BF16; P.C = L.C; P.nch = L.nch;
+  if (f) {
+    P.k = f->k; P.q = f->q; P.v = f->v; P.lr = f->lr; P.decay = f->decay; P.beta = s->momentum ? f->beta : nullptr;
+    P.gate = f->gate; P.Sref = f->S_ref; P.S0 = f->S0; P.Z0 = s->momentum ? f->Z0 : nullptr;
+    P.buf = s->window > 1 ? f->buf_in : nullptr; P.proj = f->proj;
+    P.y = f->y; P.S_end = f->S_end; P.Z_end = s->momentum ? f->Z_end : nullptr; P.buf_out = f->buf_out;
+  }
+  if (b) {
+    P.dy = b->dy; P.dS_end = b->dS_end; P.dZ_end = s->momentum ? b->dZ_end : nullptr;
+    P.dbuf_out = s->window > 1 ? b->dbuf_out : nullptr;
+    P.dk_ = b->dk; P.dq_ = b->dq; P.dv_ = b->dv; P.dlr = b->dlr; P.ddecay = b->ddecay;
+    P.dbeta = s->momentum ? b->dbeta : nullptr; P.dgate = s->gate_mode != ATLAS_GATE_NONE ? b->dgate : nullptr;
+    P.dSref = b->dS_ref; P.dS0 = b->dS0; P.dZ0 = s->momentum ? b->dZ0 : nullptr;
+    P.dbuf = s->window > 1 ? b->dbuf_in : nullptr;
+  }
+  char* sv = (char*)const_cast<void*>(saved);
+  P.st = (float*)(sv + L.st); P.delta = (float*)(sv + L.delta); P.ST = (float*)(sv + L.ST);
+  P.cs = (float*)(sv + L.cs);
+  P.phik = s->fmap_mode == ATLAS_FMAP_TENSOR ? (float*)(sv + L.phik) : nullptr;
+  P.phiq = s->fmap_mode == ATLAS_FMAP_TENSOR ? (float*)(sv + L.phiq) : nullptr;
+  if (scratch) {
+    char* sc = (char*)scratch;
+    P.adj = (float*)(sc + L.adj); P.acs = (float*)(sc + L.acs); P.dpsi = (float*)(sc + L.dpsi);
+    P.ddel = (float*)(sc + L.ddel); P.dphiR = (float*)(sc + L.dphiR); P.hdd = (float*)(sc + L.hdd);
+    P.hdp = (float*)(sc + L.hdp); P.du = (float*)(sc + L.du); P.hdu = (float*)(sc + L.hdu);
+  }
+  P.apply_mask = 1;
+  return P;
+}
+
+// ---- launch accounting and optional per-kernel CUDA-event timing ----------
+enum KernelId {
+  KID_FMAP_FWD, KID_FWD_CHUNK, KID_FWD_SCAN, KID_FWD_OUT, KID_BUF_OUT, KID_BWD_CHUNK, KID_BWD_SCAN,
+  KID_BWD_GRADS, KID_BWD_BUFOUT, KID_BWD_FINAL, KID_BWD_DSREF, KID_FMAP_BWD, KID_COUNT
+};
+const char* const kKernelNames[KID_COUNT] = {
+  "k_fmap_tensor_fwd", "k_fwd_chunk", "k_fwd_scan", "k_fwd_out", "k_buf_out", "k_bwd_chunk", "k_bwd_scan",
+  "k_bwd_grads", "k_bwd_bufout", "k_bwd_finalize", "k_bwd_dsref", "k_fmap_tensor_bwd"};
+
+constexpr int kMaxTimed = 8192;
+struct Prof {
+  std::mutex mu;
+  bool timing = false;
+  long long launches = 0;
+  int pending = 0;
+  cudaEvent_t ev[2 * kMaxTimed];
+  bool ev_ready = false;
+  int kid[kMaxTimed];
+  double ms[KID_COUNT] = {};
+  long long cnt[KID_COUNT] = {};
+};
+Prof g_prof;
+
+void prof_collect_locked() {
+  for (int i = 0; i < g_prof.pending; ++i) {
+    float ms = 0.f;
+    cudaEventSynchronize(g_prof.ev[2 * i + 1]);
+    cudaEventElapsedTime(&ms, g_prof.ev[2 * i], g_prof.ev[2 * i + 1]);
+    g_prof.ms[g_prof.kid[i]] += ms;
+    g_prof.cnt[g_prof.kid[i]] += 1;
+  }
+  g_prof.pending = 0;
+}
+
+int prof_begin(int kid, cudaStream_t st) {
+  std::lock_guard<std::mutex> lk(g_prof.mu);
+  g_prof.launches++;
+  if (!g_prof.timing) return -1;
+  if (g_prof.pending == kMaxTimed) prof_collect_locked();
+  const int i = g_prof.pending++;
+  g_prof.kid[i] = kid;
+  cudaEventRecord(g_prof.ev[2 * i], st);
+  return i;
+}
+void prof_end(int slot, cudaStream_t st) {
+  if (slot < 0) return;
+  std::lock_guard<std::mutex> lk(g_prof.mu);
+  cudaEventRecord(g_prof.ev[2 * slot + 1], st);
+}
+
+#define LAUNCH_CHECK()                                              \
+  do {                                                              \
+    if (cudaGetLastError() != cudaSuccess) return ATLAS_ERR_LAUNCH; \
+  } while (0)
+
+// Launch `kernel` with accounting: LAUNCH(id, kernel, grid, smem, stream, args...)
+#define LAUNCH(KID, KERNEL, GRID, SMEM, STREAM, ...)              \
+  do {                                                            \
+    const int slot_ = prof_begin(KID, STREAM);                    \
+    KERNEL<<<GRID, kThreads, SMEM, STREAM>>>(__VA_ARGS__);        \
+    LAUNCH_CHECK();                                               \
+    prof_end(slot_, STREAM);                                      \
+  } while (0)
+
+int run_fwd_local(const AtlasMemShape* s, const Params& P, cudaStream_t st) {
+  const Smem m = smem_sizes(s, P.C);
+  const dim3 gch(P.nch, P.N);
+  if (P.fmode == ATLAS_FMAP_TENSOR) {
+    LAUNCH(KID_FMAP_FWD, k_fmap_tensor_fwd, dim3((P.T + kFmTile - 1) / kFmTile, P.N, 2), m.fmf, st, P);
+  }
+  LAUNCH(KID_FWD_CHUNK, k_fwd_chunk, gch, m.f1, st, P);
+  return ATLAS_OK;
+}
+
+int run_fwd_finish(const AtlasMemShape* s, const Params& P, cudaStream_t st) {
+  const Smem m = smem_sizes(s, P.C);
+  const int64_t D2 = (int64_t)P.dv * P.dphi;
+  LAUNCH(KID_FWD_SCAN, k_fwd_scan, dim3((unsigned)((D2 + kThreads - 1) / kThreads), P.N), 0, st, P, 0);
+  LAUNCH(KID_FWD_OUT, k_fwd_out, dim3(P.nch, P.N), m.f3, st, P);
+  if (P.e > 1 && P.buf_out) {
+    LAUNCH(KID_BUF_OUT, k_buf_out, dim3(P.e - 1, P.N), 0, st, P);
+  }
+  return ATLAS_OK;
+}
+
+int run_bwd_local(const AtlasMemShape* s, const Params& P, cudaStream_t st) {
+  const Smem m = smem_sizes(s, P.C);
+  LAUNCH(KID_BWD_CHUNK, k_bwd_chunk, dim3(P.nch, P.N), m.b1, st, P);
+  return ATLAS_OK;
+}
+
+int run_bwd_finish(const AtlasMemShape* s, const Params& P, cudaStream_t st) {
+  const Smem m = smem_sizes(s, P.C);
+  const int64_t D2 = (int64_t)P.dv * P.dphi;
+  LAUNCH(KID_BWD_SCAN, k_bwd_scan, dim3((unsigned)((D2 + kThreads - 1) / kThreads), P.N), 0, st, P, 0);
+  LAUNCH(KID_BWD_GRADS, k_bwd_grads, dim3(P.nch, P.N), m.b3, st, P);
+  if (P.e > 1 && P.dbuf_out) {
+    LAUNCH(KID_BWD_BUFOUT, k_bwd_bufout, dim3(P.e - 1, P.N), m.bufout, st, P);
+  }
+  LAUNCH(KID_BWD_FINAL, k_bwd_finalize, dim3((P.T + kFinTile - 1) / kFinTile, P.N), m.fin, st, P);
+  if (P.dSref) {
+    const int tiles = ((P.dv + 63) / 64) * ((P.dphi + 63) / 64);
+    LAUNCH(KID_BWD_DSREF, k_bwd_dsref, dim3(tiles, P.N), m.dsref, st, P);
+  }
+  if (P.fmode == ATLAS_FMAP_TENSOR && (P.dk_ || P.dq_)) {
+    LAUNCH(KID_FMAP_BWD, k_fmap_tensor_bwd, dim3((P.T + kFmTile - 1) / kFmTile, P.N, 2), m.fmb, st, P);
+  }
+  return ATLAS_OK;
+}
+
+int check_ws(const Layout& L, const void* saved, size_t saved_bytes, const void* scratch, size_t scratch_bytes,
+             bool need_scratch) {
+  if (!saved || saved_bytes < L.saved) return ATLAS_ERR_WORKSPACE;
+  if (need_scratch && (!scratch || scratch_bytes < L.bwd)) return ATLAS_ERR_WORKSPACE;
+  return ATLAS_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int atlas_mem_abi_version(void) { return ATLAS_MEM_ABI_VERSION; }
+
+const char* atlas_mem_error_string(int code) {
+  switch (code) {
+    case ATLAS_OK: return "ok";
+    case ATLAS_ERR_INVALID_ARG: return "invalid argument (null pointer, bad enum or inconsistent sizes)";
+    case ATLAS_ERR_UNSUPPORTED: return "unsupported shape (head size > 256, window too large, or shared memory)";
+    case ATLAS_ERR_WORKSPACE: return "workspace missing or smaller than atlas_mem_workspace_size()";
+    case ATLAS_ERR_LAUNCH: return "CUDA kernel launch failed";
+    case ATLAS_ERR_DEVICE: return "device-side status reported a fault";
+    default: return "unknown error";
+  }
+}
+
+int atlas_mem_workspace_size(const AtlasMemShape* shape, size_t* saved, size_t* fwd_scratch, size_t* bwd_scratch) {
+  const int v = validate_shape(shape);
+  if (v) return v;
+  const Layout L = make_layout(shape);
+  if (saved) *saved = L.saved;
+  if (fwd_scratch) *fwd_scratch = L.fwd;
+  if (bwd_scratch) *bwd_scratch = L.bwd;
+  return ATLAS_OK;
+}
+
+int atlas_mem_forward(const AtlasMemShape* shape, const AtlasMemFwd* fwd, void* saved, size_t saved_bytes,
+                      void* scratch, size_t scratch_bytes, void* stream) {
+  (void)scratch; (void)scratch_bytes;
+  int v = validate_shape(shape);
+  if (!v) v = validate_fwd(shape, fwd, true);
+  if (v) return v;
+  const Layout L = make_layout(shape);
+  if ((v = check_ws(L, saved, saved_bytes, nullptr, 0, false))) return v;
+  if ((v = ensure_attrs())) return v;
+  const Params P = make_params(shape, L, fwd, nullptr, saved, nullptr);
+  cudaStream_t st = (cudaStream_t)stream;
+  if ((v = run_fwd_local(shape, P, st))) return v;
+  return run_fwd_finish(shape, P, st);
+}
+
+int atlas_mem_backward(const AtlasMemShape* shape, const AtlasMemFwd* fwd, const AtlasMemBwd* bwd,
+                       const void* saved, size_t saved_bytes, void* scratch, size_t scratch_bytes, void* stream) {
+  int v = validate_shape(shape);
+  if (!v) v = validate_fwd(shape, fwd, false);
+  if (v) return v;
+  if (!bwd || !bwd->dy) return ATLAS_ERR_INVALID_ARG;
+  const Layout L = make_layout(shape);
+  if ((v = check_ws(L, saved, saved_bytes, scratch, scratch_bytes, true))) return v;
+  if ((v = ensure_attrs())) return v;
+  const Params P = make_params(shape, L, fwd, bwd, saved, scratch);
+  cudaStream_t st = (cudaStream_t)stream;
+  if ((v = run_bwd_local(shape, P, st))) return v;
+  return run_bwd_finish(shape, P, st);
+}
+
+int atlas_mem_forward_local(const AtlasMemShape* shape, const AtlasMemFwd* fwd, void* saved, size_t saved_bytes,
+                            void* scratch, size_t scratch_bytes, float* seg_coef, float* seg_dS, float* seg_dZ,
+                            void* stream) {
+  (void)scratch; (void)scratch_bytes;
+  int v = validate_shape(shape);
+  if (!v) v = validate_fwd(shape, fwd, false);
+  if (v) return v;
+  if (shape->window != 1 || !seg_coef || !seg_dS || !seg_dZ) return ATLAS_ERR_INVALID_ARG;
+  const Layout L = make_layout(shape);
+  if ((v = check_ws(L, saved, saved_bytes, nullptr, 0, false))) return v;
+  if ((v = ensure_attrs())) return v;
+  Params P = make_params(shape, L, fwd, nullptr, saved, nullptr);
+  P.seg_coef = seg_coef; P.seg_dS = seg_dS; P.seg_dZ = seg_dZ;
+  cudaStream_t st = (cudaStream_t)stream;
+  if ((v = run_fwd_local(shape, P, st))) return v;
+  const int64_t D2 = (int64_t)P.dv * P.dphi;
+  LAUNCH(KID_FWD_SCAN, k_fwd_scan, dim3((unsigned)((D2 + kThreads - 1) / kThreads), P.N), 0, st, P, 1);
+  return ATLAS_OK;
+}
+
+int atlas_mem_forward_finish(const AtlasMemShape* shape, const AtlasMemFwd* fwd, void* saved, size_t saved_bytes,
+                             void* scratch, size_t scratch_bytes, void* stream) {
+  (void)scratch; (void)scratch_bytes;
+  int v = validate_shape(shape);
+  if (!v) v = validate_fwd(shape, fwd, true);
+  if (v) return v;
+  if (shape->window != 1) return ATLAS_ERR_INVALID_ARG;
+  const Layout L = make_layout(shape);
+  if ((v = check_ws(L, saved, saved_bytes, nullptr, 0, false))) return v;
+  if ((v = ensure_attrs())) return v;
+  const Params P = make_params(shape, L, fwd, nullptr, saved, nullptr);
+  return run_fwd_finish(shape, P, (cudaStream_t)stream);
+}
+
+int atlas_mem_backward_local(const AtlasMemShape* shape, const AtlasMemFwd* fwd, const AtlasMemBwd* bwd,
+                             const void* saved, size_t saved_bytes, void* scratch, size_t scratch_bytes,
+                             float* seg_coef, float* seg_dS, float* seg_dZ, void* stream) {
+  int v = validate_shape(shape);
+  if (!v) v = validate_fwd(shape, fwd, false);
+  if (v) return v;
+  if (!bwd || !bwd->dy || shape->window != 1 || !seg_coef || !seg_dS || !seg_dZ) return ATLAS_ERR_INVALID_ARG;
+  const Layout L = make_layout(shape);
+  if ((v = check_ws(L, saved, saved_bytes, scratch, scratch_bytes, true))) return v;
+  if ((v = ensure_attrs())) return v;
+  Params P = make_params(shape, L, fwd, bwd, saved, scratch);
+  P.seg_coef = seg_coef; P.seg_dS = seg_dS; P.seg_dZ = seg_dZ;
+  cudaStream_t st = (cudaStream_t)stream;
+  if ((v = run_bwd_local(shape, P, st))) return v;
+  const int64_t D2 = (int64_t)P.dv * P.dphi;
+  LAUNCH(KID_BWD_SCAN, k_bwd_scan, dim3((unsigned)((D2 + kThreads - 1) / kThreads), P.N), 0, st, P, 1);
+  return ATLAS_OK;
+}
+
+int atlas_mem_backward_finish(const AtlasMemShape* shape, const AtlasMemFwd* fwd, const AtlasMemBwd* bwd,
+                              const void* saved, size_t saved_bytes, void* scratch, size_t scratch_bytes,
+                              int apply_clamp_mask, void* stream) {
+  int v = validate_shape(shape);
+  if (!v) v = validate_fwd(shape, fwd, false);
+  if (v) return v;
+  if (!bwd || !bwd->dy || shape->window != 1) return ATLAS_ERR_INVALID_ARG;
+  const Layout L = make_layout(shape);
+  if ((v = check_ws(L, saved, saved_bytes, scratch, scratch_bytes, true))) return v;
+  if ((v = ensure_attrs())) return v;
+  Params P = make_params(shape, L, fwd, bwd, saved, scratch);
+  P.apply_mask = apply_clamp_mask ? 1 : 0;
+  return run_bwd_finish(shape, P, (cudaStream_t)stream);
+}
+
+int atlas_mem_profile_enable(int on) {
+  std::lock_guard<std::mutex> lk(g_prof.mu);
+  if (on && !g_prof.ev_ready) {
+    for (int i = 0; i < 2 * kMaxTimed; ++i)
+      if (cudaEventCreate(&g_prof.ev[i]) != cudaSuccess) return ATLAS_ERR_LAUNCH;
+    g_prof.ev_ready = true;
+  }
+  if (g_prof.pending) prof_collect_locked();
+  g_prof.timing = on != 0;
+  g_prof.launches = 0;
+  for (int k = 0; k < KID_COUNT; ++k) { g_prof.ms[k] = 0.0; g_prof.cnt[k] = 0; }
+  return ATLAS_OK;
+}
+
+int atlas_mem_profile_read(int kernel_id, double* total_ms, long long* launches) {
+  if (kernel_id < 0 || kernel_id >= KID_COUNT) return ATLAS_ERR_INVALID_ARG;
+  std::lock_guard<std::mutex> lk(g_prof.mu);
+  if (g_prof.pending) prof_collect_locked();
+  if (total_ms) *total_ms = g_prof.ms[kernel_id];
+  if (launches) *launches = g_prof.cnt[kernel_id];
+  return ATLAS_OK;
+}
+
+long long atlas_mem_launch_count(void) {
+  std::lock_guard<std::mutex> lk(g_prof.mu);
+  return g_prof.launches;
+}
+
+int atlas_mem_kernel_count(void) { return KID_COUNT; }
+
+const char* atlas_mem_kernel_name(int kernel_id) {
+  return (kernel_id >= 0 && kernel_id < KID_COUNT) ? kKernelNames[kernel_id] : "";
+}
+
+}  // extern "C"

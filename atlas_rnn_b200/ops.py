@@ -1,0 +1,153 @@
+"""Autograd boundary of the memory recurrence over the C ABI.
+
+``memory_recurrence`` is the functional form of the block the reference cells
+run inside ``_forward_impl`` (rnn_memory.py:345-393 Titans, :655-717 Omega)
+and of ``AtlasOmegaFunction.apply`` (cuda/atlas_omega_autograd.py:98-204),
+taking the per-head raw q/k (the feature map is applied in the kernels).
+All arithmetic happens in libatlas_mem.so on the caller's current CUDA stream;
+this file only checks arguments, allocates outputs / workspaces with torch and
+passes pointers.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import torch
+from torch import Tensor
+
+from . import _lib
+
+
+@dataclass(frozen=True)
+class Spec:
+    window: int = 1
+    gate_mode: int = _lib.GATE_NONE
+    fmap_mode: str = "off"
+    fmap_degree: int = 1
+    momentum: bool = True
+    chunk: int = 0
+
+
+def _shape(spec: Spec, k: Tensor, v: Tensor, d_phi: int) -> _lib.Shape:
+    N, T, dk = k.shape
+    return _lib.Shape(N=N, T=T, d_k=dk, d_phi=d_phi, d_v=v.shape[-1], window=spec.window,
+                      fmap_mode=_lib.FMAP[spec.fmap_mode], fmap_degree=spec.fmap_degree,
+                      gate_mode=spec.gate_mode, momentum=int(spec.momentum),
+                      dtype_io=_lib.BF16 if k.dtype == torch.bfloat16 else _lib.F32, chunk=spec.chunk)
+
+
+def _stream(dev) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+
+
+class MemoryRecurrenceFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, spec: Spec, k, q, v, lr, decay, beta, gate, S_ref, S0, Z0, buf, proj):
+        dev = k.device
+        N, T, _ = k.shape
+        d_phi = S_ref.shape[-1]
+        d_v = v.shape[-1]
+        shape = _shape(spec, k, v, d_phi)
+        saved_b, _, bwd_b = _lib.workspace_sizes(shape)
+        saved = torch.empty(max(saved_b, 1), dtype=torch.uint8, device=dev)
+        y = torch.empty(N, T, d_v, dtype=k.dtype, device=dev)
+        S_end = torch.empty(N, d_v, d_phi, dtype=torch.float32, device=dev)
+        Z_end = torch.empty_like(S_end) if spec.momentum else S_end.new_empty(0)
+        e = spec.window
+        buf_out = (torch.empty(N, e - 1, d_v, d_phi, dtype=torch.float32, device=dev) if e > 1
+                   else S_end.new_empty(0))
+        p = _lib.ptr
+        fwd = _lib.Fwd(k=p(k), q=p(q), v=p(v), lr=p(lr), decay=p(decay), beta=p(beta), gate=p(gate),
+                       S_ref=p(S_ref), S0=p(S0), Z0=p(Z0), buf_in=p(buf), proj=p(proj), y=p(y),
+                       S_end=p(S_end), Z_end=p(Z_end) if spec.momentum else None,
+                       buf_out=p(buf_out) if e > 1 else None)
+        _lib.check(_lib.lib().atlas_mem_forward(ctypes.byref(shape), ctypes.byref(fwd), p(saved),
+                                                 saved.numel(), None, 0, _stream(dev)), "forward")
+        ctx.spec, ctx.shape, ctx.bwd_bytes = spec, shape, bwd_b
+        ctx.saved_ws = saved
+        ctx.save_for_backward(k, q, v, lr, decay, beta, gate, S_ref, S0, Z0, buf, proj)
+        ctx.mark_non_differentiable(*([] if spec.momentum else [Z_end]), *([] if e > 1 else [buf_out]))
+        return y, S_end, Z_end, buf_out
+
+    @staticmethod
+    def backward(ctx, dy, dS_end, dZ_end, dbuf_out):
+        k, q, v, lr, decay, beta, gate, S_ref, S0, Z0, buf, proj = ctx.saved_tensors
+        spec, shape = ctx.spec, ctx.shape
+        dev = k.device
+        need = ctx.needs_input_grad  # (spec, k, q, v, lr, decay, beta, gate, S_ref, S0, Z0, buf, proj)
+        if dy is None:
+            dy = torch.zeros(k.shape[0], k.shape[1], v.shape[-1], dtype=k.dtype, device=dev)
+        dy = dy.to(k.dtype).contiguous()
+        f32c = lambda t: None if t is None or t.numel() == 0 else t.float().contiguous()
+        dS_end, dZ_end, dbuf_out = f32c(dS_end), f32c(dZ_end), f32c(dbuf_out)
+        e = spec.window
+
+        def out_like(t, flag):
+            return torch.empty_like(t) if (t is not None and flag) else None
+
+        dk, dq, dv = out_like(k, need[1]), out_like(q, need[2]), out_like(v, need[3])
+        dlr, ddecay = out_like(lr, need[4]), out_like(decay, need[5])
+        dbeta, dgate = out_like(beta, need[6]), out_like(gate, need[7])
+        dS_ref, dS0 = out_like(S_ref, need[8]), out_like(S0, need[9])
+        dZ0 = out_like(Z0, need[10])
+        dbuf = None
+        if e > 1 and need[11] and buf is not None:
+            dbuf = torch.empty_like(buf)
+        scratch = torch.empty(max(ctx.bwd_bytes, 1), dtype=torch.uint8, device=dev)
+        p = _lib.ptr
+        fwd = _lib.Fwd(k=p(k), q=p(q), v=p(v), lr=p(lr), decay=p(decay), beta=p(beta), gate=p(gate),
+                       S_ref=p(S_ref), S0=p(S0), Z0=p(Z0), buf_in=p(buf), proj=p(proj))
+        bwd = _lib.Bwd(dy=p(dy), dS_end=p(dS_end), dZ_end=p(dZ_end), dbuf_out=p(dbuf_out), dk=p(dk),
+                       dq=p(dq), dv=p(dv), dlr=p(dlr), ddecay=p(ddecay), dbeta=p(dbeta), dgate=p(dgate),
+                       dS_ref=p(dS_ref), dS0=p(dS0), dZ0=p(dZ0), dbuf_in=p(dbuf))
+        saved = ctx.saved_ws
+        _lib.check(_lib.lib().atlas_mem_backward(ctypes.byref(shape), ctypes.byref(fwd), ctypes.byref(bwd),
+                                                  p(saved), saved.numel(), p(scratch), scratch.numel(),
+                                                  _stream(dev)), "backward")
+        return (None, dk, dq, dv, dlr, ddecay, dbeta, dgate, dS_ref, dS0, dZ0, dbuf, None)
+
+
+def _io(t: Tensor | None, dtype) -> Tensor | None:
+    return None if t is None else t.to(dtype).contiguous()
+
+
+def memory_recurrence(k: Tensor, q: Tensor, v: Tensor, lr: Tensor, decay: Tensor,
+                      beta: Tensor | None = None, gate: Tensor | None = None, *, S_ref: Tensor,
+                      S0: Tensor, Z0: Tensor | None = None, omega_buffer: Tensor | None = None,
+                      window: int = 1, gate_mode: str | None = None, fmap_mode: str = "off",
+                      fmap_degree: int = 1, proj: Tensor | None = None, chunk: int = 0):
+    """Memory recurrence over N = batch*heads units.
+
+    k, q [N,T,d_k]; v [N,T,d_v]; lr (eta), decay (alpha), beta [N,T]; gate [N,T]
+    (gate_mode 'token', the reference's omega gate u) or [N,T,e] (gate_mode
+    'window', per-position window weights U[t, j] on the term of token t-j);
+    S_ref, S0, Z0 [N,d_v,d_phi]; omega_buffer [N,e-1,d_v,d_phi].
+    Returns (y [N,T,d_v], S_end (clamped to +-100), Z_end or None, new omega buffer or None).
+    io tensors run in bfloat16 when k is bfloat16, else float32; states in float32.
+    """
+    if not k.is_cuda:
+        raise RuntimeError("atlas_rnn_b200.memory_recurrence: tensors must be on a CUDA device "
+                           "(the library has no CPU path)")
+    io = torch.bfloat16 if k.dtype == torch.bfloat16 else torch.float32
+    if gate is None:
+        gm = _lib.GATE_NONE
+    elif gate_mode == "window" or (gate_mode is None and gate.dim() == 3):
+        gm = _lib.GATE_WINDOW
+    else:
+        gm = _lib.GATE_TOKEN
+    momentum = beta is not None
+    spec = Spec(window=window, gate_mode=gm, fmap_mode=fmap_mode if fmap_degree > 1 else "off",
+                fmap_degree=fmap_degree, momentum=momentum, chunk=chunk)
+    state_dtype = S0.dtype
+    f32 = lambda t: None if t is None else t.to(torch.float32).contiguous()
+    Z0c = f32(Z0) if momentum else None
+    buf = f32(omega_buffer) if window > 1 else None
+    projc = f32(proj) if spec.fmap_mode == "tensor" else None
+    y, S_end, Z_end, buf_out = MemoryRecurrenceFn.apply(
+        spec, _io(k, io), _io(q, io), _io(v, io), _io(lr, io), _io(decay, io), _io(beta, io),
+        _io(gate, io), f32(S_ref), f32(S0), Z0c, buf, projc)
+    S_end = S_end.to(state_dtype)
+    Z_end = Z_end.to(state_dtype) if momentum else None
+    buf_out = buf_out.to(state_dtype) if window > 1 else None
+    return y, S_end, Z_end, buf_out

@@ -1,0 +1,198 @@
+/*
+ * atlas_mem.h -- C ABI of the B200 memory-update library (libatlas_mem.so).
+ *
+ * The library computes the Titans-RNN / OmegaNet-RNN memory recurrence of
+ * atlas_pytorch/rnn_memory.py for N = batch*heads independent units:
+ *
+ *   phi_t = fmap(k_t), psi_t = fmap(q_t)                     rnn_memory.py:637-642
+ *   delta_t = S_ref phi_t - v_t                                rnn_memory.py:659-660
+ *   g_t = sum_{j<e} W(t, t-j) delta_{t-j} phi_{t-j}^T          rnn_memory.py:663-687
+ *   Z_t = beta_t Z_{t-1} + g_t                                 rnn_memory.py:698
+ *   S_t = alpha_t S_{t-1} - eta_t Z_t                          rnn_memory.py:699-700
+ *   y_t = S_{t-1} psi_t                                        rnn_memory.py:712-717
+ *   S_end = clamp(S_T, -100, 100), Z_end = Z_T                 rnn_memory.py:701-702
+ *   buf_out = last e-1 window terms                            rnn_memory.py:684
+ *
+ * with forward and backward. It replaces the reference's kernel-level entry
+ * AtlasOmegaFunction.apply(phi_k, phi_q, v, S_ref, lr, decay, beta, gate, S0, Z0)
+ * (atlas_pytorch/cuda/atlas_omega_autograd.py:98-153) and its pybind entries
+ * forward_exact / backward_exact (atlas_pytorch/cuda/atlas_omega.cpp:139-142),
+ * generalised to every window e, head size, feature map and momentum setting,
+ * and with the PyTorch path's semantics (clamped S_end, carried omega buffer).
+ *
+ * Conventions
+ *  - Every pointer is a device pointer to a dense row-major (contiguous) array.
+ *  - Token-major tensors are [N, T, dim]; per-token scalars are [N, T];
+ *    window gates are [N, T, e]; states are [N, d_v, d_phi]; the omega buffer
+ *    is [N, e-1, d_v, d_phi]; the tensor feature-map projection is
+ *    [d_k + d_k*d_k, d_phi].
+ *  - "io" tensors (k, q, v, gates, y and their gradients) are float32 or
+ *    bfloat16 (dtype_io); states, buffers and their gradients are float32.
+ *  - The library never allocates: the caller passes workspaces sized by
+ *    atlas_mem_workspace_size(). The "saved" workspace is written by the
+ *    forward and read by the backward; it must stay untouched in between.
+ *  - All work is enqueued on `stream` (a cudaStream_t; NULL = legacy default).
+ *  - Return value 0 = success, otherwise an ATLAS_ERR_* code (see
+ *    atlas_mem_error_string). Invalid arguments are rejected before any launch.
+ */
+#ifndef ATLAS_MEM_H
+#define ATLAS_MEM_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ATLAS_MEM_ABI_VERSION 1
+
+enum AtlasFmapMode { ATLAS_FMAP_OFF = 0, ATLAS_FMAP_ELEMENTWISE = 1, ATLAS_FMAP_TENSOR = 2 };
+enum AtlasGateMode { ATLAS_GATE_NONE = 0, ATLAS_GATE_TOKEN = 1, ATLAS_GATE_WINDOW = 2 };
+enum AtlasDtype { ATLAS_F32 = 0, ATLAS_BF16 = 1 };
+
+enum AtlasError {
+  ATLAS_OK = 0,
+  ATLAS_ERR_INVALID_ARG = 1,   /* null pointer / bad enum / inconsistent sizes   */
+  ATLAS_ERR_UNSUPPORTED = 2,   /* shape outside the supported envelope            */
+  ATLAS_ERR_WORKSPACE = 3,     /* workspace pointer missing or too small          */
+  ATLAS_ERR_LAUNCH = 4,        /* a kernel launch failed (cudaGetLastError)        */
+  ATLAS_ERR_DEVICE = 5         /* device-side status word reported a fault         */
+};
+
+/* Shapes and modes of one call. Mirrors the constructor arguments of
+ * RNNMemoryCell / OmegaRNNMemoryCell (rnn_memory.py:167-179, 426-441). */
+typedef struct AtlasMemShape {
+  int64_t N;          /* batch * heads                                         */
+  int64_t T;          /* tokens in this call                                   */
+  int32_t d_k;        /* raw key/query width (dim_head)                        */
+  int32_t d_phi;      /* feature width (= d_k unless fmap is 'tensor')         */
+  int32_t d_v;        /* value width                                           */
+  int32_t window;     /* omega window e >= 1                                   */
+  int32_t fmap_mode;  /* AtlasFmapMode                                         */
+  int32_t fmap_degree;/* polynomial degree g (elementwise: phi = sum x^i)      */
+  int32_t gate_mode;  /* AtlasGateMode                                         */
+  int32_t momentum;   /* 1 = use_momentum (beta/Z present), 0 = off            */
+  int32_t dtype_io;   /* AtlasDtype of k, q, v, gates, y and their gradients   */
+  int32_t chunk;      /* internal token chunk; 0 = library default             */
+} AtlasMemShape;
+
+/* Forward operands. Optional pointers may be NULL: beta (momentum off),
+ * gate (gate_mode NONE), Z0 (zeros), buf_in (zeros), proj (fmap != TENSOR),
+ * Z_end (momentum off), buf_out (window 1). */
+typedef struct AtlasMemFwd {
+  const void* k;       /* [N,T,d_k]  io                                         */
+  const void* q;       /* [N,T,d_k]  io                                         */
+  const void* v;       /* [N,T,d_v]  io                                         */
+  const void* lr;      /* [N,T]      io  eta   (to_lr, rnn_memory.py:645)       */
+  const void* decay;   /* [N,T]      io  alpha (to_decay, :646)                 */
+  const void* beta;    /* [N,T]      io  (to_momentum, :649)                    */
+  const void* gate;    /* [N,T] (TOKEN) or [N,T,e] (WINDOW), io                 */
+  const float* S_ref;  /* [N,d_v,d_phi] state the deltas are taken against      */
+  const float* S0;     /* [N,d_v,d_phi] carried S                               */
+  const float* Z0;     /* [N,d_v,d_phi] carried Z                               */
+  const float* buf_in; /* [N,e-1,d_v,d_phi] carried omega buffer                */
+  const float* proj;   /* [d_k+d_k^2, d_phi] tensor feature-map projection      */
+  void* y;             /* [N,T,d_v]  io  output                                 */
+  float* S_end;        /* [N,d_v,d_phi]                                         */
+  float* Z_end;        /* [N,d_v,d_phi]                                         */
+  float* buf_out;      /* [N,e-1,d_v,d_phi]                                     */
+} AtlasMemFwd;
+
+/* Backward operands: upstream gradients in, input gradients out. Optional
+ * upstream gradients (dS_end, dZ_end, dbuf_out) may be NULL (= zeros); output
+ * gradients of absent inputs may be NULL and are then not produced. */
+typedef struct AtlasMemBwd {
+  const void* dy;        /* [N,T,d_v] io                                        */
+  const float* dS_end;   /* [N,d_v,d_phi]                                       */
+  const float* dZ_end;   /* [N,d_v,d_phi]                                       */
+  const float* dbuf_out; /* [N,e-1,d_v,d_phi]                                   */
+  void* dk;              /* [N,T,d_k] io                                        */
+  void* dq;              /* [N,T,d_k] io                                        */
+  void* dv;              /* [N,T,d_v] io                                        */
+  void* dlr;             /* [N,T] io                                            */
+  void* ddecay;          /* [N,T] io                                            */
+  void* dbeta;           /* [N,T] io                                            */
+  void* dgate;           /* [N,T] or [N,T,e] io                                 */
+  float* dS_ref;         /* [N,d_v,d_phi]                                       */
+  float* dS0;            /* [N,d_v,d_phi]                                       */
+  float* dZ0;            /* [N,d_v,d_phi]                                       */
+  float* dbuf_in;        /* [N,e-1,d_v,d_phi]                                   */
+} AtlasMemBwd;
+
+/* Library version / ABI check. */
+int atlas_mem_abi_version(void);
+
+/* Human-readable text for an AtlasError code (static storage). */
+const char* atlas_mem_error_string(int code);
+
+/* Workspace sizes in bytes for a shape: `saved` lives from forward to
+ * backward, `fwd_scratch` / `bwd_scratch` only during one call. Any output
+ * pointer may be NULL. Replaces the per-call torch.empty allocations of
+ * atlas_omega_autograd.py:125-134,175-184. */
+int atlas_mem_workspace_size(const AtlasMemShape* shape, size_t* saved,
+                             size_t* fwd_scratch, size_t* bwd_scratch);
+
+/* Forward pass (AtlasOmegaFunction.forward, atlas_omega_autograd.py:98-153;
+ * semantics of OmegaRNNMemoryCell._forward_impl, rnn_memory.py:655-730). */
+int atlas_mem_forward(const AtlasMemShape* shape, const AtlasMemFwd* fwd,
+                      void* saved, size_t saved_bytes,
+                      void* scratch, size_t scratch_bytes, void* stream);
+
+/* Backward pass (AtlasOmegaFunction.backward, atlas_omega_autograd.py:155-204;
+ * gradients of the PyTorch path's autograd). `fwd` must hold the same
+ * forward operands (outputs may be NULL) and `saved` the forward's workspace. */
+int atlas_mem_backward(const AtlasMemShape* shape, const AtlasMemFwd* fwd,
+                       const AtlasMemBwd* bwd, const void* saved, size_t saved_bytes,
+                       void* scratch, size_t scratch_bytes, void* stream);
+
+/* ---- sequence-parallel pieces (no reference counterpart: the reference has
+ * no distributed code). A rank holding tokens [t_lo, t_hi) of a longer
+ * sequence runs *_local, exchanges the per-unit segment transforms with the
+ * other ranks (the host does this over NCCL), then runs *_finish with the
+ * incoming carry. The segment transform of a rank is
+ *   (S, Z) -> (a*S + b*Z + dS, c*Z + dZ)
+ * with per-unit scalars coef[N,3] = (a, b, c) and matrices dS, dZ [N,d_v,d_phi].
+ * Requires window == 1 (no cross-rank halo). */
+int atlas_mem_forward_local(const AtlasMemShape* shape, const AtlasMemFwd* fwd,
+                            void* saved, size_t saved_bytes, void* scratch,
+                            size_t scratch_bytes, float* seg_coef, float* seg_dS,
+                            float* seg_dZ, void* stream);
+/* Completes the forward given the incoming carry in fwd->S0 / fwd->Z0 (S_ref
+ * stays the call-start state of the whole sequence). */
+int atlas_mem_forward_finish(const AtlasMemShape* shape, const AtlasMemFwd* fwd,
+                             void* saved, size_t saved_bytes, void* scratch,
+                             size_t scratch_bytes, void* stream);
+/* Backward segment transform of this rank, computed from zero adjoint:
+ *   (FS, FZ) -> (a*FS + dFS, b*FS + c*FZ + dFZ)   coef[N,3] = (a, b, c). */
+int atlas_mem_backward_local(const AtlasMemShape* shape, const AtlasMemFwd* fwd,
+                             const AtlasMemBwd* bwd, const void* saved, size_t saved_bytes,
+                             void* scratch, size_t scratch_bytes, float* seg_coef,
+                             float* seg_dS, float* seg_dZ, void* stream);
+/* Completes the backward given the adjoint arriving from later ranks in
+ * bwd->dS_end / bwd->dZ_end (the last rank passes the true upstream gradients,
+ * apply_clamp_mask = 1 there only). dS_ref receives this rank's partial sum. */
+int atlas_mem_backward_finish(const AtlasMemShape* shape, const AtlasMemFwd* fwd,
+                              const AtlasMemBwd* bwd, const void* saved, size_t saved_bytes,
+                              void* scratch, size_t scratch_bytes, int apply_clamp_mask,
+                              void* stream);
+
+/* ---- measurement hooks (no reference counterpart: the reference only prints
+ * wall-clock times, tests/test_atlas_cuda.py:270-284). Every kernel launch is
+ * counted; with timing enabled each launch is bracketed by CUDA events recorded
+ * on its own stream, summed per kernel when read. */
+/* Reset counters and turn per-launch event timing on (1) or off (0). */
+int atlas_mem_profile_enable(int on);
+/* Total event-timed milliseconds and timed launches of one kernel since the
+ * last reset (waits for the pending events). */
+int atlas_mem_profile_read(int kernel_id, double* total_ms, long long* launches);
+/* Kernel launches issued since the last reset (timed or not). */
+long long atlas_mem_launch_count(void);
+/* Number of kernel ids and the name of one. */
+int atlas_mem_kernel_count(void);
+const char* atlas_mem_kernel_name(int kernel_id);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* ATLAS_MEM_H */

@@ -1,0 +1,124 @@
+"""CPU: the oracle against the reference's golden vectors and known-answer tests."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import memory_ref
+from oracle.assoc_scan_standin import AssocScan, scalar_assoc_scan, sequential_assoc_scan
+from tests.helpers import golden_files, load, oracle_run, rel_l2
+
+
+# ---- scan KATs (tests/test_rnn_all.py:832-887 of the reference) ------------------
+def test_scan_identity():
+    x0 = torch.randn(2, 4, 4)
+    out = AssocScan()(torch.ones(2, 5), torch.zeros(2, 5, 4, 4), prev=x0)
+    for t in range(5):
+        assert torch.allclose(out[:, t], x0, atol=1e-5)
+
+
+def test_scan_additive():
+    out = AssocScan()(torch.ones(1, 4), torch.ones(1, 4, 2, 2), prev=torch.zeros(1, 2, 2))
+    for t in range(4):
+        assert torch.allclose(out[:, t], torch.full((1, 2, 2), float(t + 1)))
+
+
+def test_scan_decay():
+    out = AssocScan()(torch.full((1, 4), 0.5), torch.zeros(1, 4, 2, 2), prev=torch.ones(1, 2, 2))
+    for t in range(4):
+        assert torch.allclose(out[:, t], torch.full((1, 2, 2), 0.5 ** (t + 1)), atol=1e-5)
+
+
+def test_scan_mixed():
+    out = AssocScan()(torch.full((1, 3), 0.5), torch.ones(1, 3, 2, 2), prev=torch.zeros(1, 2, 2))
+    exp = torch.tensor([1.0, 1.5, 1.75]).view(1, 3, 1, 1).expand(1, 3, 2, 2)
+    assert torch.allclose(out, exp, atol=1e-4)
+
+
+def test_split_scan_identity():
+    """scan(all)[-1] == scan(2nd half, prev=scan(1st half)[-1])  (tests/test_titans.py:680-707)."""
+    g = torch.randn(2, 128, 16).sigmoid()
+    x = torch.randn(2, 128, 16)
+    full = scalar_assoc_scan(g, x)
+    first = scalar_assoc_scan(g[:, :64], x[:, :64])
+    second = scalar_assoc_scan(g[:, 64:], x[:, 64:], prev=first[:, -1])
+    assert torch.allclose(full[:, -1], second[:, -1], atol=1e-5)
+
+
+@pytest.mark.parametrize("T", [1, 2, 3, 7, 16, 33])
+def test_logdepth_matches_sequential(T):
+    g = torch.rand(3, T, dtype=torch.float64)
+    x = torch.randn(3, T, 4, 5, dtype=torch.float64)
+    p = torch.randn(3, 4, 5, dtype=torch.float64)
+    for rp in (True, False):
+        a = scalar_assoc_scan(g, x, prev=p, remove_prev=rp)
+        b = sequential_assoc_scan(g, x, prev=p, remove_prev=rp)
+        assert torch.allclose(a, b, atol=1e-12)
+
+
+def test_window_kat():
+    """Sliding sum [1..6], window 3 (tests/test_rnn_all.py:890-896)."""
+    x = torch.arange(1, 7).float().view(1, 6, 1)
+    exp = torch.tensor([1, 3, 6, 9, 12, 15], dtype=torch.float32).view(1, 6, 1)
+    assert torch.allclose(memory_ref.sliding_sum_along_time(x, 3), exp)
+
+
+# ---- oracle vs goldens produced by the reference module ----------------------------
+@pytest.mark.parametrize("path", golden_files("core_"), ids=lambda p: p.split("/")[-1])
+def test_oracle_matches_reference_golden(path):
+    z = load(path)
+    B, H, T, d, e, gate_on, mom, deg = (int(x) for x in z["meta"])
+    mode = str(z["fmap_mode"])
+    t = lambda n: torch.from_numpy(z[n]) if n in z else None
+    inp = {"k": t("k"), "q": t("q"), "v": t("v"), "lr": t("lr"), "decay": t("decay"), "beta": t("beta"),
+           "gate": t("gate"), "S0": t("S0"), "Z0": t("Z0"), "omega_buffer": t("buf"), "proj": t("proj")}
+    up = {n: t("up_" + n) for n in ("y", "S_end", "Z_end", "buf_out")}
+    out, gr = oracle_run(inp, e, "token" if gate_on else None, mode, deg, up=up)
+    for n in ("y", "S_end", "Z_end", "buf_out"):
+        if n in z:
+            assert rel_l2(out[n], z[n]) < 1e-12, n
+    # S_ref is S0 in the reference cell: its gradient is the sum of both paths
+    names = {"k": "k", "q": "q", "v": "v", "lr": "lr", "decay": "decay", "beta": "beta", "gate": "gate",
+             "Z0": "Z0", "omega_buffer": "buf"}
+    for mine, theirs in names.items():
+        if "d_" + theirs in z:
+            assert rel_l2(gr[mine], z["d_" + theirs]) < 1e-10, mine
+    assert rel_l2(gr["S0"], z["d_S0"]) < 1e-10
+
+
+def test_window_gate_generalisation_reduces_to_token_gate():
+    """U[t, j] = u_{t-j} reproduces the reference's per-token gate exactly."""
+    torch.manual_seed(0)
+    N, T, d, e = 2, 19, 6, 4
+    D = torch.float64
+    k, q, v = (torch.randn(N, T, d, dtype=D) for _ in range(3))
+    lr, decay, beta, u = (torch.rand(N, T, dtype=D) for _ in range(4))
+    S0, Z0 = torch.randn(N, d, d, dtype=D), torch.randn(N, d, d, dtype=D)
+    # zero buffer: in token mode the buffer is stored gated, in window mode ungated
+    U = torch.zeros(N, T, e, dtype=D)
+    for j in range(e):
+        U[:, j:, j] = u[:, : T - j]
+    a = memory_ref.memory_layer(k, q, v, lr, decay, beta, u, S0, S0, Z0, None, window=e)
+    b = memory_ref.memory_layer(k, q, v, lr, decay, beta, None, S0, S0, Z0, None, window=e, U=U)
+    for x, y in zip(a[:3], b[:3]):
+        assert torch.allclose(x, y, atol=1e-12)
+
+
+@pytest.mark.parametrize("e,mom,gate", [(1, True, False), (3, True, True), (4, False, True)])
+def test_sequential_numpy_restatement_agrees(e, mom, gate):
+    torch.manual_seed(1)
+    N, T, d = 2, 11, 5
+    D = torch.float64
+    k, q, v = (torch.randn(N, T, d, dtype=D) for _ in range(3))
+    lr, decay = torch.rand(N, T, dtype=D), torch.rand(N, T, dtype=D)
+    beta = torch.rand(N, T, dtype=D) if mom else None
+    u = torch.rand(N, T, dtype=D) if gate else None
+    S0 = torch.randn(N, d, d, dtype=D)
+    Z0 = torch.randn(N, d, d, dtype=D) if mom else None
+    buf = torch.randn(N, e - 1, d, d, dtype=D) if e > 1 else None
+    a = memory_ref.memory_core(k, q, v, lr, decay, beta, u, S0, S0, Z0, buf, window=e)
+    npf = lambda t: None if t is None else t.numpy()
+    b = memory_ref.memory_core_sequential_np(*(npf(x) for x in (k, q, v, lr, decay, beta, u, S0, S0, Z0, buf)),
+                                             window=e)
+    for x, y in zip(a, b):
+        if x is not None:
+            assert np.allclose(x.numpy(), y, atol=1e-10)

@@ -1,0 +1,117 @@
+"""GPU: the CUDA path against the CPU oracle on seeded inputs, every mode.
+
+fp32 cases at rel-L2 <= 1e-5, bf16 cases (bf16 inputs, fp32 state) at <= 2e-2, on
+y, S_end, Z_end, the new omega buffer and every input gradient.
+"""
+import pytest
+import torch
+
+from atlas_rnn_b200 import memory_recurrence
+from atlas_rnn_b200.workloads import CONFIGS, Workload, make_inputs, shrink
+from tests.helpers import TOL_BF16, TOL_F32, oracle_run, rel_l2
+
+pytestmark = pytest.mark.gpu
+
+
+def run_case(w: Workload, seed=0, state_scale=0.1, tol=None, separate_sref=False, chunk=0):
+    tol = tol if tol is not None else (TOL_F32 if w.dtype == torch.float32 else TOL_BF16)
+    inp = make_inputs(w, seed=seed, device="cuda", state_scale=state_scale)
+    g = torch.Generator().manual_seed(seed + 7)
+    S_ref = (0.1 * torch.randn(w.N, w.d_v, w.d_phi, generator=g)).cuda() if separate_sref else None
+    leaves = {n: (t.clone().requires_grad_(True) if t is not None else None) for n, t in inp.items()
+              if n not in ("dy", "proj")}
+    if S_ref is not None:
+        S_ref = S_ref.clone().requires_grad_(True)
+    gm = "window" if w.gate == "window" else "token"
+    y, S_end, Z_end, nb = memory_recurrence(
+        leaves["k"], leaves["q"], leaves["v"], leaves["lr"], leaves["decay"], leaves["beta"], leaves["gate"],
+        S_ref=S_ref if S_ref is not None else leaves["S0"], S0=leaves["S0"], Z0=leaves["Z0"],
+        omega_buffer=leaves["omega_buffer"], window=w.window, gate_mode=gm, fmap_mode=w.fmap_mode,
+        fmap_degree=w.fmap_degree, proj=inp["proj"], chunk=chunk)
+    gen = torch.Generator().manual_seed(seed + 11)
+    up = {"y": inp["dy"].float().cpu(),
+          "S_end": torch.randn(S_end.shape, generator=gen),
+          "Z_end": torch.randn(S_end.shape, generator=gen) if Z_end is not None else None,
+          "buf_out": torch.randn(nb.shape, generator=gen) if nb is not None else None}
+    ref_in = dict(inp)
+    out_ref, g_ref = oracle_run(ref_in, w.window, gm if w.gate != "none" else None, w.fmap_mode, w.fmap_degree,
+                                up=up, S_ref=S_ref)
+    mine = {"y": y, "S_end": S_end, "Z_end": Z_end, "buf_out": nb}
+    errs = {}
+    for n, o in mine.items():
+        if o is not None:
+            errs[n] = rel_l2(o.float(), out_ref[n])
+    pairs = [(mine[n], up[n].to(mine[n].dtype).cuda()) for n in mine if mine[n] is not None]
+    torch.autograd.backward([p[0] for p in pairs], [p[1] for p in pairs])
+    for n, t in leaves.items():
+        if t is not None and n in g_ref:
+            errs["d_" + n] = rel_l2(t.grad.float(), g_ref[n])
+    if S_ref is not None:
+        errs["d_S_ref"] = rel_l2(S_ref.grad, g_ref["S_ref"])
+    bad = {k: v for k, v in errs.items() if not v < tol}
+    assert not bad, (bad, errs)
+    return errs
+
+
+def W(name, T, d=32, dv=None, e=1, gate="none", fm="off", deg=1, mom=True, dtype=torch.float32, N=(1, 3),
+      dphi=None):
+    dv = dv or d
+    return Workload(name, N[0], N[1], T, d, dphi or d, dv, e, gate, fm, deg, mom, dtype, 0)
+
+
+CASES_F32 = [
+    W("titans", 100),
+    W("titans_nomom", 77, mom=False),
+    W("omega_e2_token", 65, e=2, gate="token"),
+    W("omega_e4_window", 70, e=4, gate="window"),
+    W("omega_e4_elem3", 64, e=4, gate="token", fm="elementwise", deg=3),
+    W("omega_e16_token", 97, e=16, gate="token", d=64),
+    W("omega_e5_nogate", 33, e=5),
+    W("rect_dv48_dphi32", 50, d=32, dv=48, e=3, gate="token"),
+    W("tensor_fmap", 40, d=8, dphi=24, e=3, gate="token", fm="tensor", deg=2),
+    W("t1", 1, e=3, gate="token"),
+    W("t_lt_window", 3, e=8, gate="window"),
+    W("t_eq_chunk", 32, e=2, gate="token"),
+    W("t_chunk_plus1", 33, e=2, gate="token"),
+    W("t_chunk_minus1", 31, e=4, gate="window"),
+    W("d128", 70, d=128, e=4, gate="window", fm="elementwise", deg=2),
+]
+
+
+@pytest.mark.parametrize("w", CASES_F32, ids=lambda w: w.name)
+def test_fp32_vs_oracle(native_lib, w):
+    run_case(w)
+
+
+@pytest.mark.parametrize("w", CASES_F32[:6], ids=lambda w: w.name)
+def test_fp32_separate_sref(native_lib, w):
+    run_case(w, separate_sref=True)
+
+
+@pytest.mark.parametrize("w", [W("bf16_titans", 130, d=64, dtype=torch.bfloat16),
+                               W("bf16_omega_window", 99, d=64, e=4, gate="window", fm="elementwise", deg=2,
+                                 dtype=torch.bfloat16)], ids=lambda w: w.name)
+def test_bf16_vs_oracle(native_lib, w):
+    run_case(w)
+
+
+def test_config0_full(native_lib):
+    """BASELINE config 0 at full size (fp32)."""
+    run_case(CONFIGS[0], state_scale=0.0)
+    run_case(CONFIGS[0], state_scale=0.1, seed=1)
+
+
+def test_config1_slice(native_lib):
+    """BASELINE config 1 (bf16, e=4, window gates, elementwise g=2) on a batch*head slice."""
+    run_case(shrink(CONFIGS[1], B=1, H=2, T=1024), state_scale=0.0)
+
+
+def test_config4_slice(native_lib):
+    """BASELINE config 4 (tensor feature map 64 -> 256, e=16) on a small slice."""
+    run_case(shrink(CONFIGS[4], B=1, H=1, T=160), state_scale=0.1)
+
+
+@pytest.mark.parametrize("chunk", [16, 24, 64])
+def test_chunk_invariance(native_lib, chunk):
+    """The internal chunk is only a tiling (reference: test_rnn_all.py:335-374)."""
+    run_case(W("chunk_inv", 90, e=4, gate="token"), chunk=chunk)
