@@ -67,7 +67,13 @@ def lib():
                                                ctypes.c_size_t, _vp, _vp, _vp, _vp]
         L.atlas_mem_backward_finish.argtypes = [P(Shape), P(Fwd), P(Bwd), _vp, ctypes.c_size_t, _vp,
                                                 ctypes.c_size_t, ctypes.c_int, _vp]
-        for name in ("atlas_mem_workspace_size", "atlas_mem_forward", "atlas_mem_backward",
+        L.atlas_mem_profile_enable.argtypes = [ctypes.c_int]
+        L.atlas_mem_profile_read.argtypes = [ctypes.c_int, P(ctypes.c_double), P(ctypes.c_longlong)]
+        L.atlas_mem_launch_count.restype = ctypes.c_longlong
+        L.atlas_mem_kernel_count.restype = ctypes.c_int
+        L.atlas_mem_kernel_name.restype = ctypes.c_char_p
+        L.atlas_mem_kernel_name.argtypes = [ctypes.c_int]
+        for name in ("atlas_mem_profile_enable", "atlas_mem_profile_read", "atlas_mem_workspace_size", "atlas_mem_forward", "atlas_mem_backward",
                      "atlas_mem_forward_local", "atlas_mem_forward_finish", "atlas_mem_backward_local",
                      "atlas_mem_backward_finish"):
             getattr(L, name).restype = ctypes.c_int
@@ -91,3 +97,22 @@ def workspace_sizes(shape: Shape):
     check(lib().atlas_mem_workspace_size(ctypes.byref(shape), ctypes.byref(s), ctypes.byref(f),
                                          ctypes.byref(b)), "workspace_size")
     return s.value, f.value, b.value
+
+
+def profile_enable(on: bool):
+    check(lib().atlas_mem_profile_enable(int(on)), "profile_enable")
+
+
+def profile_read() -> dict:
+    """{kernel name: (total event-timed ms, timed launches)} since the last reset."""
+    L = lib()
+    out = {}
+    for i in range(L.atlas_mem_kernel_count()):
+        ms, n = ctypes.c_double(), ctypes.c_longlong()
+        check(L.atlas_mem_profile_read(i, ctypes.byref(ms), ctypes.byref(n)), "profile_read")
+        out[L.atlas_mem_kernel_name(i).decode()] = (ms.value, n.value)
+    return out
+
+
+def launch_count() -> int:
+    return int(lib().atlas_mem_launch_count())

@@ -44,6 +44,7 @@ def _stream(dev) -> ctypes.c_void_p:
 class MemoryRecurrenceFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, spec: Spec, k, q, v, lr, decay, beta, gate, S_ref, S0, Z0, buf, proj):
+        ctx.set_materialize_grads(False)  # unused outputs arrive as None, not zero tensors
         dev = k.device
         N, T, _ = k.shape
         d_phi = S_ref.shape[-1]

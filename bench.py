@@ -1,0 +1,353 @@
+"""Benchmark of the memory-layer hot path: fwd+bwd tokens/s on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config 1] [--impl reference]
+
+One step = forward + backward of the memory recurrence over one batch of the
+configuration's synthetic inputs (seeded; the distributions of the benchmark
+config), through the public API ``atlas_rnn_b200.memory_recurrence``.
+Multi-GPU (torchrun, one rank per GPU): batch*head units are independent, so
+every rank runs its own full copy of the configuration (weak scaling, no
+data-path collective); timing is the max over ranks of CUDA-event time.
+
+``--impl reference`` times the reference algorithm on the host cores instead:
+the CPU restatement in oracle/ (materialised [N,T,d,d] einsums and log-depth
+scalar scans, autograd backward), on a bounded slice of the same workload,
+scaled to the whole workload. Under torchrun only rank 0 runs it.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+from atlas_rnn_b200.workloads import CONFIGS, make_inputs, shrink  # noqa: E402
+
+METRIC = "memory-layer fwd+bwd tokens/sec"
+UNIT = "tokens/s"
+
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+# ---------------------------------------------------------------------------
+# reference arm / CPU baseline: the oracle port on host cores
+# ---------------------------------------------------------------------------
+def cpu_sample(w, n_units=1, t_tokens=512, min_seconds=10.0, max_reps=50):
+    """Time fwd+bwd of the CPU restatement on a slice; returns (tokens/s scaled
+    to the full workload, seconds per rep, reps, sample description)."""
+    from oracle import memory_ref
+    ws = shrink(w, B=1, H=n_units, T=min(t_tokens, w.T))
+    inp = make_inputs(ws, seed=0, device="cpu")
+    leaf = {k: (v.float().clone().requires_grad_(True) if v is not None else None) for k, v in inp.items()
+            if k not in ("dy", "proj")}
+    proj = inp["proj"]
+    U = leaf["gate"] if w.gate == "window" else None
+    u = leaf["gate"] if w.gate == "token" else None
+    times = []
+    t_start = time.perf_counter()
+    while (time.perf_counter() - t_start < min_seconds and len(times) < max_reps) or len(times) < 1:
+        for t in leaf.values():
+            if t is not None:
+                t.grad = None
+        t0 = time.perf_counter()
+        y, S_end, Z_end, nb = memory_ref.memory_layer(
+            leaf["k"], leaf["q"], leaf["v"], leaf["lr"], leaf["decay"], leaf["beta"], u, leaf["S0"], leaf["S0"],
+            leaf["Z0"], leaf["omega_buffer"], window=w.window, U=U, fmap_mode=w.fmap_mode,
+            fmap_degree=w.fmap_degree, proj=proj)
+        y.backward(inp["dy"].float())
+        times.append(time.perf_counter() - t0)
+    per = statistics.median(times)
+    # linear in units and tokens (the log-depth scan does O(T) work)
+    full_time = per * (w.N / ws.N) * (w.T / ws.T)
+    tok_s = w.B * w.T / full_time
+    sample = (f"oracle port fwd+bwd (fp32, torch CPU) on {ws.N} unit(s) x {ws.T} tokens of "
+              f"{w.name}, median of {len(times)} reps = {per:.3f} s, scaled linearly to "
+              f"{w.N} units x {w.T} tokens")
+    return tok_s, per, len(times), sample
+
+
+def run_reference(args, w):
+    ws, rank, _ = dist_env()
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    # warm-up then timed steps; each step is one bounded sample
+    for _ in range(args.warmup):
+        cpu_sample(w, min_seconds=0.0, max_reps=1)
+    vals, pers = [], []
+    for _ in range(args.steps):
+        v, per, _, sample = cpu_sample(w, min_seconds=0.0, max_reps=1)
+        vals.append(v)
+        pers.append(per)
+    value = statistics.median(vals)
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1000.0 * w.B * w.T / value, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": w.name, "B": w.B, "H": w.H, "T": w.T, "d_k": w.d_k, "d_v": w.d_v,
+                       "window": w.window},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id: str, rank: int):
+        self.dev = gpu_id
+        self.proc = None
+        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_rank{rank}.csv")
+
+    def __enter__(self):
+        try:
+            os.makedirs(os.path.dirname(self.path), exist_ok=True)
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.dev), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9 and parts[1].replace(".", "").isdigit():
+                rows.append(parts)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower().startswith("active")})
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": float(rows[0][2]), "reasons": reasons,
+                "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+def step_api(inp, w, leaves_from):
+    """One fwd+bwd through the public API. Returns y."""
+    from atlas_rnn_b200 import memory_recurrence
+    L = leaves_from
+    y, S_end, Z_end, nb = memory_recurrence(
+        L["k"], L["q"], L["v"], L["lr"], L["decay"], L["beta"], L["gate"], S_ref=inp["S0"], S0=inp["S0"],
+        Z0=inp["Z0"], omega_buffer=inp["omega_buffer"], window=w.window,
+        gate_mode="window" if w.gate == "window" else "token", fmap_mode=w.fmap_mode, fmap_degree=w.fmap_degree,
+        proj=inp["proj"])
+    torch.autograd.backward([y], [L["dy"]])
+    return y
+
+
+def traffic_from_profiles(kernel: str, workload: str):
+    """Per-launch DRAM bytes recorded from an ncu capture in profiles/ (or None)."""
+    path = os.path.join(ROOT, "profiles", f"{kernel}_{workload}.md")
+    if not os.path.exists(path):
+        return None
+    for line in open(path):
+        if line.strip().startswith("traffic_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+def run_ours(args, w):
+    import torch.distributed as dist
+    from atlas_rnn_b200 import _lib
+    from atlas_rnn_b200.roofline import kernel_flops, step_bytes_per_token, step_flops_per_token
+
+    ws, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    _lib.lib()
+    inp = make_inputs(w, seed=rank, device=dev)
+    names = ("k", "q", "v", "lr", "decay", "beta", "gate")
+
+    def leaves():
+        d = {n: (inp[n].detach().requires_grad_(True) if inp[n] is not None else None) for n in names}
+        d["dy"] = inp["dy"]
+        return d
+
+    def barrier():
+        if ws > 1:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize(dev)
+
+    def max_over_ranks(x):
+        if ws == 1:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return t.item()
+
+    # ---- device-resident timing (value) with per-kernel event timing
+    for _ in range(args.warmup):
+        step_api(inp, w, leaves())
+    barrier()
+    _lib.profile_enable(True)
+    st = torch.cuda.current_stream(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    props = torch.cuda.get_device_properties(dev)
+    gpu_id = ("GPU-" + str(props.uuid)) if getattr(props, "uuid", None) is not None else str(local)
+    with ClockSampler(gpu_id, rank) as clk:
+        barrier()
+        ev0.record(st)
+        for _ in range(args.steps):
+            step_api(inp, w, leaves())
+        ev1.record(st)
+        barrier()
+    ms = ev0.elapsed_time(ev1)
+    kern = _lib.profile_read()
+    launches = _lib.launch_count()
+    _lib.profile_enable(False)
+    ms = max_over_ranks(ms)
+    ms_step = ms / args.steps
+    tokens_step = w.B * w.T
+    value = ws * tokens_step * args.steps / (ms / 1000.0)
+
+    # ---- e2e through the public API with pinned host buffers
+    host = {n: inp[n].cpu().pin_memory() for n in names + ("dy",) if inp[n] is not None}
+    y_host = torch.empty((w.N, w.T, w.d_v), dtype=w.dtype).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in host.values())
+    d2h = y_host.numel() * y_host.element_size()
+
+    def e2e_step():
+        d = {n: (host[n].to(dev, non_blocking=True) if n in host else None) for n in names + ("dy",)}
+        for n in names:
+            if d[n] is not None:
+                d[n].requires_grad_(True)
+        y = step_api(inp, w, d)
+        y_host.copy_(y.detach(), non_blocking=True)
+
+    for _ in range(max(1, args.warmup // 2)):
+        e2e_step()
+    barrier()
+    ev0.record(st)
+    for _ in range(args.steps):
+        e2e_step()
+    ev1.record(st)
+    barrier()
+    e2e_ms = max_over_ranks(ev0.elapsed_time(ev1))
+    e2e_value = ws * tokens_step * args.steps / (e2e_ms / 1000.0)
+
+    # ---- roofline of the dominant kernel
+    top = max(kern.items(), key=lambda kv: kv[1][0])
+    top_name, (top_ms, top_n) = top[0], top[1]
+    peaks = {}
+    ppath = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(ppath):
+        peaks = json.load(open(ppath))
+    peak_tf = peaks.get("bf16_tflops", 1590.0)
+    try:
+        alg_flops = kernel_flops(top_name, w, int(kernel_cfg_chunk(w)))
+    except KeyError:
+        alg_flops = None
+    avg_ms = top_ms / max(top_n, 1)
+    achieved = alg_flops / (avg_ms / 1000.0) / 1e12 if alg_flops else None
+    roofline = {"kernel": top_name, "bound": "tensor", "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
+                "frac": (achieved / peak_tf) if achieved else None,
+                "peak_source": "MEASURED_PEAKS.json bf16_tflops (burst)" if peaks else "fallback 1590",
+                "traffic": traffic_from_profiles(top_name, w.name), "launch_ms": avg_ms,
+                "algorithmic_flops_per_launch": alg_flops,
+                "kernel_share": top_ms / sum(v[0] for v in kern.values())}
+    Ff, Fb = step_flops_per_token(w)
+    Bf, Bb = step_bytes_per_token(w)
+    tok_heads = w.N * w.T
+    step_roof_ms = max((Ff + Fb) * tok_heads / (peak_tf * 1e12),
+                       (Bf + Bb) * tok_heads / (peaks.get("hbm_gbs", 6650.0) * 1e9)) * 1000.0
+    clocks = clk.summary()
+
+    if rank == 0:
+        cpu = None
+        if ws == 1 and not args.no_cpu_baseline:
+            v, per, reps, sample = cpu_sample(w, min_seconds=args.cpu_seconds)
+            cpu = {"value": v, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port", "sample": sample}
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16" if w.dtype == torch.bfloat16 else "f32",
+            "data": "synthetic (seeded, benchmark-config distributions)",
+            "config": {"workload": w.name, "B": w.B, "H": w.H, "T": w.T, "d_k": w.d_k, "d_phi": w.d_phi,
+                       "d_v": w.d_v, "window": w.window, "gate": w.gate, "fmap": f"{w.fmap_mode}:{w.fmap_degree}",
+                       "momentum": w.momentum, "per_rank_units": w.N, "parallelism": f"bh-replica x{ws}",
+                       "l2": "inputs exceed L2 (no flush needed)" if tok_heads * (2 * w.d_k + w.d_v) * w.dtype.itemsize > 126e6
+                       else "inputs fit L2"},
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "gpu_launches": launches,
+            "roofline": roofline,
+            "step_roofline_ms": step_roof_ms,
+            "step_roofline_frac": step_roof_ms / ms_step,
+            "kernels_ms_per_step": {k: v[0] / args.steps for k, v in kern.items() if v[1]},
+            "clocks": clocks,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if ws > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+
+
+def kernel_cfg_chunk(w):
+    from atlas_rnn_b200.ops import Spec  # noqa: F401  (library default chunk)
+    return 32 if w.window - 1 <= 32 else w.window - 1
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--config", type=int, default=1)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--T", type=int, default=None, help="override tokens (for profiling small cases)")
+    ap.add_argument("--B", type=int, default=None)
+    args = ap.parse_args()
+    w = CONFIGS[args.config]
+    if args.T or args.B:
+        w = shrink(w, B=args.B, T=args.T)
+    if args.impl == "reference":
+        run_reference(args, w)
+    else:
+        run_ours(args, w)
+
+
+if __name__ == "__main__":
+    main()
