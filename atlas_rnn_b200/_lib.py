@@ -67,6 +67,9 @@ def lib():
                                                ctypes.c_size_t, _vp, _vp, _vp, _vp]
         L.atlas_mem_backward_finish.argtypes = [P(Shape), P(Fwd), P(Bwd), _vp, ctypes.c_size_t, _vp,
                                                 ctypes.c_size_t, ctypes.c_int, _vp]
+        L.atlas_mem_selftest_umma.argtypes = [_vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                              ctypes.c_int, _vp, _vp]
+        L.atlas_mem_selftest_umma.restype = ctypes.c_int
         L.atlas_mem_profile_enable.argtypes = [ctypes.c_int]
         L.atlas_mem_profile_read.argtypes = [ctypes.c_int, P(ctypes.c_double), P(ctypes.c_longlong)]
         L.atlas_mem_launch_count.restype = ctypes.c_longlong

@@ -4,6 +4,7 @@
 #include <mutex>
 
 #include "chunk_kernels.cuh"
+#include "umma_selftest.cuh"
 
 using namespace atlas;
 
@@ -415,6 +416,21 @@ int atlas_mem_backward_finish(const AtlasMemShape* shape, const AtlasMemFwd* fwd
   Params P = make_params(shape, L, fwd, bwd, saved, scratch);
   P.apply_mask = apply_clamp_mask ? 1 : 0;
   return run_bwd_finish(shape, P, (cudaStream_t)stream);
+}
+
+int atlas_mem_selftest_umma(const void* A, const void* B, float* D, int N, int K, int a_mn_major,
+                            int b_mn_major, int* status, void* stream) {
+  if (!A || !B || !D || !status) return ATLAS_ERR_INVALID_ARG;
+  if (N < 16 || N > 256 || N % 16 || K < 16 || K > 128 || K % 16) return ATLAS_ERR_UNSUPPORTED;
+  // operand tiles plus slack, so every descriptor read stays inside the allocation
+  const size_t smem = (size_t)(128 * K + N * K) * 2 + 65536;
+  if (cudaFuncSetAttribute((const void*)k_umma_selftest, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+      cudaSuccess)
+    return ATLAS_ERR_LAUNCH;
+  k_umma_selftest<<<1, 128, smem, (cudaStream_t)stream>>>((const __nv_bfloat16*)A, (const __nv_bfloat16*)B, D, N, K,
+                                                          a_mn_major, b_mn_major, status);
+  LAUNCH_CHECK();
+  return ATLAS_OK;
 }
 
 int atlas_mem_profile_enable(int on) {

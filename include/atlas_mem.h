@@ -177,6 +177,14 @@ int atlas_mem_backward_finish(const AtlasMemShape* shape, const AtlasMemFwd* fwd
                               void* scratch, size_t scratch_bytes, int apply_clamp_mask,
                               void* stream);
 
+/* Device self-check of the tensor-core (tcgen05) GEMM building block used by
+ * the fused kernels: D[128,N] = A[128,K] * B^T with A given as [128][K]
+ * (a_mn_major = 0) or [K][128] (1), B as [N][K] (b_mn_major = 0) or [K][N] (1);
+ * bf16 operands, fp32 D. *status (device int, zeroed by the caller) becomes
+ * nonzero if the bounded completion wait timed out. No reference counterpart. */
+int atlas_mem_selftest_umma(const void* A, const void* B, float* D, int N, int K, int a_mn_major,
+                            int b_mn_major, int* status, void* stream);
+
 /* ---- measurement hooks (no reference counterpart: the reference only prints
  * wall-clock times, tests/test_atlas_cuda.py:270-284). Every kernel launch is
  * counted; with timing enabled each launch is bracketed by CUDA events recorded
