@@ -285,6 +285,30 @@ int run_bwd_finish(const AtlasMemShape* s, const Params& P, cudaStream_t st) {
   return ATLAS_OK;
 }
 
+// ---- fixed device scratch for atlas_mem_forward_noalloc ---------------------
+// Forward workspace for callers that cannot allocate. It is a file-scope
+// device array, so every GPU that loads this library holds it until exit.
+constexpr size_t kNoAllocScratchBytes = (size_t)32 << 20;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[64];
+
+// Device address of the array on the current device. Host code cannot use the
+// symbol itself (it names a host-side stand-in), so the address is looked up
+// once per device with that device current and cached.
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return ATLAS_ERR_LAUNCH;
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_addr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) return ATLAS_ERR_LAUNCH;
+    g_noalloc_addr[dev] = p;
+  }
+  *out = g_noalloc_addr[dev];
+  return ATLAS_OK;
+}
+
 int check_ws(const Layout& L, const void* saved, size_t saved_bytes, const void* scratch, size_t scratch_bytes,
              bool need_scratch) {
   if (!saved || saved_bytes < L.saved) return ATLAS_ERR_WORKSPACE;
@@ -306,6 +330,8 @@ const char* atlas_mem_error_string(int code) {
     case ATLAS_ERR_WORKSPACE: return "workspace missing or smaller than atlas_mem_workspace_size()";
     case ATLAS_ERR_LAUNCH: return "CUDA kernel launch failed";
     case ATLAS_ERR_DEVICE: return "device-side status reported a fault";
+    case ATLAS_ERR_NOALLOC_TOO_LARGE:
+      return "shape needs more scratch than the fixed no-alloc array holds (see atlas_mem_noalloc_scratch_bytes)";
     default: return "unknown error";
   }
 }
@@ -334,6 +360,25 @@ int atlas_mem_forward(const AtlasMemShape* shape, const AtlasMemFwd* fwd, void* 
   if ((v = run_fwd_local(shape, P, st))) return v;
   return run_fwd_finish(shape, P, st);
 }
+
+int atlas_mem_forward_noalloc(const AtlasMemShape* shape, const AtlasMemFwd* fwd, void* stream) {
+  int v = validate_shape(shape);
+  if (!v) v = validate_fwd(shape, fwd, true);
+  if (v) return v;
+  const Layout L = make_layout(shape);
+  if (L.saved > kNoAllocScratchBytes) return ATLAS_ERR_NOALLOC_TOO_LARGE;
+  void* scratch = nullptr;
+  if ((v = noalloc_scratch(&scratch))) return v;
+  if ((v = ensure_attrs())) return v;
+  // Every scratch word the forward reads is written earlier in the same call,
+  // so nothing has to be cleared between calls.
+  const Params P = make_params(shape, L, fwd, nullptr, scratch, nullptr);
+  cudaStream_t st = (cudaStream_t)stream;
+  if ((v = run_fwd_local(shape, P, st))) return v;
+  return run_fwd_finish(shape, P, st);
+}
+
+size_t atlas_mem_noalloc_scratch_bytes(void) { return kNoAllocScratchBytes; }
 
 int atlas_mem_backward(const AtlasMemShape* shape, const AtlasMemFwd* fwd, const AtlasMemBwd* bwd,
                        const void* saved, size_t saved_bytes, void* scratch, size_t scratch_bytes, void* stream) {

@@ -57,7 +57,8 @@ enum AtlasError {
   ATLAS_ERR_UNSUPPORTED = 2,   /* shape outside the supported envelope            */
   ATLAS_ERR_WORKSPACE = 3,     /* workspace pointer missing or too small          */
   ATLAS_ERR_LAUNCH = 4,        /* a kernel launch failed (cudaGetLastError)        */
-  ATLAS_ERR_DEVICE = 5         /* device-side status word reported a fault         */
+  ATLAS_ERR_DEVICE = 5,        /* device-side status word reported a fault         */
+  ATLAS_ERR_NOALLOC_TOO_LARGE = 6 /* shape exceeds the fixed scratch of the no-alloc entry */
 };
 
 /* Shapes and modes of one call. Mirrors the constructor arguments of
@@ -138,6 +139,28 @@ int atlas_mem_workspace_size(const AtlasMemShape* shape, size_t* saved,
 int atlas_mem_forward(const AtlasMemShape* shape, const AtlasMemFwd* fwd,
                       void* saved, size_t saved_bytes,
                       void* scratch, size_t scratch_bytes, void* stream);
+
+/* Forward pass that allocates nothing and takes no workspace. No counterpart
+ * in the reference: it is for callers that own only their input and output
+ * buffers and cannot call cudaMalloc -- for example a plugin slot in a host
+ * framework that hands over tensors but no workspace, or a serving loop whose
+ * device memory is fully reserved by its own pool.
+ *  - Scratch lives in one fixed device array of atlas_mem_noalloc_scratch_bytes()
+ *    (32 MiB) inside the library; every GPU that loads the library holds it
+ *    until the process exits. Shapes whose forward workspace
+ *    (atlas_mem_workspace_size's `saved`) exceeds it are rejected with
+ *    ATLAS_ERR_NOALLOC_TOO_LARGE before anything is launched.
+ *  - The first call on each device looks up the array's device address with
+ *    that device current; make that first call before any stream capture.
+ *  - All calls share the one array and it keeps the last call's contents:
+ *    calls whose work overlaps on the GPU (other streams, other host threads)
+ *    race with each other. Nothing in it needs to start at zero.
+ *  - Same operands and results as atlas_mem_forward; no backward can follow
+ *    (nothing is kept for it). Calls no cudaMalloc, cudaFree or allocating
+ *    library routine. */
+int atlas_mem_forward_noalloc(const AtlasMemShape* shape, const AtlasMemFwd* fwd, void* stream);
+/* Size in bytes of the fixed scratch array used by atlas_mem_forward_noalloc. */
+size_t atlas_mem_noalloc_scratch_bytes(void);
 
 /* Backward pass (AtlasOmegaFunction.backward, atlas_omega_autograd.py:155-204;
  * gradients of the PyTorch path's autograd). `fwd` must hold the same
