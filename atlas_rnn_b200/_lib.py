@@ -67,6 +67,8 @@ def lib():
                                                ctypes.c_size_t, _vp, _vp, _vp, _vp]
         L.atlas_mem_backward_finish.argtypes = [P(Shape), P(Fwd), P(Bwd), _vp, ctypes.c_size_t, _vp,
                                                 ctypes.c_size_t, ctypes.c_int, _vp]
+        L.atlas_mem_final_state_raw.argtypes = [P(Shape), _vp, ctypes.c_size_t, _vp, _vp]
+        L.atlas_mem_final_state_raw.restype = ctypes.c_int
         L.atlas_mem_forward_noalloc.argtypes = [P(Shape), P(Fwd), _vp]
         L.atlas_mem_forward_noalloc.restype = ctypes.c_int
         L.atlas_mem_noalloc_scratch_bytes.restype = ctypes.c_size_t

@@ -99,7 +99,9 @@ int ensure_attrs() {
   const int mx = max_smem_optin();
   const void* ks[] = {(const void*)k_fwd_chunk,   (const void*)k_fwd_out,      (const void*)k_bwd_chunk,
                       (const void*)k_bwd_grads,   (const void*)k_bwd_finalize, (const void*)k_bwd_dsref,
-                      (const void*)k_bwd_bufout,  (const void*)k_fmap_tensor_fwd, (const void*)k_fmap_tensor_bwd};
+                      (const void*)k_bwd_bufout,  (const void*)k_fmap_tensor_fwd, (const void*)k_fmap_tensor_bwd,
+                      (const void*)k_fwd_scan<1>, (const void*)k_fwd_scan<4>, (const void*)k_bwd_scan<1>,
+                      (const void*)k_bwd_scan<4>};
   for (const void* k : ks)
     if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, mx) != cudaSuccess)
       return ATLAS_ERR_LAUNCH;
@@ -124,7 +126,8 @@ int validate_shape(const AtlasMemShape* s) {
   const Smem m = smem_sizes(s, C);
   const size_t mx = (size_t)max_smem_optin();
   if (mx == 0) return ATLAS_ERR_LAUNCH;
-  const size_t big[] = {m.f1, m.f3, m.b1, m.b3, m.fin, m.fmf, m.fmb};
+  const size_t scan_smem = (size_t)((s->T + C - 1) / C) * 16;
+  const size_t big[] = {m.f1, m.f3, m.b1, m.b3, m.fin, m.fmf, m.fmb, scan_smem};
   for (size_t b : big)
     if (b > mx) return ATLAS_ERR_UNSUPPORTED;
   return ATLAS_OK;
@@ -239,6 +242,23 @@ void prof_end(int slot, cudaStream_t st) {
     prof_end(slot_, STREAM);                                      \
   } while (0)
 
+// Sequential chunk scans: float4 per thread when the state size allows it.
+int launch_scan(bool fwd, const Params& P, int dry, cudaStream_t st) {
+  const int64_t D2 = (int64_t)P.dv * P.dphi;
+  const size_t smem = (size_t)P.nch * sizeof(float4);
+  const bool v4 = (D2 % 4) == 0;
+  const int64_t units = v4 ? D2 / 4 : D2;
+  const dim3 grid((unsigned)((units + kThreads - 1) / kThreads), P.N);
+  if (fwd) {
+    if (v4) LAUNCH(KID_FWD_SCAN, k_fwd_scan<4>, grid, smem, st, P, dry);
+    else LAUNCH(KID_FWD_SCAN, k_fwd_scan<1>, grid, smem, st, P, dry);
+  } else {
+    if (v4) LAUNCH(KID_BWD_SCAN, k_bwd_scan<4>, grid, smem, st, P, dry);
+    else LAUNCH(KID_BWD_SCAN, k_bwd_scan<1>, grid, smem, st, P, dry);
+  }
+  return ATLAS_OK;
+}
+
 int run_fwd_local(const AtlasMemShape* s, const Params& P, cudaStream_t st) {
   const Smem m = smem_sizes(s, P.C);
   const dim3 gch(P.nch, P.N);
@@ -251,8 +271,7 @@ int run_fwd_local(const AtlasMemShape* s, const Params& P, cudaStream_t st) {
 
 int run_fwd_finish(const AtlasMemShape* s, const Params& P, cudaStream_t st) {
   const Smem m = smem_sizes(s, P.C);
-  const int64_t D2 = (int64_t)P.dv * P.dphi;
-  LAUNCH(KID_FWD_SCAN, k_fwd_scan, dim3((unsigned)((D2 + kThreads - 1) / kThreads), P.N), 0, st, P, 0);
+  if (int v = launch_scan(true, P, 0, st)) return v;
   LAUNCH(KID_FWD_OUT, k_fwd_out, dim3(P.nch, P.N), m.f3, st, P);
   if (P.e > 1 && P.buf_out) {
     LAUNCH(KID_BUF_OUT, k_buf_out, dim3(P.e - 1, P.N), 0, st, P);
@@ -268,8 +287,7 @@ int run_bwd_local(const AtlasMemShape* s, const Params& P, cudaStream_t st) {
 
 int run_bwd_finish(const AtlasMemShape* s, const Params& P, cudaStream_t st) {
   const Smem m = smem_sizes(s, P.C);
-  const int64_t D2 = (int64_t)P.dv * P.dphi;
-  LAUNCH(KID_BWD_SCAN, k_bwd_scan, dim3((unsigned)((D2 + kThreads - 1) / kThreads), P.N), 0, st, P, 0);
+  if (int v = launch_scan(false, P, 0, st)) return v;
   LAUNCH(KID_BWD_GRADS, k_bwd_grads, dim3(P.nch, P.N), m.b3, st, P);
   if (P.e > 1 && P.dbuf_out) {
     LAUNCH(KID_BWD_BUFOUT, k_bwd_bufout, dim3(P.e - 1, P.N), m.bufout, st, P);
@@ -378,6 +396,20 @@ int atlas_mem_forward_noalloc(const AtlasMemShape* shape, const AtlasMemFwd* fwd
   return run_fwd_finish(shape, P, st);
 }
 
+int atlas_mem_final_state_raw(const AtlasMemShape* shape, const void* saved, size_t saved_bytes, float* out,
+                              void* stream) {
+  int v = validate_shape(shape);
+  if (v) return v;
+  if (!out) return ATLAS_ERR_INVALID_ARG;
+  const Layout L = make_layout(shape);
+  if ((v = check_ws(L, saved, saved_bytes, nullptr, 0, false))) return v;
+  const size_t bytes = (size_t)shape->N * shape->d_v * shape->d_phi * sizeof(float);
+  if (cudaMemcpyAsync(out, (const char*)saved + L.ST, bytes, cudaMemcpyDeviceToDevice, (cudaStream_t)stream) !=
+      cudaSuccess)
+    return ATLAS_ERR_LAUNCH;
+  return ATLAS_OK;
+}
+
 size_t atlas_mem_noalloc_scratch_bytes(void) { return kNoAllocScratchBytes; }
 
 int atlas_mem_backward(const AtlasMemShape* shape, const AtlasMemFwd* fwd, const AtlasMemBwd* bwd,
@@ -410,9 +442,7 @@ int atlas_mem_forward_local(const AtlasMemShape* shape, const AtlasMemFwd* fwd, 
   P.seg_coef = seg_coef; P.seg_dS = seg_dS; P.seg_dZ = seg_dZ;
   cudaStream_t st = (cudaStream_t)stream;
   if ((v = run_fwd_local(shape, P, st))) return v;
-  const int64_t D2 = (int64_t)P.dv * P.dphi;
-  LAUNCH(KID_FWD_SCAN, k_fwd_scan, dim3((unsigned)((D2 + kThreads - 1) / kThreads), P.N), 0, st, P, 1);
-  return ATLAS_OK;
+  return launch_scan(true, P, 1, st);
 }
 
 int atlas_mem_forward_finish(const AtlasMemShape* shape, const AtlasMemFwd* fwd, void* saved, size_t saved_bytes,
@@ -443,9 +473,7 @@ int atlas_mem_backward_local(const AtlasMemShape* shape, const AtlasMemFwd* fwd,
   P.seg_coef = seg_coef; P.seg_dS = seg_dS; P.seg_dZ = seg_dZ;
   cudaStream_t st = (cudaStream_t)stream;
   if ((v = run_bwd_local(shape, P, st))) return v;
-  const int64_t D2 = (int64_t)P.dv * P.dphi;
-  LAUNCH(KID_BWD_SCAN, k_bwd_scan, dim3((unsigned)((D2 + kThreads - 1) / kThreads), P.N), 0, st, P, 1);
-  return ATLAS_OK;
+  return launch_scan(false, P, 1, st);
 }
 
 int atlas_mem_backward_finish(const AtlasMemShape* shape, const AtlasMemFwd* fwd, const AtlasMemBwd* bwd,

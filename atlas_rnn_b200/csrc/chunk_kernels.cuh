@@ -206,43 +206,80 @@ __global__ void __launch_bounds__(kThreads) k_fwd_chunk(Params P) {
 }
 
 // ===========================================================================
-// F2: sequential scan over chunks, one thread per state element. Turns the
-// chunk increments into chunk-start states in place; writes S_end / Z_end.
-// dry = 1: start from zero, write nothing in place, emit the segment transform.
+// F2: sequential scan over chunks. Each thread owns VEC consecutive state
+// elements of one unit and walks the chunks with the increments of the next
+// two chunks already in flight. Turns the chunk increments into chunk-start
+// states in place; writes S_end / Z_end. dry = 1: start from zero, write
+// nothing in place, emit the segment transform instead.
 // ===========================================================================
+template <int VEC>
+struct VecT;
+template <>
+struct VecT<1> { using T = float; };
+template <>
+struct VecT<4> { using T = float4; };
+
+__device__ __forceinline__ float axpby(float a, float x, float b, float y, float z) { return a * x + b * y + z; }
+__device__ __forceinline__ float4 axpby(float a, float4 x, float b, float4 y, float4 z) {
+  return make_float4(a * x.x + b * y.x + z.x, a * x.y + b * y.y + z.y, a * x.z + b * y.z + z.z,
+                     a * x.w + b * y.w + z.w);
+}
+__device__ __forceinline__ float vzero(float) { return 0.f; }
+__device__ __forceinline__ float4 vzero(float4) { return make_float4(0.f, 0.f, 0.f, 0.f); }
+
+// Loads the per-chunk scalars of unit n into shared memory (nch float4).
+__device__ __forceinline__ const float4* stage_chunk_scalars(const float* src, int n, int nch, float4* dst) {
+  const float4* s4 = reinterpret_cast<const float4*>(src) + (int64_t)n * nch;
+  for (int c = threadIdx.x; c < nch; c += kThreads) dst[c] = s4[c];
+  __syncthreads();
+  return dst;
+}
+
+template <int VEC>
 __global__ void __launch_bounds__(kThreads) k_fwd_scan(Params P, int dry) {
-  const int n = blockIdx.y;
-  const int64_t D2 = (int64_t)P.dv * P.dphi;
+  using V = typename VecT<VEC>::T;
+  extern __shared__ float4 scs[];
+  const int n = blockIdx.y, nch = P.nch;
+  const int64_t D2 = (int64_t)P.dv * P.dphi, DV = D2 / VEC;
   const int64_t x = (int64_t)blockIdx.x * kThreads + threadIdx.x;
+  const float4* cs = stage_chunk_scalars(P.cs, n, nch, scs);
   if (dry && blockIdx.x == 0 && threadIdx.x == 0) {
     float A = 1.f, B = 0.f, Cc = 1.f;
-    for (int c = 0; c < P.nch; ++c) {
-      const float* s = P.cs + ((int64_t)n * P.nch + c) * 4;
-      B = s[0] * B + s[1] * Cc;
-      A = s[0] * A;
-      Cc = s[2] * Cc;
+    for (int c = 0; c < nch; ++c) {
+      B = cs[c].x * B + cs[c].y * Cc;
+      A = cs[c].x * A;
+      Cc = cs[c].z * Cc;
     }
     P.seg_coef[n * 3 + 0] = A; P.seg_coef[n * 3 + 1] = B; P.seg_coef[n * 3 + 2] = Cc;
   }
-  if (x >= D2) return;
-  float S = dry ? 0.f : P.S0[n * D2 + x];
-  float Z = (dry || !P.Z0) ? 0.f : P.Z0[n * D2 + x];
-  for (int c = 0; c < P.nch; ++c) {
-    float* base = P.st + ((int64_t)n * P.nch + c) * 2 * D2;
-    const float* s = P.cs + ((int64_t)n * P.nch + c) * 4;
-    const float dS = base[x], dZ = base[D2 + x];
-    if (!dry) { base[x] = S; base[D2 + x] = Z; }
-    const float nS = s[0] * S + s[1] * Z + dS;
-    Z = s[2] * Z + dZ;
+  if (x >= DV) return;
+  V* __restrict__ st = reinterpret_cast<V*>(P.st) + (int64_t)n * nch * 2 * DV;
+  V S = dry ? vzero(V()) : reinterpret_cast<const V*>(P.S0)[n * DV + x];
+  V Z = (dry || !P.Z0) ? vzero(V()) : reinterpret_cast<const V*>(P.Z0)[n * DV + x];
+  V dS0 = st[x], dZ0 = st[DV + x];
+  V dS1 = nch > 1 ? st[2 * DV + x] : dS0, dZ1 = nch > 1 ? st[3 * DV + x] : dZ0;
+  for (int c = 0; c < nch; ++c) {
+    V dS2 = dS1, dZ2 = dZ1;
+    if (c + 2 < nch) { dS2 = st[(int64_t)(c + 2) * 2 * DV + x]; dZ2 = st[(int64_t)(c + 2) * 2 * DV + DV + x]; }
+    if (!dry) { st[(int64_t)c * 2 * DV + x] = S; st[(int64_t)c * 2 * DV + DV + x] = Z; }
+    const float4 k = cs[c];
+    const V nS = axpby(k.x, S, k.y, Z, dS0);
+    Z = axpby(k.z, Z, 0.f, Z, dZ0);
     S = nS;
+    dS0 = dS1; dZ0 = dZ1; dS1 = dS2; dZ1 = dZ2;
   }
-  if (dry) {
-    P.seg_dS[n * D2 + x] = S;
-    P.seg_dZ[n * D2 + x] = Z;
-  } else {
-    P.ST[n * D2 + x] = S;
-    P.S_end[n * D2 + x] = fminf(fmaxf(S, -100.f), 100.f);  // rnn_memory.py:701
-    if (P.Z_end) P.Z_end[n * D2 + x] = Z;                  // rnn_memory.py:702
+  const float* Sf = reinterpret_cast<const float*>(&S);
+  const float* Zf = reinterpret_cast<const float*>(&Z);
+  for (int v = 0; v < VEC; ++v) {
+    const int64_t e = n * D2 + x * VEC + v;
+    if (dry) {
+      P.seg_dS[e] = Sf[v];
+      P.seg_dZ[e] = Zf[v];
+    } else {
+      P.ST[e] = Sf[v];
+      P.S_end[e] = fminf(fmaxf(Sf[v], -100.f), 100.f);  // rnn_memory.py:701
+      if (P.Z_end) P.Z_end[e] = Zf[v];                  // rnn_memory.py:702
+    }
   }
 }
 
@@ -358,50 +395,70 @@ __global__ void __launch_bounds__(kThreads) k_bwd_chunk(Params P) {
 }
 
 // ===========================================================================
-// B2: reverse scan over chunks: adjoint arriving at each chunk end (in place),
-// and the gradients of the carried S0 / Z0. dry = 1: segment transform.
+// B2: reverse scan over chunks (same access scheme as F2): the adjoint
+// arriving at each chunk end (in place), and the gradients of the carried
+// S0 / Z0. dry = 1: segment transform from a zero adjoint.
 // ===========================================================================
+template <int VEC>
 __global__ void __launch_bounds__(kThreads) k_bwd_scan(Params P, int dry) {
-  const int n = blockIdx.y;
-  const int64_t D2 = (int64_t)P.dv * P.dphi;
+  using V = typename VecT<VEC>::T;
+  extern __shared__ float4 scs[];
+  const int n = blockIdx.y, nch = P.nch;
+  const int64_t D2 = (int64_t)P.dv * P.dphi, DV = D2 / VEC;
   const int64_t x = (int64_t)blockIdx.x * kThreads + threadIdx.x;
+  const float4* cs = stage_chunk_scalars(P.acs, n, nch, scs);
   if (dry && blockIdx.x == 0 && threadIdx.x == 0) {
     float A = 1.f, B = 0.f, Cc = 1.f;
-    for (int c = P.nch - 1; c >= 0; --c) {
-      const float* s = P.acs + ((int64_t)n * P.nch + c) * 4;
-      B = s[1] * A + s[2] * B;
-      A = s[0] * A;
-      Cc = s[2] * Cc;
+    for (int c = nch - 1; c >= 0; --c) {
+      B = cs[c].y * A + cs[c].z * B;
+      A = cs[c].x * A;
+      Cc = cs[c].z * Cc;
     }
     P.seg_coef[n * 3 + 0] = A; P.seg_coef[n * 3 + 1] = B; P.seg_coef[n * 3 + 2] = Cc;
   }
-  if (x >= D2) return;
-  float FS = 0.f, FZ = 0.f;
+  if (x >= DV) return;
+  V FS = vzero(V()), FZ = vzero(V());
   if (!dry) {
-    if (P.dS_end) {
-      FS = P.dS_end[n * D2 + x];
-      if (P.apply_mask) {  // clamp(-100, 100) passes gradient where -100 <= S_T <= 100
-        const float s = P.ST[n * D2 + x];
-        if (!(s >= -100.f && s <= 100.f)) FS = 0.f;
+    float* fs = reinterpret_cast<float*>(&FS);
+    float* fz = reinterpret_cast<float*>(&FZ);
+    for (int v = 0; v < VEC; ++v) {
+      const int64_t e = n * D2 + x * VEC + v;
+      if (P.dS_end) {
+        fs[v] = P.dS_end[e];
+        if (P.apply_mask) {  // clamp(-100, 100) passes gradient where -100 <= S_T <= 100
+          const float s = P.ST[e];
+          if (!(s >= -100.f && s <= 100.f)) fs[v] = 0.f;
+        }
       }
+      if (P.dZ_end) fz[v] = P.dZ_end[e];
     }
-    if (P.dZ_end) FZ = P.dZ_end[n * D2 + x];
   }
-  for (int c = P.nch - 1; c >= 0; --c) {
-    float* base = P.adj + ((int64_t)n * P.nch + c) * 2 * D2;
-    const float* s = P.acs + ((int64_t)n * P.nch + c) * 4;
-    const float dS = base[x], dZ = base[D2 + x];
-    if (!dry) { base[x] = FS; base[D2 + x] = FZ; }
-    const float nFS = s[0] * FS + dS;
-    FZ = s[1] * FS + s[2] * FZ + dZ;
+  V* __restrict__ st = reinterpret_cast<V*>(P.adj) + (int64_t)n * nch * 2 * DV;
+  const int cl = nch - 1;
+  V dS0 = st[(int64_t)cl * 2 * DV + x], dZ0 = st[(int64_t)cl * 2 * DV + DV + x];
+  V dS1 = cl > 0 ? st[(int64_t)(cl - 1) * 2 * DV + x] : dS0;
+  V dZ1 = cl > 0 ? st[(int64_t)(cl - 1) * 2 * DV + DV + x] : dZ0;
+  for (int c = cl; c >= 0; --c) {
+    V dS2 = dS1, dZ2 = dZ1;
+    if (c - 2 >= 0) { dS2 = st[(int64_t)(c - 2) * 2 * DV + x]; dZ2 = st[(int64_t)(c - 2) * 2 * DV + DV + x]; }
+    if (!dry) { st[(int64_t)c * 2 * DV + x] = FS; st[(int64_t)c * 2 * DV + DV + x] = FZ; }
+    const float4 k = cs[c];
+    const V nFS = axpby(k.x, FS, 0.f, FS, dS0);
+    FZ = axpby(k.y, FS, k.z, FZ, dZ0);
     FS = nFS;
+    dS0 = dS1; dZ0 = dZ1; dS1 = dS2; dZ1 = dZ2;
   }
-  if (dry) {
-    P.seg_dS[n * D2 + x] = FS;
-    P.seg_dZ[n * D2 + x] = FZ;
-  } else {
-    if (P.dS0) P.dS0[n * D2 + x] = FS;
-    if (P.dZ0) P.dZ0[n * D2 + x] = FZ;
+  const float* fs = reinterpret_cast<const float*>(&FS);
+  const float* fz = reinterpret_cast<const float*>(&FZ);
+  for (int v = 0; v < VEC; ++v) {
+    const int64_t e = n * D2 + x * VEC + v;
+    if (dry) {
+      P.seg_dS[e] = fs[v];
+      P.seg_dZ[e] = fz[v];
+    } else {
+      if (P.dS0) P.dS0[e] = fs[v];
+      if (P.dZ0) P.dZ0[e] = fz[v];
+    }
   }
 }
 

@@ -186,6 +186,11 @@ int atlas_mem_forward_local(const AtlasMemShape* shape, const AtlasMemFwd* fwd,
 int atlas_mem_forward_finish(const AtlasMemShape* shape, const AtlasMemFwd* fwd,
                              void* saved, size_t saved_bytes, void* scratch,
                              size_t scratch_bytes, void* stream);
+/* Copies the unclamped final state S_T of the last forward (held in `saved`)
+ * to out[N,d_v,d_phi]; the rank holding the end of the sequence uses it for
+ * the clamp mask of dS_end (rnn_memory.py:701). */
+int atlas_mem_final_state_raw(const AtlasMemShape* shape, const void* saved, size_t saved_bytes, float* out,
+                              void* stream);
 /* Backward segment transform of this rank, computed from zero adjoint:
  *   (FS, FZ) -> (a*FS + dFS, b*FS + c*FZ + dFZ)   coef[N,3] = (a, b, c). */
 int atlas_mem_backward_local(const AtlasMemShape* shape, const AtlasMemFwd* fwd,

@@ -1,0 +1,58 @@
+"""GPU: sequence-parallel pieces (segment transform, carry composition, finish)
+emulated as P consecutive segments in one process, against the full-sequence call."""
+import pytest
+import torch
+
+from atlas_rnn_b200 import memory_recurrence
+from atlas_rnn_b200.ops import Spec
+from atlas_rnn_b200.parallel import Segment, compose_backward_carries, compose_forward_carries
+from atlas_rnn_b200.workloads import CONFIGS, make_inputs, shrink
+from tests.helpers import TOL_BF16, TOL_F32, rel_l2
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("dtype,T,P,d", [(torch.float32, 200, 4, 32), (torch.float32, 97, 3, 16),
+                                         (torch.bfloat16, 8192, 4, 128)])
+def test_segments_match_full_call(native_lib, dtype, T, P, d):
+    w = shrink(CONFIGS[2], B=1, H=2, T=T)
+    from dataclasses import replace
+    w = replace(w, d_k=d, d_phi=d, d_v=d, dtype=dtype)
+    inp = make_inputs(w, seed=3, device="cuda", state_scale=0.1)
+    tol = TOL_F32 if dtype == torch.float32 else TOL_BF16
+    names = ("k", "q", "v", "lr", "decay", "beta")
+    # full call with autograd
+    leaves = {n: inp[n].clone().requires_grad_(True) for n in names}
+    Sr = inp["S0"].clone().requires_grad_(True)
+    S0 = inp["S0"].clone().requires_grad_(True)
+    Z0 = inp["Z0"].clone().requires_grad_(True)
+    y, S_end, Z_end, _ = memory_recurrence(*(leaves[n] for n in names), S_ref=Sr, S0=S0, Z0=Z0)
+    g = torch.Generator().manual_seed(9)
+    dS_end = torch.randn(S_end.shape, generator=g).cuda()
+    dZ_end = torch.randn(S_end.shape, generator=g).cuda()
+    torch.autograd.backward([y, S_end, Z_end], [inp["dy"], dS_end, dZ_end])
+    # segments
+    spec = Spec(window=1, momentum=True)
+    bounds = [(r * T // P, (r + 1) * T // P) for r in range(P)]
+    segs = [Segment(spec, *(inp[n][:, lo:hi].contiguous() for n in names), inp["S0"]) for lo, hi in bounds]
+    tr = [s.forward_local() for s in segs]
+    carries, (S_T, Z_T) = compose_forward_carries([t[0] for t in tr], [t[1] for t in tr], [t[2] for t in tr],
+                                                  inp["S0"], inp["Z0"])
+    ys = [s.forward_finish(*c)[0] for s, c in zip(segs, carries)]
+    assert rel_l2(torch.cat(ys, 1).float(), y.float()) < tol
+    assert rel_l2(S_T.clamp(-100, 100), S_end) < tol
+    assert rel_l2(Z_T, Z_end) < tol
+    btr = [s.backward_local(inp["dy"][:, lo:hi].contiguous()) for s, (lo, hi) in zip(segs, bounds)]
+    FS_end = dS_end * ((S_T >= -100) & (S_T <= 100))
+    inc, (dS0, dZ0) = compose_backward_carries([t[0] for t in btr], [t[1] for t in btr], [t[2] for t in btr],
+                                               FS_end, dZ_end)
+    grads = [s.backward_finish(inp["dy"][:, lo:hi].contiguous(), *c, apply_mask=False)
+             for s, c, (lo, hi) in zip(segs, inc, bounds)]
+    for n in names:
+        got = torch.cat([gr[n] for gr in grads], 1)
+        assert rel_l2(got.float(), leaves[n].grad.float()) < tol, n
+    assert rel_l2(sum(gr["S_ref"] for gr in grads), Sr.grad) < tol
+    assert rel_l2(dS0, S0.grad) < tol
+    assert rel_l2(dZ0, Z0.grad) < tol
+    # the first segment's own dS0 equals the composed one
+    assert rel_l2(grads[0]["S0"], S0.grad) < tol
