@@ -188,8 +188,9 @@ class SeqParallelMemoryFn(torch.autograd.Function):
         coef, dFS, dFZ = seg.backward_local(dy)
         coefs, dFSs, dFZs = _gather(coef, group), _gather(dFS, group), _gather(dFZ, group)
         # every rank returned the same S_end / Z_end: their upstream gradients add up
-        FS_end = torch.zeros_like(ctx.S_T) if dS_end is None else dS_end.float().contiguous()
-        FZ_end = torch.zeros_like(ctx.S_T) if (dZ_end is None or dZ_end.numel() == 0) else dZ_end.float().contiguous()
+        # copies: the all-reduce below must not modify the caller's gradient tensors
+        FS_end = torch.zeros_like(ctx.S_T) if dS_end is None else dS_end.float().clone()
+        FZ_end = torch.zeros_like(ctx.S_T) if (dZ_end is None or dZ_end.numel() == 0) else dZ_end.float().clone()
         dist.all_reduce(FS_end, group=group)
         dist.all_reduce(FZ_end, group=group)
         FS_end = FS_end * ((ctx.S_T >= -100) & (ctx.S_T <= 100))  # clamp gradient
