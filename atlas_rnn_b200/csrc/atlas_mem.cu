@@ -3,7 +3,10 @@
 // interfaces they replace are in include/atlas_mem.h.
 #include <mutex>
 
+#include <cstdlib>
+
 #include "chunk_kernels.cuh"
+#include "tc_fwd.cuh"
 #include "umma_selftest.cuh"
 
 using namespace atlas;
@@ -14,8 +17,26 @@ constexpr size_t kAlign = 256;
 inline size_t align_up(size_t x) { return (x + kAlign - 1) & ~(kAlign - 1); }
 inline int r4(int n) { return (n + 3) & ~3; }
 
+// Kernel groups that have a tensor-core version: 1 forward chunk increments,
+// 2 forward outputs, 4 backward chunk increments, 8 backward gradients.
+constexpr int kTcAll = 15;
+constexpr int kTcImplemented = 1 | 2;
+
+// Groups that run on tensor cores for this shape: bf16 io, d_phi = d_v = 128,
+// window <= 16. ATLAS_MEM_TC=<mask> restricts them (0 = CUDA cores only).
+int tc_groups(const AtlasMemShape* s) {
+  if (s->dtype_io != ATLAS_BF16 || s->d_phi != tc::kD || s->d_v != tc::kD || s->window > 16) return 0;
+  int mask = kTcAll;
+  if (const char* env = std::getenv("ATLAS_MEM_TC")) mask = std::atoi(env);
+  return mask & kTcImplemented;
+}
+
+// Tokens per chunk: the caller's choice, else 128 - e when every chunk kernel
+// runs on tensor cores (keys = chunk + e - 1 fill a 128-row tile), else the
+// CUDA-core kernels' 32.
 int chunk_of(const AtlasMemShape* s) {
   if (s->chunk > 0) return s->chunk;
+  if (tc_groups(s) == kTcAll) return 128 - s->window;
   return s->window - 1 > 32 ? s->window - 1 : 32;
 }
 
@@ -59,7 +80,7 @@ Layout make_layout(const AtlasMemShape* s) {
 
 // Dynamic shared memory of each kernel; mirrors the SmemAlloc::take sequences.
 struct Smem {
-  size_t f1, f3, b1, b3, fin, dsref, bufout, fmf, fmb;
+  size_t f1, f3, b1, b3, fin, dsref, bufout, fmf, fmb, tc_f1, tc_f3, buf_y;
 };
 Smem smem_sizes(const AtlasMemShape* s, int C) {
   const int e = s->window, L = C, K = C + e - 1, dphi = s->d_phi, dv = s->d_v, dk = s->d_k;
@@ -78,6 +99,10 @@ Smem smem_sizes(const AtlasMemShape* s, int C) {
   m.bufout = 4 * (size_t)(dphi + dv + 32);
   m.fmf = 4 * (size_t)(r4(kFmTile * dk) + kStageFloats);
   m.fmb = 4 * (size_t)(2 * r4(kFmTile * dk) + r4(kFmTile * dphi) + kStageFloats);
+  const int tctx = tc::ctx_floats(C, e);
+  m.tc_f1 = 4 * (size_t)tc::kTileBytes + 4 * (size_t)(tctx + 2 * tc::kT);
+  m.tc_f3 = 6 * (size_t)tc::kTileBytes + 4 * (size_t)(tctx + 2 * tc::kT);
+  m.buf_y = 4 * (size_t)(ctx + r4(C * (e > 1 ? e - 1 : 1)) + r4(C * dphi));
   return m;
 }
 
@@ -101,10 +126,15 @@ int ensure_attrs() {
                       (const void*)k_bwd_grads,   (const void*)k_bwd_finalize, (const void*)k_bwd_dsref,
                       (const void*)k_bwd_bufout,  (const void*)k_fmap_tensor_fwd, (const void*)k_fmap_tensor_bwd,
                       (const void*)k_fwd_scan<1>, (const void*)k_fwd_scan<4>, (const void*)k_bwd_scan<1>,
-                      (const void*)k_bwd_scan<4>};
-  for (const void* k : ks)
-    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, mx) != cudaSuccess)
+                      (const void*)k_bwd_scan<4>, (const void*)tc::k_fwd_chunk_tc, (const void*)tc::k_fwd_out_tc,
+                      (const void*)tc::k_fwd_buf_y};
+  for (const void* k : ks) {
+    cudaFuncAttributes fa;
+    if (cudaFuncGetAttributes(&fa, k) != cudaSuccess) return ATLAS_ERR_LAUNCH;
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, mx - (int)fa.sharedSizeBytes) !=
+        cudaSuccess)
       return ATLAS_ERR_LAUNCH;
+  }
   if (dev < 64) g_attr_done[dev] = true;
   return ATLAS_OK;
 }
@@ -121,13 +151,17 @@ int validate_shape(const AtlasMemShape* s) {
   if (s->d_phi > 256 || s->d_v > 256 || s->d_k > 256) return ATLAS_ERR_UNSUPPORTED;
   if (s->N > 65535 || s->T > (int64_t)1 << 30) return ATLAS_ERR_UNSUPPORTED;
   const int C = chunk_of(s);
-  if (C < 1 || C > 64 || C < s->window - 1 || C + s->window > 127) return ATLAS_ERR_UNSUPPORTED;
+  const int tcg = tc_groups(s);
+  if (C < 1 || C < s->window - 1) return ATLAS_ERR_UNSUPPORTED;
+  if (tcg != kTcAll && (C > 64 || C + s->window > 127)) return ATLAS_ERR_UNSUPPORTED;
+  if (tcg && C + s->window > 128) return ATLAS_ERR_UNSUPPORTED;
   if ((int64_t)s->N * s->T * (s->d_v > s->d_phi ? s->d_v : s->d_phi) > ((int64_t)1 << 40)) return ATLAS_ERR_UNSUPPORTED;
   const Smem m = smem_sizes(s, C);
-  const size_t mx = (size_t)max_smem_optin();
-  if (mx == 0) return ATLAS_ERR_LAUNCH;
+  const size_t mx = (size_t)max_smem_optin() - 1024;  // static shared memory of the tensor-core kernels
+  if (mx + 1024 == 0) return ATLAS_ERR_LAUNCH;
   const size_t scan_smem = (size_t)((s->T + C - 1) / C) * 16;
-  const size_t big[] = {m.f1, m.f3, m.b1, m.b3, m.fin, m.fmf, m.fmb, scan_smem};
+  const size_t big[] = {(tcg & 1) ? 0 : m.f1, (tcg & 2) ? 0 : m.f3, (tcg & 4) ? 0 : m.b1, (tcg & 8) ? 0 : m.b3,
+                        m.fin, m.fmf, m.fmb, scan_smem, m.tc_f1, m.tc_f3, m.buf_y};
   for (size_t b : big)
     if (b > mx) return ATLAS_ERR_UNSUPPORTED;
   return ATLAS_OK;
@@ -181,11 +215,11 @@ Params make_params(const AtlasMemShape* s, const Layout& L, const AtlasMemFwd* f
 // ---- launch accounting and optional per-kernel CUDA-event timing ----------
 enum KernelId {
   KID_FMAP_FWD, KID_FWD_CHUNK, KID_FWD_SCAN, KID_FWD_OUT, KID_BUF_OUT, KID_BWD_CHUNK, KID_BWD_SCAN,
-  KID_BWD_GRADS, KID_BWD_BUFOUT, KID_BWD_FINAL, KID_BWD_DSREF, KID_FMAP_BWD, KID_COUNT
+  KID_BWD_GRADS, KID_BWD_BUFOUT, KID_BWD_FINAL, KID_BWD_DSREF, KID_FMAP_BWD, KID_FWD_CHUNK_TC, KID_FWD_OUT_TC, KID_FWD_BUF_Y, KID_COUNT
 };
 const char* const kKernelNames[KID_COUNT] = {
   "k_fmap_tensor_fwd", "k_fwd_chunk", "k_fwd_scan", "k_fwd_out", "k_buf_out", "k_bwd_chunk", "k_bwd_scan",
-  "k_bwd_grads", "k_bwd_bufout", "k_bwd_finalize", "k_bwd_dsref", "k_fmap_tensor_bwd"};
+  "k_bwd_grads", "k_bwd_bufout", "k_bwd_finalize", "k_bwd_dsref", "k_fmap_tensor_bwd", "k_fwd_chunk_tc", "k_fwd_out_tc", "k_fwd_buf_y"};
 
 constexpr int kMaxTimed = 8192;
 struct Prof {
@@ -233,6 +267,15 @@ void prof_end(int slot, cudaStream_t st) {
     if (cudaGetLastError() != cudaSuccess) return ATLAS_ERR_LAUNCH; \
   } while (0)
 
+// Launch with an explicit thread count: LAUNCH_T(id, kernel, grid, threads, smem, stream, args...)
+#define LAUNCH_T(KID, KERNEL, GRID, THREADS, SMEM, STREAM, ...)   \
+  do {                                                            \
+    const int slot_ = prof_begin(KID, STREAM);                    \
+    KERNEL<<<GRID, THREADS, SMEM, STREAM>>>(__VA_ARGS__);         \
+    LAUNCH_CHECK();                                               \
+    prof_end(slot_, STREAM);                                      \
+  } while (0)
+
 // Launch `kernel` with accounting: LAUNCH(id, kernel, grid, smem, stream, args...)
 #define LAUNCH(KID, KERNEL, GRID, SMEM, STREAM, ...)              \
   do {                                                            \
@@ -265,14 +308,20 @@ int run_fwd_local(const AtlasMemShape* s, const Params& P, cudaStream_t st) {
   if (P.fmode == ATLAS_FMAP_TENSOR) {
     LAUNCH(KID_FMAP_FWD, k_fmap_tensor_fwd, dim3((P.T + kFmTile - 1) / kFmTile, P.N, 2), m.fmf, st, P);
   }
-  LAUNCH(KID_FWD_CHUNK, k_fwd_chunk, gch, m.f1, st, P);
+  if (tc_groups(s) & 1) LAUNCH_T(KID_FWD_CHUNK_TC, tc::k_fwd_chunk_tc, gch, tc::kT, m.tc_f1, st, P);
+  else LAUNCH(KID_FWD_CHUNK, k_fwd_chunk, gch, m.f1, st, P);
   return ATLAS_OK;
 }
 
 int run_fwd_finish(const AtlasMemShape* s, const Params& P, cudaStream_t st) {
   const Smem m = smem_sizes(s, P.C);
   if (int v = launch_scan(true, P, 0, st)) return v;
-  LAUNCH(KID_FWD_OUT, k_fwd_out, dim3(P.nch, P.N), m.f3, st, P);
+  if (tc_groups(s) & 2) {
+    LAUNCH_T(KID_FWD_OUT_TC, tc::k_fwd_out_tc, dim3(P.nch, P.N), tc::kT, m.tc_f3, st, P);
+    if (P.buf && P.e > 1) LAUNCH(KID_FWD_BUF_Y, tc::k_fwd_buf_y, dim3(1, P.N), m.buf_y, st, P);
+  } else {
+    LAUNCH(KID_FWD_OUT, k_fwd_out, dim3(P.nch, P.N), m.f3, st, P);
+  }
   if (P.e > 1 && P.buf_out) {
     LAUNCH(KID_BUF_OUT, k_buf_out, dim3(P.e - 1, P.N), 0, st, P);
   }

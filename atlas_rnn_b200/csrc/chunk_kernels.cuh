@@ -20,7 +20,7 @@ struct Ctx {
   float *al, *et, *be, *u, *U;
 };
 
-__device__ __forceinline__ void load_ctx(const Params& P, SmemAlloc& sa, Ctx& cx) {
+__device__ __forceinline__ void load_ctx(const Params& P, SmemAlloc& sa, Ctx& cx, int nthreads = kThreads) {
   cx.n = blockIdx.y;
   cx.c = blockIdx.x;
   cx.t0 = cx.c * P.C;
@@ -33,18 +33,18 @@ __device__ __forceinline__ void load_ctx(const Params& P, SmemAlloc& sa, Ctx& cx
   cx.u = sa.take(P.C + P.e);
   cx.U = sa.take(P.C * P.e);
   const int64_t row0 = (int64_t)cx.n * P.T + cx.t0;
-  for (int i = threadIdx.x; i < cx.L; i += kThreads) {
+  for (int i = threadIdx.x; i < cx.L; i += nthreads) {
     cx.al[i] = ldio(P.decay, row0 + i, P.bf);                   // alpha  (to_decay)
     cx.et[i] = ldio(P.lr, row0 + i, P.bf);                      // eta    (to_lr)
     cx.be[i] = P.mom ? ldio(P.beta, row0 + i, P.bf) : 0.f;      // beta   (to_momentum)
   }
   if (P.gmode == ATLAS_GATE_TOKEN)
-    for (int j = threadIdx.x; j < cx.K; j += kThreads) {
+    for (int j = threadIdx.x; j < cx.K; j += nthreads) {
       const int p = cx.kp0 + j;
       cx.u[j] = p >= 0 ? ldio(P.gate, (int64_t)cx.n * P.T + p, P.bf) : 1.f;
     }
   if (P.gmode == ATLAS_GATE_WINDOW)
-    for (int x = threadIdx.x; x < cx.L * P.e; x += kThreads)
+    for (int x = threadIdx.x; x < cx.L * P.e; x += nthreads)
       cx.U[x] = ldio(P.gate, row0 * P.e + x, P.bf);
 }
 

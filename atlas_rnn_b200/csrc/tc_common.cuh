@@ -1,0 +1,166 @@
+// Shared pieces of the tensor-core (tcgen05) chunk kernels.
+//
+// Every tensor-core chunk kernel runs 128 threads: thread t owns TMEM lane t,
+// i.e. row t of every 128-row accumulator. Operand tiles are 128 rows x D
+// columns of bf16 in the core-matrix layout of umma.cuh (rows past the valid
+// range are zero). Head sizes d_phi = d_v = D = 128.
+#pragma once
+#include <cuda_bf16.h>
+
+#include "chunk_kernels.cuh"
+#include "umma.cuh"
+
+namespace atlas {
+namespace tc {
+
+constexpr int kT = 128;        // threads per CTA
+constexpr int kD = 128;        // head size handled by the tensor-core path
+constexpr int kTileBytes = 128 * kD * 2;
+
+struct Op {
+  uint32_t saddr;  // shared address of the tile
+  int C;           // contiguous extent of the tile (columns)
+  int mn;          // 0: K-major use (K = columns), 1: MN-major use (K = rows)
+};
+__device__ __forceinline__ Op op(const void* tile, int C, int mn) { return Op{umma::smem_u32(tile), C, mn}; }
+
+// D[tmem] (+)= A * B over `ksteps` K-steps of 16; issued by the calling thread.
+__device__ __forceinline__ void mma_chain(uint32_t d_tmem, Op A, Op B, int ksteps, int N, bool acc_first) {
+  const uint32_t idesc = umma::make_idesc(128, N, A.mn, B.mn);
+  for (int s = 0; s < ksteps; ++s) {
+    const uint64_t ad = A.mn ? umma::desc_mnmajor(A.saddr, A.C, s) : umma::desc_kmajor(A.saddr, A.C, s);
+    const uint64_t bd = B.mn ? umma::desc_mnmajor(B.saddr, B.C, s) : umma::desc_kmajor(B.saddr, B.C, s);
+    umma::mma(d_tmem, ad, bd, idesc, (s > 0 || acc_first) ? 1 : 0);
+  }
+}
+
+// Per-CTA tensor-core state: TMEM base, one mbarrier and its phase, a status word.
+struct Sync {
+  uint64_t* mbar;
+  uint32_t* tbase;
+  uint32_t phase;
+  int* status;
+};
+
+// Allocate 512 TMEM columns and init the barrier (all threads call).
+__device__ __forceinline__ uint32_t tc_setup(Sync& s) {
+  if (threadIdx.x < 32) {
+    umma::tmem_alloc(s.tbase, 512);
+    umma::tmem_relinquish();
+  }
+  if (threadIdx.x == 0) umma::mbar_init(s.mbar, 1);
+  umma::fence_before();
+  __syncthreads();
+  umma::fence_after();
+  s.phase = 0;
+  return *s.tbase;
+}
+
+// Make this thread's generic smem writes visible to the tensor core and sync.
+__device__ __forceinline__ void smem_to_tc() {
+  umma::fence_async_smem();
+  umma::fence_before();
+  __syncthreads();
+  umma::fence_after();
+}
+
+// Thread 0 commits the MMAs issued so far; everybody waits for them (bounded).
+__device__ __forceinline__ void mma_wait(Sync& s) {
+  if (threadIdx.x == 0) umma::commit(s.mbar);
+  const bool ok = umma::mbar_wait(s.mbar, s.phase);
+  if (!ok && s.status) atomicExch(s.status, 1);
+  s.phase ^= 1u;
+  umma::fence_after();
+}
+
+// Release TMEM (all threads call; after the last TMEM access).
+__device__ __forceinline__ void tc_teardown(uint32_t tm) {
+  umma::fence_before();
+  __syncthreads();
+  if (threadIdx.x < 32) umma::tmem_dealloc(tm, 512);
+}
+
+// TMEM address of row (this thread's lane) and column `col`.
+__device__ __forceinline__ uint32_t lane_addr(uint32_t tm, int col) {
+  return tm + ((uint32_t)((threadIdx.x >> 5) * 32) << 16) + (uint32_t)col;
+}
+
+// Pack 8 floats to bf16 and store one 16-byte unit of a tile.
+__device__ __forceinline__ void store_unit(unsigned char* tile, int r, int cb, int C, const float (&v)[8]) {
+  __align__(16) __nv_bfloat162 h[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+  *reinterpret_cast<uint4*>(tile + umma::unit_off(r, cb, C)) = *reinterpret_cast<uint4*>(h);
+}
+__device__ __forceinline__ void load_unit(const unsigned char* tile, int r, int cb, int C, float (&v)[8]) {
+  const uint4 u = *reinterpret_cast<const uint4*>(tile + umma::unit_off(r, cb, C));
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+
+// Fill a 128 x C tile; src(r, c0, v) fills v[0..7] for columns c0..c0+7 of row r.
+template <class F>
+__device__ __forceinline__ void fill_tile(unsigned char* tile, int C, F src) {
+  const int units = 128 * (C / 8);
+  for (int u = threadIdx.x; u < units; u += kT) {
+    const int r = u / (C / 8), cb = u - r * (C / 8);
+    float v[8];
+    src(r, cb * 8, v);
+    store_unit(tile, r, cb, C, v);
+  }
+}
+
+__device__ __forceinline__ void zero8(float (&v)[8]) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = 0.f;
+}
+
+// 8 io values starting at element `off` (bf16 as one 16-byte load when aligned).
+__device__ __forceinline__ void ld8io(const void* p, int64_t off, int bf, float (&v)[8]) {
+  if (bf) {
+    const uint4 u = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(p) + off);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __bfloat1622float2(h[i]);
+      v[2 * i] = f.x;
+      v[2 * i + 1] = f.y;
+    }
+  } else {
+    const float4 a = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p) + off);
+    const float4 b = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p) + off + 4);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  }
+}
+__device__ __forceinline__ void ld8f(const float* p, float (&v)[8]) {
+  const float4 a = *reinterpret_cast<const float4*>(p);
+  const float4 b = *reinterpret_cast<const float4*>(p + 4);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
+// phi (keys, !isq) or psi (isq) of token t, columns c0..c0+7.
+__device__ __forceinline__ void phi8(const Params& P, int n, int t, int c0, bool isq, float (&v)[8]) {
+  const int64_t row = (int64_t)n * P.T + t;
+  if (P.fmode == ATLAS_FMAP_TENSOR) {
+    ld8f((isq ? P.phiq : P.phik) + row * P.dphi + c0, v);
+    return;
+  }
+  ld8io(isq ? P.q : P.k, row * P.dk + c0, P.bf, v);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = fmap_elem(v[i], P.fmode, P.fdeg);
+}
+
+// 16 floats to global (fp32), 64 bytes.
+__device__ __forceinline__ void st16f(float* dst, const float (&v)[16]) {
+  float4* d = reinterpret_cast<float4*>(dst);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) d[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+}
+
+}  // namespace tc
+}  // namespace atlas

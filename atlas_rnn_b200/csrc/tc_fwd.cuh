@@ -1,0 +1,280 @@
+// Tensor-core (tcgen05) versions of the forward chunk kernels, bf16 operands
+// with fp32 accumulation in TMEM. Same inputs, outputs and workspace layout
+// as k_fwd_chunk / k_fwd_out (chunk_kernels.cuh).
+#pragma once
+#include "tc_common.cuh"
+
+namespace atlas {
+namespace tc {
+
+// Floats of per-chunk context (gates) for a chunk length C and window e.
+__host__ __device__ __forceinline__ int ctx_floats(int C, int e) {
+  auto r4 = [](int n) { return (n + 3) & ~3; };
+  return 3 * r4(C) + r4(C + e) + r4(C * e);
+}
+
+// Key rows of phi into a tile (zero for p < 0 and rows >= K).
+__device__ __forceinline__ void fill_keys_phi(const Params& P, const Ctx& cx, unsigned char* tile) {
+  fill_tile(tile, kD, [&](int r, int c0, float(&v)[8]) {
+    const int p = cx.kp0 + r;
+    if (r < cx.K && p >= 0) phi8(P, cx.n, p, c0, false, v);
+    else zero8(v);
+  });
+}
+// Token rows of psi (zero for rows >= L).
+__device__ __forceinline__ void fill_rows_psi(const Params& P, const Ctx& cx, unsigned char* tile) {
+  fill_tile(tile, kD, [&](int r, int c0, float(&v)[8]) {
+    if (r < cx.L) phi8(P, cx.n, cx.t0 + r, c0, true, v);
+    else zero8(v);
+  });
+}
+// A dense fp32 [128 x 128] row-major matrix into a tile.
+__device__ __forceinline__ void fill_dense(unsigned char* tile, const float* M) {
+  fill_tile(tile, kD, [&](int r, int c0, float(&v)[8]) { ld8f(M + r * kD + c0, v); });
+}
+
+// ===========================================================================
+// delta and the chunk increments (dS, dZ) on tensor cores.
+//   delta[keys x d_v] = Phi[keys x d_phi] S_ref^T - V
+//   dS[d_v x d_phi]   = (diag(cS_end) delta)^T Phi,  dZ likewise with cZ_end
+// ===========================================================================
+__global__ void __launch_bounds__(kT) k_fwd_chunk_tc(Params P) {
+  extern __shared__ __align__(1024) unsigned char sm[];
+  unsigned char* tPhi = sm;
+  unsigned char* tSref = sm + kTileBytes;
+  unsigned char* tDS = sm + 2 * kTileBytes;
+  unsigned char* tDZ = sm + 3 * kTileBytes;
+  SmemAlloc sa{reinterpret_cast<float*>(sm + 4 * kTileBytes), 0};
+  __shared__ uint64_t mbar;
+  __shared__ uint32_t tbase;
+  Ctx cx;
+  load_ctx(P, sa, cx, kT);
+  float* cSe = sa.take(kT);
+  float* cZe = sa.take(kT);
+  const int n = cx.n, c = cx.c, K = cx.K, L = cx.L, tid = threadIdx.x;
+  Sync sy{&mbar, &tbase, 0, nullptr};
+  const uint32_t tm = tc_setup(sy);
+  fill_keys_phi(P, cx, tPhi);
+  fill_dense(tSref, P.Sref + (int64_t)n * kD * kD);
+  __syncthreads();  // gates visible to the coefficient threads
+  {
+    float cs = 0.f, cz = 0.f;
+    if (tid < K)
+      for (int i = 0; i < L; ++i) {
+        cz = cx.be[i] * cz + wgt(P, cx, i, tid);
+        cs = cx.al[i] * cs - cx.et[i] * cz;
+      }
+    cSe[tid] = cs;
+    cZe[tid] = cz;
+    if (tid == kT - 1) {
+      float s = 1.f, sz = 0.f, z = 1.f;
+      for (int i = 0; i < L; ++i) {
+        z = cx.be[i] * z;
+        s = cx.al[i] * s;
+        sz = cx.al[i] * sz - cx.et[i] * z;
+      }
+      float* o = P.cs + ((int64_t)n * P.nch + c) * 4;
+      o[0] = s; o[1] = sz; o[2] = z; o[3] = 0.f;
+    }
+  }
+  smem_to_tc();
+  if (tid == 0) mma_chain(tm, op(tPhi, kD, 0), op(tSref, kD, 0), kD / 16, kD, false);
+  mma_wait(sy);
+  {  // delta rows: thread = key j
+    const int j = tid, p = cx.kp0 + j;
+    const bool valid = j < K && p >= 0;
+    const float ws = cSe[j], wz = cZe[j];
+    for (int c16 = 0; c16 < kD / 16; ++c16) {
+      float a[16];
+      umma::tmem_ld16(lane_addr(tm, c16 * 16), a);
+      umma::tmem_ld_wait();
+      if (valid) {
+        float v0[8], v1[8];
+        const int64_t off = ((int64_t)n * P.T + p) * P.dv + c16 * 16;
+        ld8io(P.v, off, P.bf, v0);
+        ld8io(P.v, off + 8, P.bf, v1);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) { a[i] -= v0[i]; a[8 + i] -= v1[i]; }
+        if (p >= cx.t0) st16f(P.delta + off, a);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) a[i] = 0.f;
+      }
+      float s0[8], s1[8], z0[8], z1[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        s0[i] = ws * a[i]; s1[i] = ws * a[8 + i];
+        z0[i] = wz * a[i]; z1[i] = wz * a[8 + i];
+      }
+      store_unit(tDS, j, 2 * c16, kD, s0);
+      store_unit(tDS, j, 2 * c16 + 1, kD, s1);
+      store_unit(tDZ, j, 2 * c16, kD, z0);
+      store_unit(tDZ, j, 2 * c16 + 1, kD, z1);
+    }
+  }
+  smem_to_tc();
+  if (tid == 0) {
+    mma_chain(tm + 128, op(tDS, kD, 1), op(tPhi, kD, 1), 8, kD, false);
+    mma_chain(tm + 256, op(tDZ, kD, 1), op(tPhi, kD, 1), 8, kD, false);
+  }
+  mma_wait(sy);
+  {  // increments: thread = state row nn
+    const int64_t D2 = (int64_t)kD * kD;
+    float* dst = P.st + ((int64_t)n * P.nch + c) * 2 * D2 + (int64_t)tid * kD;
+    const float* bufn = buf_of(P, n, c);
+    const int nb = bufn ? P.e - 1 : 0;
+    for (int c16 = 0; c16 < kD / 16; ++c16) {
+      float a[16], b[16];
+      umma::tmem_ld16(lane_addr(tm, 128 + c16 * 16), a);
+      umma::tmem_ld16(lane_addr(tm, 256 + c16 * 16), b);
+      umma::tmem_ld_wait();
+      for (int jb = 0; jb < nb; ++jb) {  // carried buffer entries of chunk 0 (dense)
+        const float* bj = bufn + (int64_t)jb * D2 + (int64_t)tid * kD + c16 * 16;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) { a[i] += cSe[jb] * bj[i]; b[i] += cZe[jb] * bj[i]; }
+      }
+      st16f(dst + c16 * 16, a);
+      st16f(dst + D2 + c16 * 16, b);
+    }
+  }
+  tc_teardown(tm);
+}
+
+// ===========================================================================
+// outputs y on tensor cores:
+//   y = (cS o Psi Phi^T) delta + diag(sS) Psi S_in^T + diag(sZ) Psi Z_in^T
+// (chunk 0 with a carried buffer adds its dense terms in k_fwd_buf_y).
+// ===========================================================================
+__global__ void __launch_bounds__(kT) k_fwd_out_tc(Params P) {
+  extern __shared__ __align__(1024) unsigned char sm[];
+  unsigned char* tPsi = sm;
+  unsigned char* tPhi = sm + kTileBytes;
+  unsigned char* tDl = sm + 2 * kTileBytes;
+  unsigned char* tMs = sm + 3 * kTileBytes;
+  unsigned char* tSin = sm + 4 * kTileBytes;
+  unsigned char* tZin = sm + 5 * kTileBytes;
+  SmemAlloc sa{reinterpret_cast<float*>(sm + 6 * kTileBytes), 0};
+  __shared__ uint64_t mbar;
+  __shared__ uint32_t tbase;
+  Ctx cx;
+  load_ctx(P, sa, cx, kT);
+  float* sSv = sa.take(kT);
+  float* sZv = sa.take(kT);
+  const int n = cx.n, c = cx.c, K = cx.K, L = cx.L, tid = threadIdx.x;
+  Sync sy{&mbar, &tbase, 0, nullptr};
+  const uint32_t tm = tc_setup(sy);
+  const int64_t D2 = (int64_t)kD * kD;
+  const float* Sin = P.st + ((int64_t)n * P.nch + c) * 2 * D2;
+  fill_rows_psi(P, cx, tPsi);
+  fill_keys_phi(P, cx, tPhi);
+  fill_tile(tDl, kD, [&](int r, int c0, float(&v)[8]) {
+    const int p = cx.kp0 + r;
+    if (r < K && p >= 0) ld8f(P.delta + ((int64_t)n * P.T + p) * P.dv + c0, v);
+    else zero8(v);
+  });
+  fill_dense(tSin, Sin);
+  fill_dense(tZin, Sin + D2);
+  __syncthreads();
+  {  // column tid of tMs: cS of key tid before each token (row i)
+    float cs = 0.f, cz = 0.f;
+    const int j = tid;
+    for (int i = 0; i < kT; ++i) {
+      const float val = (i < L && j < K) ? cs : 0.f;
+      *reinterpret_cast<__nv_bfloat16*>(tMs + umma::elem_off(i, j, kT)) = __float2bfloat16_rn(val);
+      if (i < L && j < K) {
+        cz = cx.be[i] * cz + wgt(P, cx, i, j);
+        cs = cx.al[i] * cs - cx.et[i] * cz;
+      }
+    }
+    if (tid == kT - 1) {
+      float s = 1.f, sz = 0.f, z = 1.f;
+      for (int i = 0; i < L; ++i) {
+        sSv[i] = s;
+        sZv[i] = sz;
+        z = cx.be[i] * z;
+        s = cx.al[i] * s;
+        sz = cx.al[i] * sz - cx.et[i] * z;
+      }
+    }
+  }
+  smem_to_tc();
+  if (tid == 0) {
+    mma_chain(tm, op(tPsi, kD, 0), op(tPhi, kD, 0), kD / 16, kT, false);          // A2 = Psi Phi^T
+    mma_chain(tm + 128, op(tPsi, kD, 0), op(tSin, kD, 0), kD / 16, kD, false);    // Psi S_in^T
+    mma_chain(tm + 256, op(tPsi, kD, 0), op(tZin, kD, 0), kD / 16, kD, false);    // Psi Z_in^T
+  }
+  mma_wait(sy);
+  for (int c16 = 0; c16 < kT / 16; ++c16) {  // Ms = cS o A2, row tid
+    float a[16], m0[8], m1[8];
+    umma::tmem_ld16(lane_addr(tm, c16 * 16), a);
+    umma::tmem_ld_wait();
+    load_unit(tMs, tid, 2 * c16, kT, m0);
+    load_unit(tMs, tid, 2 * c16 + 1, kT, m1);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) { m0[i] *= a[i]; m1[i] *= a[8 + i]; }
+    store_unit(tMs, tid, 2 * c16, kT, m0);
+    store_unit(tMs, tid, 2 * c16 + 1, kT, m1);
+  }
+  smem_to_tc();
+  if (tid == 0) mma_chain(tm + 384, op(tMs, kT, 0), op(tDl, kD, 1), 8, kD, false);
+  mma_wait(sy);
+  {
+    const int i = tid;
+    const float ss = i < L ? sSv[i] : 0.f, sz = i < L ? sZv[i] : 0.f;
+    for (int c16 = 0; c16 < kD / 16; ++c16) {
+      float yi[16], ps[16], pz[16];
+      umma::tmem_ld16(lane_addr(tm, 384 + c16 * 16), yi);
+      umma::tmem_ld16(lane_addr(tm, 128 + c16 * 16), ps);
+      umma::tmem_ld16(lane_addr(tm, 256 + c16 * 16), pz);
+      umma::tmem_ld_wait();
+      if (i < L) {
+        const int64_t off = ((int64_t)n * P.T + cx.t0 + i) * P.dv + c16 * 16;
+#pragma unroll
+        for (int k = 0; k < 16; ++k) stio(P.y, off + k, yi[k] + ss * ps[k] + sz * pz[k], P.bf);
+      }
+    }
+  }
+  tc_teardown(tm);
+}
+
+// Chunk 0 with a carried buffer: y_i += sum_jb cS_i[jb] Buf_jb psi_i (dense
+// buffer entries, CUDA cores). One CTA of kThreads per unit.
+__global__ void __launch_bounds__(kThreads) k_fwd_buf_y(Params P) {
+  extern __shared__ float smem[];
+  SmemAlloc sa{smem, 0};
+  Ctx cx;
+  load_ctx(P, sa, cx);  // blockIdx.x = 0: chunk 0
+  const int L = cx.L, e1 = P.e - 1, dv = P.dv, dphi = P.dphi, n = cx.n;
+  float* cSb = sa.take(L * e1);      // cS before token i for buffer key jb
+  float* psi = sa.take(L * dphi);
+  __syncthreads();
+  if ((int)threadIdx.x < e1) {
+    const int j = threadIdx.x;
+    float cs = 0.f, cz = 0.f;
+    for (int i = 0; i < L; ++i) {
+      cSb[i * e1 + j] = cs;
+      cz = cx.be[i] * cz + wgt(P, cx, i, j);
+      cs = cx.al[i] * cs - cx.et[i] * cz;
+    }
+  }
+  for (int x = threadIdx.x; x < L * dphi; x += kThreads) psi[x] = load_phi(P, n, x / dphi, x % dphi, true);
+  __syncthreads();
+  const float* bufn = P.buf + (int64_t)n * e1 * dv * dphi;
+  for (int x = threadIdx.x; x < L * dv; x += kThreads) {
+    const int i = x / dv, nn = x - i * dv;
+    float acc = 0.f;
+    for (int jb = 0; jb < e1; ++jb) {
+      const float w = cSb[i * e1 + jb];
+      if (w == 0.f) continue;
+      const float* row = bufn + ((int64_t)jb * dv + nn) * dphi;
+      float s = 0.f;
+      for (int m = 0; m < dphi; ++m) s += row[m] * psi[i * dphi + m];
+      acc += w * s;
+    }
+    const int64_t off = ((int64_t)n * P.T + i) * dv + nn;
+    stio(P.y, off, ldio(P.y, off, P.bf) + acc, P.bf);
+  }
+}
+
+}  // namespace tc
+}  // namespace atlas

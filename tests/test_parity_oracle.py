@@ -115,3 +115,19 @@ def test_config4_slice(native_lib):
 def test_chunk_invariance(native_lib, chunk):
     """The internal chunk is only a tiling (reference: test_rnn_all.py:335-374)."""
     run_case(W("chunk_inv", 90, e=4, gate="token"), chunk=chunk)
+
+
+# bf16, head size 128: the tensor-core kernels run for these (ATLAS_MEM_TC selects them)
+CASES_TC = [
+    W("tc_titans", 300, d=128, dtype=torch.bfloat16),
+    W("tc_omega_e4_window_elem", 257, d=128, e=4, gate="window", fm="elementwise", deg=2, dtype=torch.bfloat16),
+    W("tc_omega_e16_token", 200, d=128, e=16, gate="token", dtype=torch.bfloat16),
+    W("tc_nomom_e2", 130, d=128, e=2, gate="token", mom=False, dtype=torch.bfloat16),
+    W("tc_short", 5, d=128, e=3, gate="token", dtype=torch.bfloat16),
+]
+
+
+@pytest.mark.parametrize("w", CASES_TC, ids=lambda w: w.name)
+@pytest.mark.parametrize("state_scale", [0.0, 0.1])
+def test_bf16_tensor_core_path(native_lib, w, state_scale):
+    run_case(w, state_scale=state_scale)
