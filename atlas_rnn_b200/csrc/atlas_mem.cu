@@ -6,7 +6,7 @@
 #include <cstdlib>
 
 #include "chunk_kernels.cuh"
-#include "tc_fwd.cuh"
+#include "tc_bwd.cuh"
 #include "umma_selftest.cuh"
 
 using namespace atlas;
@@ -20,7 +20,7 @@ inline int r4(int n) { return (n + 3) & ~3; }
 // Kernel groups that have a tensor-core version: 1 forward chunk increments,
 // 2 forward outputs, 4 backward chunk increments, 8 backward gradients.
 constexpr int kTcAll = 15;
-constexpr int kTcImplemented = 1 | 2;
+constexpr int kTcImplemented = kTcAll;
 
 // Groups that run on tensor cores for this shape: bf16 io, d_phi = d_v = 128,
 // window <= 16. ATLAS_MEM_TC=<mask> restricts them (0 = CUDA cores only).
@@ -45,6 +45,7 @@ struct Layout {
   size_t saved, fwd, bwd;
   size_t st, delta, ST, cs, phik, phiq;                        // in saved
   size_t adj, acs, dpsi, ddel, dphiR, hdd, hdp, du, hdu;       // in bwd scratch
+  size_t xq, xf, xs, gt;                                        // in bwd scratch (tensor-core path)
 };
 
 Layout make_layout(const AtlasMemShape* s) {
@@ -74,13 +75,19 @@ Layout make_layout(const AtlasMemShape* s) {
   L.hdp = put(N * nch * (e1 ? e1 : 1) * s->d_phi * 4);
   L.du = put(N * T * 4);
   L.hdu = put(N * nch * (e1 ? e1 : 1) * 4);
+  if (tc_groups(s) & 8) {
+    L.xq = put(N * nch * 128 * 2 * 4);
+    L.xf = put(N * nch * 128 * 2 * 4);
+    L.xs = put(N * nch * 4 * 4);
+    L.gt = put(N * nch * (size_t)tc::kTileBytes);
+  }
   L.bwd = o;
   return L;
 }
 
 // Dynamic shared memory of each kernel; mirrors the SmemAlloc::take sequences.
 struct Smem {
-  size_t f1, f3, b1, b3, fin, dsref, bufout, fmf, fmb, tc_f1, tc_f3, buf_y;
+  size_t f1, f3, b1, b3, fin, dsref, bufout, fmf, fmb, tc_f1, tc_f3, buf_y, tc_b1, tc_b4, tc_b6, buf_b;
 };
 Smem smem_sizes(const AtlasMemShape* s, int C) {
   const int e = s->window, L = C, K = C + e - 1, dphi = s->d_phi, dv = s->d_v, dk = s->d_k;
@@ -103,6 +110,10 @@ Smem smem_sizes(const AtlasMemShape* s, int C) {
   m.tc_f1 = 4 * (size_t)tc::kTileBytes + 4 * (size_t)(tctx + 2 * tc::kT);
   m.tc_f3 = 6 * (size_t)tc::kTileBytes + 4 * (size_t)(tctx + 2 * tc::kT);
   m.buf_y = 4 * (size_t)(ctx + r4(C * (e > 1 ? e - 1 : 1)) + r4(C * dphi));
+  m.tc_b1 = 3 * (size_t)tc::kTileBytes + 4 * (size_t)(tctx + 2 * tc::kT);
+  m.tc_b4 = 4 * (size_t)tc::kTileBytes + 4 * (size_t)(tctx + 3 * 132 + 32);
+  m.tc_b6 = 6 * (size_t)tc::kTileBytes + 4 * (size_t)(tctx + 6 * 132 + 2 * 128 * 2 + 4 + 128);
+  m.buf_b = 4 * (size_t)(ctx + r4(C * dphi) + r4(C * dv) + 2 * r4(C * (e > 1 ? e - 1 : 1)) + 3 * r4(C + 1) + 32);
   return m;
 }
 
@@ -127,7 +138,9 @@ int ensure_attrs() {
                       (const void*)k_bwd_bufout,  (const void*)k_fmap_tensor_fwd, (const void*)k_fmap_tensor_bwd,
                       (const void*)k_fwd_scan<1>, (const void*)k_fwd_scan<4>, (const void*)k_bwd_scan<1>,
                       (const void*)k_bwd_scan<4>, (const void*)tc::k_fwd_chunk_tc, (const void*)tc::k_fwd_out_tc,
-                      (const void*)tc::k_fwd_buf_y};
+                      (const void*)tc::k_fwd_buf_y, (const void*)tc::k_bwd_chunk_tc, (const void*)tc::k_bwd_state_tc,
+                      (const void*)tc::k_bwd_adj_tc, (const void*)tc::k_bwd_intra_tc, (const void*)tc::k_bwd_buf_tc,
+                      (const void*)tc::k_bwd_gates_tc};
   for (const void* k : ks) {
     cudaFuncAttributes fa;
     if (cudaFuncGetAttributes(&fa, k) != cudaSuccess) return ATLAS_ERR_LAUNCH;
@@ -161,7 +174,8 @@ int validate_shape(const AtlasMemShape* s) {
   if (mx + 1024 == 0) return ATLAS_ERR_LAUNCH;
   const size_t scan_smem = (size_t)((s->T + C - 1) / C) * 16;
   const size_t big[] = {(tcg & 1) ? 0 : m.f1, (tcg & 2) ? 0 : m.f3, (tcg & 4) ? 0 : m.b1, (tcg & 8) ? 0 : m.b3,
-                        m.fin, m.fmf, m.fmb, scan_smem, m.tc_f1, m.tc_f3, m.buf_y};
+                        m.fin, m.fmf, m.fmb, scan_smem, tcg ? m.tc_f1 : 0, tcg ? m.tc_f3 : 0, tcg ? m.buf_y : 0,
+                        tcg ? m.tc_b6 : 0, tcg ? m.buf_b : 0};
   for (size_t b : big)
     if (b > mx) return ATLAS_ERR_UNSUPPORTED;
   return ATLAS_OK;
@@ -207,6 +221,9 @@ Params make_params(const AtlasMemShape* s, const Layout& L, const AtlasMemFwd* f
     P.adj = (float*)(sc + L.adj); P.acs = (float*)(sc + L.acs); P.dpsi = (float*)(sc + L.dpsi);
     P.ddel = (float*)(sc + L.ddel); P.dphiR = (float*)(sc + L.dphiR); P.hdd = (float*)(sc + L.hdd);
     P.hdp = (float*)(sc + L.hdp); P.du = (float*)(sc + L.du); P.hdu = (float*)(sc + L.hdu);
+    if (tc_groups(s) & 8) {
+      P.xq = (float*)(sc + L.xq); P.xf = (float*)(sc + L.xf); P.xs = (float*)(sc + L.xs); P.gt = sc + L.gt;
+    }
   }
   P.apply_mask = 1;
   return P;
@@ -215,11 +232,13 @@ Params make_params(const AtlasMemShape* s, const Layout& L, const AtlasMemFwd* f
 // ---- launch accounting and optional per-kernel CUDA-event timing ----------
 enum KernelId {
   KID_FMAP_FWD, KID_FWD_CHUNK, KID_FWD_SCAN, KID_FWD_OUT, KID_BUF_OUT, KID_BWD_CHUNK, KID_BWD_SCAN,
-  KID_BWD_GRADS, KID_BWD_BUFOUT, KID_BWD_FINAL, KID_BWD_DSREF, KID_FMAP_BWD, KID_FWD_CHUNK_TC, KID_FWD_OUT_TC, KID_FWD_BUF_Y, KID_COUNT
+  KID_BWD_GRADS, KID_BWD_BUFOUT, KID_BWD_FINAL, KID_BWD_DSREF, KID_FMAP_BWD, KID_FWD_CHUNK_TC, KID_FWD_OUT_TC, KID_FWD_BUF_Y,
+  KID_BWD_CHUNK_TC, KID_BWD_STATE_TC, KID_BWD_ADJ_TC, KID_BWD_INTRA_TC, KID_BWD_BUF_TC, KID_BWD_GATES_TC, KID_COUNT
 };
 const char* const kKernelNames[KID_COUNT] = {
   "k_fmap_tensor_fwd", "k_fwd_chunk", "k_fwd_scan", "k_fwd_out", "k_buf_out", "k_bwd_chunk", "k_bwd_scan",
-  "k_bwd_grads", "k_bwd_bufout", "k_bwd_finalize", "k_bwd_dsref", "k_fmap_tensor_bwd", "k_fwd_chunk_tc", "k_fwd_out_tc", "k_fwd_buf_y"};
+  "k_bwd_grads", "k_bwd_bufout", "k_bwd_finalize", "k_bwd_dsref", "k_fmap_tensor_bwd", "k_fwd_chunk_tc", "k_fwd_out_tc", "k_fwd_buf_y",
+  "k_bwd_chunk_tc", "k_bwd_state_tc", "k_bwd_adj_tc", "k_bwd_intra_tc", "k_bwd_buf_tc", "k_bwd_gates_tc"};
 
 constexpr int kMaxTimed = 8192;
 struct Prof {
@@ -330,14 +349,24 @@ int run_fwd_finish(const AtlasMemShape* s, const Params& P, cudaStream_t st) {
 
 int run_bwd_local(const AtlasMemShape* s, const Params& P, cudaStream_t st) {
   const Smem m = smem_sizes(s, P.C);
-  LAUNCH(KID_BWD_CHUNK, k_bwd_chunk, dim3(P.nch, P.N), m.b1, st, P);
+  if (tc_groups(s) & 4) LAUNCH_T(KID_BWD_CHUNK_TC, tc::k_bwd_chunk_tc, dim3(P.nch, P.N), tc::kT, m.tc_b1, st, P);
+  else LAUNCH(KID_BWD_CHUNK, k_bwd_chunk, dim3(P.nch, P.N), m.b1, st, P);
   return ATLAS_OK;
 }
 
 int run_bwd_finish(const AtlasMemShape* s, const Params& P, cudaStream_t st) {
   const Smem m = smem_sizes(s, P.C);
   if (int v = launch_scan(false, P, 0, st)) return v;
-  LAUNCH(KID_BWD_GRADS, k_bwd_grads, dim3(P.nch, P.N), m.b3, st, P);
+  if (tc_groups(s) & 8) {
+    const dim3 g(P.nch, P.N);
+    LAUNCH_T(KID_BWD_STATE_TC, tc::k_bwd_state_tc, g, tc::kT, m.tc_b4, st, P);
+    LAUNCH_T(KID_BWD_ADJ_TC, tc::k_bwd_adj_tc, g, tc::kT, m.tc_b4, st, P);
+    LAUNCH_T(KID_BWD_INTRA_TC, tc::k_bwd_intra_tc, g, tc::kT, m.tc_b6, st, P);
+    if (P.e > 1 && (P.buf || P.dbuf)) LAUNCH(KID_BWD_BUF_TC, tc::k_bwd_buf_tc, dim3(1, P.N), m.buf_b, st, P);
+    LAUNCH_T(KID_BWD_GATES_TC, tc::k_bwd_gates_tc, g, tc::kT, m.tc_b6, st, P);
+  } else {
+    LAUNCH(KID_BWD_GRADS, k_bwd_grads, dim3(P.nch, P.N), m.b3, st, P);
+  }
   if (P.e > 1 && P.dbuf_out) {
     LAUNCH(KID_BWD_BUFOUT, k_bwd_bufout, dim3(P.e - 1, P.N), m.bufout, st, P);
   }

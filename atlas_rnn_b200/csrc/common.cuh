@@ -40,6 +40,8 @@ struct Params {
   float *hdp;    // [N][nch][e-1][dphi] halo partials of d phi
   float *du;     // [N][T]
   float *hdu;    // [N][nch][e-1]
+  float *xq, *xf, *xs;  // Gram pieces of the tensor-core backward
+  void* gt;             // [N][nch] 128x128 bf16 Gram blocks (core-matrix tile layout)
   int apply_mask;
   // sequence-parallel segment outputs
   float *seg_coef, *seg_dS, *seg_dZ;

@@ -1,0 +1,732 @@
+// Tensor-core (tcgen05) backward chunk kernels. Together they produce what
+// k_bwd_chunk + k_bwd_grads (chunk_kernels.cuh) produce, split by operand set
+// so that each kernel keeps at most six 32 KB operand tiles in shared memory:
+//
+//   k_bwd_chunk_tc  adjoint increments dShat, dZhat of a chunk        tiles dY*eS, dY*eZ, Psi
+//   k_bwd_state_tc  Psi S_in^T, dY S_in (and Z_in): the Gram entries  tiles Psi, dY, S_in, Z_in
+//                   <dy_q psi_q^T, S_in>, and d psi's state part
+//   k_bwd_adj_tc    Phi F^T, delta F: the Gram entries <F, R_j>,      tiles Phi, delta, F_S, F_Z
+//                   d delta and d phi through F; the four <F, S> dots
+//   k_bwd_intra_tc  A1 = dY delta^T, A2 = Psi Phi^T, the Gram block   tiles Phi, delta, Psi, dY, M1, M2
+//                   G = A1 o A2 and the intra-chunk terms of d delta,
+//                   d phi, d psi
+//   k_bwd_gates_tc  d alpha, d eta, d beta and the window-gate        tiles G, cS, cZ, cZ+, eS+, eZ+
+//                   gradients as bilinear forms of the Gram matrix
+// Gram pieces travel between kernels through the backward scratch:
+//   xq[N][nch][128][2], xf[N][nch][128][2], xs[N][nch][4], G tiles [N][nch][32 KB].
+#pragma once
+#include "tc_fwd.cuh"
+
+namespace atlas {
+namespace tc {
+
+__device__ __forceinline__ int64_t chunk_id(const Params& P, const Ctx& cx) { return (int64_t)cx.n * P.nch + cx.c; }
+
+// Token rows of dy (zero for rows >= L), optionally scaled per row.
+template <class Scale>
+__device__ __forceinline__ void fill_rows_dy(const Params& P, const Ctx& cx, unsigned char* tile, Scale sc) {
+  fill_tile(tile, kD, [&](int r, int c0, float(&v)[8]) {
+    if (r < cx.L) {
+      ld8io(P.dy, ((int64_t)cx.n * P.T + cx.t0 + r) * P.dv + c0, P.bf, v);
+      const float s = sc(r);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] *= s;
+    } else {
+      zero8(v);
+    }
+  });
+}
+__device__ __forceinline__ void fill_keys_delta(const Params& P, const Ctx& cx, unsigned char* tile) {
+  fill_tile(tile, kD, [&](int r, int c0, float(&v)[8]) {
+    const int p = cx.kp0 + r;
+    if (r < cx.K && p >= 0) ld8f(P.delta + ((int64_t)cx.n * P.T + p) * P.dv + c0, v);
+    else zero8(v);
+  });
+}
+
+// Scalars of the adjoint transform of the chunk (rows r = 0..L) computed by one thread.
+__device__ __forceinline__ void adj_scalars(const Ctx& cx, float* hS, float* hZS, float* hZZ) {
+  const int L = cx.L;
+  float hs = 1.f, hzs = -cx.et[L - 1], hzz = 1.f;
+  hS[L] = hs; hZS[L] = hzs; hZZ[L] = hzz;
+  for (int r = L - 1; r >= 0; --r) {
+    const float eta = r >= 1 ? cx.et[r - 1] : 0.f;
+    hs = cx.al[r] * hs;
+    hzz = cx.be[r] * hzz;
+    hzs = cx.be[r] * hzs - eta * hs;
+    hS[r] = hs; hZS[r] = hzs; hZZ[r] = hzz;
+  }
+}
+// Scalars of the forward chunk transform (rows r = 0..L) computed by one thread.
+__device__ __forceinline__ void fwd_scalars(const Ctx& cx, float* sS, float* sZ, float* zZ) {
+  float s = 1.f, sz = 0.f, z = 1.f;
+  sS[0] = s; sZ[0] = sz; zZ[0] = z;
+  for (int i = 0; i < cx.L; ++i) {
+    z = cx.be[i] * z;
+    s = cx.al[i] * s;
+    sz = cx.al[i] * sz - cx.et[i] * z;
+    sS[i + 1] = s; sZ[i + 1] = sz; zZ[i + 1] = z;
+  }
+}
+
+// ===========================================================================
+// adjoint increments at the chunk input from the chunk's own dy:
+//   dShat = dY^T diag(eS_0) Psi,  dZhat = dY^T diag(eZ_0) Psi
+// ===========================================================================
+__global__ void __launch_bounds__(kT) k_bwd_chunk_tc(Params P) {
+  extern __shared__ __align__(1024) unsigned char sm[];
+  unsigned char* tYS = sm;
+  unsigned char* tYZ = sm + kTileBytes;
+  unsigned char* tPsi = sm + 2 * kTileBytes;
+  SmemAlloc sa{reinterpret_cast<float*>(sm + 3 * kTileBytes), 0};
+  __shared__ uint64_t mbar;
+  __shared__ uint32_t tbase;
+  Ctx cx;
+  load_ctx(P, sa, cx, kT);
+  float* eS0 = sa.take(kT);
+  float* eZ0 = sa.take(kT);
+  const int n = cx.n, L = cx.L, tid = threadIdx.x;
+  Sync sy{&mbar, &tbase, 0, nullptr};
+  const uint32_t tm = tc_setup(sy);
+  fill_rows_psi(P, cx, tPsi);
+  __syncthreads();
+  {
+    const int q = tid;
+    float es = 0.f, ez = 0.f;
+    if (q < L)
+      for (int r = L - 1; r >= 0; --r) {
+        const float eta = r >= 1 ? cx.et[r - 1] : 0.f;
+        es = cx.al[r] * es + (q == r ? 1.f : 0.f);
+        ez = cx.be[r] * ez - eta * es;
+      }
+    eS0[q] = es;
+    eZ0[q] = ez;
+    if (tid == kT - 1) {
+      float hs = 1.f, hzs = -cx.et[L - 1], hzz = 1.f;
+      for (int r = L - 1; r >= 0; --r) {
+        const float eta = r >= 1 ? cx.et[r - 1] : 0.f;
+        hs = cx.al[r] * hs;
+        hzz = cx.be[r] * hzz;
+        hzs = cx.be[r] * hzs - eta * hs;
+      }
+      float* o = P.acs + chunk_id(P, cx) * 4;
+      o[0] = hs; o[1] = hzs; o[2] = hzz; o[3] = 0.f;
+    }
+  }
+  __syncthreads();
+  fill_rows_dy(P, cx, tYS, [&](int r) { return eS0[r]; });
+  fill_rows_dy(P, cx, tYZ, [&](int r) { return eZ0[r]; });
+  smem_to_tc();
+  if (tid == 0) {
+    mma_chain(tm, op(tYS, kD, 1), op(tPsi, kD, 1), 8, kD, false);
+    mma_chain(tm + 128, op(tYZ, kD, 1), op(tPsi, kD, 1), 8, kD, false);
+  }
+  mma_wait(sy);
+  {
+    const int64_t D2 = (int64_t)kD * kD;
+    float* dst = P.adj + chunk_id(P, cx) * 2 * D2 + (int64_t)tid * kD;
+    for (int c16 = 0; c16 < kD / 16; ++c16) {
+      float a[16], b[16];
+      umma::tmem_ld16(lane_addr(tm, c16 * 16), a);
+      umma::tmem_ld16(lane_addr(tm, 128 + c16 * 16), b);
+      umma::tmem_ld_wait();
+      st16f(dst + c16 * 16, a);
+      st16f(dst + D2 + c16 * 16, b);
+    }
+  }
+  (void)n;
+  tc_teardown(tm);
+}
+
+// ===========================================================================
+// state side: G_S = Psi S_in^T, G_Z = Psi Z_in^T (-> X[D_q][S_in], X[D_q][Z_in]),
+// H_S = dY S_in, H_Z = dY Z_in (-> d psi = sS H_S + sZ H_Z, written with '=').
+// ===========================================================================
+__global__ void __launch_bounds__(kT) k_bwd_state_tc(Params P) {
+  extern __shared__ __align__(1024) unsigned char sm[];
+  unsigned char* tPsi = sm;
+  unsigned char* tY = sm + kTileBytes;
+  unsigned char* tSin = sm + 2 * kTileBytes;
+  unsigned char* tZin = sm + 3 * kTileBytes;
+  SmemAlloc sa{reinterpret_cast<float*>(sm + 4 * kTileBytes), 0};
+  __shared__ uint64_t mbar;
+  __shared__ uint32_t tbase;
+  Ctx cx;
+  load_ctx(P, sa, cx, kT);
+  float* sS = sa.take(kT + 1);
+  float* sZ = sa.take(kT + 1);
+  float* zZ = sa.take(kT + 1);
+  const int n = cx.n, L = cx.L, tid = threadIdx.x;
+  Sync sy{&mbar, &tbase, 0, nullptr};
+  const uint32_t tm = tc_setup(sy);
+  const int64_t D2 = (int64_t)kD * kD;
+  const float* Sin = P.st + chunk_id(P, cx) * 2 * D2;
+  fill_rows_psi(P, cx, tPsi);
+  fill_rows_dy(P, cx, tY, [](int) { return 1.f; });
+  fill_dense(tSin, Sin);
+  fill_dense(tZin, Sin + D2);
+  __syncthreads();
+  if (tid == 0) fwd_scalars(cx, sS, sZ, zZ);
+  smem_to_tc();
+  if (tid == 0) {
+    mma_chain(tm, op(tPsi, kD, 0), op(tSin, kD, 0), 8, kD, false);
+    mma_chain(tm + 128, op(tPsi, kD, 0), op(tZin, kD, 0), 8, kD, false);
+    mma_chain(tm + 256, op(tY, kD, 0), op(tSin, kD, 1), 8, kD, false);
+    mma_chain(tm + 384, op(tY, kD, 0), op(tZin, kD, 1), 8, kD, false);
+  }
+  mma_wait(sy);
+  {
+    const int q = tid;
+    float xs = 0.f, xz = 0.f;
+    const float ss = q < L ? sS[q] : 0.f, sz = q < L ? sZ[q] : 0.f;
+    const int64_t row = (int64_t)n * P.T + cx.t0 + q;
+    for (int c16 = 0; c16 < kD / 16; ++c16) {
+      float gs[16], gz[16], hs[16], hz[16], y0[8], y1[8];
+      umma::tmem_ld16(lane_addr(tm, c16 * 16), gs);
+      umma::tmem_ld16(lane_addr(tm, 128 + c16 * 16), gz);
+      umma::tmem_ld16(lane_addr(tm, 256 + c16 * 16), hs);
+      umma::tmem_ld16(lane_addr(tm, 384 + c16 * 16), hz);
+      umma::tmem_ld_wait();
+      if (q < L) {
+        ld8io(P.dy, row * P.dv + c16 * 16, P.bf, y0);
+        ld8io(P.dy, row * P.dv + c16 * 16 + 8, P.bf, y1);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          xs += gs[i] * y0[i] + gs[8 + i] * y1[i];
+          xz += gz[i] * y0[i] + gz[8 + i] * y1[i];
+        }
+        float d[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) d[i] = ss * hs[i] + sz * hz[i];
+        st16f(P.dpsi + row * P.dphi + c16 * 16, d);
+      }
+    }
+    float* xq = P.xq + (chunk_id(P, cx) * kT + q) * 2;
+    xq[0] = q < L ? xs : 0.f;
+    xq[1] = q < L ? xz : 0.f;
+  }
+  tc_teardown(tm);
+}
+
+// Window-summed adjoint scalars of key j: wZS_j = sum_i W(i,j) hZS_{i+1}, wZZ likewise.
+__device__ __forceinline__ void key_adj_weights(const Params& P, const Ctx& cx, int j, const float* hZS,
+                                                const float* hZZ, float& a, float& b) {
+  a = 0.f;
+  b = 0.f;
+  if (j >= cx.K) return;
+  for (int i = max(0, j - P.e + 1); i <= min(cx.L - 1, j); ++i) {
+    const float w = wgt(P, cx, i, j);
+    a += w * hZS[i + 1];
+    b += w * hZZ[i + 1];
+  }
+}
+
+// ===========================================================================
+// adjoint side: P1 = Phi F_S^T, P2 = Phi F_Z^T (-> X[F][R_j], d delta through F),
+// Q1 = delta F_S, Q2 = delta F_Z (-> d phi through F); the four <F, S_in/Z_in>.
+// d delta and d phi are written with '=' (own keys) or to the halo partials.
+// ===========================================================================
+__global__ void __launch_bounds__(kT) k_bwd_adj_tc(Params P) {
+  extern __shared__ __align__(1024) unsigned char sm[];
+  unsigned char* tPhi = sm;
+  unsigned char* tDl = sm + kTileBytes;
+  unsigned char* tFS = sm + 2 * kTileBytes;
+  unsigned char* tFZ = sm + 3 * kTileBytes;
+  SmemAlloc sa{reinterpret_cast<float*>(sm + 4 * kTileBytes), 0};
+  __shared__ uint64_t mbar;
+  __shared__ uint32_t tbase;
+  Ctx cx;
+  load_ctx(P, sa, cx, kT);
+  float* hS = sa.take(kT + 1);
+  float* hZS = sa.take(kT + 1);
+  float* hZZ = sa.take(kT + 1);
+  float* red = sa.take(32);
+  const int n = cx.n, K = cx.K, tid = threadIdx.x, e = P.e;
+  Sync sy{&mbar, &tbase, 0, nullptr};
+  const uint32_t tm = tc_setup(sy);
+  const int64_t D2 = (int64_t)kD * kD;
+  const int64_t cid = chunk_id(P, cx);
+  const float* FS = P.adj + cid * 2 * D2;
+  const float* Sin = P.st + cid * 2 * D2;
+  fill_keys_phi(P, cx, tPhi);
+  fill_keys_delta(P, cx, tDl);
+  fill_dense(tFS, FS);
+  fill_dense(tFZ, FS + D2);
+  __syncthreads();
+  if (tid == 0) adj_scalars(cx, hS, hZS, hZZ);
+  smem_to_tc();
+  if (tid == 0) {
+    mma_chain(tm, op(tPhi, kD, 0), op(tFS, kD, 0), 8, kD, false);
+    mma_chain(tm + 128, op(tPhi, kD, 0), op(tFZ, kD, 0), 8, kD, false);
+    mma_chain(tm + 256, op(tDl, kD, 0), op(tFS, kD, 1), 8, kD, false);
+    mma_chain(tm + 384, op(tDl, kD, 0), op(tFZ, kD, 1), 8, kD, false);
+  }
+  // the four Gram scalars <F_S|F_Z, S_in|Z_in> while the MMAs run
+  {
+    float s00 = 0.f, s01 = 0.f, s10 = 0.f, s11 = 0.f;
+    for (int64_t x = tid * 4; x < D2; x += kT * 4) {
+      const float4 fs = *reinterpret_cast<const float4*>(FS + x), fz = *reinterpret_cast<const float4*>(FS + D2 + x);
+      const float4 si = *reinterpret_cast<const float4*>(Sin + x), zi = *reinterpret_cast<const float4*>(Sin + D2 + x);
+      s00 += fs.x * si.x + fs.y * si.y + fs.z * si.z + fs.w * si.w;
+      s01 += fs.x * zi.x + fs.y * zi.y + fs.z * zi.z + fs.w * zi.w;
+      s10 += fz.x * si.x + fz.y * si.y + fz.z * si.z + fz.w * si.w;
+      s11 += fz.x * zi.x + fz.y * zi.y + fz.z * zi.z + fz.w * zi.w;
+    }
+    float* o = P.xs + cid * 4;
+    float v[4] = {s00, s01, s10, s11};
+    for (int k = 0; k < 4; ++k) {
+      float t = v[k];
+      for (int off = 16; off > 0; off >>= 1) t += __shfl_xor_sync(0xffffffffu, t, off);
+      if ((tid & 31) == 0) red[k * 4 + (tid >> 5)] = t;
+    }
+    __syncthreads();
+    if (tid < 4) o[tid] = red[tid * 4] + red[tid * 4 + 1] + red[tid * 4 + 2] + red[tid * 4 + 3];
+  }
+  mma_wait(sy);
+  {
+    const int j = tid, p = cx.kp0 + j;
+    float wzs, wzz;
+    key_adj_weights(P, cx, j, hZS, hZZ, wzs, wzz);
+    const bool own = j < K && p >= cx.t0, halo = j < K && p >= 0 && p < cx.t0;
+    float xS = 0.f, xZ = 0.f;
+    const int64_t drow = ((int64_t)n * P.T + (p >= 0 ? p : 0)) * P.dv;
+    float* dd = own ? P.ddel + ((int64_t)n * P.T + p) * P.dv
+                    : P.hdd + ((cid * (e > 1 ? e - 1 : 1)) + (j < e - 1 ? j : 0)) * P.dv;
+    float* dp = own ? P.dphiR + ((int64_t)n * P.T + p) * P.dphi
+                    : P.hdp + ((cid * (e > 1 ? e - 1 : 1)) + (j < e - 1 ? j : 0)) * P.dphi;
+    for (int c16 = 0; c16 < kD / 16; ++c16) {
+      float p1[16], p2[16], q1[16], q2[16];
+      umma::tmem_ld16(lane_addr(tm, c16 * 16), p1);
+      umma::tmem_ld16(lane_addr(tm, 128 + c16 * 16), p2);
+      umma::tmem_ld16(lane_addr(tm, 256 + c16 * 16), q1);
+      umma::tmem_ld16(lane_addr(tm, 384 + c16 * 16), q2);
+      umma::tmem_ld_wait();
+      if (own || halo) {
+        float dl[16], a[16], b[16];
+        ld8f(P.delta + drow + c16 * 16, *reinterpret_cast<float(*)[8]>(dl));
+        ld8f(P.delta + drow + c16 * 16 + 8, *reinterpret_cast<float(*)[8]>(dl + 8));
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          xS += p1[i] * dl[i];
+          xZ += p2[i] * dl[i];
+          a[i] = wzs * p1[i] + wzz * p2[i];
+          b[i] = wzs * q1[i] + wzz * q2[i];
+        }
+        st16f(dd + c16 * 16, a);
+        st16f(dp + c16 * 16, b);
+      }
+    }
+    float* xf = P.xf + (cid * kT + j) * 2;
+    xf[0] = xS;
+    xf[1] = xZ;
+  }
+  tc_teardown(tm);
+}
+
+// ===========================================================================
+// intra-chunk terms: A1 = dY delta^T, A2 = Psi Phi^T (token q x key j);
+// G = A1 o A2 goes to the scratch (tile layout, bf16) for the gate kernel;
+//   d delta_j += sum_q wE_j[q] A2[q][j] dy_q       (M1 = wE o A2^T, MN-major)
+//   d phi_j   += sum_q wE_j[q] A1[q][j] psi_q      (M2 = wE o A1^T)
+//   d psi_i   += sum_j cS_i[j] A1[i][j] phi_j      (M3 = cS o A1)
+// with wE_j[q] = sum_i W(i,j) eZ_{i+1}[q] the window-summed adjoint coefficient.
+// ===========================================================================
+__global__ void __launch_bounds__(kT) k_bwd_intra_tc(Params P) {
+  extern __shared__ __align__(1024) unsigned char sm[];
+  unsigned char* tPhi = sm;
+  unsigned char* tDl = sm + kTileBytes;   // delta, later M3
+  unsigned char* tPsi = sm + 2 * kTileBytes;
+  unsigned char* tY = sm + 3 * kTileBytes;
+  unsigned char* tM1 = sm + 4 * kTileBytes;
+  unsigned char* tM2 = sm + 5 * kTileBytes;
+  SmemAlloc sa{reinterpret_cast<float*>(sm + 6 * kTileBytes), 0};
+  __shared__ uint64_t mbar;
+  __shared__ uint32_t tbase;
+  Ctx cx;
+  load_ctx(P, sa, cx, kT);
+  const int n = cx.n, K = cx.K, L = cx.L, tid = threadIdx.x, e = P.e;
+  Sync sy{&mbar, &tbase, 0, nullptr};
+  const uint32_t tm = tc_setup(sy);
+  const int64_t cid = chunk_id(P, cx);
+  fill_keys_phi(P, cx, tPhi);
+  fill_keys_delta(P, cx, tDl);
+  fill_rows_psi(P, cx, tPsi);
+  fill_rows_dy(P, cx, tY, [](int) { return 1.f; });
+  __syncthreads();
+  {  // row q of M1 staging: wE_j[q] for every key j
+    const int q = tid;
+    float wl[kT];
+#pragma unroll
+    for (int j = 0; j < kT; ++j) wl[j] = 0.f;
+    if (q < L) {
+      float es = 0.f, ez = 0.f;  // eS_{L}, eZ_{L}
+      for (int i = L - 1; i >= 0; --i) {
+        // ez holds eZ_{i+1}[q]; key j gets it from token i when i <= j <= i + e - 1
+        for (int jj = 0; jj < e; ++jj) {
+          const int j = i + jj;
+          if (j < K) wl[j] += wgt(P, cx, i, j) * ez;
+        }
+        const float eta = i >= 1 ? cx.et[i - 1] : 0.f;
+        es = cx.al[i] * es + (q == i ? 1.f : 0.f);
+        ez = cx.be[i] * ez - eta * es;
+      }
+    }
+    for (int cb = 0; cb < kT / 8; ++cb) {
+      float v[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) v[k] = wl[cb * 8 + k];
+      store_unit(tM1, q, cb, kT, v);
+    }
+  }
+  smem_to_tc();
+  if (tid == 0) {
+    mma_chain(tm, op(tY, kD, 0), op(tDl, kD, 0), 8, kT, false);       // A1[q][j]
+    mma_chain(tm + 128, op(tPsi, kD, 0), op(tPhi, kD, 0), 8, kT, false);  // A2[q][j]
+  }
+  mma_wait(sy);
+  {  // column j of tDl <- cS before token i (delta is no longer needed)
+    const int j = tid;
+    float cs = 0.f, cz = 0.f;
+    for (int i = 0; i < kT; ++i) {
+      const bool live = i < L && j < K;
+      *reinterpret_cast<__nv_bfloat16*>(tDl + umma::elem_off(i, j, kT)) = __float2bfloat16_rn(live ? cs : 0.f);
+      if (live) {
+        cz = cx.be[i] * cz + wgt(P, cx, i, j);
+        cs = cx.al[i] * cs - cx.et[i] * cz;
+      }
+    }
+  }
+  __syncthreads();
+  {
+    const int q = tid;
+    unsigned char* gdst = reinterpret_cast<unsigned char*>(P.gt) + cid * kTileBytes;
+    for (int c16 = 0; c16 < kT / 16; ++c16) {
+      float a1[16], a2[16];
+      umma::tmem_ld16(lane_addr(tm, c16 * 16), a1);
+      umma::tmem_ld16(lane_addr(tm, 128 + c16 * 16), a2);
+      umma::tmem_ld_wait();
+      for (int h = 0; h < 2; ++h) {
+        const int cb = 2 * c16 + h;
+        float g[8], c3[8], w1[8], m2[8];
+        load_unit(tDl, q, cb, kT, c3);
+        load_unit(tM1, q, cb, kT, w1);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const float x1 = a1[8 * h + k], x2 = a2[8 * h + k];
+          g[k] = x1 * x2;
+          c3[k] *= x1;
+          m2[k] = w1[k] * x1;
+          w1[k] *= x2;
+        }
+        store_unit(gdst, q, cb, kT, g);
+        store_unit(tDl, q, cb, kT, c3);
+        store_unit(tM1, q, cb, kT, w1);
+        store_unit(tM2, q, cb, kT, m2);
+      }
+    }
+  }
+  smem_to_tc();
+  if (tid == 0) {
+    mma_chain(tm + 256, op(tM1, kT, 1), op(tY, kD, 1), 8, kD, false);   // I3 [j][nn]
+    mma_chain(tm + 384, op(tM2, kT, 1), op(tPsi, kD, 1), 8, kD, false); // I4 [j][m]
+    mma_chain(tm, op(tDl, kT, 0), op(tPhi, kD, 1), 8, kD, false);       // I5 [i][m]
+  }
+  mma_wait(sy);
+  {
+    const int r = tid, p = cx.kp0 + r;
+    const bool own = r < K && p >= cx.t0, halo = r < K && p >= 0 && p < cx.t0;
+    const int e1 = e > 1 ? e - 1 : 1;
+    float* dd = own ? P.ddel + ((int64_t)n * P.T + p) * P.dv : P.hdd + (cid * e1 + (r < e - 1 ? r : 0)) * P.dv;
+    float* dp = own ? P.dphiR + ((int64_t)n * P.T + p) * P.dphi : P.hdp + (cid * e1 + (r < e - 1 ? r : 0)) * P.dphi;
+    float* dq = P.dpsi + ((int64_t)n * P.T + cx.t0 + (r < L ? r : 0)) * P.dphi;
+    for (int c16 = 0; c16 < kD / 16; ++c16) {
+      float i3[16], i4[16], i5[16];
+      umma::tmem_ld16(lane_addr(tm, 256 + c16 * 16), i3);
+      umma::tmem_ld16(lane_addr(tm, 384 + c16 * 16), i4);
+      umma::tmem_ld16(lane_addr(tm, c16 * 16), i5);
+      umma::tmem_ld_wait();
+      if (own || halo)
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+          dd[c16 * 16 + k] += i3[k];
+          dp[c16 * 16 + k] += i4[k];
+        }
+      if (r < L)
+#pragma unroll
+        for (int k = 0; k < 16; ++k) dq[c16 * 16 + k] += i5[k];
+    }
+  }
+  tc_teardown(tm);
+}
+
+// ===========================================================================
+// gate gradients from the Gram matrix (token i of the chunk):
+//   d alpha_i = <Shat_i, S_{i-1}>, d eta_i = -<Shat_i, Z_i>, d beta_i = <Zhat_i, Z_{i-1}>,
+//   dW(i, j) = <Zhat_i, R_j>.
+// The G block enters through W_a = C_S G^T, W_e = C_Z+ G^T, W_b = C_Z G^T and
+// E_Z+ G (tensor cores); the F / S_in / Z_in rows and columns of the Gram
+// matrix are folded in on CUDA cores.
+// ===========================================================================
+__global__ void __launch_bounds__(kT) k_bwd_gates_tc(Params P) {
+  extern __shared__ __align__(1024) unsigned char sm[];
+  unsigned char* tG = sm;
+  unsigned char* tCS = sm + kTileBytes;    // cS_i[j]     (state before token i)
+  unsigned char* tCZp = sm + 2 * kTileBytes;  // cZ_i[j]
+  unsigned char* tCZn = sm + 3 * kTileBytes;  // cZ_{i+1}[j] (state after token i)
+  unsigned char* tES = sm + 4 * kTileBytes;   // eS_{i+1}[q]
+  unsigned char* tEZ = sm + 5 * kTileBytes;   // eZ_{i+1}[q]
+  SmemAlloc sa{reinterpret_cast<float*>(sm + 6 * kTileBytes), 0};
+  __shared__ uint64_t mbar;
+  __shared__ uint32_t tbase;
+  Ctx cx;
+  load_ctx(P, sa, cx, kT);
+  float* sS = sa.take(kT + 1);
+  float* sZ = sa.take(kT + 1);
+  float* zZ = sa.take(kT + 1);
+  float* hS = sa.take(kT + 1);
+  float* hZS = sa.take(kT + 1);
+  float* hZZ = sa.take(kT + 1);
+  float* xq = sa.take(2 * kT);
+  float* xf = sa.take(2 * kT);
+  float* xs = sa.take(4);
+  float* duj = sa.take(kT);
+  const int n = cx.n, K = cx.K, L = cx.L, tid = threadIdx.x, e = P.e;
+  Sync sy{&mbar, &tbase, 0, nullptr};
+  const uint32_t tm = tc_setup(sy);
+  const int64_t cid = chunk_id(P, cx);
+  {
+    const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const unsigned char*>(P.gt) + cid * kTileBytes);
+    uint4* dst = reinterpret_cast<uint4*>(tG);
+    for (int u = tid; u < kTileBytes / 16; u += kT) dst[u] = src[u];
+    xq[tid] = P.xq[cid * 2 * kT + tid];
+    xq[kT + tid] = P.xq[cid * 2 * kT + kT + tid];
+    xf[tid] = P.xf[cid * 2 * kT + tid];
+    xf[kT + tid] = P.xf[cid * 2 * kT + kT + tid];
+    if (tid < 4) xs[tid] = P.xs[cid * 4 + tid];
+    duj[tid] = 0.f;
+  }
+  __syncthreads();
+  {
+    const int j = tid;  // forward coefficients of key j (column j of tCS, tCZp, tCZn)
+    float cs = 0.f, cz = 0.f;
+    for (int i = 0; i < kT; ++i) {
+      const bool live = i < L && j < K;
+      float czn = 0.f;
+      if (live) {
+        czn = cx.be[i] * cz + wgt(P, cx, i, j);
+      }
+      *reinterpret_cast<__nv_bfloat16*>(tCS + umma::elem_off(i, j, kT)) = __float2bfloat16_rn(live ? cs : 0.f);
+      *reinterpret_cast<__nv_bfloat16*>(tCZp + umma::elem_off(i, j, kT)) = __float2bfloat16_rn(live ? cz : 0.f);
+      *reinterpret_cast<__nv_bfloat16*>(tCZn + umma::elem_off(i, j, kT)) = __float2bfloat16_rn(live ? czn : 0.f);
+      if (live) {
+        cz = czn;
+        cs = cx.al[i] * cs - cx.et[i] * cz;
+      }
+    }
+    const int q = tid;  // adjoint coefficients of token q (column q of tES, tEZ): rows i <- eS_{i+1}, eZ_{i+1}
+    float es = 0.f, ez = 0.f;
+    for (int i = kT - 1; i >= 0; --i) {
+      const bool live = i < L && q < L;
+      // es, ez hold eS_{i+1}[q], eZ_{i+1}[q] here
+      *reinterpret_cast<__nv_bfloat16*>(tES + umma::elem_off(i, q, kT)) = __float2bfloat16_rn(live ? es : 0.f);
+      *reinterpret_cast<__nv_bfloat16*>(tEZ + umma::elem_off(i, q, kT)) = __float2bfloat16_rn(live ? ez : 0.f);
+      if (live) {
+        const float eta = i >= 1 ? cx.et[i - 1] : 0.f;
+        es = cx.al[i] * es + (q == i ? 1.f : 0.f);
+        ez = cx.be[i] * ez - eta * es;
+      }
+    }
+    if (tid == 0) fwd_scalars(cx, sS, sZ, zZ);
+    if (tid == 32) adj_scalars(cx, hS, hZS, hZZ);
+  }
+  smem_to_tc();
+  if (tid == 0) {
+    mma_chain(tm, op(tCS, kT, 0), op(tG, kT, 0), 8, kT, false);         // W_a[i][q]
+    mma_chain(tm + 128, op(tCZn, kT, 0), op(tG, kT, 0), 8, kT, false);  // W_e[i][q]
+    mma_chain(tm + 256, op(tCZp, kT, 0), op(tG, kT, 0), 8, kT, false);  // W_b[i][q]
+    mma_chain(tm + 384, op(tEZ, kT, 0), op(tG, kT, 1), 8, kT, false);   // E_Z+ G [i][j]
+  }
+  mma_wait(sy);
+  {
+    const int i = tid;
+    float fs_cs = 0.f, fs_czn = 0.f, fs_czp = 0.f, fz_czp = 0.f;
+    float qs_es = 0.f, qz_es = 0.f, qz_ez = 0.f, wa = 0.f, we = 0.f, wb = 0.f;
+    for (int c16 = 0; c16 < kT / 16; ++c16) {
+      float A[16], E[16], B[16];
+      umma::tmem_ld16(lane_addr(tm, c16 * 16), A);
+      umma::tmem_ld16(lane_addr(tm, 128 + c16 * 16), E);
+      umma::tmem_ld16(lane_addr(tm, 256 + c16 * 16), B);
+      umma::tmem_ld_wait();
+      for (int h = 0; h < 2; ++h) {
+        const int cb = 2 * c16 + h;
+        float cs8[8], czn8[8], czp8[8], es8[8], ez8[8];
+        load_unit(tCS, i, cb, kT, cs8);
+        load_unit(tCZn, i, cb, kT, czn8);
+        load_unit(tCZp, i, cb, kT, czp8);
+        load_unit(tES, i, cb, kT, es8);
+        load_unit(tEZ, i, cb, kT, ez8);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const int x = cb * 8 + k;  // key j (for c*) or token q (for e*)
+          fs_cs += xf[2 * x] * cs8[k];
+          fs_czn += xf[2 * x] * czn8[k];
+          fs_czp += xf[2 * x] * czp8[k];
+          fz_czp += xf[2 * x + 1] * czp8[k];
+          qs_es += xq[2 * x] * es8[k];
+          qz_es += xq[2 * x + 1] * es8[k];
+          qz_ez += xq[2 * x + 1] * ez8[k];
+          wa += es8[k] * A[8 * h + k];
+          we += es8[k] * E[8 * h + k];
+          wb += ez8[k] * B[8 * h + k];
+        }
+      }
+    }
+    if (i < L) {
+      const float da = hS[i + 1] * (xs[0] * sS[i] + xs[1] * sZ[i] + fs_cs) + (qs_es * sS[i] + qz_es * sZ[i] + wa);
+      const float de = -(hS[i + 1] * (xs[1] * zZ[i + 1] + fs_czn) + (qz_es * zZ[i + 1] + we));
+      const float db = hZS[i + 1] * (xs[1] * zZ[i] + fs_czp) + hZZ[i + 1] * (xs[3] * zZ[i] + fz_czp) +
+                       (qz_ez * zZ[i] + wb);
+      const int64_t r = (int64_t)n * P.T + cx.t0 + i;
+      if (P.ddecay) stio(P.ddecay, r, da, P.bf);
+      if (P.dlr) stio(P.dlr, r, de, P.bf);
+      if (P.mom && P.dbeta) stio(P.dbeta, r, db, P.bf);
+    }
+    // window weights dW(i, j) = hZS_{i+1} X[F_S][R_j] + hZZ_{i+1} X[F_Z][R_j] + (E_Z+ G)[i][j]
+    if (P.gmode != ATLAS_GATE_NONE) {
+      for (int c16 = 0; c16 < kT / 16; ++c16) {
+        float W[16];
+        umma::tmem_ld16(lane_addr(tm, 384 + c16 * 16), W);
+        umma::tmem_ld_wait();
+        if (i < L)
+          for (int k = 0; k < 16; ++k) {
+            const int j = c16 * 16 + k, jj = i - j + e - 1;
+            if (j >= K || jj < 0 || jj >= e) continue;
+            const float val = hZS[i + 1] * xf[2 * j] + hZZ[i + 1] * xf[2 * j + 1] + W[k];
+            if (P.gmode == ATLAS_GATE_TOKEN) {
+              if (cx.kp0 + j >= 0) atomicAdd(&duj[j], val);
+            } else if (P.dgate) {
+              stio(P.dgate, ((int64_t)n * P.T + cx.t0 + i) * e + jj, val, P.bf);
+            }
+          }
+      }
+    }
+  }
+  __syncthreads();
+  if (P.gmode == ATLAS_GATE_TOKEN) {
+    const int j = tid, p = cx.kp0 + j;
+    if (j < K && p >= cx.t0) P.du[(int64_t)n * P.T + p] = duj[j];
+    else if (j < K && p >= 0) P.hdu[cid * (e - 1) + j] = duj[j];
+  }
+  tc_teardown(tm);
+}
+
+// ===========================================================================
+// chunk 0 with a carried omega buffer (dense entries Buf_jb, jb < e-1), after
+// k_bwd_intra_tc and before k_bwd_gates_tc: the Gram columns of the buffer
+// entries (X[F][Buf], G[q][Buf] = dy_q . Buf psi_q), their d psi terms, and the
+// buffer's own gradient dBuf_jb = wZS F_S + wZZ F_Z + sum_q wE_jb[q] dy_q psi_q^T.
+// CUDA cores, one CTA of kThreads per unit.
+// ===========================================================================
+__global__ void __launch_bounds__(kThreads) k_bwd_buf_tc(Params P) {
+  extern __shared__ float smem[];
+  SmemAlloc sa{smem, 0};
+  Ctx cx;
+  load_ctx(P, sa, cx);  // blockIdx.x = 0: chunk 0
+  const int L = cx.L, e1 = P.e - 1, dv = P.dv, dphi = P.dphi, n = cx.n, tid = threadIdx.x;
+  float* psi = sa.take(L * dphi);
+  float* dy = sa.take(L * dv);
+  float* cSb = sa.take(L * e1);   // cS_i[jb]
+  float* wE = sa.take(e1 * L);    // wE_jb[q]
+  float* hS = sa.take(L + 1);
+  float* hZS = sa.take(L + 1);
+  float* hZZ = sa.take(L + 1);
+  float* red = sa.take(32);
+  for (int x = tid; x < L * dphi; x += kThreads) psi[x] = load_phi(P, n, x / dphi, x % dphi, true);
+  for (int x = tid; x < L * dv; x += kThreads) dy[x] = ldio(P.dy, (int64_t)n * P.T * dv + x, P.bf);
+  for (int x = tid; x < e1 * L; x += kThreads) wE[x] = 0.f;
+  __syncthreads();
+  if (tid < e1) {
+    const int j = tid;
+    float cs = 0.f, cz = 0.f;
+    for (int i = 0; i < L; ++i) {
+      cSb[i * e1 + j] = cs;
+      cz = cx.be[i] * cz + wgt(P, cx, i, j);
+      cs = cx.al[i] * cs - cx.et[i] * cz;
+    }
+  }
+  if (tid == kThreads - 1) adj_scalars(cx, hS, hZS, hZZ);
+  if (tid < L) {  // column q of eZ; wE_jb[q] = sum_{i <= jb} W(i, jb) eZ_{i+1}[q]
+    const int q = tid;
+    float es = 0.f, ez = 0.f;
+    for (int i = L - 1; i >= 0; --i) {
+      for (int jb = i; jb < e1; ++jb) wE[jb * L + q] += wgt(P, cx, i, jb) * ez;
+      const float eta = i >= 1 ? cx.et[i - 1] : 0.f;
+      es = cx.al[i] * es + (q == i ? 1.f : 0.f);
+      ez = cx.be[i] * ez - eta * es;
+    }
+  }
+  __syncthreads();
+  const int64_t D2 = (int64_t)dv * dphi;
+  const float* FS = P.adj;  // chunk 0 of unit n
+  FS += (int64_t)n * P.nch * 2 * D2;
+  const float* FZ = FS + D2;
+  const float* bufn = P.buf ? P.buf + (int64_t)n * e1 * D2 : nullptr;
+  const int64_t cid = (int64_t)n * P.nch;
+  if (bufn) {
+    unsigned char* gt = reinterpret_cast<unsigned char*>(P.gt) + cid * kTileBytes;
+    for (int jb = 0; jb < e1; ++jb) {
+      const float* Bj = bufn + (int64_t)jb * D2;
+      float s0 = 0.f, s1 = 0.f;
+      for (int64_t x = tid; x < D2; x += kThreads) { s0 += FS[x] * Bj[x]; s1 += FZ[x] * Bj[x]; }
+      s0 = block_sum(s0, red);
+      s1 = block_sum(s1, red);
+      if (tid == 0) { P.xf[(cid * kT + jb) * 2] = s0; P.xf[(cid * kT + jb) * 2 + 1] = s1; }
+      // G[q][jb] = dy_q . (Buf_jb psi_q), one warp per q
+      for (int q = tid >> 5; q < L; q += kThreads / 32) {
+        float acc = 0.f;
+        for (int nn = tid & 31; nn < dv; nn += 32) {
+          float bp = 0.f;
+          for (int m = 0; m < dphi; ++m) bp += Bj[nn * dphi + m] * psi[q * dphi + m];
+          acc += bp * dy[q * dv + nn];
+        }
+        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+        if ((tid & 31) == 0)
+          *reinterpret_cast<__nv_bfloat16*>(gt + umma::elem_off(q, jb, kT)) = __float2bfloat16_rn(acc);
+      }
+    }
+    // d psi_i += sum_jb cS_i[jb] Buf_jb^T dy_i
+    for (int x = tid; x < L * dphi; x += kThreads) {
+      const int i = x / dphi, m = x - i * dphi;
+      float acc = 0.f;
+      for (int jb = 0; jb < e1; ++jb) {
+        const float w = cSb[i * e1 + jb];
+        if (w == 0.f) continue;
+        const float* Bj = bufn + (int64_t)jb * D2;
+        float s = 0.f;
+        for (int nn = 0; nn < dv; ++nn) s += Bj[nn * dphi + m] * dy[i * dv + nn];
+        acc += w * s;
+      }
+      P.dpsi[((int64_t)n * P.T + i) * dphi + m] += acc;
+    }
+  }
+  if (P.dbuf) {
+    float* db = P.dbuf + (int64_t)n * e1 * D2;
+    for (int jb = 0; jb < e1; ++jb) {
+      float wzs = 0.f, wzz = 0.f;
+      for (int i = 0; i <= min(L - 1, jb); ++i) {
+        const float w = wgt(P, cx, i, jb);
+        wzs += w * hZS[i + 1];
+        wzz += w * hZZ[i + 1];
+      }
+      for (int64_t x = tid; x < D2; x += kThreads) {
+        const int nn = (int)(x / dphi), m = (int)(x - (int64_t)nn * dphi);
+        float acc = wzs * FS[x] + wzz * FZ[x];
+        for (int q = 0; q < L; ++q) acc += wE[jb * L + q] * dy[q * dv + nn] * psi[q * dphi + m];
+        db[(int64_t)jb * D2 + x] = acc;
+      }
+    }
+  }
+}
+
+}  // namespace tc
+}  // namespace atlas
