@@ -83,15 +83,15 @@ __global__ void __launch_bounds__(kT) k_bwd_chunk_tc(Params P) {
   __shared__ uint32_t tbase;
   Ctx cx;
   load_ctx(P, sa, cx, kT);
-  float* eS0 = sa.take(kT);
-  float* eZ0 = sa.take(kT);
-  const int n = cx.n, L = cx.L, tid = threadIdx.x;
+  float* eS0 = sa.take(kR);
+  float* eZ0 = sa.take(kR);
+  const int L = cx.L, tid = threadIdx.x, row = row_of(), wg = wg_of();
   Sync sy{&mbar, &tbase, 0, nullptr};
   const uint32_t tm = tc_setup(sy);
   fill_rows_psi(P, cx, tPsi);
   __syncthreads();
-  {
-    const int q = tid;
+  if (wg == 0) {
+    const int q = row;
     float es = 0.f, ez = 0.f;
     if (q < L)
       for (int r = L - 1; r >= 0; --r) {
@@ -101,17 +101,16 @@ __global__ void __launch_bounds__(kT) k_bwd_chunk_tc(Params P) {
       }
     eS0[q] = es;
     eZ0[q] = ez;
-    if (tid == kT - 1) {
-      float hs = 1.f, hzs = -cx.et[L - 1], hzz = 1.f;
-      for (int r = L - 1; r >= 0; --r) {
-        const float eta = r >= 1 ? cx.et[r - 1] : 0.f;
-        hs = cx.al[r] * hs;
-        hzz = cx.be[r] * hzz;
-        hzs = cx.be[r] * hzs - eta * hs;
-      }
-      float* o = P.acs + chunk_id(P, cx) * 4;
-      o[0] = hs; o[1] = hzs; o[2] = hzz; o[3] = 0.f;
+  } else if (row == 0) {
+    float hs = 1.f, hzs = -cx.et[L - 1], hzz = 1.f;
+    for (int r = L - 1; r >= 0; --r) {
+      const float eta = r >= 1 ? cx.et[r - 1] : 0.f;
+      hs = cx.al[r] * hs;
+      hzz = cx.be[r] * hzz;
+      hzs = cx.be[r] * hzs - eta * hs;
     }
+    float* o = P.acs + chunk_id(P, cx) * 4;
+    o[0] = hs; o[1] = hzs; o[2] = hzz; o[3] = 0.f;
   }
   __syncthreads();
   fill_rows_dy(P, cx, tYS, [&](int r) { return eS0[r]; });
@@ -124,8 +123,10 @@ __global__ void __launch_bounds__(kT) k_bwd_chunk_tc(Params P) {
   mma_wait(sy);
   {
     const int64_t D2 = (int64_t)kD * kD;
-    float* dst = P.adj + chunk_id(P, cx) * 2 * D2 + (int64_t)tid * kD;
-    for (int c16 = 0; c16 < kD / 16; ++c16) {
+    float* dst = P.adj + chunk_id(P, cx) * 2 * D2 + (int64_t)row * kD;
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      const int c16 = wg * 4 + h;
       float a[16], b[16];
       umma::tmem_ld16(lane_addr(tm, c16 * 16), a);
       umma::tmem_ld16(lane_addr(tm, 128 + c16 * 16), b);
@@ -134,7 +135,6 @@ __global__ void __launch_bounds__(kT) k_bwd_chunk_tc(Params P) {
       st16f(dst + D2 + c16 * 16, b);
     }
   }
-  (void)n;
   tc_teardown(tm);
 }
 
@@ -153,10 +153,11 @@ __global__ void __launch_bounds__(kT) k_bwd_state_tc(Params P) {
   __shared__ uint32_t tbase;
   Ctx cx;
   load_ctx(P, sa, cx, kT);
-  float* sS = sa.take(kT + 1);
-  float* sZ = sa.take(kT + 1);
-  float* zZ = sa.take(kT + 1);
-  const int n = cx.n, L = cx.L, tid = threadIdx.x;
+  float* sS = sa.take(kR + 1);
+  float* sZ = sa.take(kR + 1);
+  float* zZ = sa.take(kR + 1);
+  float* part = sa.take(4 * kR);  // [warpgroup][2][row] partial dot products
+  const int n = cx.n, L = cx.L, tid = threadIdx.x, row = row_of(), wg = wg_of();
   Sync sy{&mbar, &tbase, 0, nullptr};
   const uint32_t tm = tc_setup(sy);
   const int64_t D2 = (int64_t)kD * kD;
@@ -176,11 +177,13 @@ __global__ void __launch_bounds__(kT) k_bwd_state_tc(Params P) {
   }
   mma_wait(sy);
   {
-    const int q = tid;
+    const int q = row;
     float xs = 0.f, xz = 0.f;
     const float ss = q < L ? sS[q] : 0.f, sz = q < L ? sZ[q] : 0.f;
-    const int64_t row = (int64_t)n * P.T + cx.t0 + q;
-    for (int c16 = 0; c16 < kD / 16; ++c16) {
+    const int64_t grow = (int64_t)n * P.T + cx.t0 + q;
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      const int c16 = wg * 4 + h;
       float gs[16], gz[16], hs[16], hz[16], y0[8], y1[8];
       umma::tmem_ld16(lane_addr(tm, c16 * 16), gs);
       umma::tmem_ld16(lane_addr(tm, 128 + c16 * 16), gz);
@@ -188,8 +191,8 @@ __global__ void __launch_bounds__(kT) k_bwd_state_tc(Params P) {
       umma::tmem_ld16(lane_addr(tm, 384 + c16 * 16), hz);
       umma::tmem_ld_wait();
       if (q < L) {
-        ld8io(P.dy, row * P.dv + c16 * 16, P.bf, y0);
-        ld8io(P.dy, row * P.dv + c16 * 16 + 8, P.bf, y1);
+        load_unit(tY, q, 2 * c16, kD, y0);
+        load_unit(tY, q, 2 * c16 + 1, kD, y1);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           xs += gs[i] * y0[i] + gs[8 + i] * y1[i];
@@ -198,12 +201,18 @@ __global__ void __launch_bounds__(kT) k_bwd_state_tc(Params P) {
         float d[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) d[i] = ss * hs[i] + sz * hz[i];
-        st16f(P.dpsi + row * P.dphi + c16 * 16, d);
+        st16f(P.dpsi + grow * P.dphi + c16 * 16, d);
       }
     }
-    float* xq = P.xq + (chunk_id(P, cx) * kT + q) * 2;
-    xq[0] = q < L ? xs : 0.f;
-    xq[1] = q < L ? xz : 0.f;
+    part[(wg * 2 + 0) * kR + q] = xs;
+    part[(wg * 2 + 1) * kR + q] = xz;
+  }
+  __syncthreads();
+  if (wg == 0) {
+    const int q = row;
+    float* xq = P.xq + (chunk_id(P, cx) * kR + q) * 2;
+    xq[0] = q < L ? part[q] + part[2 * kR + q] : 0.f;
+    xq[1] = q < L ? part[kR + q] + part[3 * kR + q] : 0.f;
   }
   tc_teardown(tm);
 }
@@ -237,11 +246,12 @@ __global__ void __launch_bounds__(kT) k_bwd_adj_tc(Params P) {
   __shared__ uint32_t tbase;
   Ctx cx;
   load_ctx(P, sa, cx, kT);
-  float* hS = sa.take(kT + 1);
-  float* hZS = sa.take(kT + 1);
-  float* hZZ = sa.take(kT + 1);
+  float* hS = sa.take(kR + 1);
+  float* hZS = sa.take(kR + 1);
+  float* hZZ = sa.take(kR + 1);
   float* red = sa.take(32);
-  const int n = cx.n, K = cx.K, tid = threadIdx.x, e = P.e;
+  float* part = sa.take(4 * kR);
+  const int n = cx.n, K = cx.K, tid = threadIdx.x, e = P.e, row = row_of(), wg = wg_of();
   Sync sy{&mbar, &tbase, 0, nullptr};
   const uint32_t tm = tc_setup(sy);
   const int64_t D2 = (int64_t)kD * kD;
@@ -272,29 +282,32 @@ __global__ void __launch_bounds__(kT) k_bwd_adj_tc(Params P) {
       s10 += fz.x * si.x + fz.y * si.y + fz.z * si.z + fz.w * si.w;
       s11 += fz.x * zi.x + fz.y * zi.y + fz.z * zi.z + fz.w * zi.w;
     }
-    float* o = P.xs + cid * 4;
-    float v[4] = {s00, s01, s10, s11};
+    const float v[4] = {s00, s01, s10, s11};
     for (int k = 0; k < 4; ++k) {
       float t = v[k];
       for (int off = 16; off > 0; off >>= 1) t += __shfl_xor_sync(0xffffffffu, t, off);
-      if ((tid & 31) == 0) red[k * 4 + (tid >> 5)] = t;
+      if ((tid & 31) == 0) red[k * 8 + (tid >> 5)] = t;
     }
     __syncthreads();
-    if (tid < 4) o[tid] = red[tid * 4] + red[tid * 4 + 1] + red[tid * 4 + 2] + red[tid * 4 + 3];
+    if (tid < 4) {
+      float t = 0.f;
+      for (int w = 0; w < kT / 32; ++w) t += red[tid * 8 + w];
+      P.xs[cid * 4 + tid] = t;
+    }
   }
   mma_wait(sy);
   {
-    const int j = tid, p = cx.kp0 + j;
+    const int j = row, p = cx.kp0 + j;
     float wzs, wzz;
     key_adj_weights(P, cx, j, hZS, hZZ, wzs, wzz);
     const bool own = j < K && p >= cx.t0, halo = j < K && p >= 0 && p < cx.t0;
+    const int e1 = e > 1 ? e - 1 : 1;
     float xS = 0.f, xZ = 0.f;
-    const int64_t drow = ((int64_t)n * P.T + (p >= 0 ? p : 0)) * P.dv;
-    float* dd = own ? P.ddel + ((int64_t)n * P.T + p) * P.dv
-                    : P.hdd + ((cid * (e > 1 ? e - 1 : 1)) + (j < e - 1 ? j : 0)) * P.dv;
-    float* dp = own ? P.dphiR + ((int64_t)n * P.T + p) * P.dphi
-                    : P.hdp + ((cid * (e > 1 ? e - 1 : 1)) + (j < e - 1 ? j : 0)) * P.dphi;
-    for (int c16 = 0; c16 < kD / 16; ++c16) {
+    float* dd = own ? P.ddel + ((int64_t)n * P.T + p) * P.dv : P.hdd + (cid * e1 + (j < e - 1 ? j : 0)) * P.dv;
+    float* dp = own ? P.dphiR + ((int64_t)n * P.T + p) * P.dphi : P.hdp + (cid * e1 + (j < e - 1 ? j : 0)) * P.dphi;
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      const int c16 = wg * 4 + h;
       float p1[16], p2[16], q1[16], q2[16];
       umma::tmem_ld16(lane_addr(tm, c16 * 16), p1);
       umma::tmem_ld16(lane_addr(tm, 128 + c16 * 16), p2);
@@ -303,8 +316,8 @@ __global__ void __launch_bounds__(kT) k_bwd_adj_tc(Params P) {
       umma::tmem_ld_wait();
       if (own || halo) {
         float dl[16], a[16], b[16];
-        ld8f(P.delta + drow + c16 * 16, *reinterpret_cast<float(*)[8]>(dl));
-        ld8f(P.delta + drow + c16 * 16 + 8, *reinterpret_cast<float(*)[8]>(dl + 8));
+        load_unit(tDl, j, 2 * c16, kD, *reinterpret_cast<float(*)[8]>(dl));
+        load_unit(tDl, j, 2 * c16 + 1, kD, *reinterpret_cast<float(*)[8]>(dl + 8));
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           xS += p1[i] * dl[i];
@@ -316,9 +329,14 @@ __global__ void __launch_bounds__(kT) k_bwd_adj_tc(Params P) {
         st16f(dp + c16 * 16, b);
       }
     }
-    float* xf = P.xf + (cid * kT + j) * 2;
-    xf[0] = xS;
-    xf[1] = xZ;
+    part[(wg * 2 + 0) * kR + j] = xS;
+    part[(wg * 2 + 1) * kR + j] = xZ;
+  }
+  __syncthreads();
+  if (wg == 0) {
+    float* xf = P.xf + (cid * kR + row) * 2;
+    xf[0] = part[row] + part[2 * kR + row];
+    xf[1] = part[kR + row] + part[3 * kR + row];
   }
   tc_teardown(tm);
 }
@@ -344,7 +362,7 @@ __global__ void __launch_bounds__(kT) k_bwd_intra_tc(Params P) {
   __shared__ uint32_t tbase;
   Ctx cx;
   load_ctx(P, sa, cx, kT);
-  const int n = cx.n, K = cx.K, L = cx.L, tid = threadIdx.x, e = P.e;
+  const int n = cx.n, K = cx.K, L = cx.L, tid = threadIdx.x, e = P.e, row = row_of(), wg = wg_of();
   Sync sy{&mbar, &tbase, 0, nullptr};
   const uint32_t tm = tc_setup(sy);
   const int64_t cid = chunk_id(P, cx);
@@ -353,43 +371,44 @@ __global__ void __launch_bounds__(kT) k_bwd_intra_tc(Params P) {
   fill_rows_psi(P, cx, tPsi);
   fill_rows_dy(P, cx, tY, [](int) { return 1.f; });
   __syncthreads();
-  {  // row q of M1 staging: wE_j[q] for every key j
-    const int q = tid;
-    float wl[kT];
+  {  // row q of M1 staging: wE_j[q] for the keys j of this warpgroup's column half
+    const int q = row, j0 = wg * (kR / 2);
+    float wl[kR / 2];
 #pragma unroll
-    for (int j = 0; j < kT; ++j) wl[j] = 0.f;
+    for (int j = 0; j < kR / 2; ++j) wl[j] = 0.f;
     if (q < L) {
       float es = 0.f, ez = 0.f;  // eS_{L}, eZ_{L}
       for (int i = L - 1; i >= 0; --i) {
         // ez holds eZ_{i+1}[q]; key j gets it from token i when i <= j <= i + e - 1
         for (int jj = 0; jj < e; ++jj) {
           const int j = i + jj;
-          if (j < K) wl[j] += wgt(P, cx, i, j) * ez;
+          if (j < K && j >= j0 && j < j0 + kR / 2) wl[j - j0] += wgt(P, cx, i, j) * ez;
         }
         const float eta = i >= 1 ? cx.et[i - 1] : 0.f;
         es = cx.al[i] * es + (q == i ? 1.f : 0.f);
         ez = cx.be[i] * ez - eta * es;
       }
     }
-    for (int cb = 0; cb < kT / 8; ++cb) {
+#pragma unroll
+    for (int cb = 0; cb < kR / 16; ++cb) {
       float v[8];
 #pragma unroll
       for (int k = 0; k < 8; ++k) v[k] = wl[cb * 8 + k];
-      store_unit(tM1, q, cb, kT, v);
+      store_unit(tM1, q, wg * (kR / 16) + cb, kR, v);
     }
   }
   smem_to_tc();
   if (tid == 0) {
-    mma_chain(tm, op(tY, kD, 0), op(tDl, kD, 0), 8, kT, false);       // A1[q][j]
-    mma_chain(tm + 128, op(tPsi, kD, 0), op(tPhi, kD, 0), 8, kT, false);  // A2[q][j]
+    mma_chain(tm, op(tY, kD, 0), op(tDl, kD, 0), 8, kR, false);       // A1[q][j]
+    mma_chain(tm + 128, op(tPsi, kD, 0), op(tPhi, kD, 0), 8, kR, false);  // A2[q][j]
   }
   mma_wait(sy);
-  {  // column j of tDl <- cS before token i (delta is no longer needed)
-    const int j = tid;
+  if (wg == 0) {  // column j of tDl <- cS before token i (delta is no longer needed)
+    const int j = row;
     float cs = 0.f, cz = 0.f;
-    for (int i = 0; i < kT; ++i) {
+    for (int i = 0; i < kR; ++i) {
       const bool live = i < L && j < K;
-      *reinterpret_cast<__nv_bfloat16*>(tDl + umma::elem_off(i, j, kT)) = __float2bfloat16_rn(live ? cs : 0.f);
+      *reinterpret_cast<__nv_bfloat16*>(tDl + umma::elem_off(i, j, kR)) = __float2bfloat16_rn(live ? cs : 0.f);
       if (live) {
         cz = cx.be[i] * cz + wgt(P, cx, i, j);
         cs = cx.al[i] * cs - cx.et[i] * cz;
@@ -398,18 +417,21 @@ __global__ void __launch_bounds__(kT) k_bwd_intra_tc(Params P) {
   }
   __syncthreads();
   {
-    const int q = tid;
+    const int q = row;
     unsigned char* gdst = reinterpret_cast<unsigned char*>(P.gt) + cid * kTileBytes;
-    for (int c16 = 0; c16 < kT / 16; ++c16) {
+#pragma unroll
+    for (int h4 = 0; h4 < 4; ++h4) {
+      const int c16 = wg * 4 + h4;
       float a1[16], a2[16];
       umma::tmem_ld16(lane_addr(tm, c16 * 16), a1);
       umma::tmem_ld16(lane_addr(tm, 128 + c16 * 16), a2);
       umma::tmem_ld_wait();
+#pragma unroll
       for (int h = 0; h < 2; ++h) {
         const int cb = 2 * c16 + h;
         float g[8], c3[8], w1[8], m2[8];
-        load_unit(tDl, q, cb, kT, c3);
-        load_unit(tM1, q, cb, kT, w1);
+        load_unit(tDl, q, cb, kR, c3);
+        load_unit(tM1, q, cb, kR, w1);
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
           const float x1 = a1[8 * h + k], x2 = a2[8 * h + k];
@@ -418,42 +440,45 @@ __global__ void __launch_bounds__(kT) k_bwd_intra_tc(Params P) {
           m2[k] = w1[k] * x1;
           w1[k] *= x2;
         }
-        store_unit(gdst, q, cb, kT, g);
-        store_unit(tDl, q, cb, kT, c3);
-        store_unit(tM1, q, cb, kT, w1);
-        store_unit(tM2, q, cb, kT, m2);
+        store_unit(gdst, q, cb, kR, g);
+        store_unit(tDl, q, cb, kR, c3);
+        store_unit(tM1, q, cb, kR, w1);
+        store_unit(tM2, q, cb, kR, m2);
       }
     }
   }
   smem_to_tc();
   if (tid == 0) {
-    mma_chain(tm + 256, op(tM1, kT, 1), op(tY, kD, 1), 8, kD, false);   // I3 [j][nn]
-    mma_chain(tm + 384, op(tM2, kT, 1), op(tPsi, kD, 1), 8, kD, false); // I4 [j][m]
-    mma_chain(tm, op(tDl, kT, 0), op(tPhi, kD, 1), 8, kD, false);       // I5 [i][m]
+    mma_chain(tm + 256, op(tM1, kR, 1), op(tY, kD, 1), 8, kD, false);   // I3 [j][nn]
+    mma_chain(tm + 384, op(tM2, kR, 1), op(tPsi, kD, 1), 8, kD, false); // I4 [j][m]
+    mma_chain(tm, op(tDl, kR, 0), op(tPhi, kD, 1), 8, kD, false);       // I5 [i][m]
   }
   mma_wait(sy);
   {
-    const int r = tid, p = cx.kp0 + r;
+    const int r = row, p = cx.kp0 + r;
     const bool own = r < K && p >= cx.t0, halo = r < K && p >= 0 && p < cx.t0;
     const int e1 = e > 1 ? e - 1 : 1;
     float* dd = own ? P.ddel + ((int64_t)n * P.T + p) * P.dv : P.hdd + (cid * e1 + (r < e - 1 ? r : 0)) * P.dv;
     float* dp = own ? P.dphiR + ((int64_t)n * P.T + p) * P.dphi : P.hdp + (cid * e1 + (r < e - 1 ? r : 0)) * P.dphi;
     float* dq = P.dpsi + ((int64_t)n * P.T + cx.t0 + (r < L ? r : 0)) * P.dphi;
-    for (int c16 = 0; c16 < kD / 16; ++c16) {
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      const int c16 = wg * 4 + h;
       float i3[16], i4[16], i5[16];
       umma::tmem_ld16(lane_addr(tm, 256 + c16 * 16), i3);
       umma::tmem_ld16(lane_addr(tm, 384 + c16 * 16), i4);
       umma::tmem_ld16(lane_addr(tm, c16 * 16), i5);
       umma::tmem_ld_wait();
+      // fire-and-forget adds onto the values k_bwd_state_tc / k_bwd_adj_tc wrote
       if (own || halo)
 #pragma unroll
         for (int k = 0; k < 16; ++k) {
-          dd[c16 * 16 + k] += i3[k];
-          dp[c16 * 16 + k] += i4[k];
+          atomicAdd(dd + c16 * 16 + k, i3[k]);
+          atomicAdd(dp + c16 * 16 + k, i4[k]);
         }
       if (r < L)
 #pragma unroll
-        for (int k = 0; k < 16; ++k) dq[c16 * 16 + k] += i5[k];
+        for (int k = 0; k < 16; ++k) atomicAdd(dq + c16 * 16 + k, i5[k]);
     }
   }
   tc_teardown(tm);
@@ -467,10 +492,11 @@ __global__ void __launch_bounds__(kT) k_bwd_intra_tc(Params P) {
 // E_Z+ G (tensor cores); the F / S_in / Z_in rows and columns of the Gram
 // matrix are folded in on CUDA cores.
 // ===========================================================================
+constexpr int kGateParts = 10;
 __global__ void __launch_bounds__(kT) k_bwd_gates_tc(Params P) {
   extern __shared__ __align__(1024) unsigned char sm[];
   unsigned char* tG = sm;
-  unsigned char* tCS = sm + kTileBytes;    // cS_i[j]     (state before token i)
+  unsigned char* tCS = sm + kTileBytes;       // cS_i[j]     (state before token i)
   unsigned char* tCZp = sm + 2 * kTileBytes;  // cZ_i[j]
   unsigned char* tCZn = sm + 3 * kTileBytes;  // cZ_{i+1}[j] (state after token i)
   unsigned char* tES = sm + 4 * kTileBytes;   // eS_{i+1}[q]
@@ -480,17 +506,18 @@ __global__ void __launch_bounds__(kT) k_bwd_gates_tc(Params P) {
   __shared__ uint32_t tbase;
   Ctx cx;
   load_ctx(P, sa, cx, kT);
-  float* sS = sa.take(kT + 1);
-  float* sZ = sa.take(kT + 1);
-  float* zZ = sa.take(kT + 1);
-  float* hS = sa.take(kT + 1);
-  float* hZS = sa.take(kT + 1);
-  float* hZZ = sa.take(kT + 1);
-  float* xq = sa.take(2 * kT);
-  float* xf = sa.take(2 * kT);
+  float* sS = sa.take(kR + 1);
+  float* sZ = sa.take(kR + 1);
+  float* zZ = sa.take(kR + 1);
+  float* hS = sa.take(kR + 1);
+  float* hZS = sa.take(kR + 1);
+  float* hZZ = sa.take(kR + 1);
+  float* xq = sa.take(2 * kR);
+  float* xf = sa.take(2 * kR);
   float* xs = sa.take(4);
-  float* duj = sa.take(kT);
-  const int n = cx.n, K = cx.K, L = cx.L, tid = threadIdx.x, e = P.e;
+  float* duj = sa.take(kR);
+  float* part = sa.take(kGateParts * kR);  // warpgroup 1's partial sums
+  const int n = cx.n, K = cx.K, L = cx.L, tid = threadIdx.x, e = P.e, row = row_of(), wg = wg_of();
   Sync sy{&mbar, &tbase, 0, nullptr};
   const uint32_t tm = tc_setup(sy);
   const int64_t cid = chunk_id(P, cx);
@@ -498,122 +525,126 @@ __global__ void __launch_bounds__(kT) k_bwd_gates_tc(Params P) {
     const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const unsigned char*>(P.gt) + cid * kTileBytes);
     uint4* dst = reinterpret_cast<uint4*>(tG);
     for (int u = tid; u < kTileBytes / 16; u += kT) dst[u] = src[u];
-    xq[tid] = P.xq[cid * 2 * kT + tid];
-    xq[kT + tid] = P.xq[cid * 2 * kT + kT + tid];
-    xf[tid] = P.xf[cid * 2 * kT + tid];
-    xf[kT + tid] = P.xf[cid * 2 * kT + kT + tid];
+    xq[tid] = P.xq[cid * 2 * kR + tid];
+    xf[tid] = P.xf[cid * 2 * kR + tid];
     if (tid < 4) xs[tid] = P.xs[cid * 4 + tid];
-    duj[tid] = 0.f;
+    if (tid < kR) duj[tid] = 0.f;
   }
   __syncthreads();
-  {
-    const int j = tid;  // forward coefficients of key j (column j of tCS, tCZp, tCZn)
+  if (wg == 0) {
+    const int j = row;  // forward coefficients of key j (column j of tCS, tCZp, tCZn)
     float cs = 0.f, cz = 0.f;
-    for (int i = 0; i < kT; ++i) {
+    for (int i = 0; i < kR; ++i) {
       const bool live = i < L && j < K;
-      float czn = 0.f;
-      if (live) {
-        czn = cx.be[i] * cz + wgt(P, cx, i, j);
-      }
-      *reinterpret_cast<__nv_bfloat16*>(tCS + umma::elem_off(i, j, kT)) = __float2bfloat16_rn(live ? cs : 0.f);
-      *reinterpret_cast<__nv_bfloat16*>(tCZp + umma::elem_off(i, j, kT)) = __float2bfloat16_rn(live ? cz : 0.f);
-      *reinterpret_cast<__nv_bfloat16*>(tCZn + umma::elem_off(i, j, kT)) = __float2bfloat16_rn(live ? czn : 0.f);
+      const float czn = live ? cx.be[i] * cz + wgt(P, cx, i, j) : 0.f;
+      *reinterpret_cast<__nv_bfloat16*>(tCS + umma::elem_off(i, j, kR)) = __float2bfloat16_rn(live ? cs : 0.f);
+      *reinterpret_cast<__nv_bfloat16*>(tCZp + umma::elem_off(i, j, kR)) = __float2bfloat16_rn(live ? cz : 0.f);
+      *reinterpret_cast<__nv_bfloat16*>(tCZn + umma::elem_off(i, j, kR)) = __float2bfloat16_rn(czn);
       if (live) {
         cz = czn;
         cs = cx.al[i] * cs - cx.et[i] * cz;
       }
     }
-    const int q = tid;  // adjoint coefficients of token q (column q of tES, tEZ): rows i <- eS_{i+1}, eZ_{i+1}
+    if (row == 0) fwd_scalars(cx, sS, sZ, zZ);
+  } else {
+    const int q = row;  // adjoint coefficients of token q (column q of tES, tEZ): rows i <- eS_{i+1}, eZ_{i+1}
     float es = 0.f, ez = 0.f;
-    for (int i = kT - 1; i >= 0; --i) {
+    for (int i = kR - 1; i >= 0; --i) {
       const bool live = i < L && q < L;
-      // es, ez hold eS_{i+1}[q], eZ_{i+1}[q] here
-      *reinterpret_cast<__nv_bfloat16*>(tES + umma::elem_off(i, q, kT)) = __float2bfloat16_rn(live ? es : 0.f);
-      *reinterpret_cast<__nv_bfloat16*>(tEZ + umma::elem_off(i, q, kT)) = __float2bfloat16_rn(live ? ez : 0.f);
+      *reinterpret_cast<__nv_bfloat16*>(tES + umma::elem_off(i, q, kR)) = __float2bfloat16_rn(live ? es : 0.f);
+      *reinterpret_cast<__nv_bfloat16*>(tEZ + umma::elem_off(i, q, kR)) = __float2bfloat16_rn(live ? ez : 0.f);
       if (live) {
         const float eta = i >= 1 ? cx.et[i - 1] : 0.f;
         es = cx.al[i] * es + (q == i ? 1.f : 0.f);
         ez = cx.be[i] * ez - eta * es;
       }
     }
-    if (tid == 0) fwd_scalars(cx, sS, sZ, zZ);
-    if (tid == 32) adj_scalars(cx, hS, hZS, hZZ);
+    if (row == 0) adj_scalars(cx, hS, hZS, hZZ);
   }
   smem_to_tc();
   if (tid == 0) {
-    mma_chain(tm, op(tCS, kT, 0), op(tG, kT, 0), 8, kT, false);         // W_a[i][q]
-    mma_chain(tm + 128, op(tCZn, kT, 0), op(tG, kT, 0), 8, kT, false);  // W_e[i][q]
-    mma_chain(tm + 256, op(tCZp, kT, 0), op(tG, kT, 0), 8, kT, false);  // W_b[i][q]
-    mma_chain(tm + 384, op(tEZ, kT, 0), op(tG, kT, 1), 8, kT, false);   // E_Z+ G [i][j]
+    mma_chain(tm, op(tCS, kR, 0), op(tG, kR, 0), 8, kR, false);         // W_a[i][q]
+    mma_chain(tm + 128, op(tCZn, kR, 0), op(tG, kR, 0), 8, kR, false);  // W_e[i][q]
+    mma_chain(tm + 256, op(tCZp, kR, 0), op(tG, kR, 0), 8, kR, false);  // W_b[i][q]
+    mma_chain(tm + 384, op(tEZ, kR, 0), op(tG, kR, 1), 8, kR, false);   // E_Z+ G [i][j]
   }
   mma_wait(sy);
-  {
-    const int i = tid;
-    float fs_cs = 0.f, fs_czn = 0.f, fs_czp = 0.f, fz_czp = 0.f;
-    float qs_es = 0.f, qz_es = 0.f, qz_ez = 0.f, wa = 0.f, we = 0.f, wb = 0.f;
-    for (int c16 = 0; c16 < kT / 16; ++c16) {
-      float A[16], E[16], B[16];
-      umma::tmem_ld16(lane_addr(tm, c16 * 16), A);
-      umma::tmem_ld16(lane_addr(tm, 128 + c16 * 16), E);
-      umma::tmem_ld16(lane_addr(tm, 256 + c16 * 16), B);
-      umma::tmem_ld_wait();
-      for (int h = 0; h < 2; ++h) {
-        const int cb = 2 * c16 + h;
-        float cs8[8], czn8[8], czp8[8], es8[8], ez8[8];
-        load_unit(tCS, i, cb, kT, cs8);
-        load_unit(tCZn, i, cb, kT, czn8);
-        load_unit(tCZp, i, cb, kT, czp8);
-        load_unit(tES, i, cb, kT, es8);
-        load_unit(tEZ, i, cb, kT, ez8);
+  const int i = row;
+  float acc[kGateParts];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const int x = cb * 8 + k;  // key j (for c*) or token q (for e*)
-          fs_cs += xf[2 * x] * cs8[k];
-          fs_czn += xf[2 * x] * czn8[k];
-          fs_czp += xf[2 * x] * czp8[k];
-          fz_czp += xf[2 * x + 1] * czp8[k];
-          qs_es += xq[2 * x] * es8[k];
-          qz_es += xq[2 * x + 1] * es8[k];
-          qz_ez += xq[2 * x + 1] * ez8[k];
-          wa += es8[k] * A[8 * h + k];
-          we += es8[k] * E[8 * h + k];
-          wb += ez8[k] * B[8 * h + k];
-        }
+  for (int k = 0; k < kGateParts; ++k) acc[k] = 0.f;
+#pragma unroll
+  for (int h4 = 0; h4 < 4; ++h4) {
+    const int c16 = wg * 4 + h4;
+    float A[16], E[16], B[16];
+    umma::tmem_ld16(lane_addr(tm, c16 * 16), A);
+    umma::tmem_ld16(lane_addr(tm, 128 + c16 * 16), E);
+    umma::tmem_ld16(lane_addr(tm, 256 + c16 * 16), B);
+    umma::tmem_ld_wait();
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int cb = 2 * c16 + h;
+      float cs8[8], czn8[8], czp8[8], es8[8], ez8[8];
+      load_unit(tCS, i, cb, kR, cs8);
+      load_unit(tCZn, i, cb, kR, czn8);
+      load_unit(tCZp, i, cb, kR, czp8);
+      load_unit(tES, i, cb, kR, es8);
+      load_unit(tEZ, i, cb, kR, ez8);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int x = cb * 8 + k;  // key j (for c*) or token q (for e*)
+        acc[0] += xf[2 * x] * cs8[k];        // F_S . cS_i
+        acc[1] += xf[2 * x] * czn8[k];       // F_S . cZ_{i+1}
+        acc[2] += xf[2 * x] * czp8[k];       // F_S . cZ_i
+        acc[3] += xf[2 * x + 1] * czp8[k];   // F_Z . cZ_i
+        acc[4] += xq[2 * x] * es8[k];        // eS_{i+1} . X[D][S_in]
+        acc[5] += xq[2 * x + 1] * es8[k];    // eS_{i+1} . X[D][Z_in]
+        acc[6] += xq[2 * x + 1] * ez8[k];    // eZ_{i+1} . X[D][Z_in]
+        acc[7] += es8[k] * A[8 * h + k];
+        acc[8] += es8[k] * E[8 * h + k];
+        acc[9] += ez8[k] * B[8 * h + k];
       }
     }
-    if (i < L) {
-      const float da = hS[i + 1] * (xs[0] * sS[i] + xs[1] * sZ[i] + fs_cs) + (qs_es * sS[i] + qz_es * sZ[i] + wa);
-      const float de = -(hS[i + 1] * (xs[1] * zZ[i + 1] + fs_czn) + (qz_es * zZ[i + 1] + we));
-      const float db = hZS[i + 1] * (xs[1] * zZ[i] + fs_czp) + hZZ[i + 1] * (xs[3] * zZ[i] + fz_czp) +
-                       (qz_ez * zZ[i] + wb);
-      const int64_t r = (int64_t)n * P.T + cx.t0 + i;
-      if (P.ddecay) stio(P.ddecay, r, da, P.bf);
-      if (P.dlr) stio(P.dlr, r, de, P.bf);
-      if (P.mom && P.dbeta) stio(P.dbeta, r, db, P.bf);
-    }
-    // window weights dW(i, j) = hZS_{i+1} X[F_S][R_j] + hZZ_{i+1} X[F_Z][R_j] + (E_Z+ G)[i][j]
-    if (P.gmode != ATLAS_GATE_NONE) {
-      for (int c16 = 0; c16 < kT / 16; ++c16) {
-        float W[16];
-        umma::tmem_ld16(lane_addr(tm, 384 + c16 * 16), W);
-        umma::tmem_ld_wait();
-        if (i < L)
-          for (int k = 0; k < 16; ++k) {
-            const int j = c16 * 16 + k, jj = i - j + e - 1;
-            if (j >= K || jj < 0 || jj >= e) continue;
-            const float val = hZS[i + 1] * xf[2 * j] + hZZ[i + 1] * xf[2 * j + 1] + W[k];
-            if (P.gmode == ATLAS_GATE_TOKEN) {
-              if (cx.kp0 + j >= 0) atomicAdd(&duj[j], val);
-            } else if (P.dgate) {
-              stio(P.dgate, ((int64_t)n * P.T + cx.t0 + i) * e + jj, val, P.bf);
-            }
+  }
+  if (wg == 1)
+#pragma unroll
+    for (int k = 0; k < kGateParts; ++k) part[k * kR + i] = acc[k];
+  // window weights dW(i, j) = hZS_{i+1} X[F_S][R_j] + hZZ_{i+1} X[F_Z][R_j] + (E_Z+ G)[i][j]
+  if (P.gmode != ATLAS_GATE_NONE) {
+#pragma unroll
+    for (int h4 = 0; h4 < 4; ++h4) {
+      const int c16 = wg * 4 + h4;
+      float W[16];
+      umma::tmem_ld16(lane_addr(tm, 384 + c16 * 16), W);
+      umma::tmem_ld_wait();
+      if (i < L)
+        for (int k = 0; k < 16; ++k) {
+          const int j = c16 * 16 + k, jj = i - j + e - 1;
+          if (j >= K || jj < 0 || jj >= e) continue;
+          const float val = hZS[i + 1] * xf[2 * j] + hZZ[i + 1] * xf[2 * j + 1] + W[k];
+          if (P.gmode == ATLAS_GATE_TOKEN) {
+            if (cx.kp0 + j >= 0) atomicAdd(&duj[j], val);
+          } else if (P.dgate) {
+            stio(P.dgate, ((int64_t)n * P.T + cx.t0 + i) * e + jj, val, P.bf);
           }
-      }
+        }
     }
   }
   __syncthreads();
-  if (P.gmode == ATLAS_GATE_TOKEN) {
-    const int j = tid, p = cx.kp0 + j;
+  if (wg == 0 && i < L) {
+#pragma unroll
+    for (int k = 0; k < kGateParts; ++k) acc[k] += part[k * kR + i];
+    const float da = hS[i + 1] * (xs[0] * sS[i] + xs[1] * sZ[i] + acc[0]) + (acc[4] * sS[i] + acc[5] * sZ[i] + acc[7]);
+    const float de = -(hS[i + 1] * (xs[1] * zZ[i + 1] + acc[1]) + (acc[5] * zZ[i + 1] + acc[8]));
+    const float db = hZS[i + 1] * (xs[1] * zZ[i] + acc[2]) + hZZ[i + 1] * (xs[3] * zZ[i] + acc[3]) +
+                     (acc[6] * zZ[i] + acc[9]);
+    const int64_t r = (int64_t)n * P.T + cx.t0 + i;
+    if (P.ddecay) stio(P.ddecay, r, da, P.bf);
+    if (P.dlr) stio(P.dlr, r, de, P.bf);
+    if (P.mom && P.dbeta) stio(P.dbeta, r, db, P.bf);
+  }
+  if (P.gmode == ATLAS_GATE_TOKEN && wg == 0) {
+    const int j = row, p = cx.kp0 + j;
     if (j < K && p >= cx.t0) P.du[(int64_t)n * P.T + p] = duj[j];
     else if (j < K && p >= 0) P.hdu[cid * (e - 1) + j] = duj[j];
   }
@@ -680,7 +711,7 @@ __global__ void __launch_bounds__(kThreads) k_bwd_buf_tc(Params P) {
       for (int64_t x = tid; x < D2; x += kThreads) { s0 += FS[x] * Bj[x]; s1 += FZ[x] * Bj[x]; }
       s0 = block_sum(s0, red);
       s1 = block_sum(s1, red);
-      if (tid == 0) { P.xf[(cid * kT + jb) * 2] = s0; P.xf[(cid * kT + jb) * 2 + 1] = s1; }
+      if (tid == 0) { P.xf[(cid * kR + jb) * 2] = s0; P.xf[(cid * kR + jb) * 2 + 1] = s1; }
       // G[q][jb] = dy_q . (Buf_jb psi_q), one warp per q
       for (int q = tid >> 5; q < L; q += kThreads / 32) {
         float acc = 0.f;
@@ -691,7 +722,7 @@ __global__ void __launch_bounds__(kThreads) k_bwd_buf_tc(Params P) {
         }
         for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
         if ((tid & 31) == 0)
-          *reinterpret_cast<__nv_bfloat16*>(gt + umma::elem_off(q, jb, kT)) = __float2bfloat16_rn(acc);
+          *reinterpret_cast<__nv_bfloat16*>(gt + umma::elem_off(q, jb, kR)) = __float2bfloat16_rn(acc);
       }
     }
     // d psi_i += sum_jb cS_i[jb] Buf_jb^T dy_i

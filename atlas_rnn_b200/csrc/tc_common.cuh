@@ -1,9 +1,11 @@
 // Shared pieces of the tensor-core (tcgen05) chunk kernels.
 //
-// Every tensor-core chunk kernel runs 128 threads: thread t owns TMEM lane t,
-// i.e. row t of every 128-row accumulator. Operand tiles are 128 rows x D
-// columns of bf16 in the core-matrix layout of umma.cuh (rows past the valid
-// range are zero). Head sizes d_phi = d_v = D = 128.
+// Every tensor-core chunk kernel runs 256 threads, two warpgroups. Warp w
+// reaches TMEM lanes [32 (w % 4), 32 (w % 4) + 32), so thread t owns row
+// t % 128 of every 128-row accumulator, and the two warpgroups split its
+// columns (warpgroup g takes columns [64 g, 64 g + 64) of a 128-column one).
+// Operand tiles are 128 rows x D columns of bf16 in the core-matrix layout of
+// umma.cuh (rows past the valid range are zero). d_phi = d_v = D = 128.
 #pragma once
 #include <cuda_bf16.h>
 
@@ -13,9 +15,13 @@
 namespace atlas {
 namespace tc {
 
-constexpr int kT = 128;        // threads per CTA
+constexpr int kT = 256;        // threads per CTA
+constexpr int kR = 128;        // rows of a tile / TMEM lanes
 constexpr int kD = 128;        // head size handled by the tensor-core path
-constexpr int kTileBytes = 128 * kD * 2;
+constexpr int kTileBytes = kR * kD * 2;
+
+__device__ __forceinline__ int row_of() { return threadIdx.x & (kR - 1); }  // accumulator row of this thread
+__device__ __forceinline__ int wg_of() { return threadIdx.x >> 7; }          // warpgroup: column half
 
 struct Op {
   uint32_t saddr;  // shared address of the tile
@@ -82,7 +88,7 @@ __device__ __forceinline__ void tc_teardown(uint32_t tm) {
 
 // TMEM address of row (this thread's lane) and column `col`.
 __device__ __forceinline__ uint32_t lane_addr(uint32_t tm, int col) {
-  return tm + ((uint32_t)((threadIdx.x >> 5) * 32) << 16) + (uint32_t)col;
+  return tm + ((uint32_t)(((threadIdx.x >> 5) & 3) * 32) << 16) + (uint32_t)col;
 }
 
 // Pack 8 floats to bf16 and store one 16-byte unit of a tile.
@@ -104,14 +110,23 @@ __device__ __forceinline__ void load_unit(const unsigned char* tile, int r, int 
 }
 
 // Fill a 128 x C tile; src(r, c0, v) fills v[0..7] for columns c0..c0+7 of row r.
+// Each thread gathers 8 units before storing any, so 8 loads are in flight.
 template <class F>
 __device__ __forceinline__ void fill_tile(unsigned char* tile, int C, F src) {
-  const int units = 128 * (C / 8);
-  for (int u = threadIdx.x; u < units; u += kT) {
-    const int r = u / (C / 8), cb = u - r * (C / 8);
-    float v[8];
-    src(r, cb * 8, v);
-    store_unit(tile, r, cb, C, v);
+  constexpr int kBatch = 8;
+  const int cpr = C / 8, units = 128 * cpr;
+  for (int base = threadIdx.x; base < units; base += kT * kBatch) {
+    float v[kBatch][8];
+#pragma unroll
+    for (int k = 0; k < kBatch; ++k) {
+      const int u = base + k * kT;
+      if (u < units) src(u / cpr, (u % cpr) * 8, v[k]);
+    }
+#pragma unroll
+    for (int k = 0; k < kBatch; ++k) {
+      const int u = base + k * kT;
+      if (u < units) store_unit(tile, u / cpr, u % cpr, C, v[k]);
+    }
   }
 }
 
@@ -153,6 +168,16 @@ __device__ __forceinline__ void phi8(const Params& P, int n, int t, int c0, bool
   ld8io(isq ? P.q : P.k, row * P.dk + c0, P.bf, v);
 #pragma unroll
   for (int i = 0; i < 8; ++i) v[i] = fmap_elem(v[i], P.fmode, P.fdeg);
+}
+
+// 16 floats as bf16 to global, 32 bytes.
+__device__ __forceinline__ void st16bf(void* dst, const float (&v)[16]) {
+  __align__(16) __nv_bfloat162 h[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) h[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+  uint4* d = reinterpret_cast<uint4*>(dst);
+  d[0] = reinterpret_cast<uint4*>(h)[0];
+  d[1] = reinterpret_cast<uint4*>(h)[1];
 }
 
 // 16 floats to global (fp32), 64 bytes.

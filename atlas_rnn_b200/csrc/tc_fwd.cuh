@@ -49,53 +49,63 @@ __global__ void __launch_bounds__(kT) k_fwd_chunk_tc(Params P) {
   __shared__ uint32_t tbase;
   Ctx cx;
   load_ctx(P, sa, cx, kT);
-  float* cSe = sa.take(kT);
-  float* cZe = sa.take(kT);
-  const int n = cx.n, c = cx.c, K = cx.K, L = cx.L, tid = threadIdx.x;
+  float* cSe = sa.take(kR);
+  float* cZe = sa.take(kR);
+  const int n = cx.n, c = cx.c, K = cx.K, L = cx.L, tid = threadIdx.x, row = row_of(), wg = wg_of();
   Sync sy{&mbar, &tbase, 0, nullptr};
   const uint32_t tm = tc_setup(sy);
   fill_keys_phi(P, cx, tPhi);
   fill_dense(tSref, P.Sref + (int64_t)n * kD * kD);
   __syncthreads();  // gates visible to the coefficient threads
-  {
+  if (wg == 0) {    // end coefficients of key j = row
     float cs = 0.f, cz = 0.f;
-    if (tid < K)
+    if (row < K)
       for (int i = 0; i < L; ++i) {
-        cz = cx.be[i] * cz + wgt(P, cx, i, tid);
+        cz = cx.be[i] * cz + wgt(P, cx, i, row);
         cs = cx.al[i] * cs - cx.et[i] * cz;
       }
-    cSe[tid] = cs;
-    cZe[tid] = cz;
-    if (tid == kT - 1) {
-      float s = 1.f, sz = 0.f, z = 1.f;
-      for (int i = 0; i < L; ++i) {
-        z = cx.be[i] * z;
-        s = cx.al[i] * s;
-        sz = cx.al[i] * sz - cx.et[i] * z;
-      }
-      float* o = P.cs + ((int64_t)n * P.nch + c) * 4;
-      o[0] = s; o[1] = sz; o[2] = z; o[3] = 0.f;
+    cSe[row] = cs;
+    cZe[row] = cz;
+  } else if (row == 0) {  // chunk transform scalars
+    float s = 1.f, sz = 0.f, z = 1.f;
+    for (int i = 0; i < L; ++i) {
+      z = cx.be[i] * z;
+      s = cx.al[i] * s;
+      sz = cx.al[i] * sz - cx.et[i] * z;
     }
+    float* o = P.cs + ((int64_t)n * P.nch + c) * 4;
+    o[0] = s; o[1] = sz; o[2] = z; o[3] = 0.f;
   }
   smem_to_tc();
   if (tid == 0) mma_chain(tm, op(tPhi, kD, 0), op(tSref, kD, 0), kD / 16, kD, false);
+  const int j = row, p = cx.kp0 + j;
+  const bool valid = j < K && p >= 0;
+  // this thread's half of the key's v row (bf16), fetched while the MMA runs
+  uint4 vrow[kD / 16];
+  if (valid) {
+    const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(P.v) +
+                                                      ((int64_t)n * P.T + p) * P.dv + wg * (kD / 2));
+#pragma unroll
+    for (int u = 0; u < kD / 16; ++u) vrow[u] = src[u];
+  }
   mma_wait(sy);
-  {  // delta rows: thread = key j
-    const int j = tid, p = cx.kp0 + j;
-    const bool valid = j < K && p >= 0;
+  {
     const float ws = cSe[j], wz = cZe[j];
-    for (int c16 = 0; c16 < kD / 16; ++c16) {
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      const int c16 = wg * 4 + h;
       float a[16];
       umma::tmem_ld16(lane_addr(tm, c16 * 16), a);
       umma::tmem_ld_wait();
       if (valid) {
-        float v0[8], v1[8];
-        const int64_t off = ((int64_t)n * P.T + p) * P.dv + c16 * 16;
-        ld8io(P.v, off, P.bf, v0);
-        ld8io(P.v, off + 8, P.bf, v1);
+        const __nv_bfloat162* hv = reinterpret_cast<const __nv_bfloat162*>(&vrow[2 * h]);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) { a[i] -= v0[i]; a[8 + i] -= v1[i]; }
-        if (p >= cx.t0) st16f(P.delta + off, a);
+        for (int k = 0; k < 8; ++k) {
+          const float2 f = __bfloat1622float2(hv[k]);
+          a[2 * k] -= f.x;
+          a[2 * k + 1] -= f.y;
+        }
+        if (p >= cx.t0) st16f(P.delta + ((int64_t)n * P.T + p) * P.dv + c16 * 16, a);
       } else {
 #pragma unroll
         for (int i = 0; i < 16; ++i) a[i] = 0.f;
@@ -118,18 +128,20 @@ __global__ void __launch_bounds__(kT) k_fwd_chunk_tc(Params P) {
     mma_chain(tm + 256, op(tDZ, kD, 1), op(tPhi, kD, 1), 8, kD, false);
   }
   mma_wait(sy);
-  {  // increments: thread = state row nn
+  {  // increments: row = state row nn
     const int64_t D2 = (int64_t)kD * kD;
-    float* dst = P.st + ((int64_t)n * P.nch + c) * 2 * D2 + (int64_t)tid * kD;
+    float* dst = P.st + ((int64_t)n * P.nch + c) * 2 * D2 + (int64_t)row * kD;
     const float* bufn = buf_of(P, n, c);
     const int nb = bufn ? P.e - 1 : 0;
-    for (int c16 = 0; c16 < kD / 16; ++c16) {
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      const int c16 = wg * 4 + h;
       float a[16], b[16];
       umma::tmem_ld16(lane_addr(tm, 128 + c16 * 16), a);
       umma::tmem_ld16(lane_addr(tm, 256 + c16 * 16), b);
       umma::tmem_ld_wait();
       for (int jb = 0; jb < nb; ++jb) {  // carried buffer entries of chunk 0 (dense)
-        const float* bj = bufn + (int64_t)jb * D2 + (int64_t)tid * kD + c16 * 16;
+        const float* bj = bufn + (int64_t)jb * D2 + (int64_t)row * kD + c16 * 16;
 #pragma unroll
         for (int i = 0; i < 16; ++i) { a[i] += cSe[jb] * bj[i]; b[i] += cZe[jb] * bj[i]; }
       }
@@ -158,9 +170,9 @@ __global__ void __launch_bounds__(kT) k_fwd_out_tc(Params P) {
   __shared__ uint32_t tbase;
   Ctx cx;
   load_ctx(P, sa, cx, kT);
-  float* sSv = sa.take(kT);
-  float* sZv = sa.take(kT);
-  const int n = cx.n, c = cx.c, K = cx.K, L = cx.L, tid = threadIdx.x;
+  float* sSv = sa.take(kR);
+  float* sZv = sa.take(kR);
+  const int n = cx.n, c = cx.c, K = cx.K, L = cx.L, tid = threadIdx.x, row = row_of(), wg = wg_of();
   Sync sy{&mbar, &tbase, 0, nullptr};
   const uint32_t tm = tc_setup(sy);
   const int64_t D2 = (int64_t)kD * kD;
@@ -175,62 +187,65 @@ __global__ void __launch_bounds__(kT) k_fwd_out_tc(Params P) {
   fill_dense(tSin, Sin);
   fill_dense(tZin, Sin + D2);
   __syncthreads();
-  {  // column tid of tMs: cS of key tid before each token (row i)
+  if (wg == 0) {  // column j = row of tMs: cS of key j before each token i
     float cs = 0.f, cz = 0.f;
-    const int j = tid;
-    for (int i = 0; i < kT; ++i) {
-      const float val = (i < L && j < K) ? cs : 0.f;
-      *reinterpret_cast<__nv_bfloat16*>(tMs + umma::elem_off(i, j, kT)) = __float2bfloat16_rn(val);
-      if (i < L && j < K) {
+    const int j = row;
+    for (int i = 0; i < kR; ++i) {
+      const bool live = i < L && j < K;
+      *reinterpret_cast<__nv_bfloat16*>(tMs + umma::elem_off(i, j, kR)) = __float2bfloat16_rn(live ? cs : 0.f);
+      if (live) {
         cz = cx.be[i] * cz + wgt(P, cx, i, j);
         cs = cx.al[i] * cs - cx.et[i] * cz;
       }
     }
-    if (tid == kT - 1) {
-      float s = 1.f, sz = 0.f, z = 1.f;
-      for (int i = 0; i < L; ++i) {
-        sSv[i] = s;
-        sZv[i] = sz;
-        z = cx.be[i] * z;
-        s = cx.al[i] * s;
-        sz = cx.al[i] * sz - cx.et[i] * z;
-      }
+  } else if (row == 0) {
+    float s = 1.f, sz = 0.f, z = 1.f;
+    for (int i = 0; i < L; ++i) {
+      sSv[i] = s;
+      sZv[i] = sz;
+      z = cx.be[i] * z;
+      s = cx.al[i] * s;
+      sz = cx.al[i] * sz - cx.et[i] * z;
     }
   }
   smem_to_tc();
   if (tid == 0) {
-    mma_chain(tm, op(tPsi, kD, 0), op(tPhi, kD, 0), kD / 16, kT, false);          // A2 = Psi Phi^T
+    mma_chain(tm, op(tPsi, kD, 0), op(tPhi, kD, 0), kD / 16, kR, false);          // A2 = Psi Phi^T
     mma_chain(tm + 128, op(tPsi, kD, 0), op(tSin, kD, 0), kD / 16, kD, false);    // Psi S_in^T
     mma_chain(tm + 256, op(tPsi, kD, 0), op(tZin, kD, 0), kD / 16, kD, false);    // Psi Z_in^T
   }
   mma_wait(sy);
-  for (int c16 = 0; c16 < kT / 16; ++c16) {  // Ms = cS o A2, row tid
+#pragma unroll
+  for (int h = 0; h < 4; ++h) {  // Ms = cS o A2 (row `row`, this warpgroup's columns)
+    const int c16 = wg * 4 + h;
     float a[16], m0[8], m1[8];
     umma::tmem_ld16(lane_addr(tm, c16 * 16), a);
     umma::tmem_ld_wait();
-    load_unit(tMs, tid, 2 * c16, kT, m0);
-    load_unit(tMs, tid, 2 * c16 + 1, kT, m1);
+    load_unit(tMs, row, 2 * c16, kR, m0);
+    load_unit(tMs, row, 2 * c16 + 1, kR, m1);
 #pragma unroll
     for (int i = 0; i < 8; ++i) { m0[i] *= a[i]; m1[i] *= a[8 + i]; }
-    store_unit(tMs, tid, 2 * c16, kT, m0);
-    store_unit(tMs, tid, 2 * c16 + 1, kT, m1);
+    store_unit(tMs, row, 2 * c16, kR, m0);
+    store_unit(tMs, row, 2 * c16 + 1, kR, m1);
   }
   smem_to_tc();
-  if (tid == 0) mma_chain(tm + 384, op(tMs, kT, 0), op(tDl, kD, 1), 8, kD, false);
+  if (tid == 0) mma_chain(tm + 384, op(tMs, kR, 0), op(tDl, kD, 1), 8, kD, false);
   mma_wait(sy);
   {
-    const int i = tid;
+    const int i = row;
     const float ss = i < L ? sSv[i] : 0.f, sz = i < L ? sZv[i] : 0.f;
-    for (int c16 = 0; c16 < kD / 16; ++c16) {
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      const int c16 = wg * 4 + h;
       float yi[16], ps[16], pz[16];
       umma::tmem_ld16(lane_addr(tm, 384 + c16 * 16), yi);
       umma::tmem_ld16(lane_addr(tm, 128 + c16 * 16), ps);
       umma::tmem_ld16(lane_addr(tm, 256 + c16 * 16), pz);
       umma::tmem_ld_wait();
       if (i < L) {
-        const int64_t off = ((int64_t)n * P.T + cx.t0 + i) * P.dv + c16 * 16;
 #pragma unroll
-        for (int k = 0; k < 16; ++k) stio(P.y, off + k, yi[k] + ss * ps[k] + sz * pz[k], P.bf);
+        for (int k = 0; k < 16; ++k) yi[k] += ss * ps[k] + sz * pz[k];
+        st16bf(reinterpret_cast<__nv_bfloat16*>(P.y) + ((int64_t)n * P.T + cx.t0 + i) * P.dv + c16 * 16, yi);
       }
     }
   }

@@ -164,7 +164,7 @@ def step_api(inp, w, leaves_from):
     L = leaves_from
     y, S_end, Z_end, nb = memory_recurrence(
         L["k"], L["q"], L["v"], L["lr"], L["decay"], L["beta"], L["gate"], S_ref=inp["S0"], S0=inp["S0"],
-        Z0=inp["Z0"], omega_buffer=inp["omega_buffer"], window=w.window,
+        Z0=inp["Z0"], omega_buffer=None, window=w.window,  # empty carried buffer (zeros)
         gate_mode="window" if w.gate == "window" else "token", fmap_mode=w.fmap_mode, fmap_degree=w.fmap_degree,
         proj=inp["proj"])
     torch.autograd.backward([y], [L["dy"]])
