@@ -107,7 +107,7 @@ Smem smem_sizes(const AtlasMemShape* s, int C) {
   m.fmf = 4 * (size_t)(r4(kFmTile * dk) + kStageFloats);
   m.fmb = 4 * (size_t)(2 * r4(kFmTile * dk) + r4(kFmTile * dphi) + kStageFloats);
   const int tctx = tc::ctx_floats(C, e);
-  m.tc_f1 = 4 * (size_t)tc::kTileBytes + 4 * (size_t)(tctx + 2 * tc::kR);
+  m.tc_f1 = 3 * (size_t)tc::kTileBytes + 4 * (size_t)(tctx + 2 * tc::kR);
   m.tc_f3 = 6 * (size_t)tc::kTileBytes + 4 * (size_t)(tctx + 2 * tc::kR);
   m.buf_y = 4 * (size_t)(ctx + r4(C * (e > 1 ? e - 1 : 1)) + r4(C * dphi));
   m.tc_b1 = 3 * (size_t)tc::kTileBytes + 4 * (size_t)(tctx + 2 * tc::kR);
@@ -141,7 +141,7 @@ int ensure_attrs() {
                       (const void*)k_bwd_scan<4>, (const void*)tc::k_fwd_chunk_tc, (const void*)tc::k_fwd_out_tc,
                       (const void*)tc::k_fwd_buf_y, (const void*)tc::k_bwd_chunk_tc, (const void*)tc::k_bwd_state_tc,
                       (const void*)tc::k_bwd_adj_tc, (const void*)tc::k_bwd_intra_tc, (const void*)tc::k_bwd_buf_tc,
-                      (const void*)tc::k_bwd_gates_tc};
+                      (const void*)tc::k_bwd_gates_tc, (const void*)tc::k_bwd_finalize_tc};
   for (const void* k : ks) {
     cudaFuncAttributes fa;
     if (cudaFuncGetAttributes(&fa, k) != cudaSuccess) return ATLAS_ERR_LAUNCH;
@@ -234,12 +234,12 @@ Params make_params(const AtlasMemShape* s, const Layout& L, const AtlasMemFwd* f
 enum KernelId {
   KID_FMAP_FWD, KID_FWD_CHUNK, KID_FWD_SCAN, KID_FWD_OUT, KID_BUF_OUT, KID_BWD_CHUNK, KID_BWD_SCAN,
   KID_BWD_GRADS, KID_BWD_BUFOUT, KID_BWD_FINAL, KID_BWD_DSREF, KID_FMAP_BWD, KID_FWD_CHUNK_TC, KID_FWD_OUT_TC, KID_FWD_BUF_Y,
-  KID_BWD_CHUNK_TC, KID_BWD_STATE_TC, KID_BWD_ADJ_TC, KID_BWD_INTRA_TC, KID_BWD_BUF_TC, KID_BWD_GATES_TC, KID_COUNT
+  KID_BWD_CHUNK_TC, KID_BWD_STATE_TC, KID_BWD_ADJ_TC, KID_BWD_INTRA_TC, KID_BWD_BUF_TC, KID_BWD_GATES_TC, KID_BWD_FINAL_TC, KID_COUNT
 };
 const char* const kKernelNames[KID_COUNT] = {
   "k_fmap_tensor_fwd", "k_fwd_chunk", "k_fwd_scan", "k_fwd_out", "k_buf_out", "k_bwd_chunk", "k_bwd_scan",
   "k_bwd_grads", "k_bwd_bufout", "k_bwd_finalize", "k_bwd_dsref", "k_fmap_tensor_bwd", "k_fwd_chunk_tc", "k_fwd_out_tc", "k_fwd_buf_y",
-  "k_bwd_chunk_tc", "k_bwd_state_tc", "k_bwd_adj_tc", "k_bwd_intra_tc", "k_bwd_buf_tc", "k_bwd_gates_tc"};
+  "k_bwd_chunk_tc", "k_bwd_state_tc", "k_bwd_adj_tc", "k_bwd_intra_tc", "k_bwd_buf_tc", "k_bwd_gates_tc", "k_bwd_finalize_tc"};
 
 constexpr int kMaxTimed = 8192;
 struct Prof {
@@ -371,6 +371,10 @@ int run_bwd_finish(const AtlasMemShape* s, const Params& P, cudaStream_t st) {
   if (P.e > 1 && P.dbuf_out) {
     LAUNCH(KID_BWD_BUFOUT, k_bwd_bufout, dim3(P.e - 1, P.N), m.bufout, st, P);
   }
+  if (tc_groups(s) & 8)
+    LAUNCH_T(KID_BWD_FINAL_TC, tc::k_bwd_finalize_tc, dim3((P.T + tc::kR - 1) / tc::kR, P.N), tc::kT,
+             2 * (size_t)tc::kTileBytes, st, P);
+  else
   LAUNCH(KID_BWD_FINAL, k_bwd_finalize, dim3((P.T + kFinTile - 1) / kFinTile, P.N), m.fin, st, P);
   if (P.dSref) {
     const int tiles = ((P.dv + 63) / 64) * ((P.dphi + 63) / 64);

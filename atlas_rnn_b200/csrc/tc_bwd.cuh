@@ -87,7 +87,7 @@ __global__ void __launch_bounds__(kT) k_bwd_chunk_tc(Params P) {
   float* eZ0 = sa.take(kR);
   const int L = cx.L, tid = threadIdx.x, row = row_of(), wg = wg_of();
   Sync sy{&mbar, &tbase, 0, nullptr};
-  const uint32_t tm = tc_setup(sy);
+  const uint32_t tm = tc_setup(sy, 256);
   fill_rows_psi(P, cx, tPsi);
   __syncthreads();
   if (wg == 0) {
@@ -135,7 +135,7 @@ __global__ void __launch_bounds__(kT) k_bwd_chunk_tc(Params P) {
       st16f(dst + D2 + c16 * 16, b);
     }
   }
-  tc_teardown(tm);
+  tc_teardown(tm, 256);
 }
 
 // ===========================================================================
@@ -352,7 +352,7 @@ __global__ void __launch_bounds__(kT) k_bwd_adj_tc(Params P) {
 __global__ void __launch_bounds__(kT) k_bwd_intra_tc(Params P) {
   extern __shared__ __align__(1024) unsigned char sm[];
   unsigned char* tPhi = sm;
-  unsigned char* tDl = sm + kTileBytes;   // delta, later M3
+  unsigned char* tDl = sm + kTileBytes;   // delta, later M2
   unsigned char* tPsi = sm + 2 * kTileBytes;
   unsigned char* tY = sm + 3 * kTileBytes;
   unsigned char* tM1 = sm + 4 * kTileBytes;
@@ -371,51 +371,40 @@ __global__ void __launch_bounds__(kT) k_bwd_intra_tc(Params P) {
   fill_rows_psi(P, cx, tPsi);
   fill_rows_dy(P, cx, tY, [](int) { return 1.f; });
   __syncthreads();
-  {  // row q of M1 staging: wE_j[q] for the keys j of this warpgroup's column half
-    const int q = row, j0 = wg * (kR / 2);
-    float wl[kR / 2];
-#pragma unroll
-    for (int j = 0; j < kR / 2; ++j) wl[j] = 0.f;
-    if (q < L) {
-      float es = 0.f, ez = 0.f;  // eS_{L}, eZ_{L}
-      for (int i = L - 1; i >= 0; --i) {
-        // ez holds eZ_{i+1}[q]; key j gets it from token i when i <= j <= i + e - 1
-        for (int jj = 0; jj < e; ++jj) {
-          const int j = i + jj;
-          if (j < K && j >= j0 && j < j0 + kR / 2) wl[j - j0] += wgt(P, cx, i, j) * ez;
-        }
-        const float eta = i >= 1 ? cx.et[i - 1] : 0.f;
-        es = cx.al[i] * es + (q == i ? 1.f : 0.f);
-        ez = cx.be[i] * ez - eta * es;
-      }
-    }
-#pragma unroll
-    for (int cb = 0; cb < kR / 16; ++cb) {
-      float v[8];
-#pragma unroll
-      for (int k = 0; k < 8; ++k) v[k] = wl[cb * 8 + k];
-      store_unit(tM1, q, wg * (kR / 16) + cb, kR, v);
-    }
+  // staging while the first MMAs run: tM2[i][q] <- eZ_{i+1}[q] (warpgroup 0),
+  // tM1[i][j] <- cS of key j before token i (warpgroup 1)
+  if (wg == 0) {
+    const int q = row;
+    adj_column(cx, q, [&](int i, float, float ez) { st_bf(tM2, i, q, ez); });
+    for (int i = L; i < kR; ++i) st_bf(tM2, i, q, 0.f);
+  } else {
+    const int j = row;
+    fwd_column(P, cx, j, [&](int i, float cs, float, float) { st_bf(tM1, i, j, cs); });
+    for (int i = L; i < kR; ++i) st_bf(tM1, i, j, 0.f);
   }
   smem_to_tc();
   if (tid == 0) {
     mma_chain(tm, op(tY, kD, 0), op(tDl, kD, 0), 8, kR, false);       // A1[q][j]
     mma_chain(tm + 128, op(tPsi, kD, 0), op(tPhi, kD, 0), 8, kR, false);  // A2[q][j]
   }
-  mma_wait(sy);
-  if (wg == 0) {  // column j of tDl <- cS before token i (delta is no longer needed)
-    const int j = row;
-    float cs = 0.f, cz = 0.f;
-    for (int i = 0; i < kR; ++i) {
-      const bool live = i < L && j < K;
-      *reinterpret_cast<__nv_bfloat16*>(tDl + umma::elem_off(i, j, kR)) = __float2bfloat16_rn(live ? cs : 0.f);
-      if (live) {
-        cz = cx.be[i] * cz + wgt(P, cx, i, j);
-        cs = cx.al[i] * cs - cx.et[i] * cz;
+  // window-summed adjoint coefficients of row q for this warpgroup's keys:
+  //   wE_j[q] = sum_{i <= j <= i+e-1} W(i, j) eZ_{i+1}[q]
+  float wE[kR / 2];
+  {
+    const int q = row, j0 = wg * (kR / 2);
+#pragma unroll 4
+    for (int jj = 0; jj < kR / 2; ++jj) {
+      const int j = j0 + jj;
+      float acc = 0.f;
+      for (int i = max(0, j - e + 1); i <= min(L - 1, j); ++i) {
+        const float ez = __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(tM2 + umma::elem_off(i, q, kR)));
+        acc += wgt(P, cx, i, j) * ez;
       }
+      wE[jj] = q < L ? acc : 0.f;
     }
   }
-  __syncthreads();
+  mma_wait(sy);
+  __syncthreads();  // every staging column of tM2 has been read
   {
     const int q = row;
     unsigned char* gdst = reinterpret_cast<unsigned char*>(P.gt) + cid * kTileBytes;
@@ -429,29 +418,28 @@ __global__ void __launch_bounds__(kT) k_bwd_intra_tc(Params P) {
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const int cb = 2 * c16 + h;
-        float g[8], c3[8], w1[8], m2[8];
-        load_unit(tDl, q, cb, kR, c3);
-        load_unit(tM1, q, cb, kR, w1);
+        float g[8], c3[8], m1[8], m2[8];
+        load_unit(tM1, q, cb, kR, c3);
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
-          const float x1 = a1[8 * h + k], x2 = a2[8 * h + k];
+          const float x1 = a1[8 * h + k], x2 = a2[8 * h + k], w = wE[8 * (2 * h4 + h) + k];
           g[k] = x1 * x2;
           c3[k] *= x1;
-          m2[k] = w1[k] * x1;
-          w1[k] *= x2;
+          m2[k] = w * x1;
+          m1[k] = w * x2;
         }
         store_unit(gdst, q, cb, kR, g);
-        store_unit(tDl, q, cb, kR, c3);
-        store_unit(tM1, q, cb, kR, w1);
-        store_unit(tM2, q, cb, kR, m2);
+        store_unit(tM1, q, cb, kR, c3);   // M3 = cS o A1
+        store_unit(tM2, q, cb, kR, m1);   // M1 = wE o A2^T (MN-major)
+        store_unit(tDl, q, cb, kR, m2);   // M2 = wE o A1^T (MN-major)
       }
     }
   }
   smem_to_tc();
   if (tid == 0) {
-    mma_chain(tm + 256, op(tM1, kR, 1), op(tY, kD, 1), 8, kD, false);   // I3 [j][nn]
-    mma_chain(tm + 384, op(tM2, kR, 1), op(tPsi, kD, 1), 8, kD, false); // I4 [j][m]
-    mma_chain(tm, op(tDl, kR, 0), op(tPhi, kD, 1), 8, kD, false);       // I5 [i][m]
+    mma_chain(tm + 256, op(tM2, kR, 1), op(tY, kD, 1), 8, kD, false);   // I3 [j][nn]
+    mma_chain(tm + 384, op(tDl, kR, 1), op(tPsi, kD, 1), 8, kD, false); // I4 [j][m]
+    mma_chain(tm, op(tM1, kR, 0), op(tPhi, kD, 1), 8, kD, false);       // I5 [i][m]
   }
   mma_wait(sy);
   {
@@ -533,32 +521,20 @@ __global__ void __launch_bounds__(kT) k_bwd_gates_tc(Params P) {
   __syncthreads();
   if (wg == 0) {
     const int j = row;  // forward coefficients of key j (column j of tCS, tCZp, tCZn)
-    float cs = 0.f, cz = 0.f;
-    for (int i = 0; i < kR; ++i) {
-      const bool live = i < L && j < K;
-      const float czn = live ? cx.be[i] * cz + wgt(P, cx, i, j) : 0.f;
-      *reinterpret_cast<__nv_bfloat16*>(tCS + umma::elem_off(i, j, kR)) = __float2bfloat16_rn(live ? cs : 0.f);
-      *reinterpret_cast<__nv_bfloat16*>(tCZp + umma::elem_off(i, j, kR)) = __float2bfloat16_rn(live ? cz : 0.f);
-      *reinterpret_cast<__nv_bfloat16*>(tCZn + umma::elem_off(i, j, kR)) = __float2bfloat16_rn(czn);
-      if (live) {
-        cz = czn;
-        cs = cx.al[i] * cs - cx.et[i] * cz;
-      }
-    }
+    fwd_column(P, cx, j, [&](int i, float cs, float cz, float czn) {
+      st_bf(tCS, i, j, cs);
+      st_bf(tCZp, i, j, cz);
+      st_bf(tCZn, i, j, czn);
+    });
+    for (int i = L; i < kR; ++i) { st_bf(tCS, i, j, 0.f); st_bf(tCZp, i, j, 0.f); st_bf(tCZn, i, j, 0.f); }
     if (row == 0) fwd_scalars(cx, sS, sZ, zZ);
   } else {
     const int q = row;  // adjoint coefficients of token q (column q of tES, tEZ): rows i <- eS_{i+1}, eZ_{i+1}
-    float es = 0.f, ez = 0.f;
-    for (int i = kR - 1; i >= 0; --i) {
-      const bool live = i < L && q < L;
-      *reinterpret_cast<__nv_bfloat16*>(tES + umma::elem_off(i, q, kR)) = __float2bfloat16_rn(live ? es : 0.f);
-      *reinterpret_cast<__nv_bfloat16*>(tEZ + umma::elem_off(i, q, kR)) = __float2bfloat16_rn(live ? ez : 0.f);
-      if (live) {
-        const float eta = i >= 1 ? cx.et[i - 1] : 0.f;
-        es = cx.al[i] * es + (q == i ? 1.f : 0.f);
-        ez = cx.be[i] * ez - eta * es;
-      }
-    }
+    adj_column(cx, q, [&](int i, float es, float ez) {
+      st_bf(tES, i, q, es);
+      st_bf(tEZ, i, q, ez);
+    });
+    for (int i = L; i < kR; ++i) { st_bf(tES, i, q, 0.f); st_bf(tEZ, i, q, 0.f); }
     if (row == 0) adj_scalars(cx, hS, hZS, hZZ);
   }
   smem_to_tc();
@@ -757,6 +733,121 @@ __global__ void __launch_bounds__(kThreads) k_bwd_buf_tc(Params P) {
       }
     }
   }
+}
+
+// ===========================================================================
+// per 128-token tile: fold in the halo partials of d delta / d phi / du, then
+//   dv = -d delta,  d phi = d phi_window + d delta S_ref (tensor cores),
+//   dk = d phi * fmap'(k), dq = d psi * fmap'(q)
+// (tensor feature map: d phi is left in the scratch for its own backward).
+// ===========================================================================
+__global__ void __launch_bounds__(kT) k_bwd_finalize_tc(Params P) {
+  extern __shared__ __align__(1024) unsigned char sm[];
+  unsigned char* tDD = sm;               // d delta rows (bf16)
+  unsigned char* tSR = sm + kTileBytes;  // S_ref
+  __shared__ uint64_t mbar;
+  __shared__ uint32_t tbase;
+  const int n = blockIdx.y, p0 = blockIdx.x * kR, e = P.e, tid = threadIdx.x, row = row_of(), wg = wg_of();
+  const int TT = min(kR, P.T - p0);
+  Sync sy{&mbar, &tbase, 0, nullptr};
+  const uint32_t tm = tc_setup(sy, 128);
+  const int e1 = e > 1 ? e - 1 : 1;
+  // halo slot of token p in the next chunk (keys of chunk c+1 start at t0(c+1)-(e-1))
+  auto halo = [&](int p) -> int64_t {
+    const int c = p / P.C;
+    if (e <= 1 || c + 1 >= P.nch) return -1;
+    const int hs = (c + 1) * P.C - (e - 1);
+    return p >= hs ? ((int64_t)n * P.nch + c + 1) * e1 + (p - hs) : -1;
+  };
+  fill_tile(tDD, kD, [&](int r, int c0, float(&v)[8]) {
+    if (r >= TT) { zero8(v); return; }
+    const int p = p0 + r;
+    const int64_t gi = ((int64_t)n * P.T + p) * P.dv + c0;
+    ld8f(P.ddel + gi, v);
+    const int64_t h = halo(p);
+    if (h >= 0) {
+      float a[8];
+      ld8f(P.hdd + h * P.dv + c0, a);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) v[k] += a[k];
+    }
+    // final d delta back (for dS_ref) and dv = -d delta  (delta = pred - v, rnn_memory.py:660)
+    float4* dst = reinterpret_cast<float4*>(P.ddel + gi);
+    dst[0] = make_float4(v[0], v[1], v[2], v[3]);
+    dst[1] = make_float4(v[4], v[5], v[6], v[7]);
+    if (P.dv_) {
+      __align__(16) __nv_bfloat162 hb[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) hb[k] = __floats2bfloat162_rn(-v[2 * k], -v[2 * k + 1]);
+      *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(P.dv_) + gi) = *reinterpret_cast<uint4*>(hb);
+    }
+  });
+  fill_dense(tSR, P.Sref + (int64_t)n * kD * kD);
+  smem_to_tc();
+  if (tid == 0) mma_chain(tm, op(tDD, kD, 0), op(tSR, kD, 1), 8, kD, false);  // d delta S_ref
+  // while the MMA runs: dq, and du in token-gate mode
+  if (P.fmode != ATLAS_FMAP_TENSOR && P.dq_)
+    for (int x = tid; x < TT * (P.dphi / 8); x += kT) {
+      const int r = x / (P.dphi / 8), c0 = (x % (P.dphi / 8)) * 8;
+      const int64_t gi = ((int64_t)n * P.T + p0 + r) * P.dphi + c0;
+      float g[8], q[8];
+      ld8f(P.dpsi + gi, g);
+      ld8io(P.q, gi, P.bf, q);
+      __align__(16) __nv_bfloat162 hb[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        hb[k] = __floats2bfloat162_rn(g[2 * k] * fmap_elem_grad(q[2 * k], P.fmode, P.fdeg),
+                                      g[2 * k + 1] * fmap_elem_grad(q[2 * k + 1], P.fmode, P.fdeg));
+      *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(P.dq_) + gi) = *reinterpret_cast<uint4*>(hb);
+    }
+  if (P.gmode == ATLAS_GATE_TOKEN && P.dgate)
+    for (int r = tid; r < TT; r += kT) {
+      const int p = p0 + r;
+      float d = P.du[(int64_t)n * P.T + p];
+      const int64_t h = halo(p);
+      if (h >= 0) d += P.hdu[h];
+      stio(P.dgate, (int64_t)n * P.T + p, d, P.bf);
+    }
+  mma_wait(sy);
+  {
+    const int r = row, p = p0 + r;
+    const int64_t h = r < TT ? halo(p) : -1;
+#pragma unroll
+    for (int h4 = 0; h4 < 4; ++h4) {
+      const int c16 = wg * 4 + h4;
+      float a[16];
+      umma::tmem_ld16(lane_addr(tm, c16 * 16), a);
+      umma::tmem_ld_wait();
+      if (r < TT) {
+        const int64_t gi = ((int64_t)n * P.T + p) * P.dphi + c16 * 16;
+        float w0[8], w1[8];
+        ld8f(P.dphiR + gi, w0);
+        ld8f(P.dphiR + gi + 8, w1);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) { a[k] += w0[k]; a[8 + k] += w1[k]; }
+        if (h >= 0) {
+          ld8f(P.hdp + h * P.dphi + c16 * 16, w0);
+          ld8f(P.hdp + h * P.dphi + c16 * 16 + 8, w1);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) { a[k] += w0[k]; a[8 + k] += w1[k]; }
+        }
+        if (P.fmode == ATLAS_FMAP_TENSOR) {
+          st16f(P.dphiR + gi, a);
+        } else if (P.dk_) {
+          float k0[8], k1[8];
+          ld8io(P.k, gi, P.bf, k0);
+          ld8io(P.k, gi + 8, P.bf, k1);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            a[k] *= fmap_elem_grad(k0[k], P.fmode, P.fdeg);
+            a[8 + k] *= fmap_elem_grad(k1[k], P.fmode, P.fdeg);
+          }
+          st16bf(reinterpret_cast<__nv_bfloat16*>(P.dk_) + gi, a);
+        }
+      }
+    }
+  }
+  tc_teardown(tm, 128);
 }
 
 }  // namespace tc

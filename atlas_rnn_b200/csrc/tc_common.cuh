@@ -48,10 +48,11 @@ struct Sync {
   int* status;
 };
 
-// Allocate 512 TMEM columns and init the barrier (all threads call).
-__device__ __forceinline__ uint32_t tc_setup(Sync& s) {
+// Allocate `ncols` TMEM columns (kernels using at most 256 can run two CTAs
+// per SM) and init the barrier (all threads call).
+__device__ __forceinline__ uint32_t tc_setup(Sync& s, uint32_t ncols = 512) {
   if (threadIdx.x < 32) {
-    umma::tmem_alloc(s.tbase, 512);
+    umma::tmem_alloc(s.tbase, ncols);
     umma::tmem_relinquish();
   }
   if (threadIdx.x == 0) umma::mbar_init(s.mbar, 1);
@@ -80,10 +81,10 @@ __device__ __forceinline__ void mma_wait(Sync& s) {
 }
 
 // Release TMEM (all threads call; after the last TMEM access).
-__device__ __forceinline__ void tc_teardown(uint32_t tm) {
+__device__ __forceinline__ void tc_teardown(uint32_t tm, uint32_t ncols = 512) {
   umma::fence_before();
   __syncthreads();
-  if (threadIdx.x < 32) umma::tmem_dealloc(tm, 512);
+  if (threadIdx.x < 32) umma::tmem_dealloc(tm, ncols);
 }
 
 // TMEM address of row (this thread's lane) and column `col`.

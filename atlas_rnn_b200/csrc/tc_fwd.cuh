@@ -13,6 +13,57 @@ __host__ __device__ __forceinline__ int ctx_floats(int C, int e) {
   return 3 * r4(C) + r4(C + e) + r4(C * e);
 }
 
+// Forward coefficients of key j token by token (the recurrence of fwd_coefs),
+// with the gates of 8 tokens loaded ahead of the dependent arithmetic.
+// emit(i, cS before token i, cZ before token i, cZ after token i), i = 0..L-1.
+template <class F>
+__device__ __forceinline__ void fwd_column(const Params& P, const Ctx& cx, int j, F emit) {
+  float cs = 0.f, cz = 0.f;
+  for (int i0 = 0; i0 < cx.L; i0 += 8) {
+    float al[8], et[8], be[8], w[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int i = min(i0 + k, cx.L - 1);
+      al[k] = cx.al[i]; et[k] = cx.et[i]; be[k] = cx.be[i];
+      w[k] = wgt(P, cx, i, j);
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      if (i0 + k < cx.L) {
+        const float czn = be[k] * cz + w[k];
+        emit(i0 + k, cs, cz, czn);
+        cz = czn;
+        cs = al[k] * cs - et[k] * cz;
+      }
+  }
+}
+// Adjoint coefficients of token q (the recurrence of adj_coefs), 8 tokens per
+// gate batch. emit(i, eS_{i+1}[q], eZ_{i+1}[q]) for i = L-1 down to 0.
+template <class F>
+__device__ __forceinline__ void adj_column(const Ctx& cx, int q, F emit) {
+  float es = 0.f, ez = 0.f;
+  for (int i0 = cx.L - 1; i0 >= 0; i0 -= 8) {
+    float al[8], be[8], etm[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int i = max(i0 - k, 0);
+      al[k] = cx.al[i]; be[k] = cx.be[i];
+      etm[k] = i >= 1 ? cx.et[i - 1] : 0.f;
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      if (i0 - k >= 0) {
+        const int i = i0 - k;
+        emit(i, es, ez);
+        es = al[k] * es + (q == i ? 1.f : 0.f);
+        ez = be[k] * ez - etm[k] * es;
+      }
+  }
+}
+__device__ __forceinline__ void st_bf(unsigned char* tile, int r, int c, float v) {
+  *reinterpret_cast<__nv_bfloat16*>(tile + umma::elem_off(r, c, kR)) = __float2bfloat16_rn(v);
+}
+
 // Key rows of phi into a tile (zero for p < 0 and rows >= K).
 __device__ __forceinline__ void fill_keys_phi(const Params& P, const Ctx& cx, unsigned char* tile) {
   fill_tile(tile, kD, [&](int r, int c0, float(&v)[8]) {
@@ -41,10 +92,10 @@ __device__ __forceinline__ void fill_dense(unsigned char* tile, const float* M) 
 __global__ void __launch_bounds__(kT) k_fwd_chunk_tc(Params P) {
   extern __shared__ __align__(1024) unsigned char sm[];
   unsigned char* tPhi = sm;
-  unsigned char* tSref = sm + kTileBytes;
+  unsigned char* tSref = sm + kTileBytes;  // S_ref, later diag(cZ_end) delta
   unsigned char* tDS = sm + 2 * kTileBytes;
-  unsigned char* tDZ = sm + 3 * kTileBytes;
-  SmemAlloc sa{reinterpret_cast<float*>(sm + 4 * kTileBytes), 0};
+  unsigned char* tDZ = tSref;
+  SmemAlloc sa{reinterpret_cast<float*>(sm + 3 * kTileBytes), 0};
   __shared__ uint64_t mbar;
   __shared__ uint32_t tbase;
   Ctx cx;
@@ -53,7 +104,7 @@ __global__ void __launch_bounds__(kT) k_fwd_chunk_tc(Params P) {
   float* cZe = sa.take(kR);
   const int n = cx.n, c = cx.c, K = cx.K, L = cx.L, tid = threadIdx.x, row = row_of(), wg = wg_of();
   Sync sy{&mbar, &tbase, 0, nullptr};
-  const uint32_t tm = tc_setup(sy);
+  const uint32_t tm = tc_setup(sy, 256);
   fill_keys_phi(P, cx, tPhi);
   fill_dense(tSref, P.Sref + (int64_t)n * kD * kD);
   __syncthreads();  // gates visible to the coefficient threads
@@ -125,7 +176,7 @@ __global__ void __launch_bounds__(kT) k_fwd_chunk_tc(Params P) {
   smem_to_tc();
   if (tid == 0) {
     mma_chain(tm + 128, op(tDS, kD, 1), op(tPhi, kD, 1), 8, kD, false);
-    mma_chain(tm + 256, op(tDZ, kD, 1), op(tPhi, kD, 1), 8, kD, false);
+    mma_chain(tm, op(tDZ, kD, 1), op(tPhi, kD, 1), 8, kD, false);  // over delta, already read
   }
   mma_wait(sy);
   {  // increments: row = state row nn
@@ -138,7 +189,7 @@ __global__ void __launch_bounds__(kT) k_fwd_chunk_tc(Params P) {
       const int c16 = wg * 4 + h;
       float a[16], b[16];
       umma::tmem_ld16(lane_addr(tm, 128 + c16 * 16), a);
-      umma::tmem_ld16(lane_addr(tm, 256 + c16 * 16), b);
+      umma::tmem_ld16(lane_addr(tm, c16 * 16), b);
       umma::tmem_ld_wait();
       for (int jb = 0; jb < nb; ++jb) {  // carried buffer entries of chunk 0 (dense)
         const float* bj = bufn + (int64_t)jb * D2 + (int64_t)row * kD + c16 * 16;
@@ -149,7 +200,7 @@ __global__ void __launch_bounds__(kT) k_fwd_chunk_tc(Params P) {
       st16f(dst + D2 + c16 * 16, b);
     }
   }
-  tc_teardown(tm);
+  tc_teardown(tm, 256);
 }
 
 // ===========================================================================
@@ -188,16 +239,9 @@ __global__ void __launch_bounds__(kT) k_fwd_out_tc(Params P) {
   fill_dense(tZin, Sin + D2);
   __syncthreads();
   if (wg == 0) {  // column j = row of tMs: cS of key j before each token i
-    float cs = 0.f, cz = 0.f;
     const int j = row;
-    for (int i = 0; i < kR; ++i) {
-      const bool live = i < L && j < K;
-      *reinterpret_cast<__nv_bfloat16*>(tMs + umma::elem_off(i, j, kR)) = __float2bfloat16_rn(live ? cs : 0.f);
-      if (live) {
-        cz = cx.be[i] * cz + wgt(P, cx, i, j);
-        cs = cx.al[i] * cs - cx.et[i] * cz;
-      }
-    }
+    fwd_column(P, cx, j, [&](int i, float cs, float, float) { st_bf(tMs, i, j, cs); });
+    for (int i = L; i < kR; ++i) st_bf(tMs, i, j, 0.f);
   } else if (row == 0) {
     float s = 1.f, sz = 0.f, z = 1.f;
     for (int i = 0; i < L; ++i) {
