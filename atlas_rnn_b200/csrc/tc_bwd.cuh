@@ -101,7 +101,7 @@ __global__ void __launch_bounds__(kT) k_bwd_chunk_tc(Params P) {
       }
     eS0[q] = es;
     eZ0[q] = ez;
-  } else if (row == 0) {
+  } else if (wg == 1 && row == 0) {
     float hs = 1.f, hzs = -cx.et[L - 1], hzz = 1.f;
     for (int r = L - 1; r >= 0; --r) {
       const float eta = r >= 1 ? cx.et[r - 1] : 0.f;
@@ -125,8 +125,8 @@ __global__ void __launch_bounds__(kT) k_bwd_chunk_tc(Params P) {
     const int64_t D2 = (int64_t)kD * kD;
     float* dst = P.adj + chunk_id(P, cx) * 2 * D2 + (int64_t)row * kD;
 #pragma unroll
-    for (int h = 0; h < 4; ++h) {
-      const int c16 = wg * 4 + h;
+    for (int h = 0; h < kCPW; ++h) {
+      const int c16 = wg * kCPW + h;
       float a[16], b[16];
       umma::tmem_ld16(lane_addr(tm, c16 * 16), a);
       umma::tmem_ld16(lane_addr(tm, 128 + c16 * 16), b);
@@ -156,7 +156,7 @@ __global__ void __launch_bounds__(kT) k_bwd_state_tc(Params P) {
   float* sS = sa.take(kR + 1);
   float* sZ = sa.take(kR + 1);
   float* zZ = sa.take(kR + 1);
-  float* part = sa.take(4 * kR);  // [warpgroup][2][row] partial dot products
+  float* part = sa.take(2 * kWG * kR);  // [warpgroup][2][row] partial dot products
   const int n = cx.n, L = cx.L, tid = threadIdx.x, row = row_of(), wg = wg_of();
   Sync sy{&mbar, &tbase, 0, nullptr};
   const uint32_t tm = tc_setup(sy);
@@ -182,8 +182,8 @@ __global__ void __launch_bounds__(kT) k_bwd_state_tc(Params P) {
     const float ss = q < L ? sS[q] : 0.f, sz = q < L ? sZ[q] : 0.f;
     const int64_t grow = (int64_t)n * P.T + cx.t0 + q;
 #pragma unroll
-    for (int h = 0; h < 4; ++h) {
-      const int c16 = wg * 4 + h;
+    for (int h = 0; h < kCPW; ++h) {
+      const int c16 = wg * kCPW + h;
       float gs[16], gz[16], hs[16], hz[16], y0[8], y1[8];
       umma::tmem_ld16(lane_addr(tm, c16 * 16), gs);
       umma::tmem_ld16(lane_addr(tm, 128 + c16 * 16), gz);
@@ -211,8 +211,10 @@ __global__ void __launch_bounds__(kT) k_bwd_state_tc(Params P) {
   if (wg == 0) {
     const int q = row;
     float* xq = P.xq + (chunk_id(P, cx) * kR + q) * 2;
-    xq[0] = q < L ? part[q] + part[2 * kR + q] : 0.f;
-    xq[1] = q < L ? part[kR + q] + part[3 * kR + q] : 0.f;
+    float a = 0.f, b = 0.f;
+    for (int g = 0; g < kWG; ++g) { a += part[(2 * g) * kR + q]; b += part[(2 * g + 1) * kR + q]; }
+    xq[0] = q < L ? a : 0.f;
+    xq[1] = q < L ? b : 0.f;
   }
   tc_teardown(tm);
 }
@@ -249,8 +251,8 @@ __global__ void __launch_bounds__(kT) k_bwd_adj_tc(Params P) {
   float* hS = sa.take(kR + 1);
   float* hZS = sa.take(kR + 1);
   float* hZZ = sa.take(kR + 1);
-  float* red = sa.take(32);
-  float* part = sa.take(4 * kR);
+  float* red = sa.take(4 * (kT / 32));
+  float* part = sa.take(2 * kWG * kR);
   const int n = cx.n, K = cx.K, tid = threadIdx.x, e = P.e, row = row_of(), wg = wg_of();
   Sync sy{&mbar, &tbase, 0, nullptr};
   const uint32_t tm = tc_setup(sy);
@@ -286,12 +288,12 @@ __global__ void __launch_bounds__(kT) k_bwd_adj_tc(Params P) {
     for (int k = 0; k < 4; ++k) {
       float t = v[k];
       for (int off = 16; off > 0; off >>= 1) t += __shfl_xor_sync(0xffffffffu, t, off);
-      if ((tid & 31) == 0) red[k * 8 + (tid >> 5)] = t;
+      if ((tid & 31) == 0) red[k * (kT / 32) + (tid >> 5)] = t;
     }
     __syncthreads();
     if (tid < 4) {
       float t = 0.f;
-      for (int w = 0; w < kT / 32; ++w) t += red[tid * 8 + w];
+      for (int w = 0; w < kT / 32; ++w) t += red[tid * (kT / 32) + w];
       P.xs[cid * 4 + tid] = t;
     }
   }
@@ -306,8 +308,8 @@ __global__ void __launch_bounds__(kT) k_bwd_adj_tc(Params P) {
     float* dd = own ? P.ddel + ((int64_t)n * P.T + p) * P.dv : P.hdd + (cid * e1 + (j < e - 1 ? j : 0)) * P.dv;
     float* dp = own ? P.dphiR + ((int64_t)n * P.T + p) * P.dphi : P.hdp + (cid * e1 + (j < e - 1 ? j : 0)) * P.dphi;
 #pragma unroll
-    for (int h = 0; h < 4; ++h) {
-      const int c16 = wg * 4 + h;
+    for (int h = 0; h < kCPW; ++h) {
+      const int c16 = wg * kCPW + h;
       float p1[16], p2[16], q1[16], q2[16];
       umma::tmem_ld16(lane_addr(tm, c16 * 16), p1);
       umma::tmem_ld16(lane_addr(tm, 128 + c16 * 16), p2);
@@ -335,8 +337,10 @@ __global__ void __launch_bounds__(kT) k_bwd_adj_tc(Params P) {
   __syncthreads();
   if (wg == 0) {
     float* xf = P.xf + (cid * kR + row) * 2;
-    xf[0] = part[row] + part[2 * kR + row];
-    xf[1] = part[kR + row] + part[3 * kR + row];
+    float a = 0.f, b = 0.f;
+    for (int g = 0; g < kWG; ++g) { a += part[(2 * g) * kR + row]; b += part[(2 * g + 1) * kR + row]; }
+    xf[0] = a;
+    xf[1] = b;
   }
   tc_teardown(tm);
 }
@@ -377,7 +381,7 @@ __global__ void __launch_bounds__(kT) k_bwd_intra_tc(Params P) {
     const int q = row;
     adj_column(cx, q, [&](int i, float, float ez) { st_bf(tM2, i, q, ez); });
     for (int i = L; i < kR; ++i) st_bf(tM2, i, q, 0.f);
-  } else {
+  } else if (wg == 1) {
     const int j = row;
     fwd_column(P, cx, j, [&](int i, float cs, float, float) { st_bf(tM1, i, j, cs); });
     for (int i = L; i < kR; ++i) st_bf(tM1, i, j, 0.f);
@@ -389,11 +393,11 @@ __global__ void __launch_bounds__(kT) k_bwd_intra_tc(Params P) {
   }
   // window-summed adjoint coefficients of row q for this warpgroup's keys:
   //   wE_j[q] = sum_{i <= j <= i+e-1} W(i, j) eZ_{i+1}[q]
-  float wE[kR / 2];
+  float wE[kR / kWG];
   {
-    const int q = row, j0 = wg * (kR / 2);
+    const int q = row, j0 = wg * (kR / kWG);
 #pragma unroll 4
-    for (int jj = 0; jj < kR / 2; ++jj) {
+    for (int jj = 0; jj < kR / kWG; ++jj) {
       const int j = j0 + jj;
       float acc = 0.f;
       for (int i = max(0, j - e + 1); i <= min(L - 1, j); ++i) {
@@ -409,8 +413,8 @@ __global__ void __launch_bounds__(kT) k_bwd_intra_tc(Params P) {
     const int q = row;
     unsigned char* gdst = reinterpret_cast<unsigned char*>(P.gt) + cid * kTileBytes;
 #pragma unroll
-    for (int h4 = 0; h4 < 4; ++h4) {
-      const int c16 = wg * 4 + h4;
+    for (int h4 = 0; h4 < kCPW; ++h4) {
+      const int c16 = wg * kCPW + h4;
       float a1[16], a2[16];
       umma::tmem_ld16(lane_addr(tm, c16 * 16), a1);
       umma::tmem_ld16(lane_addr(tm, 128 + c16 * 16), a2);
@@ -450,8 +454,8 @@ __global__ void __launch_bounds__(kT) k_bwd_intra_tc(Params P) {
     float* dp = own ? P.dphiR + ((int64_t)n * P.T + p) * P.dphi : P.hdp + (cid * e1 + (r < e - 1 ? r : 0)) * P.dphi;
     float* dq = P.dpsi + ((int64_t)n * P.T + cx.t0 + (r < L ? r : 0)) * P.dphi;
 #pragma unroll
-    for (int h = 0; h < 4; ++h) {
-      const int c16 = wg * 4 + h;
+    for (int h = 0; h < kCPW; ++h) {
+      const int c16 = wg * kCPW + h;
       float i3[16], i4[16], i5[16];
       umma::tmem_ld16(lane_addr(tm, 256 + c16 * 16), i3);
       umma::tmem_ld16(lane_addr(tm, 384 + c16 * 16), i4);
@@ -460,13 +464,14 @@ __global__ void __launch_bounds__(kT) k_bwd_intra_tc(Params P) {
       // fire-and-forget adds onto the values k_bwd_state_tc / k_bwd_adj_tc wrote
       if (own || halo)
 #pragma unroll
-        for (int k = 0; k < 16; ++k) {
-          atomicAdd(dd + c16 * 16 + k, i3[k]);
-          atomicAdd(dp + c16 * 16 + k, i4[k]);
+        for (int k = 0; k < 16; k += 4) {
+          atomicAdd(reinterpret_cast<float4*>(dd + c16 * 16 + k), make_float4(i3[k], i3[k + 1], i3[k + 2], i3[k + 3]));
+          atomicAdd(reinterpret_cast<float4*>(dp + c16 * 16 + k), make_float4(i4[k], i4[k + 1], i4[k + 2], i4[k + 3]));
         }
       if (r < L)
 #pragma unroll
-        for (int k = 0; k < 16; ++k) atomicAdd(dq + c16 * 16 + k, i5[k]);
+        for (int k = 0; k < 16; k += 4)
+          atomicAdd(reinterpret_cast<float4*>(dq + c16 * 16 + k), make_float4(i5[k], i5[k + 1], i5[k + 2], i5[k + 3]));
     }
   }
   tc_teardown(tm);
@@ -504,7 +509,8 @@ __global__ void __launch_bounds__(kT) k_bwd_gates_tc(Params P) {
   float* xf = sa.take(2 * kR);
   float* xs = sa.take(4);
   float* duj = sa.take(kR);
-  float* part = sa.take(kGateParts * kR);  // warpgroup 1's partial sums
+  float* part = sa.take(kGateParts * (kWG - 1) * kR);  // partial sums of warpgroups 1..
+
   const int n = cx.n, K = cx.K, L = cx.L, tid = threadIdx.x, e = P.e, row = row_of(), wg = wg_of();
   Sync sy{&mbar, &tbase, 0, nullptr};
   const uint32_t tm = tc_setup(sy);
@@ -513,8 +519,10 @@ __global__ void __launch_bounds__(kT) k_bwd_gates_tc(Params P) {
     const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const unsigned char*>(P.gt) + cid * kTileBytes);
     uint4* dst = reinterpret_cast<uint4*>(tG);
     for (int u = tid; u < kTileBytes / 16; u += kT) dst[u] = src[u];
-    xq[tid] = P.xq[cid * 2 * kR + tid];
-    xf[tid] = P.xf[cid * 2 * kR + tid];
+    if (tid < 2 * kR) {
+      xq[tid] = P.xq[cid * 2 * kR + tid];
+      xf[tid] = P.xf[cid * 2 * kR + tid];
+    }
     if (tid < 4) xs[tid] = P.xs[cid * 4 + tid];
     if (tid < kR) duj[tid] = 0.f;
   }
@@ -528,7 +536,7 @@ __global__ void __launch_bounds__(kT) k_bwd_gates_tc(Params P) {
     });
     for (int i = L; i < kR; ++i) { st_bf(tCS, i, j, 0.f); st_bf(tCZp, i, j, 0.f); st_bf(tCZn, i, j, 0.f); }
     if (row == 0) fwd_scalars(cx, sS, sZ, zZ);
-  } else {
+  } else if (wg == 1) {
     const int q = row;  // adjoint coefficients of token q (column q of tES, tEZ): rows i <- eS_{i+1}, eZ_{i+1}
     adj_column(cx, q, [&](int i, float es, float ez) {
       st_bf(tES, i, q, es);
@@ -550,8 +558,8 @@ __global__ void __launch_bounds__(kT) k_bwd_gates_tc(Params P) {
 #pragma unroll
   for (int k = 0; k < kGateParts; ++k) acc[k] = 0.f;
 #pragma unroll
-  for (int h4 = 0; h4 < 4; ++h4) {
-    const int c16 = wg * 4 + h4;
+  for (int h4 = 0; h4 < kCPW; ++h4) {
+    const int c16 = wg * kCPW + h4;
     float A[16], E[16], B[16];
     umma::tmem_ld16(lane_addr(tm, c16 * 16), A);
     umma::tmem_ld16(lane_addr(tm, 128 + c16 * 16), E);
@@ -582,14 +590,14 @@ __global__ void __launch_bounds__(kT) k_bwd_gates_tc(Params P) {
       }
     }
   }
-  if (wg == 1)
+  if (wg >= 1)
 #pragma unroll
-    for (int k = 0; k < kGateParts; ++k) part[k * kR + i] = acc[k];
+    for (int k = 0; k < kGateParts; ++k) part[((wg - 1) * kGateParts + k) * kR + i] = acc[k];
   // window weights dW(i, j) = hZS_{i+1} X[F_S][R_j] + hZZ_{i+1} X[F_Z][R_j] + (E_Z+ G)[i][j]
   if (P.gmode != ATLAS_GATE_NONE) {
 #pragma unroll
-    for (int h4 = 0; h4 < 4; ++h4) {
-      const int c16 = wg * 4 + h4;
+    for (int h4 = 0; h4 < kCPW; ++h4) {
+      const int c16 = wg * kCPW + h4;
       float W[16];
       umma::tmem_ld16(lane_addr(tm, 384 + c16 * 16), W);
       umma::tmem_ld_wait();
@@ -608,8 +616,9 @@ __global__ void __launch_bounds__(kT) k_bwd_gates_tc(Params P) {
   }
   __syncthreads();
   if (wg == 0 && i < L) {
+    for (int g = 1; g < kWG; ++g)
 #pragma unroll
-    for (int k = 0; k < kGateParts; ++k) acc[k] += part[k * kR + i];
+      for (int k = 0; k < kGateParts; ++k) acc[k] += part[((g - 1) * kGateParts + k) * kR + i];
     const float da = hS[i + 1] * (xs[0] * sS[i] + xs[1] * sZ[i] + acc[0]) + (acc[4] * sS[i] + acc[5] * sZ[i] + acc[7]);
     const float de = -(hS[i + 1] * (xs[1] * zZ[i + 1] + acc[1]) + (acc[5] * zZ[i + 1] + acc[8]));
     const float db = hZS[i + 1] * (xs[1] * zZ[i] + acc[2]) + hZZ[i + 1] * (xs[3] * zZ[i] + acc[3]) +
@@ -813,8 +822,8 @@ __global__ void __launch_bounds__(kT) k_bwd_finalize_tc(Params P) {
     const int r = row, p = p0 + r;
     const int64_t h = r < TT ? halo(p) : -1;
 #pragma unroll
-    for (int h4 = 0; h4 < 4; ++h4) {
-      const int c16 = wg * 4 + h4;
+    for (int h4 = 0; h4 < kCPW; ++h4) {
+      const int c16 = wg * kCPW + h4;
       float a[16];
       umma::tmem_ld16(lane_addr(tm, c16 * 16), a);
       umma::tmem_ld_wait();

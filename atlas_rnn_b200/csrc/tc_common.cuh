@@ -1,9 +1,9 @@
 // Shared pieces of the tensor-core (tcgen05) chunk kernels.
 //
-// Every tensor-core chunk kernel runs 256 threads, two warpgroups. Warp w
+// Every tensor-core chunk kernel runs kWG warpgroups of 128 threads. Warp w
 // reaches TMEM lanes [32 (w % 4), 32 (w % 4) + 32), so thread t owns row
-// t % 128 of every 128-row accumulator, and the two warpgroups split its
-// columns (warpgroup g takes columns [64 g, 64 g + 64) of a 128-column one).
+// t % 128 of every 128-row accumulator, and the warpgroups split its columns
+// (warpgroup g takes the 16-column groups [g kCPW, (g + 1) kCPW)).
 // Operand tiles are 128 rows x D columns of bf16 in the core-matrix layout of
 // umma.cuh (rows past the valid range are zero). d_phi = d_v = D = 128.
 #pragma once
@@ -15,8 +15,10 @@
 namespace atlas {
 namespace tc {
 
-constexpr int kT = 256;        // threads per CTA
+constexpr int kWG = 4;         // warpgroups per CTA
+constexpr int kT = 128 * kWG;  // threads per CTA
 constexpr int kR = 128;        // rows of a tile / TMEM lanes
+constexpr int kCPW = 8 / kWG;  // 16-column groups of a 128-column accumulator per warpgroup
 constexpr int kD = 128;        // head size handled by the tensor-core path
 constexpr int kTileBytes = kR * kD * 2;
 

@@ -117,7 +117,7 @@ __global__ void __launch_bounds__(kT) k_fwd_chunk_tc(Params P) {
       }
     cSe[row] = cs;
     cZe[row] = cz;
-  } else if (row == 0) {  // chunk transform scalars
+  } else if (wg == 1 && row == 0) {  // chunk transform scalars
     float s = 1.f, sz = 0.f, z = 1.f;
     for (int i = 0; i < L; ++i) {
       z = cx.be[i] * z;
@@ -132,19 +132,19 @@ __global__ void __launch_bounds__(kT) k_fwd_chunk_tc(Params P) {
   const int j = row, p = cx.kp0 + j;
   const bool valid = j < K && p >= 0;
   // this thread's half of the key's v row (bf16), fetched while the MMA runs
-  uint4 vrow[kD / 16];
+  uint4 vrow[kD / (8 * kWG)];
   if (valid) {
     const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(P.v) +
-                                                      ((int64_t)n * P.T + p) * P.dv + wg * (kD / 2));
+                                                      ((int64_t)n * P.T + p) * P.dv + wg * (kD / kWG));
 #pragma unroll
-    for (int u = 0; u < kD / 16; ++u) vrow[u] = src[u];
+    for (int u = 0; u < kD / (8 * kWG); ++u) vrow[u] = src[u];
   }
   mma_wait(sy);
   {
     const float ws = cSe[j], wz = cZe[j];
 #pragma unroll
-    for (int h = 0; h < 4; ++h) {
-      const int c16 = wg * 4 + h;
+    for (int h = 0; h < kCPW; ++h) {
+      const int c16 = wg * kCPW + h;
       float a[16];
       umma::tmem_ld16(lane_addr(tm, c16 * 16), a);
       umma::tmem_ld_wait();
@@ -185,8 +185,8 @@ __global__ void __launch_bounds__(kT) k_fwd_chunk_tc(Params P) {
     const float* bufn = buf_of(P, n, c);
     const int nb = bufn ? P.e - 1 : 0;
 #pragma unroll
-    for (int h = 0; h < 4; ++h) {
-      const int c16 = wg * 4 + h;
+    for (int h = 0; h < kCPW; ++h) {
+      const int c16 = wg * kCPW + h;
       float a[16], b[16];
       umma::tmem_ld16(lane_addr(tm, 128 + c16 * 16), a);
       umma::tmem_ld16(lane_addr(tm, c16 * 16), b);
@@ -242,7 +242,7 @@ __global__ void __launch_bounds__(kT) k_fwd_out_tc(Params P) {
     const int j = row;
     fwd_column(P, cx, j, [&](int i, float cs, float, float) { st_bf(tMs, i, j, cs); });
     for (int i = L; i < kR; ++i) st_bf(tMs, i, j, 0.f);
-  } else if (row == 0) {
+  } else if (wg == 1 && row == 0) {
     float s = 1.f, sz = 0.f, z = 1.f;
     for (int i = 0; i < L; ++i) {
       sSv[i] = s;
@@ -260,8 +260,8 @@ __global__ void __launch_bounds__(kT) k_fwd_out_tc(Params P) {
   }
   mma_wait(sy);
 #pragma unroll
-  for (int h = 0; h < 4; ++h) {  // Ms = cS o A2 (row `row`, this warpgroup's columns)
-    const int c16 = wg * 4 + h;
+  for (int h = 0; h < kCPW; ++h) {  // Ms = cS o A2 (row `row`, this warpgroup's columns)
+    const int c16 = wg * kCPW + h;
     float a[16], m0[8], m1[8];
     umma::tmem_ld16(lane_addr(tm, c16 * 16), a);
     umma::tmem_ld_wait();
@@ -279,8 +279,8 @@ __global__ void __launch_bounds__(kT) k_fwd_out_tc(Params P) {
     const int i = row;
     const float ss = i < L ? sSv[i] : 0.f, sz = i < L ? sZv[i] : 0.f;
 #pragma unroll
-    for (int h = 0; h < 4; ++h) {
-      const int c16 = wg * 4 + h;
+    for (int h = 0; h < kCPW; ++h) {
+      const int c16 = wg * kCPW + h;
       float yi[16], ps[16], pz[16];
       umma::tmem_ld16(lane_addr(tm, 384 + c16 * 16), yi);
       umma::tmem_ld16(lane_addr(tm, 128 + c16 * 16), ps);
