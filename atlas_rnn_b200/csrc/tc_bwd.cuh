@@ -24,7 +24,8 @@ __device__ __forceinline__ int64_t chunk_id(const Params& P, const Ctx& cx) { re
 
 // Token rows of dy (zero for rows >= L), optionally scaled per row.
 template <class Scale>
-__device__ __forceinline__ void fill_rows_dy(const Params& P, const Ctx& cx, unsigned char* tile, Scale sc) {
+__device__ __forceinline__ void fill_rows_dy(const Params& P, const Ctx& cx, unsigned char* tile, Scale sc,
+                                             int first = 0, int count = kT) {
   fill_tile(tile, kD, [&](int r, int c0, float(&v)[8]) {
     if (r < cx.L) {
       ld8io(P.dy, ((int64_t)cx.n * P.T + cx.t0 + r) * P.dv + c0, P.bf, v);
@@ -34,14 +35,15 @@ __device__ __forceinline__ void fill_rows_dy(const Params& P, const Ctx& cx, uns
     } else {
       zero8(v);
     }
-  });
+  }, first, count);
 }
-__device__ __forceinline__ void fill_keys_delta(const Params& P, const Ctx& cx, unsigned char* tile) {
+__device__ __forceinline__ void fill_keys_delta(const Params& P, const Ctx& cx, unsigned char* tile, int first = 0,
+                                                int count = kT) {
   fill_tile(tile, kD, [&](int r, int c0, float(&v)[8]) {
     const int p = cx.kp0 + r;
     if (r < cx.K && p >= 0) ld8f(P.delta + ((int64_t)cx.n * P.T + p) * P.dv + c0, v);
     else zero8(v);
-  });
+  }, first, count);
 }
 
 // Scalars of the adjoint transform of the chunk (rows r = 0..L) computed by one thread.
@@ -162,12 +164,12 @@ __global__ void __launch_bounds__(kT) k_bwd_state_tc(Params P) {
   const uint32_t tm = tc_setup(sy);
   const int64_t D2 = (int64_t)kD * kD;
   const float* Sin = P.st + chunk_id(P, cx) * 2 * D2;
-  fill_rows_psi(P, cx, tPsi);
-  fill_rows_dy(P, cx, tY, [](int) { return 1.f; });
-  fill_dense(tSin, Sin);
-  fill_dense(tZin, Sin + D2);
   __syncthreads();
   if (tid == 0) fwd_scalars(cx, sS, sZ, zZ);
+  fill_rows_psi(P, cx, tPsi, 128, kT - 128);
+  fill_rows_dy(P, cx, tY, [](int) { return 1.f; }, 128, kT - 128);
+  fill_dense(tSin, Sin, 128, kT - 128);
+  fill_dense(tZin, Sin + D2, 128, kT - 128);
   smem_to_tc();
   if (tid == 0) {
     mma_chain(tm, op(tPsi, kD, 0), op(tSin, kD, 0), 8, kD, false);
@@ -260,12 +262,12 @@ __global__ void __launch_bounds__(kT) k_bwd_adj_tc(Params P) {
   const int64_t cid = chunk_id(P, cx);
   const float* FS = P.adj + cid * 2 * D2;
   const float* Sin = P.st + cid * 2 * D2;
-  fill_keys_phi(P, cx, tPhi);
-  fill_keys_delta(P, cx, tDl);
-  fill_dense(tFS, FS);
-  fill_dense(tFZ, FS + D2);
   __syncthreads();
   if (tid == 0) adj_scalars(cx, hS, hZS, hZZ);
+  fill_keys_phi(P, cx, tPhi, 128, kT - 128);
+  fill_keys_delta(P, cx, tDl, 128, kT - 128);
+  fill_dense(tFS, FS, 128, kT - 128);
+  fill_dense(tFZ, FS + D2, 128, kT - 128);
   smem_to_tc();
   if (tid == 0) {
     mma_chain(tm, op(tPhi, kD, 0), op(tFS, kD, 0), 8, kD, false);
@@ -515,18 +517,19 @@ __global__ void __launch_bounds__(kT) k_bwd_gates_tc(Params P) {
   Sync sy{&mbar, &tbase, 0, nullptr};
   const uint32_t tm = tc_setup(sy);
   const int64_t cid = chunk_id(P, cx);
-  {
+  __syncthreads();
+  if (wg >= 2) {
+    const int me = tid - kFillFirst;
     const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const unsigned char*>(P.gt) + cid * kTileBytes);
     uint4* dst = reinterpret_cast<uint4*>(tG);
-    for (int u = tid; u < kTileBytes / 16; u += kT) dst[u] = src[u];
-    if (tid < 2 * kR) {
-      xq[tid] = P.xq[cid * 2 * kR + tid];
-      xf[tid] = P.xf[cid * 2 * kR + tid];
+    for (int u = me; u < kTileBytes / 16; u += kFillCount) dst[u] = src[u];
+    if (me < 2 * kR) {
+      xq[me] = P.xq[cid * 2 * kR + me];
+      xf[me] = P.xf[cid * 2 * kR + me];
     }
-    if (tid < 4) xs[tid] = P.xs[cid * 4 + tid];
-    if (tid < kR) duj[tid] = 0.f;
+    if (me < 4) xs[me] = P.xs[cid * 4 + me];
+    if (me < kR) duj[me] = 0.f;
   }
-  __syncthreads();
   if (wg == 0) {
     const int j = row;  // forward coefficients of key j (column j of tCS, tCZp, tCZn)
     fwd_column(P, cx, j, [&](int i, float cs, float cz, float czn) {

@@ -113,25 +113,30 @@ __device__ __forceinline__ void load_unit(const unsigned char* tile, int r, int 
 }
 
 // Fill a 128 x C tile; src(r, c0, v) fills v[0..7] for columns c0..c0+7 of row r.
-// Each thread gathers 8 units before storing any, so 8 loads are in flight.
+// Threads [first, first + count) take part (the others return at once); each
+// gathers 8 units before storing any, so 8 loads are in flight per thread.
 template <class F>
-__device__ __forceinline__ void fill_tile(unsigned char* tile, int C, F src) {
+__device__ __forceinline__ void fill_tile(unsigned char* tile, int C, F src, int first = 0, int count = kT) {
   constexpr int kBatch = 8;
+  const int me = (int)threadIdx.x - first;
+  if (me < 0 || me >= count) return;
   const int cpr = C / 8, units = 128 * cpr;
-  for (int base = threadIdx.x; base < units; base += kT * kBatch) {
+  for (int base = me; base < units; base += count * kBatch) {
     float v[kBatch][8];
 #pragma unroll
     for (int k = 0; k < kBatch; ++k) {
-      const int u = base + k * kT;
+      const int u = base + k * count;
       if (u < units) src(u / cpr, (u % cpr) * 8, v[k]);
     }
 #pragma unroll
     for (int k = 0; k < kBatch; ++k) {
-      const int u = base + k * kT;
+      const int u = base + k * count;
       if (u < units) store_unit(tile, u / cpr, u % cpr, C, v[k]);
     }
   }
 }
+// Warpgroups 2.. load tiles while warpgroups 0 and 1 run coefficient recurrences.
+constexpr int kFillFirst = 256, kFillCount = kT - 256;
 
 __device__ __forceinline__ void zero8(float (&v)[8]) {
 #pragma unroll

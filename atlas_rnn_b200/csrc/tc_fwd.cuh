@@ -65,23 +65,25 @@ __device__ __forceinline__ void st_bf(unsigned char* tile, int r, int c, float v
 }
 
 // Key rows of phi into a tile (zero for p < 0 and rows >= K).
-__device__ __forceinline__ void fill_keys_phi(const Params& P, const Ctx& cx, unsigned char* tile) {
+__device__ __forceinline__ void fill_keys_phi(const Params& P, const Ctx& cx, unsigned char* tile, int first = 0,
+                                              int count = kT) {
   fill_tile(tile, kD, [&](int r, int c0, float(&v)[8]) {
     const int p = cx.kp0 + r;
     if (r < cx.K && p >= 0) phi8(P, cx.n, p, c0, false, v);
     else zero8(v);
-  });
+  }, first, count);
 }
 // Token rows of psi (zero for rows >= L).
-__device__ __forceinline__ void fill_rows_psi(const Params& P, const Ctx& cx, unsigned char* tile) {
+__device__ __forceinline__ void fill_rows_psi(const Params& P, const Ctx& cx, unsigned char* tile, int first = 0,
+                                              int count = kT) {
   fill_tile(tile, kD, [&](int r, int c0, float(&v)[8]) {
     if (r < cx.L) phi8(P, cx.n, cx.t0 + r, c0, true, v);
     else zero8(v);
-  });
+  }, first, count);
 }
 // A dense fp32 [128 x 128] row-major matrix into a tile.
-__device__ __forceinline__ void fill_dense(unsigned char* tile, const float* M) {
-  fill_tile(tile, kD, [&](int r, int c0, float(&v)[8]) { ld8f(M + r * kD + c0, v); });
+__device__ __forceinline__ void fill_dense(unsigned char* tile, const float* M, int first = 0, int count = kT) {
+  fill_tile(tile, kD, [&](int r, int c0, float(&v)[8]) { ld8f(M + r * kD + c0, v); }, first, count);
 }
 
 // ===========================================================================
