@@ -17,18 +17,18 @@ constexpr size_t kAlign = 256;
 inline size_t align_up(size_t x) { return (x + kAlign - 1) & ~(kAlign - 1); }
 inline int r4(int n) { return (n + 3) & ~3; }
 
-// Kernel groups that have a tensor-core version: 1 forward chunk increments,
-// 2 forward outputs, 4 backward chunk increments, 8 backward gradients.
+// The chunk kernels have tensor-core versions (1 forward chunk increments,
+// 2 forward outputs, 4 backward chunk increments, 8 backward gradients); a
+// shape runs either all of them or none, since they share bf16 workspaces.
 constexpr int kTcAll = 15;
-constexpr int kTcImplemented = kTcAll;
 
-// Groups that run on tensor cores for this shape: bf16 io, d_phi = d_v = 128,
-// window <= 16. ATLAS_MEM_TC=<mask> restricts them (0 = CUDA cores only).
+// Tensor cores for bf16 io with d_phi = d_v = 128 and window <= 16;
+// ATLAS_MEM_TC=0 selects the CUDA-core kernels instead.
 int tc_groups(const AtlasMemShape* s) {
   if (s->dtype_io != ATLAS_BF16 || s->d_phi != tc::kD || s->d_v != tc::kD || s->window > 16) return 0;
-  int mask = kTcAll;
-  if (const char* env = std::getenv("ATLAS_MEM_TC")) mask = std::atoi(env);
-  return mask & kTcImplemented;
+  if (const char* env = std::getenv("ATLAS_MEM_TC"))
+    if (std::atoi(env) == 0) return 0;
+  return kTcAll;
 }
 
 // Tokens per chunk: the caller's choice, else 128 - e when every chunk kernel
@@ -43,9 +43,9 @@ int chunk_of(const AtlasMemShape* s) {
 struct Layout {
   int C, nch;
   size_t saved, fwd, bwd;
-  size_t st, delta, ST, cs, phik, phiq;                        // in saved
+  size_t st, delta, ST, cs, phik, phiq, dlb, stb;              // in saved
   size_t adj, acs, dpsi, ddel, dphiR, hdd, hdp, du, hdu;       // in bwd scratch
-  size_t xq, xf, xs, gt;                                        // in bwd scratch (tensor-core path)
+  size_t xq, xf, xs, gt, adjb;                                  // in bwd scratch (tensor-core path)
 };
 
 Layout make_layout(const AtlasMemShape* s) {
@@ -57,8 +57,11 @@ Layout make_layout(const AtlasMemShape* s) {
   const bool tens = s->fmap_mode == ATLAS_FMAP_TENSOR;
   size_t o = 0;
   auto put = [&](size_t bytes) { const size_t at = o; o = align_up(o + bytes); return at; };
+  const bool tcm = tc_groups(s) == kTcAll;
   L.st = put(N * nch * 2 * D2 * 4);
-  L.delta = put(N * T * s->d_v * 4);
+  L.delta = tcm ? 0 : put(N * T * s->d_v * 4);
+  L.dlb = tcm ? put(N * T * s->d_v * 2) : 0;
+  L.stb = tcm ? put(N * nch * 2 * (size_t)tc::kTileBytes) : 0;
   L.ST = put(N * D2 * 4);
   L.cs = put(N * nch * 4 * 4);
   L.phik = tens ? put(N * T * s->d_phi * 4) : 0;
@@ -80,6 +83,7 @@ Layout make_layout(const AtlasMemShape* s) {
     L.xf = put(N * nch * 128 * 2 * 4);
     L.xs = put(N * nch * 4 * 4);
     L.gt = put(N * nch * (size_t)tc::kTileBytes);
+    L.adjb = put(N * nch * 2 * (size_t)tc::kTileBytes);
   }
   L.bwd = o;
   return L;
@@ -213,7 +217,11 @@ Params make_params(const AtlasMemShape* s, const Layout& L, const AtlasMemFwd* f
     P.dbuf = s->window > 1 ? b->dbuf_in : nullptr;
   }
   char* sv = (char*)const_cast<void*>(saved);
-  P.st = (float*)(sv + L.st); P.delta = (float*)(sv + L.delta); P.ST = (float*)(sv + L.ST);
+  const bool tcm = tc_groups(s) == kTcAll;
+  P.st = (float*)(sv + L.st); P.ST = (float*)(sv + L.ST);
+  P.delta = tcm ? nullptr : (float*)(sv + L.delta);
+  P.dlb = tcm ? (__nv_bfloat16*)(sv + L.dlb) : nullptr;
+  P.stb = tcm ? (unsigned char*)(sv + L.stb) : nullptr;
   P.cs = (float*)(sv + L.cs);
   P.phik = s->fmap_mode == ATLAS_FMAP_TENSOR ? (float*)(sv + L.phik) : nullptr;
   P.phiq = s->fmap_mode == ATLAS_FMAP_TENSOR ? (float*)(sv + L.phiq) : nullptr;
@@ -224,6 +232,7 @@ Params make_params(const AtlasMemShape* s, const Layout& L, const AtlasMemFwd* f
     P.hdp = (float*)(sc + L.hdp); P.du = (float*)(sc + L.du); P.hdu = (float*)(sc + L.hdu);
     if (tc_groups(s) & 8) {
       P.xq = (float*)(sc + L.xq); P.xf = (float*)(sc + L.xf); P.xs = (float*)(sc + L.xs); P.gt = sc + L.gt;
+      P.adjb = (unsigned char*)(sc + L.adjb);
     }
   }
   P.apply_mask = 1;

@@ -235,6 +235,16 @@ __device__ __forceinline__ const float4* stage_chunk_scalars(const float* src, i
   return dst;
 }
 
+// Writes 4 consecutive state elements (element offset e0 of a 128x128 state)
+// as bf16 into the core-matrix tile layout used by the tensor-core kernels.
+__device__ __forceinline__ void st4_tile(unsigned char* tile, int64_t e0, float4 v) {
+  const int r = (int)(e0 >> 7), c = (int)(e0 & 127);
+  const uint32_t off = (uint32_t)(((r >> 3) * 16 + (c >> 3)) * 128 + (r & 7) * 16 + (c & 7) * 2);
+  __align__(8) __nv_bfloat162 h[2] = {__floats2bfloat162_rn(v.x, v.y), __floats2bfloat162_rn(v.z, v.w)};
+  *reinterpret_cast<uint2*>(tile + off) = *reinterpret_cast<uint2*>(h);
+}
+__device__ __forceinline__ void st4_tile(unsigned char*, int64_t, float) {}
+
 template <int VEC>
 __global__ void __launch_bounds__(kThreads) k_fwd_scan(Params P, int dry) {
   using V = typename VecT<VEC>::T;
@@ -261,7 +271,16 @@ __global__ void __launch_bounds__(kThreads) k_fwd_scan(Params P, int dry) {
   for (int c = 0; c < nch; ++c) {
     V dS2 = dS1, dZ2 = dZ1;
     if (c + 2 < nch) { dS2 = st[(int64_t)(c + 2) * 2 * DV + x]; dZ2 = st[(int64_t)(c + 2) * 2 * DV + DV + x]; }
-    if (!dry) { st[(int64_t)c * 2 * DV + x] = S; st[(int64_t)c * 2 * DV + DV + x] = Z; }
+    if (!dry) {
+      if (P.stb) {  // tensor-core path: bf16 tiles, the fp32 increments stay as they are
+        unsigned char* t = P.stb + ((int64_t)n * nch + c) * 2 * 32768;
+        st4_tile(t, x * VEC, S);
+        st4_tile(t + 32768, x * VEC, Z);
+      } else {
+        st[(int64_t)c * 2 * DV + x] = S;
+        st[(int64_t)c * 2 * DV + DV + x] = Z;
+      }
+    }
     const float4 k = cs[c];
     const V nS = axpby(k.x, S, k.y, Z, dS0);
     Z = axpby(k.z, Z, 0.f, Z, dZ0);
@@ -350,10 +369,10 @@ __global__ void __launch_bounds__(kThreads) k_buf_out(Params P) {
     return;
   }
   const float w = P.gmode == ATLAS_GATE_TOKEN ? ldio(P.gate, (int64_t)n * P.T + p, P.bf) : 1.f;
-  const float* dl = P.delta + ((int64_t)n * P.T + p) * P.dv;
+  const int64_t drow = (int64_t)n * P.T + p;
   for (int64_t x = threadIdx.x; x < D2; x += kThreads) {
     const int nn = (int)(x / P.dphi), mm = (int)(x - (int64_t)nn * P.dphi);
-    dst[x] = (dl[nn] * load_phi(P, n, p, mm, false)) * w;
+    dst[x] = (delta_at(P, drow, nn) * load_phi(P, n, p, mm, false)) * w;
   }
 }
 
@@ -441,7 +460,16 @@ __global__ void __launch_bounds__(kThreads) k_bwd_scan(Params P, int dry) {
   for (int c = cl; c >= 0; --c) {
     V dS2 = dS1, dZ2 = dZ1;
     if (c - 2 >= 0) { dS2 = st[(int64_t)(c - 2) * 2 * DV + x]; dZ2 = st[(int64_t)(c - 2) * 2 * DV + DV + x]; }
-    if (!dry) { st[(int64_t)c * 2 * DV + x] = FS; st[(int64_t)c * 2 * DV + DV + x] = FZ; }
+    if (!dry) {
+      if (P.adjb) {
+        unsigned char* t = P.adjb + ((int64_t)n * nch + c) * 2 * 32768;
+        st4_tile(t, x * VEC, FS);
+        st4_tile(t + 32768, x * VEC, FZ);
+      } else {
+        st[(int64_t)c * 2 * DV + x] = FS;
+        st[(int64_t)c * 2 * DV + DV + x] = FZ;
+      }
+    }
     const float4 k = cs[c];
     const V nFS = axpby(k.x, FS, 0.f, FS, dS0);
     FZ = axpby(k.y, FS, k.z, FZ, dZ0);
@@ -708,7 +736,7 @@ __global__ void __launch_bounds__(kThreads) k_bwd_bufout(Params P) {
   float* dl = smem + dphi;   // [dv]
   float* red = dl + dv;      // [32]
   for (int m = threadIdx.x; m < dphi; m += kThreads) ph[m] = load_phi(P, n, p, m, false);
-  for (int nn = threadIdx.x; nn < dv; nn += kThreads) dl[nn] = P.delta[((int64_t)n * P.T + p) * dv + nn];
+  for (int nn = threadIdx.x; nn < dv; nn += kThreads) dl[nn] = delta_at(P, (int64_t)n * P.T + p, nn);
   __syncthreads();
   const float w = P.gmode == ATLAS_GATE_TOKEN ? ldio(P.gate, (int64_t)n * P.T + p, P.bf) : 1.f;
   for (int nn = threadIdx.x; nn < dv; nn += kThreads) {

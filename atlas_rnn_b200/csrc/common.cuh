@@ -41,6 +41,10 @@ struct Params {
   float *du;     // [N][T]
   float *hdu;    // [N][nch][e-1]
   float *xq, *xf, *xs;  // Gram pieces of the tensor-core backward
+  // tensor-core path: bf16 copies the chunk kernels read as raw 16-byte units
+  __nv_bfloat16* dlb;   // [N][T][dv] delta (replaces `delta`)
+  unsigned char* stb;   // [N][nch][2] 128x128 bf16 tiles of the chunk-start S, Z
+  unsigned char* adjb;  // [N][nch][2] 128x128 bf16 tiles of the adjoint at each chunk end
   void* gt;             // [N][nch] 128x128 bf16 Gram blocks (core-matrix tile layout)
   int apply_mask;
   // sequence-parallel segment outputs
@@ -69,6 +73,11 @@ __device__ __forceinline__ float fmap_elem_grad(float x, int mode, int deg) {
   float d = 1.f, pw = 1.f;
   for (int i = 2; i <= deg; ++i) { pw = pw * x; d += (float)i * pw; }
   return d;
+}
+
+// delta of row `row` (= n*T + t), component nn, from whichever copy is kept.
+__device__ __forceinline__ float delta_at(const Params& P, int64_t row, int nn) {
+  return P.dlb ? __bfloat162float(P.dlb[row * P.dv + nn]) : P.delta[row * P.dv + nn];
 }
 
 // phi of token `t` (key side if !isq), component m.

@@ -39,10 +39,9 @@ __device__ __forceinline__ void fill_rows_dy(const Params& P, const Ctx& cx, uns
 }
 __device__ __forceinline__ void fill_keys_delta(const Params& P, const Ctx& cx, unsigned char* tile, int first = 0,
                                                 int count = kT) {
-  fill_tile(tile, kD, [&](int r, int c0, float(&v)[8]) {
+  fill_rows_raw(tile, [&](int r) -> const __nv_bfloat16* {
     const int p = cx.kp0 + r;
-    if (r < cx.K && p >= 0) ld8f(P.delta + ((int64_t)cx.n * P.T + p) * P.dv + c0, v);
-    else zero8(v);
+    return (r < cx.K && p >= 0) ? P.dlb + ((int64_t)cx.n * P.T + p) * P.dv : nullptr;
   }, first, count);
 }
 
@@ -163,13 +162,13 @@ __global__ void __launch_bounds__(kT) k_bwd_state_tc(Params P) {
   Sync sy{&mbar, &tbase, 0, nullptr};
   const uint32_t tm = tc_setup(sy);
   const int64_t D2 = (int64_t)kD * kD;
-  const float* Sin = P.st + chunk_id(P, cx) * 2 * D2;
+  const unsigned char* Sin = P.stb + chunk_id(P, cx) * 2 * kTileBytes;
   __syncthreads();
   if (tid == 0) fwd_scalars(cx, sS, sZ, zZ);
   fill_rows_psi(P, cx, tPsi, 128, kT - 128);
   fill_rows_dy(P, cx, tY, [](int) { return 1.f; }, 128, kT - 128);
-  fill_dense(tSin, Sin, 128, kT - 128);
-  fill_dense(tZin, Sin + D2, 128, kT - 128);
+  copy_tile(tSin, Sin, 128, kT - 128);
+  copy_tile(tZin, Sin + kTileBytes, 128, kT - 128);
   smem_to_tc();
   if (tid == 0) {
     mma_chain(tm, op(tPsi, kD, 0), op(tSin, kD, 0), 8, kD, false);
@@ -260,14 +259,14 @@ __global__ void __launch_bounds__(kT) k_bwd_adj_tc(Params P) {
   const uint32_t tm = tc_setup(sy);
   const int64_t D2 = (int64_t)kD * kD;
   const int64_t cid = chunk_id(P, cx);
-  const float* FS = P.adj + cid * 2 * D2;
-  const float* Sin = P.st + cid * 2 * D2;
+  const unsigned char* FS = P.adjb + cid * 2 * kTileBytes;
+  const unsigned char* Sin = P.stb + cid * 2 * kTileBytes;
   __syncthreads();
   if (tid == 0) adj_scalars(cx, hS, hZS, hZZ);
   fill_keys_phi(P, cx, tPhi, 128, kT - 128);
   fill_keys_delta(P, cx, tDl, 128, kT - 128);
-  fill_dense(tFS, FS, 128, kT - 128);
-  fill_dense(tFZ, FS + D2, 128, kT - 128);
+  copy_tile(tFS, FS, 128, kT - 128);
+  copy_tile(tFZ, FS + kTileBytes, 128, kT - 128);
   smem_to_tc();
   if (tid == 0) {
     mma_chain(tm, op(tPhi, kD, 0), op(tFS, kD, 0), 8, kD, false);
@@ -278,13 +277,23 @@ __global__ void __launch_bounds__(kT) k_bwd_adj_tc(Params P) {
   // the four Gram scalars <F_S|F_Z, S_in|Z_in> while the MMAs run
   {
     float s00 = 0.f, s01 = 0.f, s10 = 0.f, s11 = 0.f;
-    for (int64_t x = tid * 4; x < D2; x += kT * 4) {
-      const float4 fs = *reinterpret_cast<const float4*>(FS + x), fz = *reinterpret_cast<const float4*>(FS + D2 + x);
-      const float4 si = *reinterpret_cast<const float4*>(Sin + x), zi = *reinterpret_cast<const float4*>(Sin + D2 + x);
-      s00 += fs.x * si.x + fs.y * si.y + fs.z * si.z + fs.w * si.w;
-      s01 += fs.x * zi.x + fs.y * zi.y + fs.z * zi.z + fs.w * zi.w;
-      s10 += fz.x * si.x + fz.y * si.y + fz.z * si.z + fz.w * si.w;
-      s11 += fz.x * zi.x + fz.y * zi.y + fz.z * zi.z + fz.w * zi.w;
+    // the four tiles share one layout, so the dot products run over raw units
+    for (int u = tid; u < kTileBytes / 16; u += kT) {
+      const uint4 a = reinterpret_cast<const uint4*>(FS)[u], b = reinterpret_cast<const uint4*>(FS + kTileBytes)[u];
+      const uint4 c = reinterpret_cast<const uint4*>(Sin)[u], d = reinterpret_cast<const uint4*>(Sin + kTileBytes)[u];
+      const __nv_bfloat162* fa = reinterpret_cast<const __nv_bfloat162*>(&a);
+      const __nv_bfloat162* fb = reinterpret_cast<const __nv_bfloat162*>(&b);
+      const __nv_bfloat162* fc = reinterpret_cast<const __nv_bfloat162*>(&c);
+      const __nv_bfloat162* fd = reinterpret_cast<const __nv_bfloat162*>(&d);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 fs = __bfloat1622float2(fa[k]), fz = __bfloat1622float2(fb[k]);
+        const float2 si = __bfloat1622float2(fc[k]), zi = __bfloat1622float2(fd[k]);
+        s00 += fs.x * si.x + fs.y * si.y;
+        s01 += fs.x * zi.x + fs.y * zi.y;
+        s10 += fz.x * si.x + fz.y * si.y;
+        s11 += fz.x * zi.x + fz.y * zi.y;
+      }
     }
     const float v[4] = {s00, s01, s10, s11};
     for (int k = 0; k < 4; ++k) {
@@ -686,9 +695,11 @@ __global__ void __launch_bounds__(kThreads) k_bwd_buf_tc(Params P) {
   }
   __syncthreads();
   const int64_t D2 = (int64_t)dv * dphi;
-  const float* FS = P.adj;  // chunk 0 of unit n
-  FS += (int64_t)n * P.nch * 2 * D2;
-  const float* FZ = FS + D2;
+  // adjoint at the end of chunk 0 of unit n (bf16 tiles)
+  const unsigned char* FSt = P.adjb + (int64_t)n * P.nch * 2 * kTileBytes;
+  const unsigned char* FZt = FSt + kTileBytes;
+  auto FS = [&](int64_t x) { return bf_at(FSt, (int)(x / dphi), (int)(x % dphi)); };
+  auto FZ = [&](int64_t x) { return bf_at(FZt, (int)(x / dphi), (int)(x % dphi)); };
   const float* bufn = P.buf ? P.buf + (int64_t)n * e1 * D2 : nullptr;
   const int64_t cid = (int64_t)n * P.nch;
   if (bufn) {
@@ -696,7 +707,7 @@ __global__ void __launch_bounds__(kThreads) k_bwd_buf_tc(Params P) {
     for (int jb = 0; jb < e1; ++jb) {
       const float* Bj = bufn + (int64_t)jb * D2;
       float s0 = 0.f, s1 = 0.f;
-      for (int64_t x = tid; x < D2; x += kThreads) { s0 += FS[x] * Bj[x]; s1 += FZ[x] * Bj[x]; }
+      for (int64_t x = tid; x < D2; x += kThreads) { s0 += FS(x) * Bj[x]; s1 += FZ(x) * Bj[x]; }
       s0 = block_sum(s0, red);
       s1 = block_sum(s1, red);
       if (tid == 0) { P.xf[(cid * kR + jb) * 2] = s0; P.xf[(cid * kR + jb) * 2 + 1] = s1; }
@@ -739,7 +750,7 @@ __global__ void __launch_bounds__(kThreads) k_bwd_buf_tc(Params P) {
       }
       for (int64_t x = tid; x < D2; x += kThreads) {
         const int nn = (int)(x / dphi), m = (int)(x - (int64_t)nn * dphi);
-        float acc = wzs * FS[x] + wzz * FZ[x];
+        float acc = wzs * FS(x) + wzz * FZ(x);
         for (int q = 0; q < L; ++q) acc += wE[jb * L + q] * dy[q * dv + nn] * psi[q * dphi + m];
         db[(int64_t)jb * D2 + x] = acc;
       }

@@ -158,7 +158,7 @@ __global__ void __launch_bounds__(kT) k_fwd_chunk_tc(Params P) {
           a[2 * k] -= f.x;
           a[2 * k + 1] -= f.y;
         }
-        if (p >= cx.t0) st16f(P.delta + ((int64_t)n * P.T + p) * P.dv + c16 * 16, a);
+        if (p >= cx.t0) st16bf(P.dlb + ((int64_t)n * P.T + p) * P.dv + c16 * 16, a);
       } else {
 #pragma unroll
         for (int i = 0; i < 16; ++i) a[i] = 0.f;
@@ -228,17 +228,15 @@ __global__ void __launch_bounds__(kT) k_fwd_out_tc(Params P) {
   const int n = cx.n, c = cx.c, K = cx.K, L = cx.L, tid = threadIdx.x, row = row_of(), wg = wg_of();
   Sync sy{&mbar, &tbase, 0, nullptr};
   const uint32_t tm = tc_setup(sy);
-  const int64_t D2 = (int64_t)kD * kD;
-  const float* Sin = P.st + ((int64_t)n * P.nch + c) * 2 * D2;
+  const unsigned char* Sin = P.stb + ((int64_t)n * P.nch + c) * 2 * kTileBytes;
   fill_rows_psi(P, cx, tPsi);
   fill_keys_phi(P, cx, tPhi);
-  fill_tile(tDl, kD, [&](int r, int c0, float(&v)[8]) {
+  fill_rows_raw(tDl, [&](int r) -> const __nv_bfloat16* {
     const int p = cx.kp0 + r;
-    if (r < K && p >= 0) ld8f(P.delta + ((int64_t)n * P.T + p) * P.dv + c0, v);
-    else zero8(v);
+    return (r < K && p >= 0) ? P.dlb + ((int64_t)n * P.T + p) * P.dv : nullptr;
   });
-  fill_dense(tSin, Sin);
-  fill_dense(tZin, Sin + D2);
+  copy_tile(tSin, Sin);
+  copy_tile(tZin, Sin + kTileBytes);
   __syncthreads();
   if (wg == 0) {  // column j = row of tMs: cS of key j before each token i
     const int j = row;
