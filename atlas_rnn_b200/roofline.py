@@ -33,8 +33,15 @@ def step_bytes_per_token(w: Workload) -> tuple[float, float]:
     return float(Bf), float(Bb)
 
 
+def tc_chunk(w: Workload) -> int:
+    """Tokens per chunk of the tensor-core path (keys = chunk + e - 1 fill 128 rows)."""
+    return 128 - w.window
+
+
 def kernel_flops(name: str, w: Workload, C: int) -> float:
-    """Algorithmic flops of one launch of a chunk kernel over the whole workload."""
+    """Algorithmic flops of one launch of a chunk kernel over the whole workload:
+    the contractions the chunked decomposition has to do (multiply-adds x 2),
+    without the padding of the 128-row tensor-core tiles."""
     e, dv, dp = w.window, w.d_v, w.d_phi
     total = 0.0
     for t0 in range(0, w.T, C):
@@ -46,6 +53,20 @@ def kernel_flops(name: str, w: Workload, C: int) -> float:
             fma = L * K * dp + L * dv * (K + 2 * dp)
         elif name == "k_bwd_chunk":
             fma = 2 * dv * L * dp
+        elif name == "k_fwd_chunk_tc":
+            fma = K * dp * dv + 2 * dv * K * dp
+        elif name == "k_fwd_out_tc":
+            fma = L * K * dp + 2 * L * dp * dv + L * K * dv
+        elif name == "k_bwd_chunk_tc":
+            fma = 2 * dv * L * dp
+        elif name == "k_bwd_state_tc":
+            fma = 2 * L * dp * dv + 2 * L * dv * dp
+        elif name == "k_bwd_adj_tc":
+            fma = 2 * K * dp * dv + 2 * K * dv * dp + 4 * dv * dp
+        elif name == "k_bwd_intra_tc":
+            fma = L * K * dv + L * K * dp + K * L * dv + K * L * dp + L * K * dp
+        elif name == "k_bwd_gates_tc":
+            fma = 4 * L * K * L
         elif name == "k_bwd_grads":
             fma = (L * K * dv + L * K * dp + L * 2 * dv * dp + 2 * K * dp * dv + 3 * (L + 2) * (K + 2) * L
                    + L * K * (L + 2) + K * L * dv + K * dp * (2 * dv + L) + L * dp * (2 * dv + K) + 4 * dv * dp)

@@ -123,7 +123,7 @@ class ClockSampler:
             os.makedirs(os.path.dirname(self.path), exist_ok=True)
             self.f = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.dev), f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "20"],
                                          stdout=self.f, stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
@@ -324,14 +324,18 @@ def run_ours(args, w):
 
 
 def kernel_cfg_chunk(w):
-    from atlas_rnn_b200.ops import Spec  # noqa: F401  (library default chunk)
+    """Tokens per chunk the library picks for this workload (its default rule)."""
+    from atlas_rnn_b200.roofline import tc_chunk
+    tensor_cores = w.dtype == torch.bfloat16 and w.d_phi == 128 and w.d_v == 128 and w.window <= 16
+    if tensor_cores and os.environ.get("ATLAS_MEM_TC", "1") != "0":
+        return tc_chunk(w)
     return 32 if w.window - 1 <= 32 else w.window - 1
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--config", type=int, default=1)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
