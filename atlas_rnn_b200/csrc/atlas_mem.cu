@@ -113,12 +113,13 @@ Smem smem_sizes(const AtlasMemShape* s, int C) {
   const int tctx = tc::ctx_floats(C, e);
   m.tc_f1 = 3 * (size_t)tc::kTileBytes + 4 * (size_t)(tctx + 2 * tc::kR);
   m.tc_f3 = 6 * (size_t)tc::kTileBytes + 4 * (size_t)(tctx + 2 * tc::kR);
-  m.buf_y = 4 * (size_t)(ctx + r4(C * (e > 1 ? e - 1 : 1)) + r4(C * dphi));
+  m.buf_y = 4 * (size_t)(ctx + r4(C * (e > 1 ? e - 1 : 1)) + r4(C * dphi) + kStageFloats);
   m.tc_b1 = 3 * (size_t)tc::kTileBytes + 4 * (size_t)(tctx + 2 * tc::kR);
   m.tc_b4 = 4 * (size_t)tc::kTileBytes + 4 * (size_t)(tctx + 3 * 132 + 4 * (tc::kT / 32) + 2 * tc::kWG * tc::kR);
   m.tc_b6 = 6 * (size_t)tc::kTileBytes +
             4 * (size_t)(tctx + 6 * 132 + 4 * tc::kR + 4 + tc::kR + tc::kGateParts * (tc::kWG - 1) * tc::kR);
-  m.buf_b = 4 * (size_t)(ctx + r4(C * dphi) + r4(C * dv) + 2 * r4(C * (e > 1 ? e - 1 : 1)) + 3 * r4(C + 1) + 32);
+  m.buf_b = 4 * (size_t)(ctx + r4(C * dphi) + r4(C * dv) + 3 * r4(C * (e > 1 ? e - 1 : 1)) + 3 * r4(C + 1) + 32 +
+                         kStageFloats);
   return m;
 }
 
@@ -347,7 +348,8 @@ int run_fwd_finish(const AtlasMemShape* s, const Params& P, cudaStream_t st) {
   if (int v = launch_scan(true, P, 0, st)) return v;
   if (tc_groups(s) & 2) {
     LAUNCH_T(KID_FWD_OUT_TC, tc::k_fwd_out_tc, dim3(P.nch, P.N), tc::kT, m.tc_f3, st, P);
-    if (P.buf && P.e > 1) LAUNCH(KID_FWD_BUF_Y, tc::k_fwd_buf_y, dim3(1, P.N), m.buf_y, st, P);
+    if (P.buf && P.e > 1)
+      LAUNCH(KID_FWD_BUF_Y, tc::k_fwd_buf_y, dim3((P.dv + 63) / 64, P.N), m.buf_y, st, P);
   } else {
     LAUNCH(KID_FWD_OUT, k_fwd_out, dim3(P.nch, P.N), m.f3, st, P);
   }

@@ -20,9 +20,10 @@ struct Ctx {
   float *al, *et, *be, *u, *U;
 };
 
-__device__ __forceinline__ void load_ctx(const Params& P, SmemAlloc& sa, Ctx& cx, int nthreads = kThreads) {
+__device__ __forceinline__ void load_ctx(const Params& P, SmemAlloc& sa, Ctx& cx, int nthreads = kThreads,
+                                         int chunk = -1) {
   cx.n = blockIdx.y;
-  cx.c = blockIdx.x;
+  cx.c = chunk >= 0 ? chunk : blockIdx.x;
   cx.t0 = cx.c * P.C;
   cx.L = min(P.C, P.T - cx.t0);
   cx.K = cx.L + P.e - 1;

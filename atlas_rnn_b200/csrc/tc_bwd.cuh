@@ -653,25 +653,27 @@ __global__ void __launch_bounds__(kT) k_bwd_gates_tc(Params P) {
 // k_bwd_intra_tc and before k_bwd_gates_tc: the Gram columns of the buffer
 // entries (X[F][Buf], G[q][Buf] = dy_q . Buf psi_q), their d psi terms, and the
 // buffer's own gradient dBuf_jb = wZS F_S + wZZ F_Z + sum_q wE_jb[q] dy_q psi_q^T.
-// CUDA cores, one CTA of kThreads per unit.
+// Block GEMMs on CUDA cores, one CTA of kThreads per unit.
 // ===========================================================================
 __global__ void __launch_bounds__(kThreads) k_bwd_buf_tc(Params P) {
   extern __shared__ float smem[];
   SmemAlloc sa{smem, 0};
   Ctx cx;
-  load_ctx(P, sa, cx);  // blockIdx.x = 0: chunk 0
+  load_ctx(P, sa, cx, kThreads, 0);
   const int L = cx.L, e1 = P.e - 1, dv = P.dv, dphi = P.dphi, n = cx.n, tid = threadIdx.x;
   float* psi = sa.take(L * dphi);
   float* dy = sa.take(L * dv);
   float* cSb = sa.take(L * e1);   // cS_i[jb]
   float* wE = sa.take(e1 * L);    // wE_jb[q]
+  float* gacc = sa.take(L * e1);  // G[q][jb]
   float* hS = sa.take(L + 1);
   float* hZS = sa.take(L + 1);
   float* hZZ = sa.take(L + 1);
   float* red = sa.take(32);
+  float* stage = sa.take(kStageFloats);
   for (int x = tid; x < L * dphi; x += kThreads) psi[x] = load_phi(P, n, x / dphi, x % dphi, true);
   for (int x = tid; x < L * dv; x += kThreads) dy[x] = ldio(P.dy, (int64_t)n * P.T * dv + x, P.bf);
-  for (int x = tid; x < e1 * L; x += kThreads) wE[x] = 0.f;
+  for (int x = tid; x < e1 * L; x += kThreads) { wE[x] = 0.f; gacc[x] = 0.f; }
   __syncthreads();
   if (tid < e1) {
     const int j = tid;
@@ -698,45 +700,37 @@ __global__ void __launch_bounds__(kThreads) k_bwd_buf_tc(Params P) {
   // adjoint at the end of chunk 0 of unit n (bf16 tiles)
   const unsigned char* FSt = P.adjb + (int64_t)n * P.nch * 2 * kTileBytes;
   const unsigned char* FZt = FSt + kTileBytes;
-  auto FS = [&](int64_t x) { return bf_at(FSt, (int)(x / dphi), (int)(x % dphi)); };
-  auto FZ = [&](int64_t x) { return bf_at(FZt, (int)(x / dphi), (int)(x % dphi)); };
   const float* bufn = P.buf ? P.buf + (int64_t)n * e1 * D2 : nullptr;
   const int64_t cid = (int64_t)n * P.nch;
   if (bufn) {
-    unsigned char* gt = reinterpret_cast<unsigned char*>(P.gt) + cid * kTileBytes;
     for (int jb = 0; jb < e1; ++jb) {
       const float* Bj = bufn + (int64_t)jb * D2;
       float s0 = 0.f, s1 = 0.f;
-      for (int64_t x = tid; x < D2; x += kThreads) { s0 += FS(x) * Bj[x]; s1 += FZ(x) * Bj[x]; }
+      for (int64_t x = tid; x < D2; x += kThreads) {
+        const int r = (int)(x / dphi), c = (int)(x - (int64_t)r * dphi);
+        s0 += bf_at(FSt, r, c) * Bj[x];
+        s1 += bf_at(FZt, r, c) * Bj[x];
+      }
       s0 = block_sum(s0, red);
       s1 = block_sum(s1, red);
       if (tid == 0) { P.xf[(cid * kR + jb) * 2] = s0; P.xf[(cid * kR + jb) * 2 + 1] = s1; }
-      // G[q][jb] = dy_q . (Buf_jb psi_q), one warp per q
-      for (int q = tid >> 5; q < L; q += kThreads / 32) {
-        float acc = 0.f;
-        for (int nn = tid & 31; nn < dv; nn += 32) {
-          float bp = 0.f;
-          for (int m = 0; m < dphi; ++m) bp += Bj[nn * dphi + m] * psi[q * dphi + m];
-          acc += bp * dy[q * dv + nn];
-        }
-        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-        if ((tid & 31) == 0)
-          *reinterpret_cast<__nv_bfloat16*>(gt + umma::elem_off(q, jb, kR)) = __float2bfloat16_rn(acc);
-      }
     }
+    // G[q][jb] = sum_nn dy_q[nn] (Buf_jb psi_q)[nn]
+    bgemm(stage, L, e1 * dv,
+          [&](int q, int c, float acc) { atomicAdd(&gacc[q * e1 + c / dv], acc * dy[q * dv + c % dv]); },
+          seg(dphi, [&](int q, int m) { return psi[q * dphi + m]; },
+              [&](int m, int c) { return bufn[(int64_t)c * dphi + m]; }));
     // d psi_i += sum_jb cS_i[jb] Buf_jb^T dy_i
-    for (int x = tid; x < L * dphi; x += kThreads) {
-      const int i = x / dphi, m = x - i * dphi;
-      float acc = 0.f;
-      for (int jb = 0; jb < e1; ++jb) {
-        const float w = cSb[i * e1 + jb];
-        if (w == 0.f) continue;
-        const float* Bj = bufn + (int64_t)jb * D2;
-        float s = 0.f;
-        for (int nn = 0; nn < dv; ++nn) s += Bj[nn * dphi + m] * dy[i * dv + nn];
-        acc += w * s;
-      }
-      P.dpsi[((int64_t)n * P.T + i) * dphi + m] += acc;
+    bgemm(stage, L, dphi,
+          [&](int i, int m, float acc) { P.dpsi[((int64_t)n * P.T + i) * dphi + m] += acc; },
+          seg(e1 * dv,
+              [&](int i, int kk) { return cSb[i * e1 + kk / dv] * dy[i * dv + kk % dv]; },
+              [&](int kk, int m) { return bufn[(int64_t)kk * dphi + m]; }));
+    __syncthreads();
+    unsigned char* gt = reinterpret_cast<unsigned char*>(P.gt) + cid * kTileBytes;
+    for (int x = tid; x < L * e1; x += kThreads) {
+      const int q = x / e1, jb = x % e1;
+      *reinterpret_cast<__nv_bfloat16*>(gt + umma::elem_off(q, jb, kR)) = __float2bfloat16_rn(gacc[x]);
     }
   }
   if (P.dbuf) {
@@ -748,12 +742,12 @@ __global__ void __launch_bounds__(kThreads) k_bwd_buf_tc(Params P) {
         wzs += w * hZS[i + 1];
         wzz += w * hZZ[i + 1];
       }
-      for (int64_t x = tid; x < D2; x += kThreads) {
-        const int nn = (int)(x / dphi), m = (int)(x - (int64_t)nn * dphi);
-        float acc = wzs * FS(x) + wzz * FZ(x);
-        for (int q = 0; q < L; ++q) acc += wE[jb * L + q] * dy[q * dv + nn] * psi[q * dphi + m];
-        db[(int64_t)jb * D2 + x] = acc;
-      }
+      bgemm(stage, dv, dphi,
+            [&](int nn, int m, float acc) {
+              db[(int64_t)jb * D2 + (int64_t)nn * dphi + m] = acc + wzs * bf_at(FSt, nn, m) + wzz * bf_at(FZt, nn, m);
+            },
+            seg(L, [&](int nn, int q) { return wE[jb * L + q] * dy[q * dv + nn]; },
+                [&](int q, int m) { return psi[q * dphi + m]; }));
     }
   }
 }

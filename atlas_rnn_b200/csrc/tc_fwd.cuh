@@ -297,15 +297,17 @@ __global__ void __launch_bounds__(kT) k_fwd_out_tc(Params P) {
 }
 
 // Chunk 0 with a carried buffer: y_i += sum_jb cS_i[jb] Buf_jb psi_i (dense
-// buffer entries, CUDA cores). One CTA of kThreads per unit.
+// buffer entries) as one block GEMM over K = (e-1) d_phi on CUDA cores.
+// Grid (column tiles of d_v, unit).
 __global__ void __launch_bounds__(kThreads) k_fwd_buf_y(Params P) {
   extern __shared__ float smem[];
   SmemAlloc sa{smem, 0};
   Ctx cx;
-  load_ctx(P, sa, cx);  // blockIdx.x = 0: chunk 0
-  const int L = cx.L, e1 = P.e - 1, dv = P.dv, dphi = P.dphi, n = cx.n;
+  load_ctx(P, sa, cx, kThreads, 0);  // chunk 0 (blockIdx.x picks the column tile)
+  const int L = cx.L, e1 = P.e - 1, dv = P.dv, dphi = P.dphi, n = cx.n, nn0 = blockIdx.x * 64;
   float* cSb = sa.take(L * e1);      // cS before token i for buffer key jb
   float* psi = sa.take(L * dphi);
+  float* stage = sa.take(kStageFloats);
   __syncthreads();
   if ((int)threadIdx.x < e1) {
     const int j = threadIdx.x;
@@ -319,20 +321,20 @@ __global__ void __launch_bounds__(kThreads) k_fwd_buf_y(Params P) {
   for (int x = threadIdx.x; x < L * dphi; x += kThreads) psi[x] = load_phi(P, n, x / dphi, x % dphi, true);
   __syncthreads();
   const float* bufn = P.buf + (int64_t)n * e1 * dv * dphi;
-  for (int x = threadIdx.x; x < L * dv; x += kThreads) {
-    const int i = x / dv, nn = x - i * dv;
-    float acc = 0.f;
-    for (int jb = 0; jb < e1; ++jb) {
-      const float w = cSb[i * e1 + jb];
-      if (w == 0.f) continue;
-      const float* row = bufn + ((int64_t)jb * dv + nn) * dphi;
-      float s = 0.f;
-      for (int m = 0; m < dphi; ++m) s += row[m] * psi[i * dphi + m];
-      acc += w * s;
-    }
-    const int64_t off = ((int64_t)n * P.T + i) * dv + nn;
-    stio(P.y, off, ldio(P.y, off, P.bf) + acc, P.bf);
-  }
+  bgemm(stage, L, min(64, dv - nn0),
+        [&](int i, int c, float acc) {
+          const int64_t off = ((int64_t)n * P.T + i) * dv + nn0 + c;
+          stio(P.y, off, ldio(P.y, off, P.bf) + acc, P.bf);
+        },
+        seg(e1 * dphi,
+            [&](int i, int kk) {
+              const int jb = kk / dphi;
+              return cSb[i * e1 + jb] * psi[i * dphi + kk - jb * dphi];
+            },
+            [&](int kk, int c) {
+              const int jb = kk / dphi;
+              return bufn[((int64_t)jb * dv + nn0 + c) * dphi + kk - jb * dphi];
+            }));
 }
 
 }  // namespace tc

@@ -32,6 +32,7 @@ sys.path.insert(0, ROOT)
 from atlas_rnn_b200.workloads import CONFIGS, make_inputs, shrink  # noqa: E402
 
 METRIC = "memory-layer fwd+bwd tokens/sec"
+WITH_BUFFER = False  # pass the (zero) carried omega buffer as the modules do after init_state
 UNIT = "tokens/s"
 
 
@@ -164,7 +165,7 @@ def step_api(inp, w, leaves_from):
     L = leaves_from
     y, S_end, Z_end, nb = memory_recurrence(
         L["k"], L["q"], L["v"], L["lr"], L["decay"], L["beta"], L["gate"], S_ref=inp["S0"], S0=inp["S0"],
-        Z0=inp["Z0"], omega_buffer=None, window=w.window,  # empty carried buffer (zeros)
+        Z0=inp["Z0"], omega_buffer=inp["omega_buffer"] if WITH_BUFFER else None, window=w.window,
         gate_mode="window" if w.gate == "window" else "token", fmap_mode=w.fmap_mode, fmap_degree=w.fmap_degree,
         proj=inp["proj"])
     torch.autograd.backward([y], [L["dy"]])
@@ -343,7 +344,10 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--T", type=int, default=None, help="override tokens (for profiling small cases)")
     ap.add_argument("--B", type=int, default=None)
+    ap.add_argument("--with-buffer", action="store_true", help="pass the zero omega buffer explicitly")
     args = ap.parse_args()
+    global WITH_BUFFER
+    WITH_BUFFER = args.with_buffer
     w = CONFIGS[args.config]
     if args.T or args.B:
         w = shrink(w, B=args.B, T=args.T)
