@@ -3,6 +3,7 @@
 // interfaces they replace are in include/atlas_mem.h.
 #include <mutex>
 
+#include <algorithm>
 #include <cstdlib>
 
 #include "chunk_kernels.cuh"
@@ -146,7 +147,7 @@ int ensure_attrs() {
                       (const void*)k_bwd_scan<4>, (const void*)tc::k_fwd_chunk_tc, (const void*)tc::k_fwd_out_tc,
                       (const void*)tc::k_fwd_buf_y, (const void*)tc::k_bwd_chunk_tc, (const void*)tc::k_bwd_state_tc,
                       (const void*)tc::k_bwd_adj_tc, (const void*)tc::k_bwd_intra_tc, (const void*)tc::k_bwd_buf_tc,
-                      (const void*)tc::k_bwd_gates_tc, (const void*)tc::k_bwd_finalize_tc};
+                      (const void*)tc::k_bwd_gates_tc, (const void*)tc::k_bwd_finalize_tc, (const void*)tc::k_bwd_dsref_tc};
   for (const void* k : ks) {
     cudaFuncAttributes fa;
     if (cudaFuncGetAttributes(&fa, k) != cudaSuccess) return ATLAS_ERR_LAUNCH;
@@ -244,12 +245,12 @@ Params make_params(const AtlasMemShape* s, const Layout& L, const AtlasMemFwd* f
 enum KernelId {
   KID_FMAP_FWD, KID_FWD_CHUNK, KID_FWD_SCAN, KID_FWD_OUT, KID_BUF_OUT, KID_BWD_CHUNK, KID_BWD_SCAN,
   KID_BWD_GRADS, KID_BWD_BUFOUT, KID_BWD_FINAL, KID_BWD_DSREF, KID_FMAP_BWD, KID_FWD_CHUNK_TC, KID_FWD_OUT_TC, KID_FWD_BUF_Y,
-  KID_BWD_CHUNK_TC, KID_BWD_STATE_TC, KID_BWD_ADJ_TC, KID_BWD_INTRA_TC, KID_BWD_BUF_TC, KID_BWD_GATES_TC, KID_BWD_FINAL_TC, KID_COUNT
+  KID_BWD_CHUNK_TC, KID_BWD_STATE_TC, KID_BWD_ADJ_TC, KID_BWD_INTRA_TC, KID_BWD_BUF_TC, KID_BWD_GATES_TC, KID_BWD_FINAL_TC, KID_BWD_DSREF_TC, KID_COUNT
 };
 const char* const kKernelNames[KID_COUNT] = {
   "k_fmap_tensor_fwd", "k_fwd_chunk", "k_fwd_scan", "k_fwd_out", "k_buf_out", "k_bwd_chunk", "k_bwd_scan",
   "k_bwd_grads", "k_bwd_bufout", "k_bwd_finalize", "k_bwd_dsref", "k_fmap_tensor_bwd", "k_fwd_chunk_tc", "k_fwd_out_tc", "k_fwd_buf_y",
-  "k_bwd_chunk_tc", "k_bwd_state_tc", "k_bwd_adj_tc", "k_bwd_intra_tc", "k_bwd_buf_tc", "k_bwd_gates_tc", "k_bwd_finalize_tc"};
+  "k_bwd_chunk_tc", "k_bwd_state_tc", "k_bwd_adj_tc", "k_bwd_intra_tc", "k_bwd_buf_tc", "k_bwd_gates_tc", "k_bwd_finalize_tc", "k_bwd_dsref_tc"};
 
 constexpr int kMaxTimed = 8192;
 struct Prof {
@@ -388,8 +389,19 @@ int run_bwd_finish(const AtlasMemShape* s, const Params& P, cudaStream_t st) {
   else
   LAUNCH(KID_BWD_FINAL, k_bwd_finalize, dim3((P.T + kFinTile - 1) / kFinTile, P.N), m.fin, st, P);
   if (P.dSref) {
-    const int tiles = ((P.dv + 63) / 64) * ((P.dphi + 63) / 64);
-    LAUNCH(KID_BWD_DSREF, k_bwd_dsref, dim3(tiles, P.N), m.dsref, st, P);
+    if (tc_groups(s) & 8) {
+      // about two CTAs per SM over (token segment, unit)
+      const int ntiles = (P.T + tc::kR - 1) / tc::kR;
+      const int segs = std::max(1, std::min(ntiles, (2 * 148 + P.N - 1) / P.N));
+      const int per = (ntiles + segs - 1) / segs;
+      if (cudaMemsetAsync(P.dSref, 0, (size_t)P.N * P.dv * P.dphi * sizeof(float), st) != cudaSuccess)
+        return ATLAS_ERR_LAUNCH;
+      LAUNCH_T(KID_BWD_DSREF_TC, tc::k_bwd_dsref_tc, dim3((ntiles + per - 1) / per, P.N), tc::kT,
+               2 * (size_t)tc::kTileBytes, st, P, per);
+    } else {
+      const int tiles = ((P.dv + 63) / 64) * ((P.dphi + 63) / 64);
+      LAUNCH(KID_BWD_DSREF, k_bwd_dsref, dim3(tiles, P.N), m.dsref, st, P);
+    }
   }
   if (P.fmode == ATLAS_FMAP_TENSOR && (P.dk_ || P.dq_)) {
     LAUNCH(KID_FMAP_BWD, k_fmap_tensor_bwd, dim3((P.T + kFmTile - 1) / kFmTile, P.N, 2), m.fmb, st, P);

@@ -867,5 +867,51 @@ __global__ void __launch_bounds__(kT) k_bwd_finalize_tc(Params P) {
   tc_teardown(tm, 128);
 }
 
+// ===========================================================================
+// dS_ref = sum_t d delta_t phi_t^T  (delta = S_ref phi - v, rnn_memory.py:659):
+// a reduction over the tokens of a unit on tensor cores. CTA (segment, unit)
+// accumulates its 128-token tiles in TMEM, then adds into dS_ref (zeroed by
+// the host) with vector atomics.
+// ===========================================================================
+__global__ void __launch_bounds__(kT) k_bwd_dsref_tc(Params P, int tiles_per_cta) {
+  extern __shared__ __align__(1024) unsigned char sm[];
+  unsigned char* tDD = sm;               // d delta rows (bf16), MN-major A: [M = d_v, K = tokens]
+  unsigned char* tPh = sm + kTileBytes;  // phi rows,             MN-major B: [N = d_phi, K = tokens]
+  __shared__ uint64_t mbar;
+  __shared__ uint32_t tbase;
+  const int n = blockIdx.y, tid = threadIdx.x, row = row_of(), wg = wg_of();
+  const int ntiles = (P.T + kR - 1) / kR;
+  const int tb = blockIdx.x * tiles_per_cta, te = min(ntiles, tb + tiles_per_cta);
+  Sync sy{&mbar, &tbase, 0, nullptr};
+  const uint32_t tm = tc_setup(sy, 128);
+  for (int t = tb; t < te; ++t) {
+    const int p0 = t * kR, TT = min(kR, P.T - p0);
+    fill_tile(tDD, kD, [&](int r, int c0, float(&v)[8]) {
+      if (r < TT) ld8f(P.ddel + ((int64_t)n * P.T + p0 + r) * P.dv + c0, v);
+      else zero8(v);
+    });
+    fill_tile(tPh, kD, [&](int r, int c0, float(&v)[8]) {
+      if (r < TT) phi8(P, n, p0 + r, c0, false, v);
+      else zero8(v);
+    });
+    smem_to_tc();
+    if (tid == 0) mma_chain(tm, op(tDD, kD, 1), op(tPh, kD, 1), 8, kD, t > tb);
+    mma_wait(sy);  // the tiles are refilled next iteration
+  }
+  if (te > tb) {
+    float* dst = P.dSref + ((int64_t)n * kD + row) * kD;
+    for (int h = 0; h < kCPW; ++h) {
+      const int c16 = wg * kCPW + h;
+      float a[16];
+      umma::tmem_ld16(lane_addr(tm, c16 * 16), a);
+      umma::tmem_ld_wait();
+#pragma unroll
+      for (int k = 0; k < 16; k += 4)
+        atomicAdd(reinterpret_cast<float4*>(dst + c16 * 16 + k), make_float4(a[k], a[k + 1], a[k + 2], a[k + 3]));
+    }
+  }
+  tc_teardown(tm, 128);
+}
+
 }  // namespace tc
 }  // namespace atlas

@@ -136,13 +136,13 @@ class Segment:
                                                         _stream(self.dev)), "backward_local")
         return coef, dS, dZ
 
-    def backward_finish(self, dy, FS, FZ, apply_mask: bool):
-        g = {n: torch.empty_like(t) for n, t in (("k", self.k), ("q", self.q), ("v", self.v), ("lr", self.lr),
-                                                 ("decay", self.decay), ("S_ref", self.S_ref))}
+    def backward_finish(self, dy, FS, FZ, apply_mask: bool, need=None):
+        """Input gradients of this segment; `need` names the ones to produce (default: all)."""
+        names = [("k", self.k), ("q", self.q), ("v", self.v), ("lr", self.lr), ("decay", self.decay),
+                 ("S_ref", self.S_ref), ("S0", self.S_ref)]
         if self.spec.momentum:
-            g["beta"] = torch.empty_like(self.beta)
-            g["Z0"] = torch.empty_like(self.S_ref)
-        g["S0"] = torch.empty_like(self.S_ref)
+            names += [("beta", self.beta), ("Z0", self.S_ref)]
+        g = {n: torch.empty_like(t) for n, t in names if need is None or n in need}
         f = self._fwd_struct(self.S_in, self.Z_in)
         b = self._bwd_struct(dy, FS.contiguous(), FZ.contiguous() if FZ is not None else None, g)
         p = _lib.ptr
@@ -196,10 +196,13 @@ class SeqParallelMemoryFn(torch.autograd.Function):
         FS_end = FS_end * ((ctx.S_T >= -100) & (ctx.S_T <= 100))  # clamp gradient
         incoming, (dS0, dZ0) = compose_backward_carries(coefs, dFSs, dFZs, FS_end, FZ_end)
         FS, FZ = incoming[r]
-        g = seg.backward_finish(dy, FS, FZ if spec.momentum else None, apply_mask=False)
-        dist.all_reduce(g["S_ref"], group=group)
-        return (None, None, g["k"], g["q"], g["v"], g["lr"], g["decay"], g.get("beta"), g["S_ref"], dS0,
-                dZ0 if spec.momentum else None)
+        flags = ctx.needs_input_grad  # (spec, group, k, q, v, lr, decay, beta, S_ref, S0, Z0)
+        need = {n for n, f in zip(("k", "q", "v", "lr", "decay", "beta", "S_ref"), flags[2:9]) if f}
+        g = seg.backward_finish(dy, FS, FZ if spec.momentum else None, apply_mask=False, need=need)
+        if "S_ref" in g:
+            dist.all_reduce(g["S_ref"], group=group)
+        return (None, None, g.get("k"), g.get("q"), g.get("v"), g.get("lr"), g.get("decay"), g.get("beta"),
+                g.get("S_ref"), dS0 if flags[9] else None, dZ0 if (spec.momentum and flags[10]) else None)
 
 
 def seq_parallel_memory(k, q, v, lr, decay, beta, *, S_ref, S0, Z0=None, group=None, fmap_mode="off",

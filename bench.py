@@ -114,17 +114,21 @@ class ClockSampler:
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_id: str, rank: int):
-        self.dev = gpu_id
+    def __init__(self, gpu_ids, rank: int):
+        # rank 0 samples every GPU of the job; the other ranks sample nothing
+        self.ids = gpu_ids
+        self.rank = rank
         self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_rank{rank}.csv")
+        self.path = os.path.join(ROOT, "gpurun_out", "clocks.csv")
 
     def __enter__(self):
+        if self.rank != 0:
+            return self
         try:
             os.makedirs(os.path.dirname(self.path), exist_ok=True)
             self.f = open(self.path, "w")
-            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.dev), f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "20"],
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", ",".join(self.ids), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
                                          stdout=self.f, stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
@@ -172,6 +176,16 @@ def step_api(inp, w, leaves_from):
     return y
 
 
+def step_seqpar(inp, w, leaves_from):
+    """One fwd+bwd of this rank's token slice, sequence-parallel over all ranks."""
+    from atlas_rnn_b200.parallel import seq_parallel_memory
+    L = leaves_from
+    y, S_end, Z_end = seq_parallel_memory(L["k"], L["q"], L["v"], L["lr"], L["decay"], L["beta"], S_ref=inp["S0"],
+                                          S0=inp["S0"], Z0=inp["Z0"])
+    torch.autograd.backward([y], [L["dy"]])
+    return y
+
+
 def traffic_from_profiles(kernel: str, workload: str):
     """Per-launch DRAM bytes recorded from an ncu capture in profiles/ (or None)."""
     path = os.path.join(ROOT, "profiles", f"{kernel}_{workload}.md")
@@ -197,6 +211,14 @@ def run_ours(args, w):
     if ws > 1:
         dist.init_process_group("nccl", device_id=dev)
     _lib.lib()
+    # long-context configs with window 1 run sequence-parallel across the ranks
+    # (strong scaling: the ranks share one sequence); the others run one copy
+    # of the configuration per rank (weak scaling)
+    seqpar = ws > 1 and w.window == 1 and w.gate == "none"
+    w_full = w
+    if seqpar:
+        w = shrink(w, T=w.T // ws)
+    step = step_seqpar if seqpar else step_api
     inp = make_inputs(w, seed=rank, device=dev)
     names = ("k", "q", "v", "lr", "decay", "beta", "gate")
 
@@ -219,18 +241,25 @@ def run_ours(args, w):
 
     # ---- device-resident timing (value) with per-kernel event timing
     for _ in range(args.warmup):
-        step_api(inp, w, leaves())
+        step(inp, w, leaves())
     barrier()
     _lib.profile_enable(True)
     st = torch.cuda.current_stream(dev)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     props = torch.cuda.get_device_properties(dev)
-    gpu_id = ("GPU-" + str(props.uuid)) if getattr(props, "uuid", None) is not None else str(local)
-    with ClockSampler(gpu_id, rank) as clk:
+    my_id = ("GPU-" + str(props.uuid)) if getattr(props, "uuid", None) is not None else str(local)
+    ids = [my_id]
+    if ws > 1:
+        gathered = [None] * ws
+        dist.all_gather_object(gathered, my_id)
+        ids = gathered
+    with ClockSampler(ids, rank) as clk:
         barrier()
         ev0.record(st)
+        h0 = time.perf_counter()
         for _ in range(args.steps):
-            step_api(inp, w, leaves())
+            step(inp, w, leaves())
+        host_ms = (time.perf_counter() - h0) * 1000.0 / args.steps  # enqueue time per step
         ev1.record(st)
         barrier()
     ms = ev0.elapsed_time(ev1)
@@ -239,7 +268,7 @@ def run_ours(args, w):
     _lib.profile_enable(False)
     ms = max_over_ranks(ms)
     ms_step = ms / args.steps
-    tokens_step = w.B * w.T
+    tokens_step = w.B * w.T  # this rank's tokens per step
     value = ws * tokens_step * args.steps / (ms / 1000.0)
 
     # ---- e2e through the public API with pinned host buffers
@@ -253,7 +282,7 @@ def run_ours(args, w):
         for n in names:
             if d[n] is not None:
                 d[n].requires_grad_(True)
-        y = step_api(inp, w, d)
+        y = step(inp, w, d)
         y_host.copy_(y.detach(), non_blocking=True)
 
     for _ in range(max(1, args.warmup // 2)):
@@ -301,16 +330,20 @@ def run_ours(args, w):
             cpu = {"value": v, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port", "sample": sample}
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+            "scaling": "strong" if seqpar else "weak",
             "vs_baseline": None, "dtype": "bf16" if w.dtype == torch.bfloat16 else "f32",
             "data": "synthetic (seeded, benchmark-config distributions)",
-            "config": {"workload": w.name, "B": w.B, "H": w.H, "T": w.T, "d_k": w.d_k, "d_phi": w.d_phi,
+            "config": {"workload": w.name, "B": w.B, "H": w.H, "T": w_full.T, "d_k": w.d_k, "d_phi": w.d_phi,
                        "d_v": w.d_v, "window": w.window, "gate": w.gate, "fmap": f"{w.fmap_mode}:{w.fmap_degree}",
-                       "momentum": w.momentum, "per_rank_units": w.N, "parallelism": f"bh-replica x{ws}",
+                       "momentum": w.momentum, "per_rank_units": w.N,
+                       "parallelism": (f"sequence-parallel x{ws} (T/{ws} per rank, NCCL carry exchange)" if seqpar
+                                       else f"bh-replica x{ws}"),
                        "l2": "inputs exceed L2 (no flush needed)" if tok_heads * (2 * w.d_k + w.d_v) * w.dtype.itemsize > 126e6
                        else "inputs fit L2"},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": launches,
+            "host_enqueue_ms_per_step": host_ms,
             "roofline": roofline,
             "step_roofline_ms": step_roof_ms,
             "step_roofline_frac": step_roof_ms / ms_step,
