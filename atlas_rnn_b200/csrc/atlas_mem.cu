@@ -224,6 +224,7 @@ Params make_params(const AtlasMemShape* s, const Layout& L, const AtlasMemFwd* f
   P.delta = tcm ? nullptr : (float*)(sv + L.delta);
   P.dlb = tcm ? (__nv_bfloat16*)(sv + L.dlb) : nullptr;
   P.stb = tcm ? (unsigned char*)(sv + L.stb) : nullptr;
+  P.inc_bf16 = tcm ? 1 : 0;
   P.cs = (float*)(sv + L.cs);
   P.phik = s->fmap_mode == ATLAS_FMAP_TENSOR ? (float*)(sv + L.phik) : nullptr;
   P.phiq = s->fmap_mode == ATLAS_FMAP_TENSOR ? (float*)(sv + L.phiq) : nullptr;

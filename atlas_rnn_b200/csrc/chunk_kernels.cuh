@@ -246,6 +246,20 @@ __device__ __forceinline__ void st4_tile(unsigned char* tile, int64_t e0, float4
 }
 __device__ __forceinline__ void st4_tile(unsigned char*, int64_t, float) {}
 
+// Chunk increment i (in units of V) of a unit: fp32, or bf16 on the tensor-core path.
+template <class V>
+__device__ __forceinline__ V ld_inc(const V* f32, const __nv_bfloat16* b16, int64_t i);
+template <>
+__device__ __forceinline__ float ld_inc<float>(const float* f32, const __nv_bfloat16*, int64_t i) { return f32[i]; }
+template <>
+__device__ __forceinline__ float4 ld_inc<float4>(const float4* f32, const __nv_bfloat16* b16, int64_t i) {
+  if (!b16) return f32[i];
+  const uint2 u = *reinterpret_cast<const uint2*>(b16 + i * 4);
+  const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+  const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+  return make_float4(a.x, a.y, b.x, b.y);
+}
+
 template <int VEC>
 __global__ void __launch_bounds__(kThreads) k_fwd_scan(Params P, int dry) {
   using V = typename VecT<VEC>::T;
@@ -265,13 +279,16 @@ __global__ void __launch_bounds__(kThreads) k_fwd_scan(Params P, int dry) {
   }
   if (x >= DV) return;
   V* __restrict__ st = reinterpret_cast<V*>(P.st) + (int64_t)n * nch * 2 * DV;
+  const __nv_bfloat16* sb =
+      P.inc_bf16 ? reinterpret_cast<const __nv_bfloat16*>(P.st) + (int64_t)n * nch * 2 * D2 : nullptr;
+  auto ld = [&](int64_t i) { return ld_inc<V>(st, sb, i); };
   V S = dry ? vzero(V()) : reinterpret_cast<const V*>(P.S0)[n * DV + x];
   V Z = (dry || !P.Z0) ? vzero(V()) : reinterpret_cast<const V*>(P.Z0)[n * DV + x];
-  V dS0 = st[x], dZ0 = st[DV + x];
-  V dS1 = nch > 1 ? st[2 * DV + x] : dS0, dZ1 = nch > 1 ? st[3 * DV + x] : dZ0;
+  V dS0 = ld(x), dZ0 = ld(DV + x);
+  V dS1 = nch > 1 ? ld(2 * DV + x) : dS0, dZ1 = nch > 1 ? ld(3 * DV + x) : dZ0;
   for (int c = 0; c < nch; ++c) {
     V dS2 = dS1, dZ2 = dZ1;
-    if (c + 2 < nch) { dS2 = st[(int64_t)(c + 2) * 2 * DV + x]; dZ2 = st[(int64_t)(c + 2) * 2 * DV + DV + x]; }
+    if (c + 2 < nch) { dS2 = ld((int64_t)(c + 2) * 2 * DV + x); dZ2 = ld((int64_t)(c + 2) * 2 * DV + DV + x); }
     if (!dry) {
       if (P.stb) {  // tensor-core path: bf16 tiles, the fp32 increments stay as they are
         unsigned char* t = P.stb + ((int64_t)n * nch + c) * 2 * 32768;
@@ -454,13 +471,16 @@ __global__ void __launch_bounds__(kThreads) k_bwd_scan(Params P, int dry) {
     }
   }
   V* __restrict__ st = reinterpret_cast<V*>(P.adj) + (int64_t)n * nch * 2 * DV;
+  const __nv_bfloat16* sb =
+      P.inc_bf16 ? reinterpret_cast<const __nv_bfloat16*>(P.adj) + (int64_t)n * nch * 2 * D2 : nullptr;
+  auto ld = [&](int64_t i) { return ld_inc<V>(st, sb, i); };
   const int cl = nch - 1;
-  V dS0 = st[(int64_t)cl * 2 * DV + x], dZ0 = st[(int64_t)cl * 2 * DV + DV + x];
-  V dS1 = cl > 0 ? st[(int64_t)(cl - 1) * 2 * DV + x] : dS0;
-  V dZ1 = cl > 0 ? st[(int64_t)(cl - 1) * 2 * DV + DV + x] : dZ0;
+  V dS0 = ld((int64_t)cl * 2 * DV + x), dZ0 = ld((int64_t)cl * 2 * DV + DV + x);
+  V dS1 = cl > 0 ? ld((int64_t)(cl - 1) * 2 * DV + x) : dS0;
+  V dZ1 = cl > 0 ? ld((int64_t)(cl - 1) * 2 * DV + DV + x) : dZ0;
   for (int c = cl; c >= 0; --c) {
     V dS2 = dS1, dZ2 = dZ1;
-    if (c - 2 >= 0) { dS2 = st[(int64_t)(c - 2) * 2 * DV + x]; dZ2 = st[(int64_t)(c - 2) * 2 * DV + DV + x]; }
+    if (c - 2 >= 0) { dS2 = ld((int64_t)(c - 2) * 2 * DV + x); dZ2 = ld((int64_t)(c - 2) * 2 * DV + DV + x); }
     if (!dry) {
       if (P.adjb) {
         unsigned char* t = P.adjb + ((int64_t)n * nch + c) * 2 * 32768;

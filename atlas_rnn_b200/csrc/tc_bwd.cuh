@@ -124,7 +124,7 @@ __global__ void __launch_bounds__(kT) k_bwd_chunk_tc(Params P) {
   mma_wait(sy);
   {
     const int64_t D2 = (int64_t)kD * kD;
-    float* dst = P.adj + chunk_id(P, cx) * 2 * D2 + (int64_t)row * kD;
+    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(P.adj) + chunk_id(P, cx) * 2 * D2 + (int64_t)row * kD;
 #pragma unroll
     for (int h = 0; h < kCPW; ++h) {
       const int c16 = wg * kCPW + h;
@@ -132,8 +132,8 @@ __global__ void __launch_bounds__(kT) k_bwd_chunk_tc(Params P) {
       umma::tmem_ld16(lane_addr(tm, c16 * 16), a);
       umma::tmem_ld16(lane_addr(tm, 128 + c16 * 16), b);
       umma::tmem_ld_wait();
-      st16f(dst + c16 * 16, a);
-      st16f(dst + D2 + c16 * 16, b);
+      st16bf(dst + c16 * 16, a);
+      st16bf(dst + D2 + c16 * 16, b);
     }
   }
   tc_teardown(tm, 256);

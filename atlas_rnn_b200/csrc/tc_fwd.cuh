@@ -183,7 +183,6 @@ __global__ void __launch_bounds__(kT) k_fwd_chunk_tc(Params P) {
   mma_wait(sy);
   {  // increments: row = state row nn
     const int64_t D2 = (int64_t)kD * kD;
-    float* dst = P.st + ((int64_t)n * P.nch + c) * 2 * D2 + (int64_t)row * kD;
     const float* bufn = buf_of(P, n, c);
     const int nb = bufn ? P.e - 1 : 0;
 #pragma unroll
@@ -198,8 +197,9 @@ __global__ void __launch_bounds__(kT) k_fwd_chunk_tc(Params P) {
 #pragma unroll
         for (int i = 0; i < 16; ++i) { a[i] += cSe[jb] * bj[i]; b[i] += cZe[jb] * bj[i]; }
       }
-      st16f(dst + c16 * 16, a);
-      st16f(dst + D2 + c16 * 16, b);
+      __nv_bfloat16* db = reinterpret_cast<__nv_bfloat16*>(P.st) + ((int64_t)n * P.nch + c) * 2 * D2 + (int64_t)row * kD;
+      st16bf(db + c16 * 16, a);
+      st16bf(db + D2 + c16 * 16, b);
     }
   }
   tc_teardown(tm, 256);
