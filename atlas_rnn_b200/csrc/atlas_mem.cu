@@ -146,8 +146,8 @@ int ensure_attrs() {
                       (const void*)k_fwd_scan<1>, (const void*)k_fwd_scan<4>, (const void*)k_bwd_scan<1>,
                       (const void*)k_bwd_scan<4>, (const void*)tc::k_fwd_chunk_tc, (const void*)tc::k_fwd_out_tc,
                       (const void*)tc::k_fwd_buf_y, (const void*)tc::k_bwd_chunk_tc, (const void*)tc::k_bwd_state_tc,
-                      (const void*)tc::k_bwd_adj_tc, (const void*)tc::k_bwd_intra_tc, (const void*)tc::k_bwd_buf_tc,
-                      (const void*)tc::k_bwd_gates_tc, (const void*)tc::k_bwd_finalize_tc, (const void*)tc::k_bwd_dsref_tc};
+                      (const void*)tc::k_bwd_buf_tc,
+                      (const void*)tc::k_bwd_gates_tc, (const void*)tc::k_bwd_finalize_tc, (const void*)tc::k_bwd_dsref_tc, (const void*)tc::k_bwd_keys_tc};
   for (const void* k : ks) {
     cudaFuncAttributes fa;
     if (cudaFuncGetAttributes(&fa, k) != cudaSuccess) return ATLAS_ERR_LAUNCH;
@@ -246,12 +246,12 @@ Params make_params(const AtlasMemShape* s, const Layout& L, const AtlasMemFwd* f
 enum KernelId {
   KID_FMAP_FWD, KID_FWD_CHUNK, KID_FWD_SCAN, KID_FWD_OUT, KID_BUF_OUT, KID_BWD_CHUNK, KID_BWD_SCAN,
   KID_BWD_GRADS, KID_BWD_BUFOUT, KID_BWD_FINAL, KID_BWD_DSREF, KID_FMAP_BWD, KID_FWD_CHUNK_TC, KID_FWD_OUT_TC, KID_FWD_BUF_Y,
-  KID_BWD_CHUNK_TC, KID_BWD_STATE_TC, KID_BWD_ADJ_TC, KID_BWD_INTRA_TC, KID_BWD_BUF_TC, KID_BWD_GATES_TC, KID_BWD_FINAL_TC, KID_BWD_DSREF_TC, KID_COUNT
+  KID_BWD_CHUNK_TC, KID_BWD_STATE_TC, KID_BWD_BUF_TC, KID_BWD_GATES_TC, KID_BWD_FINAL_TC, KID_BWD_DSREF_TC, KID_BWD_KEYS_TC, KID_COUNT
 };
 const char* const kKernelNames[KID_COUNT] = {
   "k_fmap_tensor_fwd", "k_fwd_chunk", "k_fwd_scan", "k_fwd_out", "k_buf_out", "k_bwd_chunk", "k_bwd_scan",
   "k_bwd_grads", "k_bwd_bufout", "k_bwd_finalize", "k_bwd_dsref", "k_fmap_tensor_bwd", "k_fwd_chunk_tc", "k_fwd_out_tc", "k_fwd_buf_y",
-  "k_bwd_chunk_tc", "k_bwd_state_tc", "k_bwd_adj_tc", "k_bwd_intra_tc", "k_bwd_buf_tc", "k_bwd_gates_tc", "k_bwd_finalize_tc", "k_bwd_dsref_tc"};
+  "k_bwd_chunk_tc", "k_bwd_state_tc", "k_bwd_buf_tc", "k_bwd_gates_tc", "k_bwd_finalize_tc", "k_bwd_dsref_tc", "k_bwd_keys_tc"};
 
 constexpr int kMaxTimed = 8192;
 struct Prof {
@@ -374,8 +374,7 @@ int run_bwd_finish(const AtlasMemShape* s, const Params& P, cudaStream_t st) {
   if (tc_groups(s) & 8) {
     const dim3 g(P.nch, P.N);
     LAUNCH_T(KID_BWD_STATE_TC, tc::k_bwd_state_tc, g, tc::kT, m.tc_b4, st, P);
-    LAUNCH_T(KID_BWD_ADJ_TC, tc::k_bwd_adj_tc, g, tc::kT, m.tc_b4, st, P);
-    LAUNCH_T(KID_BWD_INTRA_TC, tc::k_bwd_intra_tc, g, tc::kT, m.tc_b6, st, P);
+    LAUNCH_T(KID_BWD_KEYS_TC, tc::k_bwd_keys_tc, g, tc::kT, m.tc_b6, st, P);
     if (P.e > 1 && (P.buf || P.dbuf)) LAUNCH(KID_BWD_BUF_TC, tc::k_bwd_buf_tc, dim3(1, P.N), m.buf_b, st, P);
     LAUNCH_T(KID_BWD_GATES_TC, tc::k_bwd_gates_tc, g, tc::kT, m.tc_b6, st, P);
   } else {

@@ -5,11 +5,10 @@
 //   k_bwd_chunk_tc  adjoint increments dShat, dZhat of a chunk        tiles dY*eS, dY*eZ, Psi
 //   k_bwd_state_tc  Psi S_in^T, dY S_in (and Z_in): the Gram entries  tiles Psi, dY, S_in, Z_in
 //                   <dy_q psi_q^T, S_in>, and d psi's state part
-//   k_bwd_adj_tc    Phi F^T, delta F: the Gram entries <F, R_j>,      tiles Phi, delta, F_S, F_Z
-//                   d delta and d phi through F; the four <F, S> dots
-//   k_bwd_intra_tc  A1 = dY delta^T, A2 = Psi Phi^T, the Gram block   tiles Phi, delta, Psi, dY, M1, M2
-//                   G = A1 o A2 and the intra-chunk terms of d delta,
-//                   d phi, d psi
+//   k_bwd_keys_tc   Phi F^T, delta F (Gram entries <F, R_j>, d delta   tiles Phi, delta, F_S|Psi,
+//                   and d phi through F, the four <F, S> dots), then   F_Z|dY, M1, M3
+//                   A1 = dY delta^T, A2 = Psi Phi^T, the Gram block
+//                   G = A1 o A2 and the intra-chunk terms
 //   k_bwd_gates_tc  d alpha, d eta, d beta and the window-gate        tiles G, cS, cZ, cZ+, eS+, eZ+
 //                   gradients as bilinear forms of the Gram matrix
 // Gram pieces travel between kernels through the backward scratch:
@@ -234,17 +233,23 @@ __device__ __forceinline__ void key_adj_weights(const Params& P, const Ctx& cx, 
 }
 
 // ===========================================================================
-// adjoint side: P1 = Phi F_S^T, P2 = Phi F_Z^T (-> X[F][R_j], d delta through F),
-// Q1 = delta F_S, Q2 = delta F_Z (-> d phi through F); the four <F, S_in/Z_in>.
-// d delta and d phi are written with '=' (own keys) or to the halo partials.
+// key-side backward in one pass (replaces k_bwd_adj_tc + k_bwd_intra_tc):
+//   phase 1  P1 = Phi F_S^T, P2 = Phi F_Z^T, Q1 = delta F_S, Q2 = delta F_Z
+//            -> X[F][R_j]; d delta = wZS P1 + wZZ P2 and d phi = wZS Q1 + wZZ Q2 are
+//            written back into TMEM (tcgen05.st) over P1 and Q1
+//   phase 2  A1 = dY delta^T, A2 = Psi Phi^T -> G = A1 o A2 (scratch), M1, M2, M3
+//   phase 3  d delta += M1 dY, d phi += M2 Psi (accumulating in TMEM), I5 = M3 Phi
+//   out      d delta, d phi written once (own keys / halo partials); d psi += I5
 // ===========================================================================
-__global__ void __launch_bounds__(kT) k_bwd_adj_tc(Params P) {
+__global__ void __launch_bounds__(kT) k_bwd_keys_tc(Params P) {
   extern __shared__ __align__(1024) unsigned char sm[];
   unsigned char* tPhi = sm;
-  unsigned char* tDl = sm + kTileBytes;
-  unsigned char* tFS = sm + 2 * kTileBytes;
-  unsigned char* tFZ = sm + 3 * kTileBytes;
-  SmemAlloc sa{reinterpret_cast<float*>(sm + 4 * kTileBytes), 0};
+  unsigned char* tDl = sm + kTileBytes;       // delta, later M2
+  unsigned char* tFS = sm + 2 * kTileBytes;   // F_S, later Psi
+  unsigned char* tFZ = sm + 3 * kTileBytes;   // F_Z, later dY
+  unsigned char* tM3 = sm + 4 * kTileBytes;   // cS staging, later M3
+  unsigned char* tM1 = sm + 5 * kTileBytes;   // eZ staging, later M1
+  SmemAlloc sa{reinterpret_cast<float*>(sm + 6 * kTileBytes), 0};
   __shared__ uint64_t mbar;
   __shared__ uint32_t tbase;
   Ctx cx;
@@ -254,30 +259,35 @@ __global__ void __launch_bounds__(kT) k_bwd_adj_tc(Params P) {
   float* hZZ = sa.take(kR + 1);
   float* red = sa.take(4 * (kT / 32));
   float* part = sa.take(2 * kWG * kR);
-  const int n = cx.n, K = cx.K, tid = threadIdx.x, e = P.e, row = row_of(), wg = wg_of();
+  const int n = cx.n, K = cx.K, L = cx.L, tid = threadIdx.x, e = P.e, row = row_of(), wg = wg_of();
   Sync sy{&mbar, &tbase, 0, nullptr};
   const uint32_t tm = tc_setup(sy);
-  const int64_t D2 = (int64_t)kD * kD;
   const int64_t cid = chunk_id(P, cx);
   const unsigned char* FS = P.adjb + cid * 2 * kTileBytes;
   const unsigned char* Sin = P.stb + cid * 2 * kTileBytes;
   __syncthreads();
-  if (tid == 0) adj_scalars(cx, hS, hZS, hZZ);
+  // loads (all but warpgroup 0) and staging columns (warpgroup 0: eZ column q, then cS column j)
   fill_keys_phi(P, cx, tPhi, 128, kT - 128);
   fill_keys_delta(P, cx, tDl, 128, kT - 128);
   copy_tile(tFS, FS, 128, kT - 128);
   copy_tile(tFZ, FS + kTileBytes, 128, kT - 128);
+  if (wg == 0) {
+    adj_column(cx, row, [&](int i, float, float ez) { st_bf(tM1, i, row, ez); });
+    for (int i = L; i < kR; ++i) st_bf(tM1, i, row, 0.f);
+    fwd_column(P, cx, row, [&](int i, float cs, float, float) { st_bf(tM3, i, row, cs); });
+    for (int i = L; i < kR; ++i) st_bf(tM3, i, row, 0.f);
+    if (row == 0) adj_scalars(cx, hS, hZS, hZZ);
+  }
   smem_to_tc();
   if (tid == 0) {
-    mma_chain(tm, op(tPhi, kD, 0), op(tFS, kD, 0), 8, kD, false);
-    mma_chain(tm + 128, op(tPhi, kD, 0), op(tFZ, kD, 0), 8, kD, false);
-    mma_chain(tm + 256, op(tDl, kD, 0), op(tFS, kD, 1), 8, kD, false);
-    mma_chain(tm + 384, op(tDl, kD, 0), op(tFZ, kD, 1), 8, kD, false);
+    mma_chain(tm, op(tPhi, kD, 0), op(tFS, kD, 0), 8, kD, false);        // P1
+    mma_chain(tm + 128, op(tPhi, kD, 0), op(tFZ, kD, 0), 8, kD, false);  // P2
+    mma_chain(tm + 256, op(tDl, kD, 0), op(tFS, kD, 1), 8, kD, false);  // Q1
+    mma_chain(tm + 384, op(tDl, kD, 0), op(tFZ, kD, 1), 8, kD, false);  // Q2
   }
-  // the four Gram scalars <F_S|F_Z, S_in|Z_in> while the MMAs run
+  // the four Gram scalars <F_S|F_Z, S_in|Z_in> while the MMAs run (raw bf16 tiles)
   {
     float s00 = 0.f, s01 = 0.f, s10 = 0.f, s11 = 0.f;
-    // the four tiles share one layout, so the dot products run over raw units
     for (int u = tid; u < kTileBytes / 16; u += kT) {
       const uint4 a = reinterpret_cast<const uint4*>(FS)[u], b = reinterpret_cast<const uint4*>(FS + kTileBytes)[u];
       const uint4 c = reinterpret_cast<const uint4*>(Sin)[u], d = reinterpret_cast<const uint4*>(Sin + kTileBytes)[u];
@@ -308,102 +318,7 @@ __global__ void __launch_bounds__(kT) k_bwd_adj_tc(Params P) {
       P.xs[cid * 4 + tid] = t;
     }
   }
-  mma_wait(sy);
-  {
-    const int j = row, p = cx.kp0 + j;
-    float wzs, wzz;
-    key_adj_weights(P, cx, j, hZS, hZZ, wzs, wzz);
-    const bool own = j < K && p >= cx.t0, halo = j < K && p >= 0 && p < cx.t0;
-    const int e1 = e > 1 ? e - 1 : 1;
-    float xS = 0.f, xZ = 0.f;
-    float* dd = own ? P.ddel + ((int64_t)n * P.T + p) * P.dv : P.hdd + (cid * e1 + (j < e - 1 ? j : 0)) * P.dv;
-    float* dp = own ? P.dphiR + ((int64_t)n * P.T + p) * P.dphi : P.hdp + (cid * e1 + (j < e - 1 ? j : 0)) * P.dphi;
-#pragma unroll
-    for (int h = 0; h < kCPW; ++h) {
-      const int c16 = wg * kCPW + h;
-      float p1[16], p2[16], q1[16], q2[16];
-      umma::tmem_ld16(lane_addr(tm, c16 * 16), p1);
-      umma::tmem_ld16(lane_addr(tm, 128 + c16 * 16), p2);
-      umma::tmem_ld16(lane_addr(tm, 256 + c16 * 16), q1);
-      umma::tmem_ld16(lane_addr(tm, 384 + c16 * 16), q2);
-      umma::tmem_ld_wait();
-      if (own || halo) {
-        float dl[16], a[16], b[16];
-        load_unit(tDl, j, 2 * c16, kD, *reinterpret_cast<float(*)[8]>(dl));
-        load_unit(tDl, j, 2 * c16 + 1, kD, *reinterpret_cast<float(*)[8]>(dl + 8));
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          xS += p1[i] * dl[i];
-          xZ += p2[i] * dl[i];
-          a[i] = wzs * p1[i] + wzz * p2[i];
-          b[i] = wzs * q1[i] + wzz * q2[i];
-        }
-        st16f(dd + c16 * 16, a);
-        st16f(dp + c16 * 16, b);
-      }
-    }
-    part[(wg * 2 + 0) * kR + j] = xS;
-    part[(wg * 2 + 1) * kR + j] = xZ;
-  }
-  __syncthreads();
-  if (wg == 0) {
-    float* xf = P.xf + (cid * kR + row) * 2;
-    float a = 0.f, b = 0.f;
-    for (int g = 0; g < kWG; ++g) { a += part[(2 * g) * kR + row]; b += part[(2 * g + 1) * kR + row]; }
-    xf[0] = a;
-    xf[1] = b;
-  }
-  tc_teardown(tm);
-}
-
-// ===========================================================================
-// intra-chunk terms: A1 = dY delta^T, A2 = Psi Phi^T (token q x key j);
-// G = A1 o A2 goes to the scratch (tile layout, bf16) for the gate kernel;
-//   d delta_j += sum_q wE_j[q] A2[q][j] dy_q       (M1 = wE o A2^T, MN-major)
-//   d phi_j   += sum_q wE_j[q] A1[q][j] psi_q      (M2 = wE o A1^T)
-//   d psi_i   += sum_j cS_i[j] A1[i][j] phi_j      (M3 = cS o A1)
-// with wE_j[q] = sum_i W(i,j) eZ_{i+1}[q] the window-summed adjoint coefficient.
-// ===========================================================================
-__global__ void __launch_bounds__(kT) k_bwd_intra_tc(Params P) {
-  extern __shared__ __align__(1024) unsigned char sm[];
-  unsigned char* tPhi = sm;
-  unsigned char* tDl = sm + kTileBytes;   // delta, later M2
-  unsigned char* tPsi = sm + 2 * kTileBytes;
-  unsigned char* tY = sm + 3 * kTileBytes;
-  unsigned char* tM1 = sm + 4 * kTileBytes;
-  unsigned char* tM2 = sm + 5 * kTileBytes;
-  SmemAlloc sa{reinterpret_cast<float*>(sm + 6 * kTileBytes), 0};
-  __shared__ uint64_t mbar;
-  __shared__ uint32_t tbase;
-  Ctx cx;
-  load_ctx(P, sa, cx, kT);
-  const int n = cx.n, K = cx.K, L = cx.L, tid = threadIdx.x, e = P.e, row = row_of(), wg = wg_of();
-  Sync sy{&mbar, &tbase, 0, nullptr};
-  const uint32_t tm = tc_setup(sy);
-  const int64_t cid = chunk_id(P, cx);
-  fill_keys_phi(P, cx, tPhi);
-  fill_keys_delta(P, cx, tDl);
-  fill_rows_psi(P, cx, tPsi);
-  fill_rows_dy(P, cx, tY, [](int) { return 1.f; });
-  __syncthreads();
-  // staging while the first MMAs run: tM2[i][q] <- eZ_{i+1}[q] (warpgroup 0),
-  // tM1[i][j] <- cS of key j before token i (warpgroup 1)
-  if (wg == 0) {
-    const int q = row;
-    adj_column(cx, q, [&](int i, float, float ez) { st_bf(tM2, i, q, ez); });
-    for (int i = L; i < kR; ++i) st_bf(tM2, i, q, 0.f);
-  } else if (wg == 1) {
-    const int j = row;
-    fwd_column(P, cx, j, [&](int i, float cs, float, float) { st_bf(tM1, i, j, cs); });
-    for (int i = L; i < kR; ++i) st_bf(tM1, i, j, 0.f);
-  }
-  smem_to_tc();
-  if (tid == 0) {
-    mma_chain(tm, op(tY, kD, 0), op(tDl, kD, 0), 8, kR, false);       // A1[q][j]
-    mma_chain(tm + 128, op(tPsi, kD, 0), op(tPhi, kD, 0), 8, kR, false);  // A2[q][j]
-  }
-  // window-summed adjoint coefficients of row q for this warpgroup's keys:
-  //   wE_j[q] = sum_{i <= j <= i+e-1} W(i, j) eZ_{i+1}[q]
+  // window-summed adjoint coefficients of row q for this warpgroup's keys (from the eZ staging)
   float wE[kR / kWG];
   {
     const int q = row, j0 = wg * (kR / kWG);
@@ -411,30 +326,71 @@ __global__ void __launch_bounds__(kT) k_bwd_intra_tc(Params P) {
     for (int jj = 0; jj < kR / kWG; ++jj) {
       const int j = j0 + jj;
       float acc = 0.f;
-      for (int i = max(0, j - e + 1); i <= min(L - 1, j); ++i) {
-        const float ez = __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(tM2 + umma::elem_off(i, q, kR)));
-        acc += wgt(P, cx, i, j) * ez;
-      }
+      for (int i = max(0, j - e + 1); i <= min(L - 1, j); ++i) acc += wgt(P, cx, i, j) * bf_at(tM1, i, q);
       wE[jj] = q < L ? acc : 0.f;
     }
   }
   mma_wait(sy);
-  __syncthreads();  // every staging column of tM2 has been read
-  {
+  {  // phase-1 epilogue, row j: X[F][R_j]; F parts of d delta / d phi back into TMEM
+    const int j = row;
+    float wzs, wzz;
+    key_adj_weights(P, cx, j, hZS, hZZ, wzs, wzz);
+    float xS = 0.f, xZ = 0.f;
+    for (int h = 0; h < kCPW; ++h) {
+      const int c16 = wg * kCPW + h;
+      float p1[16], p2[16], q1[16], q2[16], dl[16];
+      umma::tmem_ld16(lane_addr(tm, c16 * 16), p1);
+      umma::tmem_ld16(lane_addr(tm, 128 + c16 * 16), p2);
+      umma::tmem_ld16(lane_addr(tm, 256 + c16 * 16), q1);
+      umma::tmem_ld16(lane_addr(tm, 384 + c16 * 16), q2);
+      umma::tmem_ld_wait();
+      load_unit(tDl, j, 2 * c16, kD, *reinterpret_cast<float(*)[8]>(dl));
+      load_unit(tDl, j, 2 * c16 + 1, kD, *reinterpret_cast<float(*)[8]>(dl + 8));
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        xS += p1[i] * dl[i];
+        xZ += p2[i] * dl[i];
+        p1[i] = wzs * p1[i] + wzz * p2[i];
+        q1[i] = wzs * q1[i] + wzz * q2[i];
+      }
+      umma::tmem_st16(lane_addr(tm, c16 * 16), p1);
+      umma::tmem_st16(lane_addr(tm, 256 + c16 * 16), q1);
+    }
+    umma::tmem_st_wait();
+    part[(wg * 2 + 0) * kR + j] = xS;
+    part[(wg * 2 + 1) * kR + j] = xZ;
+  }
+  umma::fence_before();
+  __syncthreads();  // F tiles and the P2 / Q2 columns are free
+  if (wg == 0) {
+    float a = 0.f, b = 0.f;
+    for (int g = 0; g < kWG; ++g) { a += part[(2 * g) * kR + row]; b += part[(2 * g + 1) * kR + row]; }
+    float* xf = P.xf + (cid * kR + row) * 2;
+    xf[0] = row < K ? a : 0.f;
+    xf[1] = row < K ? b : 0.f;
+  }
+  fill_rows_psi(P, cx, tFS);
+  fill_rows_dy(P, cx, tFZ, [](int) { return 1.f; });
+  smem_to_tc();
+  if (tid == 0) {
+    mma_chain(tm + 128, op(tFZ, kD, 0), op(tDl, kD, 0), 8, kR, false);   // A1[q][j] = dY delta^T
+    mma_chain(tm + 384, op(tFS, kD, 0), op(tPhi, kD, 0), 8, kR, false);  // A2[q][j] = Psi Phi^T
+  }
+  mma_wait(sy);
+  {  // phase-2 epilogue, row q: G, M3 = cS o A1, M1 = wE o A2^T, M2 = wE o A1^T
     const int q = row;
     unsigned char* gdst = reinterpret_cast<unsigned char*>(P.gt) + cid * kTileBytes;
-#pragma unroll
     for (int h4 = 0; h4 < kCPW; ++h4) {
       const int c16 = wg * kCPW + h4;
       float a1[16], a2[16];
-      umma::tmem_ld16(lane_addr(tm, c16 * 16), a1);
-      umma::tmem_ld16(lane_addr(tm, 128 + c16 * 16), a2);
+      umma::tmem_ld16(lane_addr(tm, 128 + c16 * 16), a1);
+      umma::tmem_ld16(lane_addr(tm, 384 + c16 * 16), a2);
       umma::tmem_ld_wait();
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const int cb = 2 * c16 + h;
         float g[8], c3[8], m1[8], m2[8];
-        load_unit(tM1, q, cb, kR, c3);
+        load_unit(tM3, q, cb, kR, c3);
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
           const float x1 = a1[8 * h + k], x2 = a2[8 * h + k], w = wE[8 * (2 * h4 + h) + k];
@@ -444,17 +400,17 @@ __global__ void __launch_bounds__(kT) k_bwd_intra_tc(Params P) {
           m1[k] = w * x2;
         }
         store_unit(gdst, q, cb, kR, g);
-        store_unit(tM1, q, cb, kR, c3);   // M3 = cS o A1
-        store_unit(tM2, q, cb, kR, m1);   // M1 = wE o A2^T (MN-major)
-        store_unit(tDl, q, cb, kR, m2);   // M2 = wE o A1^T (MN-major)
+        store_unit(tM3, q, cb, kR, c3);
+        store_unit(tDl, q, cb, kR, m2);  // delta no longer needed
+        store_unit(tM1, q, cb, kR, m1);  // eZ staging already read into wE
       }
     }
   }
   smem_to_tc();
   if (tid == 0) {
-    mma_chain(tm + 256, op(tM2, kR, 1), op(tY, kD, 1), 8, kD, false);   // I3 [j][nn]
-    mma_chain(tm + 384, op(tDl, kR, 1), op(tPsi, kD, 1), 8, kD, false); // I4 [j][m]
-    mma_chain(tm, op(tM1, kR, 0), op(tPhi, kD, 1), 8, kD, false);       // I5 [i][m]
+    mma_chain(tm, op(tM1, kR, 1), op(tFZ, kD, 1), 8, kD, true);          // d delta += M1 dY
+    mma_chain(tm + 256, op(tDl, kR, 1), op(tFS, kD, 1), 8, kD, true);    // d phi   += M2 Psi
+    mma_chain(tm + 128, op(tM3, kR, 0), op(tPhi, kD, 1), 8, kD, false);  // I5 = M3 Phi
   }
   mma_wait(sy);
   {
@@ -464,24 +420,20 @@ __global__ void __launch_bounds__(kT) k_bwd_intra_tc(Params P) {
     float* dd = own ? P.ddel + ((int64_t)n * P.T + p) * P.dv : P.hdd + (cid * e1 + (r < e - 1 ? r : 0)) * P.dv;
     float* dp = own ? P.dphiR + ((int64_t)n * P.T + p) * P.dphi : P.hdp + (cid * e1 + (r < e - 1 ? r : 0)) * P.dphi;
     float* dq = P.dpsi + ((int64_t)n * P.T + cx.t0 + (r < L ? r : 0)) * P.dphi;
-#pragma unroll
     for (int h = 0; h < kCPW; ++h) {
       const int c16 = wg * kCPW + h;
-      float i3[16], i4[16], i5[16];
-      umma::tmem_ld16(lane_addr(tm, 256 + c16 * 16), i3);
-      umma::tmem_ld16(lane_addr(tm, 384 + c16 * 16), i4);
-      umma::tmem_ld16(lane_addr(tm, c16 * 16), i5);
+      float a[16], b[16], i5[16];
+      umma::tmem_ld16(lane_addr(tm, c16 * 16), a);
+      umma::tmem_ld16(lane_addr(tm, 256 + c16 * 16), b);
+      umma::tmem_ld16(lane_addr(tm, 128 + c16 * 16), i5);
       umma::tmem_ld_wait();
-      // fire-and-forget adds onto the values k_bwd_state_tc / k_bwd_adj_tc wrote
-      if (own || halo)
-#pragma unroll
-        for (int k = 0; k < 16; k += 4) {
-          atomicAdd(reinterpret_cast<float4*>(dd + c16 * 16 + k), make_float4(i3[k], i3[k + 1], i3[k + 2], i3[k + 3]));
-          atomicAdd(reinterpret_cast<float4*>(dp + c16 * 16 + k), make_float4(i4[k], i4[k + 1], i4[k + 2], i4[k + 3]));
-        }
+      if (own || halo) {
+        st16f(dd + c16 * 16, a);
+        st16f(dp + c16 * 16, b);
+      }
       if (r < L)
 #pragma unroll
-        for (int k = 0; k < 16; k += 4)
+        for (int k = 0; k < 16; k += 4)  // onto the state part k_bwd_state_tc wrote
           atomicAdd(reinterpret_cast<float4*>(dq + c16 * 16 + k), make_float4(i5[k], i5[k + 1], i5[k + 2], i5[k + 3]));
     }
   }

@@ -61,10 +61,9 @@ def kernel_flops(name: str, w: Workload, C: int) -> float:
             fma = 2 * dv * L * dp
         elif name == "k_bwd_state_tc":
             fma = 2 * L * dp * dv + 2 * L * dv * dp
-        elif name == "k_bwd_adj_tc":
-            fma = 2 * K * dp * dv + 2 * K * dv * dp + 4 * dv * dp
-        elif name == "k_bwd_intra_tc":
-            fma = L * K * dv + L * K * dp + K * L * dv + K * L * dp + L * K * dp
+        elif name == "k_bwd_keys_tc":
+            fma = (2 * K * dp * dv + 2 * K * dv * dp + 4 * dv * dp
+                   + L * K * dv + L * K * dp + K * L * dv + K * L * dp + L * K * dp)
         elif name == "k_bwd_gates_tc":
             fma = 4 * L * K * L
         elif name == "k_bwd_grads":
