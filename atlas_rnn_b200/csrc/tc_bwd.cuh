@@ -602,7 +602,7 @@ __global__ void __launch_bounds__(kT) k_bwd_gates_tc(Params P) {
 
 // ===========================================================================
 // chunk 0 with a carried omega buffer (dense entries Buf_jb, jb < e-1), after
-// k_bwd_intra_tc and before k_bwd_gates_tc: the Gram columns of the buffer
+// k_bwd_keys_tc and before k_bwd_gates_tc: the Gram columns of the buffer
 // entries (X[F][Buf], G[q][Buf] = dy_q . Buf psi_q), their d psi terms, and the
 // buffer's own gradient dBuf_jb = wZS F_S + wZZ F_Z + sum_q wE_jb[q] dy_q psi_q^T.
 // Block GEMMs on CUDA cores, one CTA of kThreads per unit.
