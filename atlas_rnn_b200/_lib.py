@@ -10,7 +10,7 @@ import ctypes
 import os
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "libatlas_mem.so")
+LIB_PATH = os.environ.get("ATLAS_MEM_LIB") or os.path.join(_HERE, "libatlas_mem.so")
 
 FMAP = {"off": 0, "elementwise": 1, "tensor": 2}
 GATE_NONE, GATE_TOKEN, GATE_WINDOW = 0, 1, 2

@@ -116,9 +116,10 @@ Smem smem_sizes(const AtlasMemShape* s, int C) {
   m.tc_f3 = 6 * (size_t)tc::kTileBytes + 4 * (size_t)(tctx + 2 * tc::kR);
   m.buf_y = 4 * (size_t)(ctx + r4(C * (e > 1 ? e - 1 : 1)) + r4(C * dphi) + kStageFloats);
   m.tc_b1 = 3 * (size_t)tc::kTileBytes + 4 * (size_t)(tctx + 2 * tc::kR);
-  m.tc_b4 = 4 * (size_t)tc::kTileBytes + 4 * (size_t)(tctx + 3 * 132 + 4 * (tc::kT / 32) + 2 * tc::kWG * tc::kR);
+  m.tc_b4 = 6 * (size_t)tc::kTileBytes + 4 * (size_t)(tctx + 3 * 132 + 4 * (tc::kT / 32) + 2 * tc::kWG * tc::kR);
   m.tc_b6 = 6 * (size_t)tc::kTileBytes +
-            4 * (size_t)(tctx + 6 * 132 + 4 * tc::kR + 4 + tc::kR + tc::kGateParts * (tc::kWG - 1) * tc::kR);
+            4 * (size_t)(tctx + std::max(6 * 132 + 4 * tc::kR + 4 + tc::kR + tc::kGateParts * (tc::kWG - 1) * tc::kR,
+                                          3 * 132 + 2 * tc::kWG * tc::kR + 16 * tc::kR));
   m.buf_b = 4 * (size_t)(ctx + r4(C * dphi) + r4(C * dv) + 3 * r4(C * (e > 1 ? e - 1 : 1)) + 3 * r4(C + 1) + 32 +
                          kStageFloats);
   return m;
@@ -634,6 +635,20 @@ int atlas_mem_profile_read(int kernel_id, double* total_ms, long long* launches)
   if (launches) *launches = g_prof.cnt[kernel_id];
   return ATLAS_OK;
 }
+
+#ifdef ATLAS_PHASE_PROF
+// Latency-study build only (not part of the ABI header): copy out, and optionally
+// clear, the 64 phase counters of atlas::PhaseClock.
+int atlas_mem_phase_read(unsigned long long* out, int reset) {
+  cudaDeviceSynchronize();
+  if (cudaMemcpyFromSymbol(out, atlas::g_phase, sizeof(unsigned long long) * 64) != cudaSuccess) return ATLAS_ERR_LAUNCH;
+  if (reset) {
+    static const unsigned long long zero[64] = {};
+    if (cudaMemcpyToSymbol(atlas::g_phase, zero, sizeof(zero)) != cudaSuccess) return ATLAS_ERR_LAUNCH;
+  }
+  return ATLAS_OK;
+}
+#endif
 
 long long atlas_mem_launch_count(void) {
   std::lock_guard<std::mutex> lk(g_prof.mu);

@@ -180,6 +180,35 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 }
 
 // Bump allocator over dynamic shared memory (floats).
+// Phase clock for latency studies (built only with -DATLAS_PHASE_PROF): each
+// mark() closes a phase at a block-wide barrier and adds its SM-clock cycles,
+// summed over CTAs, to g_phase[slot]. Without the macro mark() is empty.
+#ifdef ATLAS_PHASE_PROF
+__device__ unsigned long long g_phase[64];
+__device__ __forceinline__ long long sm_clock() {
+  long long c;
+  asm volatile("mov.u64 %0, %%clock64;" : "=l"(c));
+  return c;
+}
+struct PhaseClock {
+  long long t;
+  __device__ PhaseClock() : t(sm_clock()) {}
+  __device__ void mark(int slot) {
+    __syncthreads();
+    const long long now = sm_clock();
+    if (threadIdx.x == 0) atomicAdd(&g_phase[slot], (unsigned long long)(now - t));
+    t = now;
+  }
+  // cycles since the last mark, added by the calling thread (no barrier)
+  __device__ void lap(int slot) { atomicAdd(&g_phase[slot], (unsigned long long)(sm_clock() - t)); }
+};
+#else
+struct PhaseClock {
+  __device__ void mark(int) {}
+  __device__ void lap(int) {}
+};
+#endif
+
 struct SmemAlloc {
   float* base;
   int off;

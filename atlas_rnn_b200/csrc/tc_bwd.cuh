@@ -140,15 +140,20 @@ __global__ void __launch_bounds__(kT) k_bwd_chunk_tc(Params P) {
 
 // ===========================================================================
 // state side: G_S = Psi S_in^T, G_Z = Psi Z_in^T (-> X[D_q][S_in], X[D_q][Z_in]),
-// H_S = dY S_in, H_Z = dY Z_in (-> d psi = sS H_S + sZ H_Z, written with '=').
+// H_S = dY S_in, H_Z = dY Z_in (-> d psi = sS H_S + sZ H_Z, written with '='),
+// and the four Gram scalars <F_S|F_Z, S_in|Z_in> from the staged tiles while
+// the MMAs run.
 // ===========================================================================
 __global__ void __launch_bounds__(kT) k_bwd_state_tc(Params P) {
+  PhaseClock pc;
   extern __shared__ __align__(1024) unsigned char sm[];
   unsigned char* tPsi = sm;
   unsigned char* tY = sm + kTileBytes;
   unsigned char* tSin = sm + 2 * kTileBytes;
   unsigned char* tZin = sm + 3 * kTileBytes;
-  SmemAlloc sa{reinterpret_cast<float*>(sm + 4 * kTileBytes), 0};
+  unsigned char* tFS = sm + 4 * kTileBytes;
+  unsigned char* tFZ = sm + 5 * kTileBytes;
+  SmemAlloc sa{reinterpret_cast<float*>(sm + 6 * kTileBytes), 0};
   __shared__ uint64_t mbar;
   __shared__ uint32_t tbase;
   Ctx cx;
@@ -156,18 +161,27 @@ __global__ void __launch_bounds__(kT) k_bwd_state_tc(Params P) {
   float* sS = sa.take(kR + 1);
   float* sZ = sa.take(kR + 1);
   float* zZ = sa.take(kR + 1);
+  float* red = sa.take(4 * (kT / 32));
   float* part = sa.take(2 * kWG * kR);  // [warpgroup][2][row] partial dot products
   const int n = cx.n, L = cx.L, tid = threadIdx.x, row = row_of(), wg = wg_of();
   Sync sy{&mbar, &tbase, 0, nullptr};
   const uint32_t tm = tc_setup(sy);
-  const int64_t D2 = (int64_t)kD * kD;
-  const unsigned char* Sin = P.stb + chunk_id(P, cx) * 2 * kTileBytes;
+  const int64_t cid = chunk_id(P, cx);
+  const unsigned char* Sin = P.stb + cid * 2 * kTileBytes;
+  const unsigned char* FS = P.adjb + cid * 2 * kTileBytes;
+  async_rows_psi(P, cx, tPsi);
+  async_rows_dy(P, cx, tY);
+  async_copy_tile(tSin, Sin);
+  async_copy_tile(tZin, Sin + kTileBytes);
+  async_copy_tile(tFS, FS);
+  async_copy_tile(tFZ, FS + kTileBytes);
   __syncthreads();
+  pc.mark(32);
   if (tid == 0) fwd_scalars(cx, sS, sZ, zZ);
-  fill_rows_psi(P, cx, tPsi, 128, kT - 128);
-  fill_rows_dy(P, cx, tY, [](int) { return 1.f; }, 128, kT - 128);
-  copy_tile(tSin, Sin, 128, kT - 128);
-  copy_tile(tZin, Sin + kTileBytes, 128, kT - 128);
+  async_wait();
+  __syncthreads();
+  phi_xform(P, tPsi);
+  pc.mark(33);
   smem_to_tc();
   if (tid == 0) {
     mma_chain(tm, op(tPsi, kD, 0), op(tSin, kD, 0), 8, kD, false);
@@ -175,7 +189,35 @@ __global__ void __launch_bounds__(kT) k_bwd_state_tc(Params P) {
     mma_chain(tm + 256, op(tY, kD, 0), op(tSin, kD, 1), 8, kD, false);
     mma_chain(tm + 384, op(tY, kD, 0), op(tZin, kD, 1), 8, kD, false);
   }
+  {  // <F_S|F_Z, S_in|Z_in>: elementwise over the raw tiles (same layout for all four)
+    float s00 = 0.f, s01 = 0.f, s10 = 0.f, s11 = 0.f;
+    for (int u = tid; u < kTileBytes / 16; u += kT) {
+      const uint4 a = reinterpret_cast<const uint4*>(tFS)[u], b = reinterpret_cast<const uint4*>(tFZ)[u];
+      const uint4 c = reinterpret_cast<const uint4*>(tSin)[u], d = reinterpret_cast<const uint4*>(tZin)[u];
+      const __nv_bfloat162* fa = reinterpret_cast<const __nv_bfloat162*>(&a);
+      const __nv_bfloat162* fb = reinterpret_cast<const __nv_bfloat162*>(&b);
+      const __nv_bfloat162* fc = reinterpret_cast<const __nv_bfloat162*>(&c);
+      const __nv_bfloat162* fd = reinterpret_cast<const __nv_bfloat162*>(&d);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 fs = __bfloat1622float2(fa[k]), fz = __bfloat1622float2(fb[k]);
+        const float2 si = __bfloat1622float2(fc[k]), zi = __bfloat1622float2(fd[k]);
+        s00 += fs.x * si.x + fs.y * si.y;
+        s01 += fs.x * zi.x + fs.y * zi.y;
+        s10 += fz.x * si.x + fz.y * si.y;
+        s11 += fz.x * zi.x + fz.y * zi.y;
+      }
+    }
+    const float v[4] = {s00, s01, s10, s11};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      float t = v[k];
+      for (int off = 16; off > 0; off >>= 1) t += __shfl_xor_sync(0xffffffffu, t, off);
+      if ((tid & 31) == 0) red[k * (kT / 32) + (tid >> 5)] = t;
+    }
+  }
   mma_wait(sy);
+  pc.mark(34);
   {
     const int q = row;
     float xs = 0.f, xz = 0.f;
@@ -208,14 +250,20 @@ __global__ void __launch_bounds__(kT) k_bwd_state_tc(Params P) {
     part[(wg * 2 + 1) * kR + q] = xz;
   }
   __syncthreads();
+  pc.mark(35);
   if (wg == 0) {
     const int q = row;
-    float* xq = P.xq + (chunk_id(P, cx) * kR + q) * 2;
+    float* xq = P.xq + (cid * kR + q) * 2;
     float a = 0.f, b = 0.f;
     for (int g = 0; g < kWG; ++g) { a += part[(2 * g) * kR + q]; b += part[(2 * g + 1) * kR + q]; }
     xq[0] = q < L ? a : 0.f;
     xq[1] = q < L ? b : 0.f;
+  } else if (wg == 1 && row < 4) {
+    float t = 0.f;
+    for (int w = 0; w < kT / 32; ++w) t += red[row * (kT / 32) + w];
+    P.xs[cid * 4 + row] = t;
   }
+  pc.mark(36);
   tc_teardown(tm);
 }
 
@@ -232,23 +280,93 @@ __device__ __forceinline__ void key_adj_weights(const Params& P, const Ctx& cx, 
   }
 }
 
+// Window weights by token and offset: Wt[i * E + k] = W(i, i + k) (zero for
+// k >= e), all threads.
+__device__ __forceinline__ int pow2_window(int e) { return e <= 1 ? 1 : e <= 2 ? 2 : e <= 4 ? 4 : e <= 8 ? 8 : 16; }
+__device__ __forceinline__ void window_weights(const Params& P, const Ctx& cx, float* Wt) {
+  const int E = pow2_window(P.e);
+  for (int x = threadIdx.x; x < cx.L * E; x += blockDim.x) {
+    const int i = x / E, k = x - i * E;
+    Wt[x] = k < P.e ? wgt(P, cx, i, i + k) : 0.f;
+  }
+}
+
+// Adjoint column of token q (the recurrence of adj_column) folded straight into
+// the window sums wE_q[j] = sum_i W(i, j) eZ_{i+1}[q], i in [j-e+1, j] cap [0, L),
+// written as row q of the bf16 tile tW (columns = keys j). E >= e is a power of
+// two: acc[k] holds key i + k while token i is processed, and key i + E - 1 is
+// complete once token i has been added. Gates and weights of 4 tokens are
+// loaded ahead of the dependent arithmetic.
+template <int E>
+__device__ __forceinline__ void adj_wE_row(const Ctx& cx, int q, unsigned char* tW, const float* Wt) {
+  constexpr int kB = 4;
+  const int L = cx.L;
+  for (int j = L + E - 1; j < kR; ++j) st_bf(tW, q, j, 0.f);
+  float acc[E];
+#pragma unroll
+  for (int k = 0; k < E; ++k) acc[k] = 0.f;
+  float es = 0.f, ez = 0.f;
+  for (int i0 = L - 1; i0 >= 0; i0 -= kB) {
+    float al[kB], be[kB], etm[kB], w[kB][E];
+#pragma unroll
+    for (int b = 0; b < kB; ++b) {
+      const int i = max(i0 - b, 0);
+      al[b] = cx.al[i];
+      be[b] = cx.be[i];
+      etm[b] = i >= 1 ? cx.et[i - 1] : 0.f;
+#pragma unroll
+      for (int k = 0; k < E; ++k) w[b][k] = Wt[i * E + k];
+    }
+#pragma unroll
+    for (int b = 0; b < kB; ++b) {
+      const int i = i0 - b;
+      if (i >= 0) {
+#pragma unroll
+        for (int k = 0; k < E; ++k) acc[k] += w[b][k] * ez;
+        if (i + E - 1 < kR) st_bf(tW, q, i + E - 1, acc[E - 1]);
+#pragma unroll
+        for (int k = E - 1; k > 0; --k) acc[k] = acc[k - 1];
+        acc[0] = 0.f;
+        es = al[b] * es + (q == i ? 1.f : 0.f);
+        ez = be[b] * ez - etm[b] * es;
+      }
+    }
+  }
+#pragma unroll
+  for (int k = 1; k < E; ++k) st_bf(tW, q, k - 1, acc[k]);
+}
+__device__ __forceinline__ void adj_wE_row_any(const Params& P, const Ctx& cx, int q, unsigned char* tW,
+                                               const float* Wt) {
+  switch (pow2_window(P.e)) {
+    case 1: adj_wE_row<1>(cx, q, tW, Wt); break;
+    case 2: adj_wE_row<2>(cx, q, tW, Wt); break;
+    case 4: adj_wE_row<4>(cx, q, tW, Wt); break;
+    case 8: adj_wE_row<8>(cx, q, tW, Wt); break;
+    default: adj_wE_row<16>(cx, q, tW, Wt); break;
+  }
+}
+
 // ===========================================================================
-// key-side backward in one pass (replaces k_bwd_adj_tc + k_bwd_intra_tc):
+// key-side backward in one pass:
 //   phase 1  P1 = Phi F_S^T, P2 = Phi F_Z^T, Q1 = delta F_S, Q2 = delta F_Z
 //            -> X[F][R_j]; d delta = wZS P1 + wZZ P2 and d phi = wZS Q1 + wZZ Q2 are
 //            written back into TMEM (tcgen05.st) over P1 and Q1
 //   phase 2  A1 = dY delta^T, A2 = Psi Phi^T -> G = A1 o A2 (scratch), M1, M2, M3
 //   phase 3  d delta += M1 dY, d phi += M2 Psi (accumulating in TMEM), I5 = M3 Phi
 //   out      d delta, d phi written once (own keys / halo partials); d psi += I5
+// Operand tiles arrive by cp.async while warpgroup 0 builds the window-summed
+// adjoint weights wE (tile tM1), warpgroup 1 the forward coefficients cS (tile
+// tM3) and one thread of warpgroup 2 the adjoint transform scalars.
 // ===========================================================================
 __global__ void __launch_bounds__(kT) k_bwd_keys_tc(Params P) {
+  PhaseClock pc;
   extern __shared__ __align__(1024) unsigned char sm[];
   unsigned char* tPhi = sm;
   unsigned char* tDl = sm + kTileBytes;       // delta, later M2
   unsigned char* tFS = sm + 2 * kTileBytes;   // F_S, later Psi
   unsigned char* tFZ = sm + 3 * kTileBytes;   // F_Z, later dY
-  unsigned char* tM3 = sm + 4 * kTileBytes;   // cS staging, later M3
-  unsigned char* tM1 = sm + 5 * kTileBytes;   // eZ staging, later M1
+  unsigned char* tM3 = sm + 4 * kTileBytes;   // cS, later M3
+  unsigned char* tM1 = sm + 5 * kTileBytes;   // wE, later M1
   SmemAlloc sa{reinterpret_cast<float*>(sm + 6 * kTileBytes), 0};
   __shared__ uint64_t mbar;
   __shared__ uint32_t tbase;
@@ -257,27 +375,40 @@ __global__ void __launch_bounds__(kT) k_bwd_keys_tc(Params P) {
   float* hS = sa.take(kR + 1);
   float* hZS = sa.take(kR + 1);
   float* hZZ = sa.take(kR + 1);
-  float* red = sa.take(4 * (kT / 32));
   float* part = sa.take(2 * kWG * kR);
+  float* Wt = sa.take(kR * 16);
   const int n = cx.n, K = cx.K, L = cx.L, tid = threadIdx.x, e = P.e, row = row_of(), wg = wg_of();
   Sync sy{&mbar, &tbase, 0, nullptr};
   const uint32_t tm = tc_setup(sy);
   const int64_t cid = chunk_id(P, cx);
   const unsigned char* FS = P.adjb + cid * 2 * kTileBytes;
-  const unsigned char* Sin = P.stb + cid * 2 * kTileBytes;
+  async_keys_phi(P, cx, tPhi);
+  async_keys_delta(P, cx, tDl);
+  async_copy_tile(tFS, FS);
+  async_copy_tile(tFZ, FS + kTileBytes);
+  __syncthreads();  // gates of load_ctx visible
+  window_weights(P, cx, Wt);
   __syncthreads();
-  // loads (all but warpgroup 0) and staging columns (warpgroup 0: eZ column q, then cS column j)
-  fill_keys_phi(P, cx, tPhi, 128, kT - 128);
-  fill_keys_delta(P, cx, tDl, 128, kT - 128);
-  copy_tile(tFS, FS, 128, kT - 128);
-  copy_tile(tFZ, FS + kTileBytes, 128, kT - 128);
+  pc.mark(0);
   if (wg == 0) {
-    adj_column(cx, row, [&](int i, float, float ez) { st_bf(tM1, i, row, ez); });
-    for (int i = L; i < kR; ++i) st_bf(tM1, i, row, 0.f);
+    adj_wE_row_any(P, cx, row, tM1, Wt);
+    if (row == 0) pc.lap(11);
+  } else if (wg == 1) {
     fwd_column(P, cx, row, [&](int i, float cs, float, float) { st_bf(tM3, i, row, cs); });
     for (int i = L; i < kR; ++i) st_bf(tM3, i, row, 0.f);
-    if (row == 0) adj_scalars(cx, hS, hZS, hZZ);
+    if (row == 0) pc.lap(12);
+  } else if (wg == 2 && row == 0) {
+    adj_scalars(cx, hS, hZS, hZZ);
+    pc.lap(13);
   }
+  async_wait();
+  if (tid == 384) pc.lap(14);
+  if (wg > 0) {
+    loaders_sync();
+    phi_xform(P, tPhi, 128, kT - 128);
+    if (tid == 384) pc.lap(15);
+  }
+  pc.mark(1);
   smem_to_tc();
   if (tid == 0) {
     mma_chain(tm, op(tPhi, kD, 0), op(tFS, kD, 0), 8, kD, false);        // P1
@@ -285,52 +416,10 @@ __global__ void __launch_bounds__(kT) k_bwd_keys_tc(Params P) {
     mma_chain(tm + 256, op(tDl, kD, 0), op(tFS, kD, 1), 8, kD, false);  // Q1
     mma_chain(tm + 384, op(tDl, kD, 0), op(tFZ, kD, 1), 8, kD, false);  // Q2
   }
-  // the four Gram scalars <F_S|F_Z, S_in|Z_in> while the MMAs run (raw bf16 tiles)
-  {
-    float s00 = 0.f, s01 = 0.f, s10 = 0.f, s11 = 0.f;
-    for (int u = tid; u < kTileBytes / 16; u += kT) {
-      const uint4 a = reinterpret_cast<const uint4*>(FS)[u], b = reinterpret_cast<const uint4*>(FS + kTileBytes)[u];
-      const uint4 c = reinterpret_cast<const uint4*>(Sin)[u], d = reinterpret_cast<const uint4*>(Sin + kTileBytes)[u];
-      const __nv_bfloat162* fa = reinterpret_cast<const __nv_bfloat162*>(&a);
-      const __nv_bfloat162* fb = reinterpret_cast<const __nv_bfloat162*>(&b);
-      const __nv_bfloat162* fc = reinterpret_cast<const __nv_bfloat162*>(&c);
-      const __nv_bfloat162* fd = reinterpret_cast<const __nv_bfloat162*>(&d);
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const float2 fs = __bfloat1622float2(fa[k]), fz = __bfloat1622float2(fb[k]);
-        const float2 si = __bfloat1622float2(fc[k]), zi = __bfloat1622float2(fd[k]);
-        s00 += fs.x * si.x + fs.y * si.y;
-        s01 += fs.x * zi.x + fs.y * zi.y;
-        s10 += fz.x * si.x + fz.y * si.y;
-        s11 += fz.x * zi.x + fz.y * zi.y;
-      }
-    }
-    const float v[4] = {s00, s01, s10, s11};
-    for (int k = 0; k < 4; ++k) {
-      float t = v[k];
-      for (int off = 16; off > 0; off >>= 1) t += __shfl_xor_sync(0xffffffffu, t, off);
-      if ((tid & 31) == 0) red[k * (kT / 32) + (tid >> 5)] = t;
-    }
-    __syncthreads();
-    if (tid < 4) {
-      float t = 0.f;
-      for (int w = 0; w < kT / 32; ++w) t += red[tid * (kT / 32) + w];
-      P.xs[cid * 4 + tid] = t;
-    }
-  }
-  // window-summed adjoint coefficients of row q for this warpgroup's keys (from the eZ staging)
-  float wE[kR / kWG];
-  {
-    const int q = row, j0 = wg * (kR / kWG);
-#pragma unroll 4
-    for (int jj = 0; jj < kR / kWG; ++jj) {
-      const int j = j0 + jj;
-      float acc = 0.f;
-      for (int i = max(0, j - e + 1); i <= min(L - 1, j); ++i) acc += wgt(P, cx, i, j) * bf_at(tM1, i, q);
-      wE[jj] = q < L ? acc : 0.f;
-    }
-  }
   mma_wait(sy);
+  pc.mark(4);
+  async_rows_psi(P, cx, tFS);  // F tiles are free once the phase-1 MMAs are done
+  async_rows_dy(P, cx, tFZ);
   {  // phase-1 epilogue, row j: X[F][R_j]; F parts of d delta / d phi back into TMEM
     const int j = row;
     float wzs, wzz;
@@ -361,7 +450,8 @@ __global__ void __launch_bounds__(kT) k_bwd_keys_tc(Params P) {
     part[(wg * 2 + 1) * kR + j] = xZ;
   }
   umma::fence_before();
-  __syncthreads();  // F tiles and the P2 / Q2 columns are free
+  async_wait();
+  __syncthreads();  // psi / dY rows landed; P2 / Q2 columns are free
   if (wg == 0) {
     float a = 0.f, b = 0.f;
     for (int g = 0; g < kWG; ++g) { a += part[(2 * g) * kR + row]; b += part[(2 * g + 1) * kR + row]; }
@@ -369,14 +459,15 @@ __global__ void __launch_bounds__(kT) k_bwd_keys_tc(Params P) {
     xf[0] = row < K ? a : 0.f;
     xf[1] = row < K ? b : 0.f;
   }
-  fill_rows_psi(P, cx, tFS);
-  fill_rows_dy(P, cx, tFZ, [](int) { return 1.f; });
+  phi_xform(P, tFS);
+  pc.mark(6);
   smem_to_tc();
   if (tid == 0) {
     mma_chain(tm + 128, op(tFZ, kD, 0), op(tDl, kD, 0), 8, kR, false);   // A1[q][j] = dY delta^T
     mma_chain(tm + 384, op(tFS, kD, 0), op(tPhi, kD, 0), 8, kR, false);  // A2[q][j] = Psi Phi^T
   }
   mma_wait(sy);
+  pc.mark(7);
   {  // phase-2 epilogue, row q: G, M3 = cS o A1, M1 = wE o A2^T, M2 = wE o A1^T
     const int q = row;
     unsigned char* gdst = reinterpret_cast<unsigned char*>(P.gt) + cid * kTileBytes;
@@ -389,23 +480,25 @@ __global__ void __launch_bounds__(kT) k_bwd_keys_tc(Params P) {
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const int cb = 2 * c16 + h;
-        float g[8], c3[8], m1[8], m2[8];
+        float g[8], c3[8], w[8], m2[8];
         load_unit(tM3, q, cb, kR, c3);
+        load_unit(tM1, q, cb, kR, w);
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
-          const float x1 = a1[8 * h + k], x2 = a2[8 * h + k], w = wE[8 * (2 * h4 + h) + k];
+          const float x1 = a1[8 * h + k], x2 = a2[8 * h + k];
           g[k] = x1 * x2;
           c3[k] *= x1;
-          m2[k] = w * x1;
-          m1[k] = w * x2;
+          m2[k] = w[k] * x1;
+          w[k] *= x2;  // M1
         }
         store_unit(gdst, q, cb, kR, g);
         store_unit(tM3, q, cb, kR, c3);
         store_unit(tDl, q, cb, kR, m2);  // delta no longer needed
-        store_unit(tM1, q, cb, kR, m1);  // eZ staging already read into wE
+        store_unit(tM1, q, cb, kR, w);
       }
     }
   }
+  pc.mark(8);
   smem_to_tc();
   if (tid == 0) {
     mma_chain(tm, op(tM1, kR, 1), op(tFZ, kD, 1), 8, kD, true);          // d delta += M1 dY
@@ -413,6 +506,7 @@ __global__ void __launch_bounds__(kT) k_bwd_keys_tc(Params P) {
     mma_chain(tm + 128, op(tM3, kR, 0), op(tPhi, kD, 1), 8, kD, false);  // I5 = M3 Phi
   }
   mma_wait(sy);
+  pc.mark(9);
   {
     const int r = row, p = cx.kp0 + r;
     const bool own = r < K && p >= cx.t0, halo = r < K && p >= 0 && p < cx.t0;
@@ -437,6 +531,7 @@ __global__ void __launch_bounds__(kT) k_bwd_keys_tc(Params P) {
           atomicAdd(reinterpret_cast<float4*>(dq + c16 * 16 + k), make_float4(i5[k], i5[k + 1], i5[k + 2], i5[k + 3]));
     }
   }
+  pc.mark(10);
   tc_teardown(tm);
 }
 
@@ -450,6 +545,7 @@ __global__ void __launch_bounds__(kT) k_bwd_keys_tc(Params P) {
 // ===========================================================================
 constexpr int kGateParts = 10;
 __global__ void __launch_bounds__(kT) k_bwd_gates_tc(Params P) {
+  PhaseClock pc;
   extern __shared__ __align__(1024) unsigned char sm[];
   unsigned char* tG = sm;
   unsigned char* tCS = sm + kTileBytes;       // cS_i[j]     (state before token i)
@@ -479,6 +575,7 @@ __global__ void __launch_bounds__(kT) k_bwd_gates_tc(Params P) {
   const uint32_t tm = tc_setup(sy);
   const int64_t cid = chunk_id(P, cx);
   __syncthreads();
+  pc.mark(24);
   if (wg >= 2) {
     const int me = tid - kFillFirst;
     const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const unsigned char*>(P.gt) + cid * kTileBytes);
@@ -509,6 +606,7 @@ __global__ void __launch_bounds__(kT) k_bwd_gates_tc(Params P) {
     for (int i = L; i < kR; ++i) { st_bf(tES, i, q, 0.f); st_bf(tEZ, i, q, 0.f); }
     if (row == 0) adj_scalars(cx, hS, hZS, hZZ);
   }
+  pc.mark(25);
   smem_to_tc();
   if (tid == 0) {
     mma_chain(tm, op(tCS, kR, 0), op(tG, kR, 0), 8, kR, false);         // W_a[i][q]
@@ -517,6 +615,7 @@ __global__ void __launch_bounds__(kT) k_bwd_gates_tc(Params P) {
     mma_chain(tm + 384, op(tEZ, kR, 0), op(tG, kR, 1), 8, kR, false);   // E_Z+ G [i][j]
   }
   mma_wait(sy);
+  pc.mark(26);
   const int i = row;
   float acc[kGateParts];
 #pragma unroll
@@ -557,6 +656,7 @@ __global__ void __launch_bounds__(kT) k_bwd_gates_tc(Params P) {
   if (wg >= 1)
 #pragma unroll
     for (int k = 0; k < kGateParts; ++k) part[((wg - 1) * kGateParts + k) * kR + i] = acc[k];
+  pc.mark(27);
   // window weights dW(i, j) = hZS_{i+1} X[F_S][R_j] + hZZ_{i+1} X[F_Z][R_j] + (E_Z+ G)[i][j]
   if (P.gmode != ATLAS_GATE_NONE) {
 #pragma unroll
@@ -579,6 +679,7 @@ __global__ void __launch_bounds__(kT) k_bwd_gates_tc(Params P) {
     }
   }
   __syncthreads();
+  pc.mark(28);
   if (wg == 0 && i < L) {
     for (int g = 1; g < kWG; ++g)
 #pragma unroll
@@ -597,7 +698,8 @@ __global__ void __launch_bounds__(kT) k_bwd_gates_tc(Params P) {
     if (j < K && p >= cx.t0) P.du[(int64_t)n * P.T + p] = duj[j];
     else if (j < K && p >= 0) P.hdu[cid * (e - 1) + j] = duj[j];
   }
-  tc_teardown(tm);
+  tc_teardown(tm);  pc.mark(29);
+
 }
 
 // ===========================================================================

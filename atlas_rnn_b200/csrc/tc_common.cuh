@@ -182,6 +182,59 @@ __device__ __forceinline__ void fill_rows_raw(unsigned char* tile, F rowp, int f
     }
   }
 }
+// ---------------------------------------------------------------------------
+// Asynchronous tile loads (cp.async, 16 bytes, L2 only). Every thread issues
+// its copies without waiting, so a whole tile set is in flight at once; a zero
+// unit is a copy of 0 source bytes (the destination is zero-filled). The
+// caller ends the set with async_wait() (own copies) and a block barrier, and
+// may then rewrite units in place (feature map, row scaling) before the MMA.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void cp16(void* dst_smem, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(umma::smem_u32(dst_smem)), "l"(src),
+               "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void async_wait() {
+  asm volatile("cp.async.commit_group;\n" ::: "memory");
+  asm volatile("cp.async.wait_all;\n" ::: "memory");
+}
+// A 32 KB tile already in the core-matrix layout.
+__device__ __forceinline__ void async_copy_tile(unsigned char* tile, const unsigned char* src, int first = 0,
+                                                int count = kT) {
+  const int me = (int)threadIdx.x - first;
+  if (me < 0 || me >= count) return;
+  for (int u = me; u < kTileBytes / 16; u += count) cp16(tile + 16 * u, src + 16 * u, true);
+}
+// Rows of a bf16 row-major [*, 128] matrix: rowp(r) is row r or nullptr (zero row).
+// `base` is any valid global address (the source operand of a zero-filled copy).
+template <class F>
+__device__ __forceinline__ void async_rows(unsigned char* tile, F rowp, const void* base, int first = 0,
+                                           int count = kT) {
+  constexpr int kCpr = kD / 8;
+  const int me = (int)threadIdx.x - first;
+  if (me < 0 || me >= count) return;
+  for (int u = me; u < kTileBytes / 16; u += count) {
+    const int r = u / kCpr, cb = u % kCpr;
+    const __nv_bfloat16* row = rowp(r);
+    cp16(tile + umma::unit_off(r, cb, kD), row ? static_cast<const void*>(row + cb * 8) : base, row != nullptr);
+  }
+}
+// Rewrite every unit of rows [0, rows) in place: f(r, v[8]) (after the barrier
+// that follows async_wait()).
+template <class F>
+__device__ __forceinline__ void xform_rows(unsigned char* tile, int rows, F f, int first = 0, int count = kT) {
+  constexpr int kCpr = kD / 8;
+  const int me = (int)threadIdx.x - first;
+  if (me < 0 || me >= count) return;
+  for (int u = me; u < rows * kCpr; u += count) {
+    const int r = u / kCpr, cb = u % kCpr;
+    float v[8];
+    load_unit(tile, r, cb, kD, v);
+    f(r, v);
+    store_unit(tile, r, cb, kD, v);
+  }
+}
+
 __device__ __forceinline__ float bf_at(const unsigned char* tile, int r, int c) {
   return __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(tile + umma::elem_off(r, c, kD)));
 }

@@ -81,6 +81,52 @@ __device__ __forceinline__ void fill_rows_psi(const Params& P, const Ctx& cx, un
     else zero8(v);
   }, first, count);
 }
+// Asynchronous forms: raw bf16 k / q rows (cp.async), then phi_xform() applies
+// the elementwise feature map in place after async_wait() and a barrier. With
+// the tensor feature map (fp32 phi buffers) the rows are converted synchronously.
+__device__ __forceinline__ void async_keys_phi(const Params& P, const Ctx& cx, unsigned char* tile, int first = 0,
+                                               int count = kT) {
+  if (P.fmode == ATLAS_FMAP_TENSOR) { fill_keys_phi(P, cx, tile, first, count); return; }
+  const __nv_bfloat16* k = reinterpret_cast<const __nv_bfloat16*>(P.k);
+  async_rows(tile, [&](int r) -> const __nv_bfloat16* {
+    const int p = cx.kp0 + r;
+    return (r < cx.K && p >= 0) ? k + ((int64_t)cx.n * P.T + p) * P.dk : nullptr;
+  }, P.k, first, count);
+}
+__device__ __forceinline__ void async_rows_psi(const Params& P, const Ctx& cx, unsigned char* tile, int first = 0,
+                                               int count = kT) {
+  if (P.fmode == ATLAS_FMAP_TENSOR) { fill_rows_psi(P, cx, tile, first, count); return; }
+  const __nv_bfloat16* q = reinterpret_cast<const __nv_bfloat16*>(P.q);
+  async_rows(tile, [&](int r) -> const __nv_bfloat16* {
+    return r < cx.L ? q + ((int64_t)cx.n * P.T + cx.t0 + r) * P.dk : nullptr;
+  }, P.q, first, count);
+}
+__device__ __forceinline__ void phi_xform(const Params& P, unsigned char* tile, int first = 0, int count = kT) {
+  if (P.fmode != ATLAS_FMAP_ELEMENTWISE || P.fdeg <= 1) return;
+  xform_rows(tile, kR, [&](int, float(&v)[8]) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = fmap_elem(v[i], P.fmode, P.fdeg);
+  }, first, count);
+}
+// Rows of the bf16 delta buffer for the chunk's keys (zero for p < 0, rows >= K).
+__device__ __forceinline__ void async_keys_delta(const Params& P, const Ctx& cx, unsigned char* tile, int first = 0,
+                                                 int count = kT) {
+  async_rows(tile, [&](int r) -> const __nv_bfloat16* {
+    const int p = cx.kp0 + r;
+    return (r < cx.K && p >= 0) ? P.dlb + ((int64_t)cx.n * P.T + p) * P.dv : nullptr;
+  }, P.dlb, first, count);
+}
+// Token rows of dy (bf16; zero for rows >= L).
+__device__ __forceinline__ void async_rows_dy(const Params& P, const Ctx& cx, unsigned char* tile, int first = 0,
+                                              int count = kT) {
+  const __nv_bfloat16* dy = reinterpret_cast<const __nv_bfloat16*>(P.dy);
+  async_rows(tile, [&](int r) -> const __nv_bfloat16* {
+    return r < cx.L ? dy + ((int64_t)cx.n * P.T + cx.t0 + r) * P.dv : nullptr;
+  }, P.dy, first, count);
+}
+// Named barrier over warpgroups 1..kWG-1 (the loaders while warpgroup 0 is busy).
+__device__ __forceinline__ void loaders_sync() { asm volatile("bar.sync 1, %0;\n" ::"n"(kT - 128) : "memory"); }
+
 // A dense fp32 [128 x 128] row-major matrix into a tile.
 __device__ __forceinline__ void fill_dense(unsigned char* tile, const float* M, int first = 0, int count = kT) {
   fill_tile(tile, kD, [&](int r, int c0, float(&v)[8]) { ld8f(M + r * kD + c0, v); }, first, count);
@@ -211,6 +257,7 @@ __global__ void __launch_bounds__(kT) k_fwd_chunk_tc(Params P) {
 // (chunk 0 with a carried buffer adds its dense terms in k_fwd_buf_y).
 // ===========================================================================
 __global__ void __launch_bounds__(kT) k_fwd_out_tc(Params P) {
+  PhaseClock pc;
   extern __shared__ __align__(1024) unsigned char sm[];
   unsigned char* tPsi = sm;
   unsigned char* tPhi = sm + kTileBytes;
@@ -228,6 +275,7 @@ __global__ void __launch_bounds__(kT) k_fwd_out_tc(Params P) {
   const int n = cx.n, c = cx.c, K = cx.K, L = cx.L, tid = threadIdx.x, row = row_of(), wg = wg_of();
   Sync sy{&mbar, &tbase, 0, nullptr};
   const uint32_t tm = tc_setup(sy);
+  pc.mark(16);
   const unsigned char* Sin = P.stb + ((int64_t)n * P.nch + c) * 2 * kTileBytes;
   fill_rows_psi(P, cx, tPsi);
   fill_keys_phi(P, cx, tPhi);
@@ -238,6 +286,7 @@ __global__ void __launch_bounds__(kT) k_fwd_out_tc(Params P) {
   copy_tile(tSin, Sin);
   copy_tile(tZin, Sin + kTileBytes);
   __syncthreads();
+  pc.mark(17);
   if (wg == 0) {  // column j = row of tMs: cS of key j before each token i
     const int j = row;
     fwd_column(P, cx, j, [&](int i, float cs, float, float) { st_bf(tMs, i, j, cs); });
@@ -252,6 +301,7 @@ __global__ void __launch_bounds__(kT) k_fwd_out_tc(Params P) {
       sz = cx.al[i] * sz - cx.et[i] * z;
     }
   }
+  pc.mark(18);
   smem_to_tc();
   if (tid == 0) {
     mma_chain(tm, op(tPsi, kD, 0), op(tPhi, kD, 0), kD / 16, kR, false);          // A2 = Psi Phi^T
@@ -259,6 +309,7 @@ __global__ void __launch_bounds__(kT) k_fwd_out_tc(Params P) {
     mma_chain(tm + 256, op(tPsi, kD, 0), op(tZin, kD, 0), kD / 16, kD, false);    // Psi Z_in^T
   }
   mma_wait(sy);
+  pc.mark(19);
 #pragma unroll
   for (int h = 0; h < kCPW; ++h) {  // Ms = cS o A2 (row `row`, this warpgroup's columns)
     const int c16 = wg * kCPW + h;
@@ -272,9 +323,11 @@ __global__ void __launch_bounds__(kT) k_fwd_out_tc(Params P) {
     store_unit(tMs, row, 2 * c16, kR, m0);
     store_unit(tMs, row, 2 * c16 + 1, kR, m1);
   }
+  pc.mark(20);
   smem_to_tc();
   if (tid == 0) mma_chain(tm + 384, op(tMs, kR, 0), op(tDl, kD, 1), 8, kD, false);
   mma_wait(sy);
+  pc.mark(21);
   {
     const int i = row;
     const float ss = i < L ? sSv[i] : 0.f, sz = i < L ? sZv[i] : 0.f;
@@ -293,7 +346,8 @@ __global__ void __launch_bounds__(kT) k_fwd_out_tc(Params P) {
       }
     }
   }
-  tc_teardown(tm);
+  tc_teardown(tm);  pc.mark(22);
+
 }
 
 // Chunk 0 with a carried buffer: y_i += sum_jb cS_i[jb] Buf_jb psi_i (dense
