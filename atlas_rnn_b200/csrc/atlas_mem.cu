@@ -44,7 +44,7 @@ int chunk_of(const AtlasMemShape* s) {
 struct Layout {
   int C, nch;
   size_t saved, fwd, bwd;
-  size_t st, delta, ST, cs, phik, phiq, dlb, stb;              // in saved
+  size_t st, delta, ST, cs, phik, phiq, dlb, stb, srb;         // in saved
   size_t adj, acs, dpsi, ddel, dphiR, hdd, hdp, du, hdu;       // in bwd scratch
   size_t xq, xf, xs, gt, adjb;                                  // in bwd scratch (tensor-core path)
 };
@@ -63,6 +63,7 @@ Layout make_layout(const AtlasMemShape* s) {
   L.delta = tcm ? 0 : put(N * T * s->d_v * 4);
   L.dlb = tcm ? put(N * T * s->d_v * 2) : 0;
   L.stb = tcm ? put(N * nch * 2 * (size_t)tc::kTileBytes) : 0;
+  L.srb = tcm ? put(N * (size_t)tc::kTileBytes) : 0;
   L.ST = put(N * D2 * 4);
   L.cs = put(N * nch * 4 * 4);
   L.phik = tens ? put(N * T * s->d_phi * 4) : 0;
@@ -225,6 +226,7 @@ Params make_params(const AtlasMemShape* s, const Layout& L, const AtlasMemFwd* f
   P.delta = tcm ? nullptr : (float*)(sv + L.delta);
   P.dlb = tcm ? (__nv_bfloat16*)(sv + L.dlb) : nullptr;
   P.stb = tcm ? (unsigned char*)(sv + L.stb) : nullptr;
+  P.srb = tcm ? (unsigned char*)(sv + L.srb) : nullptr;
   P.inc_bf16 = tcm ? 1 : 0;
   P.cs = (float*)(sv + L.cs);
   P.phik = s->fmap_mode == ATLAS_FMAP_TENSOR ? (float*)(sv + L.phik) : nullptr;
@@ -247,12 +249,12 @@ Params make_params(const AtlasMemShape* s, const Layout& L, const AtlasMemFwd* f
 enum KernelId {
   KID_FMAP_FWD, KID_FWD_CHUNK, KID_FWD_SCAN, KID_FWD_OUT, KID_BUF_OUT, KID_BWD_CHUNK, KID_BWD_SCAN,
   KID_BWD_GRADS, KID_BWD_BUFOUT, KID_BWD_FINAL, KID_BWD_DSREF, KID_FMAP_BWD, KID_FWD_CHUNK_TC, KID_FWD_OUT_TC, KID_FWD_BUF_Y,
-  KID_BWD_CHUNK_TC, KID_BWD_STATE_TC, KID_BWD_BUF_TC, KID_BWD_GATES_TC, KID_BWD_FINAL_TC, KID_BWD_DSREF_TC, KID_BWD_KEYS_TC, KID_COUNT
+  KID_BWD_CHUNK_TC, KID_BWD_STATE_TC, KID_BWD_BUF_TC, KID_BWD_GATES_TC, KID_BWD_FINAL_TC, KID_BWD_DSREF_TC, KID_BWD_KEYS_TC, KID_SREF_TILE, KID_COUNT
 };
 const char* const kKernelNames[KID_COUNT] = {
   "k_fmap_tensor_fwd", "k_fwd_chunk", "k_fwd_scan", "k_fwd_out", "k_buf_out", "k_bwd_chunk", "k_bwd_scan",
   "k_bwd_grads", "k_bwd_bufout", "k_bwd_finalize", "k_bwd_dsref", "k_fmap_tensor_bwd", "k_fwd_chunk_tc", "k_fwd_out_tc", "k_fwd_buf_y",
-  "k_bwd_chunk_tc", "k_bwd_state_tc", "k_bwd_buf_tc", "k_bwd_gates_tc", "k_bwd_finalize_tc", "k_bwd_dsref_tc", "k_bwd_keys_tc"};
+  "k_bwd_chunk_tc", "k_bwd_state_tc", "k_bwd_buf_tc", "k_bwd_gates_tc", "k_bwd_finalize_tc", "k_bwd_dsref_tc", "k_bwd_keys_tc", "k_sref_tile"};
 
 constexpr int kMaxTimed = 8192;
 struct Prof {
@@ -341,7 +343,10 @@ int run_fwd_local(const AtlasMemShape* s, const Params& P, cudaStream_t st) {
   if (P.fmode == ATLAS_FMAP_TENSOR) {
     LAUNCH(KID_FMAP_FWD, k_fmap_tensor_fwd, dim3((P.T + kFmTile - 1) / kFmTile, P.N, 2), m.fmf, st, P);
   }
-  if (tc_groups(s) & 1) LAUNCH_T(KID_FWD_CHUNK_TC, tc::k_fwd_chunk_tc, gch, tc::kT, m.tc_f1, st, P);
+  if (tc_groups(s) & 1) {
+    LAUNCH(KID_SREF_TILE, tc::k_sref_tile, dim3(P.N), 0, st, P);
+    LAUNCH_T(KID_FWD_CHUNK_TC, tc::k_fwd_chunk_tc, gch, tc::kT, m.tc_f1, st, P);
+  }
   else LAUNCH(KID_FWD_CHUNK, k_fwd_chunk, gch, m.f1, st, P);
   return ATLAS_OK;
 }

@@ -20,14 +20,18 @@ struct Ctx {
   float *al, *et, *be, *u, *U;
 };
 
-__device__ __forceinline__ void load_ctx(const Params& P, SmemAlloc& sa, Ctx& cx, int nthreads = kThreads,
-                                         int chunk = -1) {
+// Geometry of the chunk (unit n = blockIdx.y, chunk c = blockIdx.x unless given).
+__device__ __forceinline__ void ctx_geom(const Params& P, Ctx& cx, int chunk = -1) {
   cx.n = blockIdx.y;
   cx.c = chunk >= 0 ? chunk : blockIdx.x;
   cx.t0 = cx.c * P.C;
   cx.L = min(P.C, P.T - cx.t0);
   cx.K = cx.L + P.e - 1;
   cx.kp0 = cx.t0 - (P.e - 1);
+}
+__device__ __forceinline__ void load_ctx(const Params& P, SmemAlloc& sa, Ctx& cx, int nthreads = kThreads,
+                                         int chunk = -1) {
+  ctx_geom(P, cx, chunk);
   cx.al = sa.take(P.C);
   cx.et = sa.take(P.C);
   cx.be = sa.take(P.C);

@@ -44,6 +44,7 @@ struct Params {
   // tensor-core path: bf16 copies the chunk kernels read as raw 16-byte units
   __nv_bfloat16* dlb;   // [N][T][dv] delta (replaces `delta`)
   unsigned char* stb;   // [N][nch][2] 128x128 bf16 tiles of the chunk-start S, Z
+  unsigned char* srb;   // [N] S_ref as a 128x128 bf16 operand tile
   unsigned char* adjb;  // [N][nch][2] 128x128 bf16 tiles of the adjoint at each chunk end
   int inc_bf16;         // chunk increments in `st` / `adj` are bf16 (tensor-core path)
   void* gt;             // [N][nch] 128x128 bf16 Gram blocks (core-matrix tile layout)

@@ -82,25 +82,20 @@ __global__ void __launch_bounds__(kT) k_bwd_chunk_tc(Params P) {
   __shared__ uint64_t mbar;
   __shared__ uint32_t tbase;
   Ctx cx;
+  ctx_geom(P, cx);
+  async_rows_psi(P, cx, tPsi);
+  async_rows_dy(P, cx, tYS);
   load_ctx(P, sa, cx, kT);
   float* eS0 = sa.take(kR);
   float* eZ0 = sa.take(kR);
   const int L = cx.L, tid = threadIdx.x, row = row_of(), wg = wg_of();
   Sync sy{&mbar, &tbase, 0, nullptr};
   const uint32_t tm = tc_setup(sy, 256);
-  fill_rows_psi(P, cx, tPsi);
-  __syncthreads();
-  if (wg == 0) {
-    const int q = row;
+  if (wg == 0) {  // adjoint weights of token q at the chunk input
     float es = 0.f, ez = 0.f;
-    if (q < L)
-      for (int r = L - 1; r >= 0; --r) {
-        const float eta = r >= 1 ? cx.et[r - 1] : 0.f;
-        es = cx.al[r] * es + (q == r ? 1.f : 0.f);
-        ez = cx.be[r] * ez - eta * es;
-      }
-    eS0[q] = es;
-    eZ0[q] = ez;
+    adj_column(cx, row, [](int, float, float) {}, &es, &ez);
+    eS0[row] = es;
+    eZ0[row] = ez;
   } else if (wg == 1 && row == 0) {
     float hs = 1.f, hzs = -cx.et[L - 1], hzz = 1.f;
     for (int r = L - 1; r >= 0; --r) {
@@ -112,9 +107,22 @@ __global__ void __launch_bounds__(kT) k_bwd_chunk_tc(Params P) {
     float* o = P.acs + chunk_id(P, cx) * 4;
     o[0] = hs; o[1] = hzs; o[2] = hzz; o[3] = 0.f;
   }
+  async_wait();
   __syncthreads();
-  fill_rows_dy(P, cx, tYS, [&](int r) { return eS0[r]; });
-  fill_rows_dy(P, cx, tYZ, [&](int r) { return eZ0[r]; });
+  {  // dY rows scaled by eS0 (in place) and by eZ0 (into tYZ); psi feature map
+    constexpr int kCpr = kD / 8;
+    for (int u = tid; u < kR * kCpr; u += kT) {
+      const int r = u / kCpr, cb = u % kCpr;
+      float v[8], z[8];
+      load_unit(tYS, r, cb, kD, v);
+      const float a = eS0[r], b = eZ0[r];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) { z[k] = b * v[k]; v[k] *= a; }
+      store_unit(tYS, r, cb, kD, v);
+      store_unit(tYZ, r, cb, kD, z);
+    }
+    phi_xform(P, tPsi);
+  }
   smem_to_tc();
   if (tid == 0) {
     mma_chain(tm, op(tYS, kD, 1), op(tPsi, kD, 1), 8, kD, false);
@@ -557,6 +565,9 @@ __global__ void __launch_bounds__(kT) k_bwd_gates_tc(Params P) {
   __shared__ uint64_t mbar;
   __shared__ uint32_t tbase;
   Ctx cx;
+  ctx_geom(P, cx);
+  const int64_t cid = chunk_id(P, cx);
+  async_copy_tile(tG, reinterpret_cast<const unsigned char*>(P.gt) + cid * kTileBytes);
   load_ctx(P, sa, cx, kT);
   float* sS = sa.take(kR + 1);
   float* sZ = sa.take(kR + 1);
@@ -571,23 +582,16 @@ __global__ void __launch_bounds__(kT) k_bwd_gates_tc(Params P) {
   float* part = sa.take(kGateParts * (kWG - 1) * kR);  // partial sums of warpgroups 1..
 
   const int n = cx.n, K = cx.K, L = cx.L, tid = threadIdx.x, e = P.e, row = row_of(), wg = wg_of();
-  Sync sy{&mbar, &tbase, 0, nullptr};
-  const uint32_t tm = tc_setup(sy);
-  const int64_t cid = chunk_id(P, cx);
-  __syncthreads();
-  pc.mark(24);
-  if (wg >= 2) {
-    const int me = tid - kFillFirst;
-    const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const unsigned char*>(P.gt) + cid * kTileBytes);
-    uint4* dst = reinterpret_cast<uint4*>(tG);
-    for (int u = me; u < kTileBytes / 16; u += kFillCount) dst[u] = src[u];
-    if (me < 2 * kR) {
-      xq[me] = P.xq[cid * 2 * kR + me];
-      xf[me] = P.xf[cid * 2 * kR + me];
-    }
-    if (me < 4) xs[me] = P.xs[cid * 4 + me];
-    if (me < kR) duj[me] = 0.f;
+  if (tid < 2 * kR / 4) {
+    cp16(xq + 4 * tid, P.xq + cid * 2 * kR + 4 * tid, true);
+    cp16(xf + 4 * tid, P.xf + cid * 2 * kR + 4 * tid, true);
+  } else if (tid == 2 * kR / 4) {
+    cp16(xs, P.xs + cid * 4, true);
   }
+  if (tid < kR) duj[tid] = 0.f;
+  Sync sy{&mbar, &tbase, 0, nullptr};
+  const uint32_t tm = tc_setup(sy);  // (its barrier also publishes the gates)
+  pc.mark(24);
   if (wg == 0) {
     const int j = row;  // forward coefficients of key j (column j of tCS, tCZp, tCZn)
     fwd_column(P, cx, j, [&](int i, float cs, float cz, float czn) {
@@ -596,7 +600,6 @@ __global__ void __launch_bounds__(kT) k_bwd_gates_tc(Params P) {
       st_bf(tCZn, i, j, czn);
     });
     for (int i = L; i < kR; ++i) { st_bf(tCS, i, j, 0.f); st_bf(tCZp, i, j, 0.f); st_bf(tCZn, i, j, 0.f); }
-    if (row == 0) fwd_scalars(cx, sS, sZ, zZ);
   } else if (wg == 1) {
     const int q = row;  // adjoint coefficients of token q (column q of tES, tEZ): rows i <- eS_{i+1}, eZ_{i+1}
     adj_column(cx, q, [&](int i, float es, float ez) {
@@ -604,8 +607,12 @@ __global__ void __launch_bounds__(kT) k_bwd_gates_tc(Params P) {
       st_bf(tEZ, i, q, ez);
     });
     for (int i = L; i < kR; ++i) { st_bf(tES, i, q, 0.f); st_bf(tEZ, i, q, 0.f); }
-    if (row == 0) adj_scalars(cx, hS, hZS, hZZ);
+  } else if (wg == 2 && row == 0) {
+    fwd_scalars(cx, sS, sZ, zZ);
+  } else if (wg == 3 && row == 0) {
+    adj_scalars(cx, hS, hZS, hZZ);
   }
+  async_wait();
   pc.mark(25);
   smem_to_tc();
   if (tid == 0) {
@@ -820,6 +827,7 @@ __global__ void __launch_bounds__(kT) k_bwd_finalize_tc(Params P) {
   __shared__ uint32_t tbase;
   const int n = blockIdx.y, p0 = blockIdx.x * kR, e = P.e, tid = threadIdx.x, row = row_of(), wg = wg_of();
   const int TT = min(kR, P.T - p0);
+  async_copy_tile(tSR, P.srb + (int64_t)n * kTileBytes);
   Sync sy{&mbar, &tbase, 0, nullptr};
   const uint32_t tm = tc_setup(sy, 128);
   const int e1 = e > 1 ? e - 1 : 1;
@@ -853,7 +861,7 @@ __global__ void __launch_bounds__(kT) k_bwd_finalize_tc(Params P) {
       *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(P.dv_) + gi) = *reinterpret_cast<uint4*>(hb);
     }
   });
-  fill_dense(tSR, P.Sref + (int64_t)n * kD * kD);
+  async_wait();
   smem_to_tc();
   if (tid == 0) mma_chain(tm, op(tDD, kD, 0), op(tSR, kD, 1), 8, kD, false);  // d delta S_ref
   // while the MMA runs: dq, and du in token-gate mode

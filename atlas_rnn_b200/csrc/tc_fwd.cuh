@@ -39,8 +39,10 @@ __device__ __forceinline__ void fwd_column(const Params& P, const Ctx& cx, int j
 }
 // Adjoint coefficients of token q (the recurrence of adj_coefs), 8 tokens per
 // gate batch. emit(i, eS_{i+1}[q], eZ_{i+1}[q]) for i = L-1 down to 0.
+// With es_end / ez_end given, the values after token 0 (eS_0[q], eZ_0[q]) are returned there.
 template <class F>
-__device__ __forceinline__ void adj_column(const Ctx& cx, int q, F emit) {
+__device__ __forceinline__ void adj_column(const Ctx& cx, int q, F emit, float* es_end = nullptr,
+                                           float* ez_end = nullptr) {
   float es = 0.f, ez = 0.f;
   for (int i0 = cx.L - 1; i0 >= 0; i0 -= 8) {
     float al[8], be[8], etm[8];
@@ -59,6 +61,8 @@ __device__ __forceinline__ void adj_column(const Ctx& cx, int q, F emit) {
         ez = be[k] * ez - etm[k] * es;
       }
   }
+  if (es_end) *es_end = es;
+  if (ez_end) *ez_end = ez;
 }
 __device__ __forceinline__ void st_bf(unsigned char* tile, int r, int c, float v) {
   *reinterpret_cast<__nv_bfloat16*>(tile + umma::elem_off(r, c, kR)) = __float2bfloat16_rn(v);
@@ -132,6 +136,19 @@ __device__ __forceinline__ void fill_dense(unsigned char* tile, const float* M, 
   fill_tile(tile, kD, [&](int r, int c0, float(&v)[8]) { ld8f(M + r * kD + c0, v); }, first, count);
 }
 
+// S_ref of every unit as one bf16 operand tile (core-matrix layout), once per
+// call: the chunk kernels then copy it raw. Grid (N), 256 threads.
+__global__ void __launch_bounds__(256) k_sref_tile(Params P) {
+  const float* M = P.Sref + (int64_t)blockIdx.x * kD * kD;
+  unsigned char* dst = P.srb + (int64_t)blockIdx.x * kTileBytes;
+  for (int u = threadIdx.x; u < kTileBytes / 16; u += blockDim.x) {
+    const int r = u / (kD / 8), cb = u % (kD / 8);
+    float v[8];
+    ld8f(M + r * kD + cb * 8, v);
+    store_unit(dst, r, cb, kD, v);
+  }
+}
+
 // ===========================================================================
 // delta and the chunk increments (dS, dZ) on tensor cores.
 //   delta[keys x d_v] = Phi[keys x d_phi] S_ref^T - V
@@ -147,24 +164,25 @@ __global__ void __launch_bounds__(kT) k_fwd_chunk_tc(Params P) {
   __shared__ uint64_t mbar;
   __shared__ uint32_t tbase;
   Ctx cx;
+  ctx_geom(P, cx);
+  async_keys_phi(P, cx, tPhi);
+  async_copy_tile(tSref, P.srb + (int64_t)cx.n * kTileBytes);
   load_ctx(P, sa, cx, kT);
   float* cSe = sa.take(kR);
   float* cZe = sa.take(kR);
   const int n = cx.n, c = cx.c, K = cx.K, L = cx.L, tid = threadIdx.x, row = row_of(), wg = wg_of();
   Sync sy{&mbar, &tbase, 0, nullptr};
-  const uint32_t tm = tc_setup(sy, 256);
-  fill_keys_phi(P, cx, tPhi);
-  fill_dense(tSref, P.Sref + (int64_t)n * kD * kD);
-  __syncthreads();  // gates visible to the coefficient threads
-  if (wg == 0) {    // end coefficients of key j = row
-    float cs = 0.f, cz = 0.f;
-    if (row < K)
-      for (int i = 0; i < L; ++i) {
-        cz = cx.be[i] * cz + wgt(P, cx, i, row);
-        cs = cx.al[i] * cs - cx.et[i] * cz;
+  const uint32_t tm = tc_setup(sy, 256);  // (its barrier also publishes the gates)
+  if (wg == 0) {  // end coefficients of key j = row
+    float cs_end = 0.f, cz_end = 0.f;
+    fwd_column(P, cx, row, [&](int i, float cs, float, float czn) {
+      if (i == L - 1) {
+        cz_end = czn;
+        cs_end = cx.al[i] * cs - cx.et[i] * czn;
       }
-    cSe[row] = cs;
-    cZe[row] = cz;
+    });
+    cSe[row] = cs_end;
+    cZe[row] = cz_end;
   } else if (wg == 1 && row == 0) {  // chunk transform scalars
     float s = 1.f, sz = 0.f, z = 1.f;
     for (int i = 0; i < L; ++i) {
@@ -174,6 +192,11 @@ __global__ void __launch_bounds__(kT) k_fwd_chunk_tc(Params P) {
     }
     float* o = P.cs + ((int64_t)n * P.nch + c) * 4;
     o[0] = s; o[1] = sz; o[2] = z; o[3] = 0.f;
+  }
+  async_wait();
+  if (wg > 0) {
+    loaders_sync();
+    phi_xform(P, tPhi, 128, kT - 128);
   }
   smem_to_tc();
   if (tid == 0) mma_chain(tm, op(tPhi, kD, 0), op(tSref, kD, 0), kD / 16, kD, false);
@@ -269,24 +292,22 @@ __global__ void __launch_bounds__(kT) k_fwd_out_tc(Params P) {
   __shared__ uint64_t mbar;
   __shared__ uint32_t tbase;
   Ctx cx;
+  ctx_geom(P, cx);
+  {  // every operand tile in flight before anything else
+    const unsigned char* Sin = P.stb + ((int64_t)cx.n * P.nch + cx.c) * 2 * kTileBytes;
+    async_rows_psi(P, cx, tPsi);
+    async_keys_phi(P, cx, tPhi);
+    async_keys_delta(P, cx, tDl);
+    async_copy_tile(tSin, Sin);
+    async_copy_tile(tZin, Sin + kTileBytes);
+  }
   load_ctx(P, sa, cx, kT);
   float* sSv = sa.take(kR);
   float* sZv = sa.take(kR);
-  const int n = cx.n, c = cx.c, K = cx.K, L = cx.L, tid = threadIdx.x, row = row_of(), wg = wg_of();
+  const int n = cx.n, L = cx.L, tid = threadIdx.x, row = row_of(), wg = wg_of();
   Sync sy{&mbar, &tbase, 0, nullptr};
-  const uint32_t tm = tc_setup(sy);
+  const uint32_t tm = tc_setup(sy);  // (its barrier also publishes the gates)
   pc.mark(16);
-  const unsigned char* Sin = P.stb + ((int64_t)n * P.nch + c) * 2 * kTileBytes;
-  fill_rows_psi(P, cx, tPsi);
-  fill_keys_phi(P, cx, tPhi);
-  fill_rows_raw(tDl, [&](int r) -> const __nv_bfloat16* {
-    const int p = cx.kp0 + r;
-    return (r < K && p >= 0) ? P.dlb + ((int64_t)n * P.T + p) * P.dv : nullptr;
-  });
-  copy_tile(tSin, Sin);
-  copy_tile(tZin, Sin + kTileBytes);
-  __syncthreads();
-  pc.mark(17);
   if (wg == 0) {  // column j = row of tMs: cS of key j before each token i
     const int j = row;
     fwd_column(P, cx, j, [&](int i, float cs, float, float) { st_bf(tMs, i, j, cs); });
@@ -301,7 +322,13 @@ __global__ void __launch_bounds__(kT) k_fwd_out_tc(Params P) {
       sz = cx.al[i] * sz - cx.et[i] * z;
     }
   }
-  pc.mark(18);
+  async_wait();
+  if (wg > 0) {
+    loaders_sync();
+    phi_xform(P, tPsi, 128, kT - 128);
+    phi_xform(P, tPhi, 128, kT - 128);
+  }
+  pc.mark(17);
   smem_to_tc();
   if (tid == 0) {
     mma_chain(tm, op(tPsi, kD, 0), op(tPhi, kD, 0), kD / 16, kR, false);          // A2 = Psi Phi^T
@@ -346,8 +373,8 @@ __global__ void __launch_bounds__(kT) k_fwd_out_tc(Params P) {
       }
     }
   }
-  tc_teardown(tm);  pc.mark(22);
-
+  pc.mark(22);
+  tc_teardown(tm);
 }
 
 // Chunk 0 with a carried buffer: y_i += sum_jb cS_i[jb] Buf_jb psi_i (dense
