@@ -666,9 +666,11 @@ __global__ void __launch_bounds__(kT) k_bwd_gates_tc(Params P) {
   pc.mark(27);
   // window weights dW(i, j) = hZS_{i+1} X[F_S][R_j] + hZZ_{i+1} X[F_Z][R_j] + (E_Z+ G)[i][j]
   if (P.gmode != ATLAS_GATE_NONE) {
+    const int rb = (threadIdx.x >> 5) & 3;  // this warp's rows [32 rb, 32 rb + 32)
 #pragma unroll
     for (int h4 = 0; h4 < kCPW; ++h4) {
       const int c16 = wg * kCPW + h4;
+      if (c16 * 16 + 15 < 32 * rb || c16 * 16 > 32 * rb + 31 + e - 1) continue;  // no window key here (warp-uniform)
       float W[16];
       umma::tmem_ld16(lane_addr(tm, 384 + c16 * 16), W);
       umma::tmem_ld_wait();

@@ -110,16 +110,36 @@ def run_reference(args, w):
 # clocks during the timed region
 # ---------------------------------------------------------------------------
 class ClockSampler:
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    """nvidia-smi clock/throttle samples (every 50 ms, rank 0, all GPUs of the job).
+
+    Sampling starts on entry and waits for the first row, so that the timed region
+    that follows is covered; summary() keeps the rows stamped inside
+    [mark_start(), mark_end()] (the nearest row when the region is shorter than
+    one period).
+    """
+    Q = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, gpu_ids, rank: int):
-        # rank 0 samples every GPU of the job; the other ranks sample nothing
         self.ids = gpu_ids
         self.rank = rank
         self.proc = None
         self.path = os.path.join(ROOT, "gpurun_out", "clocks.csv")
+        self.t0 = self.t1 = None
+
+    def _rows(self):
+        import datetime
+        rows = []
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 10 and parts[2].replace(".", "").isdigit():
+                try:
+                    ts = datetime.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                except ValueError:
+                    continue
+                rows.append((ts, parts[1:]))
+        return rows
 
     def __enter__(self):
         if self.rank != 0:
@@ -128,11 +148,22 @@ class ClockSampler:
             os.makedirs(os.path.dirname(self.path), exist_ok=True)
             self.f = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", "-i", ",".join(self.ids), f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
                                          stdout=self.f, stderr=subprocess.DEVNULL)
+            deadline = time.time() + 10.0
+            while time.time() < deadline and not self._rows():
+                time.sleep(0.02)
         except Exception:
             self.proc = None
         return self
+
+    def mark_start(self):
+        self.t0 = time.time()
+
+    def mark_end(self):
+        self.t1 = time.time()
+        if self.proc is not None:  # one more period so the region's last samples land
+            time.sleep(0.12)
 
     def __exit__(self, *a):
         if self.proc is not None:
@@ -146,13 +177,19 @@ class ClockSampler:
     def summary(self):
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        rows = []
-        for line in open(self.path):
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) >= 9 and parts[1].replace(".", "").isdigit():
-                rows.append(parts)
-        if not rows:
+        allrows = self._rows()
+        if not allrows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        t0 = self.t0 if self.t0 is not None else allrows[0][0]
+        t1 = self.t1 if self.t1 is not None else allrows[-1][0]
+        rows = [r for ts, r in allrows if t0 <= ts <= t1]
+        if not rows:  # region shorter than one period: the sample nearest to its middle, per GPU
+            mid = 0.5 * (t0 + t1)
+            best = {}
+            for ts, r in allrows:
+                if r[0] not in best or abs(ts - mid) < abs(best[r[0]][0] - mid):
+                    best[r[0]] = (ts, r)
+            rows = [r for _, r in best.values()]
         sm = [float(r[1]) for r in rows]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower().startswith("active")})
@@ -255,6 +292,7 @@ def run_ours(args, w):
         ids = gathered
     with ClockSampler(ids, rank) as clk:
         barrier()
+        clk.mark_start()
         ev0.record(st)
         h0 = time.perf_counter()
         for _ in range(args.steps):
@@ -262,6 +300,7 @@ def run_ours(args, w):
         host_ms = (time.perf_counter() - h0) * 1000.0 / args.steps  # enqueue time per step
         ev1.record(st)
         barrier()
+        clk.mark_end()
     ms = ev0.elapsed_time(ev1)
     kern = _lib.profile_read()
     launches = _lib.launch_count()
@@ -369,7 +408,7 @@ def kernel_cfg_chunk(w):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--config", type=int, default=1)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
