@@ -288,93 +288,30 @@ __device__ __forceinline__ void key_adj_weights(const Params& P, const Ctx& cx, 
   }
 }
 
-// Window weights by token and offset: Wt[i * E + k] = W(i, i + k) (zero for
-// k >= e), all threads.
-__device__ __forceinline__ int pow2_window(int e) { return e <= 1 ? 1 : e <= 2 ? 2 : e <= 4 ? 4 : e <= 8 ? 8 : 16; }
-__device__ __forceinline__ void window_weights(const Params& P, const Ctx& cx, float* Wt) {
-  const int E = pow2_window(P.e);
-  for (int x = threadIdx.x; x < cx.L * E; x += blockDim.x) {
-    const int i = x / E, k = x - i * E;
-    Wt[x] = k < P.e ? wgt(P, cx, i, i + k) : 0.f;
-  }
-}
-
-// Adjoint column of token q (the recurrence of adj_column) folded straight into
-// the window sums wE_q[j] = sum_i W(i, j) eZ_{i+1}[q], i in [j-e+1, j] cap [0, L),
-// written as row q of the bf16 tile tW (columns = keys j). E >= e is a power of
-// two: acc[k] holds key i + k while token i is processed, and key i + E - 1 is
-// complete once token i has been added. Gates and weights of 4 tokens are
-// loaded ahead of the dependent arithmetic.
-template <int E>
-__device__ __forceinline__ void adj_wE_row(const Ctx& cx, int q, unsigned char* tW, const float* Wt) {
-  constexpr int kB = 4;
-  const int L = cx.L;
-  for (int j = L + E - 1; j < kR; ++j) st_bf(tW, q, j, 0.f);
-  float acc[E];
-#pragma unroll
-  for (int k = 0; k < E; ++k) acc[k] = 0.f;
-  float es = 0.f, ez = 0.f;
-  for (int i0 = L - 1; i0 >= 0; i0 -= kB) {
-    float al[kB], be[kB], etm[kB], w[kB][E];
-#pragma unroll
-    for (int b = 0; b < kB; ++b) {
-      const int i = max(i0 - b, 0);
-      al[b] = cx.al[i];
-      be[b] = cx.be[i];
-      etm[b] = i >= 1 ? cx.et[i - 1] : 0.f;
-#pragma unroll
-      for (int k = 0; k < E; ++k) w[b][k] = Wt[i * E + k];
-    }
-#pragma unroll
-    for (int b = 0; b < kB; ++b) {
-      const int i = i0 - b;
-      if (i >= 0) {
-#pragma unroll
-        for (int k = 0; k < E; ++k) acc[k] += w[b][k] * ez;
-        if (i + E - 1 < kR) st_bf(tW, q, i + E - 1, acc[E - 1]);
-#pragma unroll
-        for (int k = E - 1; k > 0; --k) acc[k] = acc[k - 1];
-        acc[0] = 0.f;
-        es = al[b] * es + (q == i ? 1.f : 0.f);
-        ez = be[b] * ez - etm[b] * es;
-      }
-    }
-  }
-#pragma unroll
-  for (int k = 1; k < E; ++k) st_bf(tW, q, k - 1, acc[k]);
-}
-__device__ __forceinline__ void adj_wE_row_any(const Params& P, const Ctx& cx, int q, unsigned char* tW,
-                                               const float* Wt) {
-  switch (pow2_window(P.e)) {
-    case 1: adj_wE_row<1>(cx, q, tW, Wt); break;
-    case 2: adj_wE_row<2>(cx, q, tW, Wt); break;
-    case 4: adj_wE_row<4>(cx, q, tW, Wt); break;
-    case 8: adj_wE_row<8>(cx, q, tW, Wt); break;
-    default: adj_wE_row<16>(cx, q, tW, Wt); break;
-  }
-}
-
 // ===========================================================================
 // key-side backward in one pass:
 //   phase 1  P1 = Phi F_S^T, P2 = Phi F_Z^T, Q1 = delta F_S, Q2 = delta F_Z
 //            -> X[F][R_j]; d delta = wZS P1 + wZZ P2 and d phi = wZS Q1 + wZZ Q2 are
 //            written back into TMEM (tcgen05.st) over P1 and Q1
-//   phase 2  A1 = dY delta^T, A2 = Psi Phi^T -> G = A1 o A2 (scratch), M1, M2, M3
-//   phase 3  d delta += M1 dY, d phi += M2 Psi (accumulating in TMEM), I5 = M3 Phi
+//   phase 2  A1 = dY delta^T, A2 = Psi Phi^T -> G = A1 o A2 (scratch), M3 = cS o A1,
+//            M1 = cS o A2
+//   phase 3  d delta += M1 dY, d phi += M3^T Psi (accumulating in TMEM), I5 = M3 Phi
 //   out      d delta, d phi written once (own keys / halo partials); d psi += I5
-// Operand tiles arrive by cp.async while warpgroup 0 builds the window-summed
-// adjoint weights wE (tile tM1), warpgroup 1 the forward coefficients cS (tile
-// tM3) and one thread of warpgroup 2 the adjoint transform scalars.
+// The window-summed adjoint weight of key j for token q, sum_i W(i, j) eZ_{i+1}[q],
+// equals the forward coefficient cS_q[j] (both are
+// -sum_{n<q} prod_{l=n+1}^{q-1} alpha_l eta_n sum_{m<=n} prod_{l=m+1}^{n} beta_l W(m, j)),
+// so one coefficient tile (cS, built by warpgroup 0 while the operand tiles
+// arrive by cp.async) serves the adjoint weights as well, and M2 = wE o A1 = M3.
 // ===========================================================================
 __global__ void __launch_bounds__(kT) k_bwd_keys_tc(Params P) {
   PhaseClock pc;
   extern __shared__ __align__(1024) unsigned char sm[];
   unsigned char* tPhi = sm;
-  unsigned char* tDl = sm + kTileBytes;       // delta, later M2
+  unsigned char* tDl = sm + kTileBytes;       // delta
   unsigned char* tFS = sm + 2 * kTileBytes;   // F_S, later Psi
   unsigned char* tFZ = sm + 3 * kTileBytes;   // F_Z, later dY
-  unsigned char* tM3 = sm + 4 * kTileBytes;   // cS, later M3
-  unsigned char* tM1 = sm + 5 * kTileBytes;   // wE, later M1
+  unsigned char* tM3 = sm + 4 * kTileBytes;   // cS, later M3 (= M2)
+  unsigned char* tM1 = sm + 5 * kTileBytes;   // M1
   SmemAlloc sa{reinterpret_cast<float*>(sm + 6 * kTileBytes), 0};
   __shared__ uint64_t mbar;
   __shared__ uint32_t tbase;
@@ -384,7 +321,6 @@ __global__ void __launch_bounds__(kT) k_bwd_keys_tc(Params P) {
   float* hZS = sa.take(kR + 1);
   float* hZZ = sa.take(kR + 1);
   float* part = sa.take(2 * kWG * kR);
-  float* Wt = sa.take(kR * 16);
   const int n = cx.n, K = cx.K, L = cx.L, tid = threadIdx.x, e = P.e, row = row_of(), wg = wg_of();
   Sync sy{&mbar, &tbase, 0, nullptr};
   const uint32_t tm = tc_setup(sy);
@@ -395,22 +331,16 @@ __global__ void __launch_bounds__(kT) k_bwd_keys_tc(Params P) {
   async_copy_tile(tFS, FS);
   async_copy_tile(tFZ, FS + kTileBytes);
   __syncthreads();  // gates of load_ctx visible
-  window_weights(P, cx, Wt);
-  __syncthreads();
   pc.mark(0);
   if (wg == 0) {
-    adj_wE_row_any(P, cx, row, tM1, Wt);
-    if (row == 0) pc.lap(11);
-  } else if (wg == 1) {
     fwd_column(P, cx, row, [&](int i, float cs, float, float) { st_bf(tM3, i, row, cs); });
     for (int i = L; i < kR; ++i) st_bf(tM3, i, row, 0.f);
     if (row == 0) pc.lap(12);
-  } else if (wg == 2 && row == 0) {
+  } else if (wg == 1 && row == 0) {
     adj_scalars(cx, hS, hZS, hZZ);
     pc.lap(13);
   }
   async_wait();
-  if (tid == 384) pc.lap(14);
   if (wg > 0) {
     loaders_sync();
     phi_xform(P, tPhi, 128, kT - 128);
@@ -476,7 +406,7 @@ __global__ void __launch_bounds__(kT) k_bwd_keys_tc(Params P) {
   }
   mma_wait(sy);
   pc.mark(7);
-  {  // phase-2 epilogue, row q: G, M3 = cS o A1, M1 = wE o A2^T, M2 = wE o A1^T
+  {  // phase-2 epilogue, row q: G, M3 = cS o A1, M1 = cS o A2
     const int q = row;
     unsigned char* gdst = reinterpret_cast<unsigned char*>(P.gt) + cid * kTileBytes;
     for (int h4 = 0; h4 < kCPW; ++h4) {
@@ -488,21 +418,18 @@ __global__ void __launch_bounds__(kT) k_bwd_keys_tc(Params P) {
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const int cb = 2 * c16 + h;
-        float g[8], c3[8], w[8], m2[8];
+        float g[8], c3[8], m1[8];
         load_unit(tM3, q, cb, kR, c3);
-        load_unit(tM1, q, cb, kR, w);
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
           const float x1 = a1[8 * h + k], x2 = a2[8 * h + k];
           g[k] = x1 * x2;
+          m1[k] = c3[k] * x2;
           c3[k] *= x1;
-          m2[k] = w[k] * x1;
-          w[k] *= x2;  // M1
         }
         store_unit(gdst, q, cb, kR, g);
         store_unit(tM3, q, cb, kR, c3);
-        store_unit(tDl, q, cb, kR, m2);  // delta no longer needed
-        store_unit(tM1, q, cb, kR, w);
+        store_unit(tM1, q, cb, kR, m1);
       }
     }
   }
@@ -510,7 +437,7 @@ __global__ void __launch_bounds__(kT) k_bwd_keys_tc(Params P) {
   smem_to_tc();
   if (tid == 0) {
     mma_chain(tm, op(tM1, kR, 1), op(tFZ, kD, 1), 8, kD, true);          // d delta += M1 dY
-    mma_chain(tm + 256, op(tDl, kR, 1), op(tFS, kD, 1), 8, kD, true);    // d phi   += M2 Psi
+    mma_chain(tm + 256, op(tM3, kR, 1), op(tFS, kD, 1), 8, kD, true);    // d phi   += M2 Psi (M2 = M3)
     mma_chain(tm + 128, op(tM3, kR, 0), op(tPhi, kD, 1), 8, kD, false);  // I5 = M3 Phi
   }
   mma_wait(sy);
