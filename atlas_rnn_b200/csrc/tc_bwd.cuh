@@ -93,7 +93,7 @@ __global__ void __launch_bounds__(kT) k_bwd_chunk_tc(Params P) {
   const uint32_t tm = tc_setup(sy, 256);
   if (wg == 0) {  // adjoint weights of token q at the chunk input
     float es = 0.f, ez = 0.f;
-    adj_column(cx, row, [](int, float, float) {}, &es, &ez);
+    adj_column_z(cx, row, [](int, float, float) {}, &es, &ez);
     eS0[row] = es;
     eZ0[row] = ez;
   } else if (wg == 1 && row == 0) {
@@ -330,11 +330,11 @@ __global__ void __launch_bounds__(kT) k_bwd_keys_tc(Params P) {
   async_keys_delta(P, cx, tDl);
   async_copy_tile(tFS, FS);
   async_copy_tile(tFZ, FS + kTileBytes);
-  __syncthreads();  // gates of load_ctx visible
+  zero_tile(tM3);
+  __syncthreads();  // gates of load_ctx visible, tM3 zero
   pc.mark(0);
   if (wg == 0) {
-    fwd_column(P, cx, row, [&](int i, float cs, float, float) { st_bf(tM3, i, row, cs); });
-    for (int i = L; i < kR; ++i) st_bf(tM3, i, row, 0.f);
+    fwd_column_z(P, cx, row, [&](int i, float cs, float, float) { st_bf(tM3, i, row, cs); });
     if (row == 0) pc.lap(12);
   } else if (wg == 1 && row == 0) {
     adj_scalars(cx, hS, hZS, hZZ);
@@ -516,24 +516,27 @@ __global__ void __launch_bounds__(kT) k_bwd_gates_tc(Params P) {
     cp16(xs, P.xs + cid * 4, true);
   }
   if (tid < kR) duj[tid] = 0.f;
+  zero_tile(tCS);
+  zero_tile(tCZp);
+  zero_tile(tCZn);
+  zero_tile(tES);
+  zero_tile(tEZ);
   Sync sy{&mbar, &tbase, 0, nullptr};
   const uint32_t tm = tc_setup(sy);  // (its barrier also publishes the gates)
   pc.mark(24);
   if (wg == 0) {
-    const int j = row;  // forward coefficients of key j (column j of tCS, tCZp, tCZn)
-    fwd_column(P, cx, j, [&](int i, float cs, float cz, float czn) {
+    const int j = row;  // forward coefficients of key j (column j of tCS, tCZp, tCZn; tiles zero-filled)
+    fwd_column_z(P, cx, j, [&](int i, float cs, float cz, float czn) {
       st_bf(tCS, i, j, cs);
       st_bf(tCZp, i, j, cz);
       st_bf(tCZn, i, j, czn);
     });
-    for (int i = L; i < kR; ++i) { st_bf(tCS, i, j, 0.f); st_bf(tCZp, i, j, 0.f); st_bf(tCZn, i, j, 0.f); }
   } else if (wg == 1) {
     const int q = row;  // adjoint coefficients of token q (column q of tES, tEZ): rows i <- eS_{i+1}, eZ_{i+1}
-    adj_column(cx, q, [&](int i, float es, float ez) {
+    adj_column_z(cx, q, [&](int i, float es, float ez) {
       st_bf(tES, i, q, es);
       st_bf(tEZ, i, q, ez);
     });
-    for (int i = L; i < kR; ++i) { st_bf(tES, i, q, 0.f); st_bf(tEZ, i, q, 0.f); }
   } else if (wg == 2 && row == 0) {
     fwd_scalars(cx, sS, sZ, zZ);
   } else if (wg == 3 && row == 0) {

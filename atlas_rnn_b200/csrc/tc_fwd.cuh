@@ -37,6 +37,85 @@ __device__ __forceinline__ void fwd_column(const Params& P, const Ctx& cx, int j
       }
   }
 }
+__device__ __forceinline__ void zero_tile(unsigned char* tile) {
+  for (int u = threadIdx.x; u < kTileBytes / 16; u += blockDim.x)
+    reinterpret_cast<uint4*>(tile)[u] = make_uint4(0u, 0u, 0u, 0u);
+}
+// fwd_column without the structurally zero rows: key j has no coefficient before
+// its first window token j - e + 1, receives window weights up to token j and
+// then evolves homogeneously, so only tokens [max(0, j - e + 1), L) are emitted
+// (the caller zero-fills the tile rows beforehand) and the weight lookup runs
+// for at most e of them. Same emit(i, cS before i, cZ before i, cZ after i).
+template <class F>
+__device__ __forceinline__ void fwd_column_z(const Params& P, const Ctx& cx, int j, F emit) {
+  const int L = cx.L;
+  int i = max(0, j - (P.e - 1));
+  const int wend = min(L, j + 1);
+  float cs = 0.f, cz = 0.f;
+  for (; i < wend; ++i) {
+    const float czn = cx.be[i] * cz + wgt(P, cx, i, j);
+    emit(i, cs, cz, czn);
+    cz = czn;
+    cs = cx.al[i] * cs - cx.et[i] * cz;
+  }
+  for (; i + 4 <= L; i += 4) {
+    float al[4], et[4], be[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) { al[k] = cx.al[i + k]; et[k] = cx.et[i + k]; be[k] = cx.be[i + k]; }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float czn = be[k] * cz;
+      emit(i + k, cs, cz, czn);
+      cz = czn;
+      cs = al[k] * cs - et[k] * cz;
+    }
+  }
+  for (; i < L; ++i) {
+    const float czn = cx.be[i] * cz;
+    emit(i, cs, cz, czn);
+    cz = czn;
+    cs = cx.al[i] * cs - cx.et[i] * cz;
+  }
+}
+// adj_column without the structurally zero rows: token q's adjoint coefficients
+// vanish for rows i >= q, so only rows [0, q) are emitted (descending; the
+// caller zero-fills the tile). Same emit(i, eS_{i+1}[q], eZ_{i+1}[q]).
+// With es_end / ez_end given, the values after token 0 (eS_0[q], eZ_0[q]) are returned there.
+template <class F>
+__device__ __forceinline__ void adj_column_z(const Ctx& cx, int q, F emit, float* es_end = nullptr,
+                                             float* ez_end = nullptr) {
+  if (q >= cx.L) {
+    if (es_end) *es_end = 0.f;
+    if (ez_end) *ez_end = 0.f;
+    return;
+  }
+  float es = 1.f, ez = -(q >= 1 ? cx.et[q - 1] : 0.f);  // after token q
+  int i = q - 1;
+  for (; i - 3 >= 0; i -= 4) {
+    float al[4], be[4], etm[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      al[k] = cx.al[i - k];
+      be[k] = cx.be[i - k];
+      etm[k] = i - k >= 1 ? cx.et[i - k - 1] : 0.f;
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      emit(i - k, es, ez);
+      es = al[k] * es;
+      ez = be[k] * ez - etm[k] * es;
+    }
+  }
+  for (; i >= 0; --i) {
+    emit(i, es, ez);
+    const float etm = i >= 1 ? cx.et[i - 1] : 0.f;
+    es = cx.al[i] * es;
+    ez = cx.be[i] * ez - etm * es;
+  }
+  if (es_end) *es_end = es;
+  if (ez_end) *ez_end = ez;
+}
+
 // Adjoint coefficients of token q (the recurrence of adj_coefs), 8 tokens per
 // gate batch. emit(i, eS_{i+1}[q], eZ_{i+1}[q]) for i = L-1 down to 0.
 // With es_end / ez_end given, the values after token 0 (eS_0[q], eZ_0[q]) are returned there.
@@ -301,6 +380,7 @@ __global__ void __launch_bounds__(kT) k_fwd_out_tc(Params P) {
     async_copy_tile(tSin, Sin);
     async_copy_tile(tZin, Sin + kTileBytes);
   }
+  zero_tile(tMs);
   load_ctx(P, sa, cx, kT);
   float* sSv = sa.take(kR);
   float* sZv = sa.take(kR);
@@ -308,10 +388,9 @@ __global__ void __launch_bounds__(kT) k_fwd_out_tc(Params P) {
   Sync sy{&mbar, &tbase, 0, nullptr};
   const uint32_t tm = tc_setup(sy);  // (its barrier also publishes the gates)
   pc.mark(16);
-  if (wg == 0) {  // column j = row of tMs: cS of key j before each token i
+  if (wg == 0) {  // column j = row of tMs: cS of key j before each token i (tile zero-filled)
     const int j = row;
-    fwd_column(P, cx, j, [&](int i, float cs, float, float) { st_bf(tMs, i, j, cs); });
-    for (int i = L; i < kR; ++i) st_bf(tMs, i, j, 0.f);
+    fwd_column_z(P, cx, j, [&](int i, float cs, float, float) { st_bf(tMs, i, j, cs); });
   } else if (wg == 1 && row == 0) {
     float s = 1.f, sz = 0.f, z = 1.f;
     for (int i = 0; i < L; ++i) {
