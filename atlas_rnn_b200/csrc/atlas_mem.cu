@@ -8,6 +8,7 @@
 
 #include "chunk_kernels.cuh"
 #include "tc_bwd.cuh"
+#include "tc_scan.cuh"
 #include "umma_selftest.cuh"
 
 using namespace atlas;
@@ -320,8 +321,45 @@ void prof_end(int slot, cudaStream_t st) {
   } while (0)
 
 // Sequential chunk scans: float4 per thread when the state size allows it.
+int sm_count() {
+  static int cached[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (!cached[dev]) {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) v = 148;
+    cached[dev] = v;
+  }
+  return cached[dev];
+}
+
+// One resident wave of tc::k_{fwd,bwd}_scan_tc (F <= 4 float4 slots per thread, rounds beyond that).
+int launch_scan_tc(bool fwd, const Params& P, cudaStream_t st) {
+  const int grid = sm_count();
+  const int64_t G = (int64_t)grid * tc::kScanThreads, total = (int64_t)P.N * tc::kDV4;
+  const int64_t need = (total + G - 1) / G;
+  const int F = need <= 1 ? 1 : need <= 2 ? 2 : 4;
+  const int rounds = (int)((need + F - 1) / F);
+  for (int r = 0; r < rounds; ++r) {
+#define SCAN_TC(FF)                                                                                   \
+  if (fwd) LAUNCH_T(KID_FWD_SCAN, tc::k_fwd_scan_tc<FF>, dim3(grid), tc::kScanThreads, 0, st, P, r); \
+  else LAUNCH_T(KID_BWD_SCAN, tc::k_bwd_scan_tc<FF>, dim3(grid), tc::kScanThreads, 0, st, P, r);
+    switch (F) {
+      case 1: SCAN_TC(1) break;
+      case 2: SCAN_TC(2) break;
+      default: SCAN_TC(4) break;
+    }
+#undef SCAN_TC
+  }
+  return ATLAS_OK;
+}
+
 int launch_scan(bool fwd, const Params& P, int dry, cudaStream_t st) {
   const int64_t D2 = (int64_t)P.dv * P.dphi;
+  if (!dry && P.inc_bf16 && (fwd ? P.stb != nullptr : P.adjb != nullptr) && P.dv == tc::kD && P.dphi == tc::kD &&
+      (int64_t)P.N * tc::kDV4 < ((int64_t)1 << 31) && std::getenv("ATLAS_MEM_SCAN_GENERIC") == nullptr)
+    return launch_scan_tc(fwd, P, st);
   const size_t smem = (size_t)P.nch * sizeof(float4);
   const bool v4 = (D2 % 4) == 0;
   const int64_t units = v4 ? D2 / 4 : D2;
