@@ -149,7 +149,8 @@ int ensure_attrs() {
                       (const void*)k_bwd_scan<4>, (const void*)tc::k_fwd_chunk_tc, (const void*)tc::k_fwd_out_tc,
                       (const void*)tc::k_fwd_buf_y, (const void*)tc::k_bwd_chunk_tc, (const void*)tc::k_bwd_state_tc,
                       (const void*)tc::k_bwd_buf_tc,
-                      (const void*)tc::k_bwd_gates_tc, (const void*)tc::k_bwd_finalize_tc, (const void*)tc::k_bwd_dsref_tc, (const void*)tc::k_bwd_keys_tc};
+                      (const void*)tc::k_bwd_gates_tc, (const void*)tc::k_bwd_finalize_tc, (const void*)tc::k_bwd_dsref_tc, (const void*)tc::k_bwd_keys_tc,
+                      (const void*)tc::k_fwd_scan_tc, (const void*)tc::k_bwd_scan_tc};
   for (const void* k : ks) {
     cudaFuncAttributes fa;
     if (cudaFuncGetAttributes(&fa, k) != cudaSuccess) return ATLAS_ERR_LAUNCH;
@@ -334,23 +335,14 @@ int sm_count() {
   return cached[dev];
 }
 
-// One resident wave of tc::k_{fwd,bwd}_scan_tc (F <= 4 float4 slots per thread, rounds beyond that).
+// One resident wave of tc::k_{fwd,bwd}_scan_tc (kScanF groups of 8 elements per thread, rounds beyond that).
 int launch_scan_tc(bool fwd, const Params& P, cudaStream_t st) {
   const int grid = sm_count();
-  const int64_t G = (int64_t)grid * tc::kScanThreads, total = (int64_t)P.N * tc::kDV4;
-  const int64_t need = (total + G - 1) / G;
-  const int F = need <= 1 ? 1 : need <= 2 ? 2 : 4;
-  const int rounds = (int)((need + F - 1) / F);
+  const int64_t G = (int64_t)grid * tc::kScanThreads, total = (int64_t)P.N * tc::kOct;
+  const int rounds = (int)((total + G * tc::kScanF - 1) / (G * tc::kScanF));
   for (int r = 0; r < rounds; ++r) {
-#define SCAN_TC(FF)                                                                                   \
-  if (fwd) LAUNCH_T(KID_FWD_SCAN, tc::k_fwd_scan_tc<FF>, dim3(grid), tc::kScanThreads, 0, st, P, r); \
-  else LAUNCH_T(KID_BWD_SCAN, tc::k_bwd_scan_tc<FF>, dim3(grid), tc::kScanThreads, 0, st, P, r);
-    switch (F) {
-      case 1: SCAN_TC(1) break;
-      case 2: SCAN_TC(2) break;
-      default: SCAN_TC(4) break;
-    }
-#undef SCAN_TC
+    if (fwd) LAUNCH_T(KID_FWD_SCAN, tc::k_fwd_scan_tc, dim3(grid), tc::kScanThreads, tc::kScanRingBytes, st, P, r);
+    else LAUNCH_T(KID_BWD_SCAN, tc::k_bwd_scan_tc, dim3(grid), tc::kScanThreads, tc::kScanRingBytes, st, P, r);
   }
   return ATLAS_OK;
 }
@@ -358,7 +350,7 @@ int launch_scan_tc(bool fwd, const Params& P, cudaStream_t st) {
 int launch_scan(bool fwd, const Params& P, int dry, cudaStream_t st) {
   const int64_t D2 = (int64_t)P.dv * P.dphi;
   if (!dry && P.inc_bf16 && (fwd ? P.stb != nullptr : P.adjb != nullptr) && P.dv == tc::kD && P.dphi == tc::kD &&
-      (int64_t)P.N * tc::kDV4 < ((int64_t)1 << 31) && std::getenv("ATLAS_MEM_SCAN_GENERIC") == nullptr)
+      (int64_t)P.N * tc::kOct < ((int64_t)1 << 31) && std::getenv("ATLAS_MEM_SCAN_GENERIC") == nullptr)
     return launch_scan_tc(fwd, P, st);
   const size_t smem = (size_t)P.nch * sizeof(float4);
   const bool v4 = (D2 % 4) == 0;
