@@ -74,6 +74,7 @@ __device__ __forceinline__ void fwd_scalars(const Ctx& cx, float* sS, float* sZ,
 //   dShat = dY^T diag(eS_0) Psi,  dZhat = dY^T diag(eZ_0) Psi
 // ===========================================================================
 __global__ void __launch_bounds__(kT) k_bwd_chunk_tc(Params P) {
+  PhaseClock pc;
   extern __shared__ __align__(1024) unsigned char sm[];
   unsigned char* tYS = sm;
   unsigned char* tYZ = sm + kTileBytes;
@@ -91,6 +92,7 @@ __global__ void __launch_bounds__(kT) k_bwd_chunk_tc(Params P) {
   const int L = cx.L, tid = threadIdx.x, row = row_of(), wg = wg_of();
   Sync sy{&mbar, &tbase, 0, nullptr};
   const uint32_t tm = tc_setup(sy, 256);
+  pc.mark(48);
   if (wg == 0) {  // adjoint weights of token q at the chunk input
     float es = 0.f, ez = 0.f;
     adj_column_z(cx, row, [](int, float, float) {}, &es, &ez);
@@ -109,26 +111,30 @@ __global__ void __launch_bounds__(kT) k_bwd_chunk_tc(Params P) {
   }
   async_wait();
   __syncthreads();
+  pc.mark(49);
   {  // dY rows scaled by eS0 (in place) and by eZ0 (into tYZ); psi feature map
     constexpr int kCpr = kD / 8;
     for (int u = tid; u < kR * kCpr; u += kT) {
-      const int r = u / kCpr, cb = u % kCpr;
+      int r, cb;
+      unit_rc(u, kCpr, r, cb);
       float v[8], z[8];
-      load_unit(tYS, r, cb, kD, v);
+      unpack_unit(*reinterpret_cast<const uint4*>(tYS + 16 * u), v);
       const float a = eS0[r], b = eZ0[r];
 #pragma unroll
       for (int k = 0; k < 8; ++k) { z[k] = b * v[k]; v[k] *= a; }
-      store_unit(tYS, r, cb, kD, v);
-      store_unit(tYZ, r, cb, kD, z);
+      *reinterpret_cast<uint4*>(tYS + 16 * u) = pack_unit(v);
+      *reinterpret_cast<uint4*>(tYZ + 16 * u) = pack_unit(z);
     }
     phi_xform(P, tPsi);
   }
+  pc.mark(50);
   smem_to_tc();
   if (tid == 0) {
     mma_chain(tm, op(tYS, kD, 1), op(tPsi, kD, 1), 8, kD, false);
     mma_chain(tm + 128, op(tYZ, kD, 1), op(tPsi, kD, 1), 8, kD, false);
   }
   mma_wait(sy);
+  pc.mark(51);
   {
     const int64_t D2 = (int64_t)kD * kD;
     __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(P.adj) + chunk_id(P, cx) * 2 * D2 + (int64_t)row * kD;
@@ -143,7 +149,8 @@ __global__ void __launch_bounds__(kT) k_bwd_chunk_tc(Params P) {
       st16bf(dst + D2 + c16 * 16, b);
     }
   }
-  tc_teardown(tm, 256);
+  tc_teardown(tm, 256);  pc.mark(52);
+
 }
 
 // ===========================================================================
@@ -752,6 +759,7 @@ __global__ void __launch_bounds__(kThreads) k_bwd_buf_tc(Params P) {
 // (tensor feature map: d phi is left in the scratch for its own backward).
 // ===========================================================================
 __global__ void __launch_bounds__(kT) k_bwd_finalize_tc(Params P) {
+  PhaseClock pc;
   extern __shared__ __align__(1024) unsigned char sm[];
   unsigned char* tDD = sm;               // d delta rows (bf16)
   unsigned char* tSR = sm + kTileBytes;  // S_ref
@@ -792,7 +800,8 @@ __global__ void __launch_bounds__(kT) k_bwd_finalize_tc(Params P) {
       for (int k = 0; k < 4; ++k) hb[k] = __floats2bfloat162_rn(-v[2 * k], -v[2 * k + 1]);
       *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(P.dv_) + gi) = *reinterpret_cast<uint4*>(hb);
     }
-  });
+  }, 0, kT, /*rowmajor=*/true);
+  pc.mark(56);
   async_wait();
   smem_to_tc();
   if (tid == 0) mma_chain(tm, op(tDD, kD, 0), op(tSR, kD, 1), 8, kD, false);  // d delta S_ref
@@ -819,7 +828,9 @@ __global__ void __launch_bounds__(kT) k_bwd_finalize_tc(Params P) {
       if (h >= 0) d += P.hdu[h];
       stio(P.dgate, (int64_t)n * P.T + p, d, P.bf);
     }
+  pc.mark(57);
   mma_wait(sy);
+  pc.mark(58);
   {
     const int r = row, p = p0 + r;
     const int64_t h = r < TT ? halo(p) : -1;
@@ -858,7 +869,8 @@ __global__ void __launch_bounds__(kT) k_bwd_finalize_tc(Params P) {
       }
     }
   }
-  tc_teardown(tm, 128);
+  tc_teardown(tm, 128);  pc.mark(59);
+
 }
 
 // ===========================================================================

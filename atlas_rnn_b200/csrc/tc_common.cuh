@@ -95,6 +95,21 @@ __device__ __forceinline__ uint32_t lane_addr(uint32_t tm, int col) {
 }
 
 // Pack 8 floats to bf16 and store one 16-byte unit of a tile.
+__device__ __forceinline__ uint4 pack_unit(const float (&v)[8]) {
+  __align__(16) __nv_bfloat162 h[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+  return *reinterpret_cast<uint4*>(h);
+}
+__device__ __forceinline__ void unpack_unit(uint4 u, float (&v)[8]) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
 __device__ __forceinline__ void store_unit(unsigned char* tile, int r, int cb, int C, const float (&v)[8]) {
   __align__(16) __nv_bfloat162 h[4];
 #pragma unroll
@@ -112,11 +127,23 @@ __device__ __forceinline__ void load_unit(const unsigned char* tile, int r, int 
   }
 }
 
+// Unit u of a 128 x C tile (cpr = C / 8 units per row) in shared-memory address
+// order: unit_off(r, cb, C) == 16 u, so consecutive threads touch consecutive
+// 16-byte units (no bank conflicts), and a warp covers 8 rows x 4 column blocks
+// (64 contiguous bytes of each source row).
+__device__ __forceinline__ void unit_rc(int u, int cpr, int& r, int& cb) {
+  r = ((u >> 3) / cpr) * 8 + (u & 7);
+  cb = (u >> 3) % cpr;
+}
+
 // Fill a 128 x C tile; src(r, c0, v) fills v[0..7] for columns c0..c0+7 of row r.
+// Units go in shared-memory order (unit_rc) unless rowmajor, which walks the
+// source rows in order (for sources that also write global rows back).
 // Threads [first, first + count) take part (the others return at once); each
 // gathers 8 units before storing any, so 8 loads are in flight per thread.
 template <class F>
-__device__ __forceinline__ void fill_tile(unsigned char* tile, int C, F src, int first = 0, int count = kT) {
+__device__ __forceinline__ void fill_tile(unsigned char* tile, int C, F src, int first = 0, int count = kT,
+                                          bool rowmajor = false) {
   constexpr int kBatch = 8;
   const int me = (int)threadIdx.x - first;
   if (me < 0 || me >= count) return;
@@ -126,12 +153,16 @@ __device__ __forceinline__ void fill_tile(unsigned char* tile, int C, F src, int
 #pragma unroll
     for (int k = 0; k < kBatch; ++k) {
       const int u = base + k * count;
-      if (u < units) src(u / cpr, (u % cpr) * 8, v[k]);
+      int r, cb;
+      if (rowmajor) { r = u / cpr; cb = u % cpr; } else { unit_rc(u, cpr, r, cb); }
+      if (u < units) src(r, cb * 8, v[k]);
     }
 #pragma unroll
     for (int k = 0; k < kBatch; ++k) {
       const int u = base + k * count;
-      if (u < units) store_unit(tile, u / cpr, u % cpr, C, v[k]);
+      if (u >= units) continue;
+      if (rowmajor) store_unit(tile, u / cpr, u % cpr, C, v[k]);
+      else *reinterpret_cast<uint4*>(tile + 16 * u) = pack_unit(v[k]);
     }
   }
 }
@@ -170,15 +201,16 @@ __device__ __forceinline__ void fill_rows_raw(unsigned char* tile, F rowp, int f
     for (int k = 0; k < kBatch; ++k) {
       const int u = base + k * count;
       if (u < kUnits) {
-        const __nv_bfloat16* row = rowp(u / kCpr);
-        v[k] = row ? reinterpret_cast<const uint4*>(row)[u % kCpr] : make_uint4(0u, 0u, 0u, 0u);
+        int r, cb;
+        unit_rc(u, kCpr, r, cb);
+        const __nv_bfloat16* row = rowp(r);
+        v[k] = row ? reinterpret_cast<const uint4*>(row)[cb] : make_uint4(0u, 0u, 0u, 0u);
       }
     }
 #pragma unroll
     for (int k = 0; k < kBatch; ++k) {
       const int u = base + k * count;
-      if (u < kUnits)
-        *reinterpret_cast<uint4*>(tile + umma::unit_off(u / kCpr, u % kCpr, kD)) = v[k];
+      if (u < kUnits) *reinterpret_cast<uint4*>(tile + 16 * u) = v[k];
     }
   }
 }
@@ -214,9 +246,10 @@ __device__ __forceinline__ void async_rows(unsigned char* tile, F rowp, const vo
   const int me = (int)threadIdx.x - first;
   if (me < 0 || me >= count) return;
   for (int u = me; u < kTileBytes / 16; u += count) {
-    const int r = u / kCpr, cb = u % kCpr;
+    int r, cb;
+    unit_rc(u, kCpr, r, cb);
     const __nv_bfloat16* row = rowp(r);
-    cp16(tile + umma::unit_off(r, cb, kD), row ? static_cast<const void*>(row + cb * 8) : base, row != nullptr);
+    cp16(tile + 16 * u, row ? static_cast<const void*>(row + cb * 8) : base, row != nullptr);
   }
 }
 // Rewrite every unit of rows [0, rows) in place: f(r, v[8]) (after the barrier
@@ -226,12 +259,14 @@ __device__ __forceinline__ void xform_rows(unsigned char* tile, int rows, F f, i
   constexpr int kCpr = kD / 8;
   const int me = (int)threadIdx.x - first;
   if (me < 0 || me >= count) return;
-  for (int u = me; u < rows * kCpr; u += count) {
-    const int r = u / kCpr, cb = u % kCpr;
+  for (int u = me; u < kR * kCpr; u += count) {
+    int r, cb;
+    unit_rc(u, kCpr, r, cb);
+    if (r >= rows) continue;
     float v[8];
-    load_unit(tile, r, cb, kD, v);
+    unpack_unit(*reinterpret_cast<const uint4*>(tile + 16 * u), v);
     f(r, v);
-    store_unit(tile, r, cb, kD, v);
+    *reinterpret_cast<uint4*>(tile + 16 * u) = pack_unit(v);
   }
 }
 

@@ -221,10 +221,11 @@ __global__ void __launch_bounds__(256) k_sref_tile(Params P) {
   const float* M = P.Sref + (int64_t)blockIdx.x * kD * kD;
   unsigned char* dst = P.srb + (int64_t)blockIdx.x * kTileBytes;
   for (int u = threadIdx.x; u < kTileBytes / 16; u += blockDim.x) {
-    const int r = u / (kD / 8), cb = u % (kD / 8);
+    int r, cb;
+    unit_rc(u, kD / 8, r, cb);
     float v[8];
     ld8f(M + r * kD + cb * 8, v);
-    store_unit(dst, r, cb, kD, v);
+    *reinterpret_cast<uint4*>(dst + 16 * u) = pack_unit(v);
   }
 }
 
@@ -234,6 +235,7 @@ __global__ void __launch_bounds__(256) k_sref_tile(Params P) {
 //   dS[d_v x d_phi]   = (diag(cS_end) delta)^T Phi,  dZ likewise with cZ_end
 // ===========================================================================
 __global__ void __launch_bounds__(kT) k_fwd_chunk_tc(Params P) {
+  PhaseClock pc;
   extern __shared__ __align__(1024) unsigned char sm[];
   unsigned char* tPhi = sm;
   unsigned char* tSref = sm + kTileBytes;  // S_ref, later diag(cZ_end) delta
@@ -252,6 +254,7 @@ __global__ void __launch_bounds__(kT) k_fwd_chunk_tc(Params P) {
   const int n = cx.n, c = cx.c, K = cx.K, L = cx.L, tid = threadIdx.x, row = row_of(), wg = wg_of();
   Sync sy{&mbar, &tbase, 0, nullptr};
   const uint32_t tm = tc_setup(sy, 256);  // (its barrier also publishes the gates)
+  pc.mark(40);
   if (wg == 0) {  // end coefficients of key j = row
     float cs_end = 0.f, cz_end = 0.f;
     fwd_column(P, cx, row, [&](int i, float cs, float, float czn) {
@@ -277,6 +280,7 @@ __global__ void __launch_bounds__(kT) k_fwd_chunk_tc(Params P) {
     loaders_sync();
     phi_xform(P, tPhi, 128, kT - 128);
   }
+  pc.mark(41);
   smem_to_tc();
   if (tid == 0) mma_chain(tm, op(tPhi, kD, 0), op(tSref, kD, 0), kD / 16, kD, false);
   const int j = row, p = cx.kp0 + j;
@@ -290,6 +294,7 @@ __global__ void __launch_bounds__(kT) k_fwd_chunk_tc(Params P) {
     for (int u = 0; u < kD / (8 * kWG); ++u) vrow[u] = src[u];
   }
   mma_wait(sy);
+  pc.mark(42);
   {
     const float ws = cSe[j], wz = cZe[j];
 #pragma unroll
@@ -323,12 +328,14 @@ __global__ void __launch_bounds__(kT) k_fwd_chunk_tc(Params P) {
       store_unit(tDZ, j, 2 * c16 + 1, kD, z1);
     }
   }
+  pc.mark(43);
   smem_to_tc();
   if (tid == 0) {
     mma_chain(tm + 128, op(tDS, kD, 1), op(tPhi, kD, 1), 8, kD, false);
     mma_chain(tm, op(tDZ, kD, 1), op(tPhi, kD, 1), 8, kD, false);  // over delta, already read
   }
   mma_wait(sy);
+  pc.mark(44);
   {  // increments: row = state row nn
     const int64_t D2 = (int64_t)kD * kD;
     const float* bufn = buf_of(P, n, c);
@@ -350,7 +357,8 @@ __global__ void __launch_bounds__(kT) k_fwd_chunk_tc(Params P) {
       st16bf(db + D2 + c16 * 16, b);
     }
   }
-  tc_teardown(tm, 256);
+  tc_teardown(tm, 256);  pc.mark(45);
+
 }
 
 // ===========================================================================
