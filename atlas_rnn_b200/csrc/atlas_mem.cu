@@ -114,10 +114,10 @@ Smem smem_sizes(const AtlasMemShape* s, int C) {
   m.fmf = 4 * (size_t)(r4(kFmTile * dk) + kStageFloats);
   m.fmb = 4 * (size_t)(2 * r4(kFmTile * dk) + r4(kFmTile * dphi) + kStageFloats);
   const int tctx = tc::ctx_floats(C, e);
-  m.tc_f1 = 3 * (size_t)tc::kTileBytes + 4 * (size_t)(tctx + 2 * tc::kR);
-  m.tc_f3 = 6 * (size_t)tc::kTileBytes + 4 * (size_t)(tctx + 2 * tc::kR);
+  m.tc_f1 = 3 * (size_t)tc::kTileBytes + 4 * (size_t)(tctx + 5 * tc::kR);
+  m.tc_f3 = 6 * (size_t)tc::kTileBytes + 4 * (size_t)(tctx + 3 * 132);
   m.buf_y = 4 * (size_t)(ctx + r4(C * (e > 1 ? e - 1 : 1)) + r4(C * dphi) + kStageFloats);
-  m.tc_b1 = 3 * (size_t)tc::kTileBytes + 4 * (size_t)(tctx + 2 * tc::kR);
+  m.tc_b1 = 3 * (size_t)tc::kTileBytes + 4 * (size_t)(tctx + 6 * 132);
   m.tc_b4 = 6 * (size_t)tc::kTileBytes + 4 * (size_t)(tctx + 3 * 132 + 4 * (tc::kT / 32) + 2 * tc::kWG * tc::kR);
   m.tc_b6 = 6 * (size_t)tc::kTileBytes +
             4 * (size_t)(tctx + 6 * 132 + 4 * tc::kR + 4 + tc::kR + tc::kGateParts * (tc::kWG - 1) * tc::kR);

@@ -87,27 +87,29 @@ __global__ void __launch_bounds__(kT) k_bwd_chunk_tc(Params P) {
   async_rows_psi(P, cx, tPsi);
   async_rows_dy(P, cx, tYS);
   load_ctx(P, sa, cx, kT);
-  float* eS0 = sa.take(kR);
-  float* eZ0 = sa.take(kR);
+  float* eS0 = sa.take(kR + 1);
+  float* eZ0 = sa.take(kR + 1);
+  float* zZ = sa.take(kR + 1);
+  float* hS = sa.take(kR + 1);
+  float* hZS = sa.take(kR + 1);
+  float* hZZ = sa.take(kR + 1);
   const int L = cx.L, tid = threadIdx.x, row = row_of(), wg = wg_of();
   Sync sy{&mbar, &tbase, 0, nullptr};
   const uint32_t tm = tc_setup(sy, 256);
   pc.mark(48);
-  if (wg == 0) {  // adjoint weights of token q at the chunk input
-    float es = 0.f, ez = 0.f;
-    adj_column_z(cx, row, [](int, float, float) {}, &es, &ez);
-    eS0[row] = es;
-    eZ0[row] = ez;
-  } else if (wg == 1 && row == 0) {
-    float hs = 1.f, hzs = -cx.et[L - 1], hzz = 1.f;
-    for (int r = L - 1; r >= 0; --r) {
-      const float eta = r >= 1 ? cx.et[r - 1] : 0.f;
-      hs = cx.al[r] * hs;
-      hzz = cx.be[r] * hzz;
-      hzs = cx.be[r] * hzs - eta * hs;
+  // adjoint weights of token q at the chunk input: eS_0[q], eZ_0[q] equal the
+  // forward state scalars sS[q], sZ[q] (the adjoint and forward recurrences are
+  // transposes of each other); the chunk's adjoint transform is hS, hZS, hZZ at row 0
+  if (tid < 32) {
+    fwd_scalars_warp(cx, eS0, eZ0, zZ);
+    if (tid == 0)
+      for (int q = L; q < kR; ++q) { eS0[q] = 0.f; eZ0[q] = 0.f; }
+  } else if (tid < 64) {
+    adj_scalars_warp(cx, hS, hZS, hZZ);
+    if (tid == 32) {
+      float* o = P.acs + chunk_id(P, cx) * 4;
+      o[0] = hS[0]; o[1] = hZS[0]; o[2] = hZZ[0]; o[3] = 0.f;
     }
-    float* o = P.acs + chunk_id(P, cx) * 4;
-    o[0] = hs; o[1] = hzs; o[2] = hzz; o[3] = 0.f;
   }
   async_wait();
   __syncthreads();
@@ -192,7 +194,7 @@ __global__ void __launch_bounds__(kT) k_bwd_state_tc(Params P) {
   async_copy_tile(tFZ, FS + kTileBytes);
   __syncthreads();
   pc.mark(32);
-  if (tid == 0) fwd_scalars(cx, sS, sZ, zZ);
+  if (tid < 32) fwd_scalars_warp(cx, sS, sZ, zZ);
   async_wait();
   __syncthreads();
   phi_xform(P, tPsi);
@@ -343,9 +345,8 @@ __global__ void __launch_bounds__(kT) k_bwd_keys_tc(Params P) {
   if (wg == 0) {
     fwd_column_z(P, cx, row, [&](int i, float cs, float, float) { st_bf(tM3, i, row, cs); });
     if (row == 0) pc.lap(12);
-  } else if (wg == 1 && row == 0) {
-    adj_scalars(cx, hS, hZS, hZZ);
-    pc.lap(13);
+  } else if (wg == 1 && row < 32) {
+    adj_scalars_warp(cx, hS, hZS, hZZ);
   }
   async_wait();
   if (wg > 0) {
@@ -544,10 +545,10 @@ __global__ void __launch_bounds__(kT) k_bwd_gates_tc(Params P) {
       st_bf(tES, i, q, es);
       st_bf(tEZ, i, q, ez);
     });
-  } else if (wg == 2 && row == 0) {
-    fwd_scalars(cx, sS, sZ, zZ);
-  } else if (wg == 3 && row == 0) {
-    adj_scalars(cx, hS, hZS, hZZ);
+  } else if (wg == 2 && row < 32) {
+    fwd_scalars_warp(cx, sS, sZ, zZ);
+  } else if (wg == 3 && row < 32) {
+    adj_scalars_warp(cx, hS, hZS, hZZ);
   }
   async_wait();
   pc.mark(25);

@@ -127,6 +127,80 @@ __device__ __forceinline__ void load_unit(const unsigned char* tile, int r, int 
   }
 }
 
+// Affine recurrence over the L <= 128 tokens of a chunk on one warp (all 32
+// lanes call it): x = x0 before the first step, then x <- a(i) x + b(i) for
+// i = 0 .. L-1 (FWD) or i = L-1 .. 0 (!FWD); out(i, x) receives x after step i.
+// Each lane composes 4 consecutive steps into one affine map; the lane maps
+// are combined by 5 shuffle rounds (prefix of maps), so the chain costs
+// O(log) instead of L dependent steps.
+template <bool FWD, class FA, class FB, class FO>
+__device__ __forceinline__ void warp_affine_scan(int L, float x0, FA fa, FB fb, FO out) {
+  const int lane = threadIdx.x & 31;
+  float ak[4], bk[4], A = 1.f, B = 0.f;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int st = 4 * lane + k, i = FWD ? st : L - 1 - st;
+    ak[k] = 1.f;
+    bk[k] = 0.f;
+    if (st < L) {
+      ak[k] = fa(i);
+      bk[k] = fb(i);
+    }
+    B = ak[k] * B + bk[k];
+    A = ak[k] * A;
+  }
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {  // inclusive prefix of the lane maps
+    const float Ap = __shfl_up_sync(0xffffffffu, A, off), Bp = __shfl_up_sync(0xffffffffu, B, off);
+    if (lane >= off) {
+      B = A * Bp + B;
+      A = A * Ap;
+    }
+  }
+  float Ae = __shfl_up_sync(0xffffffffu, A, 1), Be = __shfl_up_sync(0xffffffffu, B, 1);
+  if (lane == 0) { Ae = 1.f; Be = 0.f; }
+  float x = Ae * x0 + Be;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int st = 4 * lane + k, i = FWD ? st : L - 1 - st;
+    if (st < L) {
+      x = ak[k] * x + bk[k];
+      out(i, x);
+    }
+  }
+}
+
+// State-path scalars of the chunk after i tokens (i = 0..L), one warp:
+// sS[i] = prod alpha, zZ[i] = prod beta, sZ[i+1] = alpha_i sZ[i] - eta_i zZ[i+1].
+__device__ __forceinline__ void fwd_scalars_warp(const Ctx& cx, float* sS, float* sZ, float* zZ) {
+  const int L = cx.L;
+  if ((threadIdx.x & 31) == 0) { sS[0] = 1.f; sZ[0] = 0.f; zZ[0] = 1.f; }
+  warp_affine_scan<true>(L, 1.f, [&](int i) { return cx.al[i]; }, [](int) { return 0.f; },
+                         [&](int i, float x) { sS[i + 1] = x; });
+  warp_affine_scan<true>(L, 1.f, [&](int i) { return cx.be[i]; }, [](int) { return 0.f; },
+                         [&](int i, float x) { zZ[i + 1] = x; });
+  __syncwarp();
+  warp_affine_scan<true>(L, 0.f, [&](int i) { return cx.al[i]; }, [&](int i) { return -cx.et[i] * zZ[i + 1]; },
+                         [&](int i, float x) { sZ[i + 1] = x; });
+  __syncwarp();
+}
+// Adjoint-transform scalars of the chunk from its end down to row r (r = 0..L),
+// one warp: hS[r] = alpha_r hS[r+1], hZZ[r] = beta_r hZZ[r+1],
+// hZS[r] = beta_r hZS[r+1] - eta_{r-1} hS[r]; hS[L] = hZZ[L] = 1, hZS[L] = -eta_{L-1}.
+__device__ __forceinline__ void adj_scalars_warp(const Ctx& cx, float* hS, float* hZS, float* hZZ) {
+  const int L = cx.L;
+  if ((threadIdx.x & 31) == 0) { hS[L] = 1.f; hZZ[L] = 1.f; hZS[L] = -cx.et[L - 1]; }
+  warp_affine_scan<false>(L, 1.f, [&](int r) { return cx.al[r]; }, [](int) { return 0.f; },
+                          [&](int r, float x) { hS[r] = x; });
+  warp_affine_scan<false>(L, 1.f, [&](int r) { return cx.be[r]; }, [](int) { return 0.f; },
+                          [&](int r, float x) { hZZ[r] = x; });
+  __syncwarp();
+  warp_affine_scan<false>(L, -cx.et[L - 1], [&](int r) { return cx.be[r]; },
+                          [&](int r) { return -(r >= 1 ? cx.et[r - 1] : 0.f) * hS[r]; },
+                          [&](int r, float x) { hZS[r] = x; });
+  __syncwarp();
+}
+
 // Unit u of a 128 x C tile (cpr = C / 8 units per row) in shared-memory address
 // order: unit_off(r, cb, C) == 16 u, so consecutive threads touch consecutive
 // 16-byte units (no bank conflicts), and a warp covers 8 rows x 4 column blocks

@@ -251,35 +251,47 @@ __global__ void __launch_bounds__(kT) k_fwd_chunk_tc(Params P) {
   load_ctx(P, sa, cx, kT);
   float* cSe = sa.take(kR);
   float* cZe = sa.take(kR);
+  float* Asuf = sa.take(kR);
+  float* Bsuf = sa.take(kR);
+  float* Hs = sa.take(kR);
   const int n = cx.n, c = cx.c, K = cx.K, L = cx.L, tid = threadIdx.x, row = row_of(), wg = wg_of();
   Sync sy{&mbar, &tbase, 0, nullptr};
   const uint32_t tm = tc_setup(sy, 256);  // (its barrier also publishes the gates)
   pc.mark(40);
-  if (wg == 0) {  // end coefficients of key j = row
-    float cs_end = 0.f, cz_end = 0.f;
-    fwd_column(P, cx, row, [&](int i, float cs, float, float czn) {
-      if (i == L - 1) {
-        cz_end = czn;
-        cs_end = cx.al[i] * cs - cx.et[i] * czn;
-      }
-    });
-    cSe[row] = cs_end;
-    cZe[row] = cz_end;
-  } else if (wg == 1 && row == 0) {  // chunk transform scalars
-    float s = 1.f, sz = 0.f, z = 1.f;
-    for (int i = 0; i < L; ++i) {
-      z = cx.be[i] * z;
-      s = cx.al[i] * s;
-      sz = cx.al[i] * sz - cx.et[i] * z;
+  // End coefficients of key j from suffix sequences of the chunk (no per-key chain):
+  //   cZ_end[j] = sum_m W(m, j) Bsuf[m],   Bsuf[m] = prod_{l > m} beta_l
+  //   cS_end[j] = -sum_m W(m, j) H[m],     H[m] = Asuf[m] eta_m + beta_{m+1} H[m+1],
+  // Asuf[m] = prod_{l > m} alpha_l, m over the key's window tokens only; the chunk
+  // transform is (alpha_0 Asuf[0], -beta_0 H[0], beta_0 Bsuf[0]).
+  if (tid < 32) {
+    warp_affine_scan<false>(L, 1.f, [&](int m) { return m < L - 1 ? cx.al[m + 1] : 1.f; }, [](int) { return 0.f; },
+                            [&](int m, float x) { Asuf[m] = x; });
+    __syncwarp();
+    warp_affine_scan<false>(L, 0.f, [&](int m) { return m < L - 1 ? cx.be[m + 1] : 0.f; },
+                            [&](int m) { return Asuf[m] * cx.et[m]; }, [&](int m, float x) { Hs[m] = x; });
+  } else if (tid < 64) {
+    warp_affine_scan<false>(L, 1.f, [&](int m) { return m < L - 1 ? cx.be[m + 1] : 1.f; }, [](int) { return 0.f; },
+                            [&](int m, float x) { Bsuf[m] = x; });
+  }
+  __syncthreads();
+  if (wg == 0) {
+    const int j = row;
+    float cs = 0.f, cz = 0.f;
+    for (int m = max(0, j - (P.e - 1)); m <= min(L - 1, j); ++m) {
+      const float w = wgt(P, cx, m, j);
+      cz += w * Bsuf[m];
+      cs -= w * Hs[m];
     }
-    float* o = P.cs + ((int64_t)n * P.nch + c) * 4;
-    o[0] = s; o[1] = sz; o[2] = z; o[3] = 0.f;
+    cSe[j] = cs;
+    cZe[j] = cz;
+    if (j == 0) {
+      float* o = P.cs + ((int64_t)n * P.nch + c) * 4;
+      o[0] = cx.al[0] * Asuf[0]; o[1] = -cx.be[0] * Hs[0]; o[2] = cx.be[0] * Bsuf[0]; o[3] = 0.f;
+    }
   }
   async_wait();
-  if (wg > 0) {
-    loaders_sync();
-    phi_xform(P, tPhi, 128, kT - 128);
-  }
+  __syncthreads();
+  phi_xform(P, tPhi);
   pc.mark(41);
   smem_to_tc();
   if (tid == 0) mma_chain(tm, op(tPhi, kD, 0), op(tSref, kD, 0), kD / 16, kD, false);
@@ -390,8 +402,9 @@ __global__ void __launch_bounds__(kT) k_fwd_out_tc(Params P) {
   }
   zero_tile(tMs);
   load_ctx(P, sa, cx, kT);
-  float* sSv = sa.take(kR);
-  float* sZv = sa.take(kR);
+  float* sSv = sa.take(kR + 1);
+  float* sZv = sa.take(kR + 1);
+  float* zZv = sa.take(kR + 1);
   const int n = cx.n, L = cx.L, tid = threadIdx.x, row = row_of(), wg = wg_of();
   Sync sy{&mbar, &tbase, 0, nullptr};
   const uint32_t tm = tc_setup(sy);  // (its barrier also publishes the gates)
@@ -399,15 +412,8 @@ __global__ void __launch_bounds__(kT) k_fwd_out_tc(Params P) {
   if (wg == 0) {  // column j = row of tMs: cS of key j before each token i (tile zero-filled)
     const int j = row;
     fwd_column_z(P, cx, j, [&](int i, float cs, float, float) { st_bf(tMs, i, j, cs); });
-  } else if (wg == 1 && row == 0) {
-    float s = 1.f, sz = 0.f, z = 1.f;
-    for (int i = 0; i < L; ++i) {
-      sSv[i] = s;
-      sZv[i] = sz;
-      z = cx.be[i] * z;
-      s = cx.al[i] * s;
-      sz = cx.al[i] * sz - cx.et[i] * z;
-    }
+  } else if (wg == 1 && row < 32) {
+    fwd_scalars_warp(cx, sSv, sZv, zZv);  // state-path scalars before token i
   }
   async_wait();
   if (wg > 0) {
