@@ -47,7 +47,7 @@ struct Layout {
   size_t saved, fwd, bwd;
   size_t st, delta, ST, cs, phik, phiq, dlb, stb, srb;         // in saved
   size_t adj, acs, dpsi, ddel, dphiR, hdd, hdp, du, hdu;       // in bwd scratch
-  size_t xq, xf, xs, gt, adjb;                                  // in bwd scratch (tensor-core path)
+  size_t xq, xf, xs, gt, adjb, ddb, dpb;                        // in bwd scratch (tensor-core path)
 };
 
 Layout make_layout(const AtlasMemShape* s) {
@@ -87,6 +87,8 @@ Layout make_layout(const AtlasMemShape* s) {
     L.xs = put(N * nch * 4 * 4);
     L.gt = put(N * nch * (size_t)tc::kTileBytes);
     L.adjb = put(N * nch * 2 * (size_t)tc::kTileBytes);
+    L.ddb = put(N * T * s->d_v * 2);
+    L.dpb = put(N * T * s->d_phi * 2);
   }
   L.bwd = o;
   return L;
@@ -240,6 +242,8 @@ Params make_params(const AtlasMemShape* s, const Layout& L, const AtlasMemFwd* f
     if (tc_groups(s) & 8) {
       P.xq = (float*)(sc + L.xq); P.xf = (float*)(sc + L.xf); P.xs = (float*)(sc + L.xs); P.gt = sc + L.gt;
       P.adjb = (unsigned char*)(sc + L.adjb);
+      P.ddb = (__nv_bfloat16*)(sc + L.ddb);
+      P.dpb = (__nv_bfloat16*)(sc + L.dpb);
     }
   }
   P.apply_mask = 1;

@@ -767,12 +767,16 @@ __global__ void __launch_bounds__(kThreads) k_bwd_bufout(Params P) {
   for (int nn = threadIdx.x; nn < dv; nn += kThreads) {
     float s = 0.f;
     for (int m = 0; m < dphi; ++m) s += G[nn * dphi + m] * ph[m];
-    P.ddel[((int64_t)n * P.T + p) * dv + nn] += w * s;
+    const int64_t o = ((int64_t)n * P.T + p) * dv + nn;
+    if (P.ddb) P.ddb[o] = __float2bfloat16_rn(__bfloat162float(P.ddb[o]) + w * s);  // tensor-core hand-off
+    else P.ddel[o] += w * s;
   }
   for (int m = threadIdx.x; m < dphi; m += kThreads) {
     float s = 0.f;
     for (int nn = 0; nn < dv; ++nn) s += G[nn * dphi + m] * dl[nn];
-    P.dphiR[((int64_t)n * P.T + p) * dphi + m] += w * s;
+    const int64_t o = ((int64_t)n * P.T + p) * dphi + m;
+    if (P.dpb) P.dpb[o] = __float2bfloat16_rn(__bfloat162float(P.dpb[o]) + w * s);
+    else P.dphiR[o] += w * s;
   }
   if (P.gmode == ATLAS_GATE_TOKEN) {
     float s = 0.f;

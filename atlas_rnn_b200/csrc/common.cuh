@@ -48,6 +48,8 @@ struct Params {
   unsigned char* adjb;  // [N][nch][2] 128x128 bf16 tiles of the adjoint at each chunk end
   int inc_bf16;         // chunk increments in `st` / `adj` are bf16 (tensor-core path)
   void* gt;             // [N][nch] 128x128 bf16 Gram blocks (core-matrix tile layout)
+  __nv_bfloat16* ddb;   // [N][T][dv]   d delta of each chunk's own keys (bf16 hand-off to finalize)
+  __nv_bfloat16* dpb;   // [N][T][dphi] d phi of each chunk's own keys (bf16 hand-off to finalize)
   int apply_mask;
   // sequence-parallel segment outputs
   float *seg_coef, *seg_dS, *seg_dZ;

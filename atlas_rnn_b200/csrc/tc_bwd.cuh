@@ -454,8 +454,11 @@ __global__ void __launch_bounds__(kT) k_bwd_keys_tc(Params P) {
     const int r = row, p = cx.kp0 + r;
     const bool own = r < K && p >= cx.t0, halo = r < K && p >= 0 && p < cx.t0;
     const int e1 = e > 1 ? e - 1 : 1;
-    float* dd = own ? P.ddel + ((int64_t)n * P.T + p) * P.dv : P.hdd + (cid * e1 + (r < e - 1 ? r : 0)) * P.dv;
-    float* dp = own ? P.dphiR + ((int64_t)n * P.T + p) * P.dphi : P.hdp + (cid * e1 + (r < e - 1 ? r : 0)) * P.dphi;
+    // own keys: bf16 hand-off to finalize; halo keys (of the previous chunk's tokens): fp32 partials
+    __nv_bfloat16* ddo = P.ddb + ((int64_t)n * P.T + (own ? p : 0)) * P.dv;
+    __nv_bfloat16* dpo = P.dpb + ((int64_t)n * P.T + (own ? p : 0)) * P.dphi;
+    float* ddh = P.hdd + (cid * e1 + (r < e - 1 ? r : 0)) * P.dv;
+    float* dph = P.hdp + (cid * e1 + (r < e - 1 ? r : 0)) * P.dphi;
     float* dq = P.dpsi + ((int64_t)n * P.T + cx.t0 + (r < L ? r : 0)) * P.dphi;
     for (int h = 0; h < kCPW; ++h) {
       const int c16 = wg * kCPW + h;
@@ -464,9 +467,12 @@ __global__ void __launch_bounds__(kT) k_bwd_keys_tc(Params P) {
       umma::tmem_ld16(lane_addr(tm, 256 + c16 * 16), b);
       umma::tmem_ld16(lane_addr(tm, 128 + c16 * 16), i5);
       umma::tmem_ld_wait();
-      if (own || halo) {
-        st16f(dd + c16 * 16, a);
-        st16f(dp + c16 * 16, b);
+      if (own) {
+        st16bf(ddo + c16 * 16, a);
+        st16bf(dpo + c16 * 16, b);
+      } else if (halo) {
+        st16f(ddh + c16 * 16, a);
+        st16f(dph + c16 * 16, b);
       }
       if (r < L)
 #pragma unroll
@@ -783,7 +789,7 @@ __global__ void __launch_bounds__(kT) k_bwd_finalize_tc(Params P) {
     if (r >= TT) { zero8(v); return; }
     const int p = p0 + r;
     const int64_t gi = ((int64_t)n * P.T + p) * P.dv + c0;
-    ld8f(P.ddel + gi, v);
+    ld8io(P.ddb, gi, 1, v);
     const int64_t h = halo(p);
     if (h >= 0) {
       float a[8];
@@ -791,10 +797,12 @@ __global__ void __launch_bounds__(kT) k_bwd_finalize_tc(Params P) {
 #pragma unroll
       for (int k = 0; k < 8; ++k) v[k] += a[k];
     }
-    // final d delta back (for dS_ref) and dv = -d delta  (delta = pred - v, rnn_memory.py:660)
-    float4* dst = reinterpret_cast<float4*>(P.ddel + gi);
-    dst[0] = make_float4(v[0], v[1], v[2], v[3]);
-    dst[1] = make_float4(v[4], v[5], v[6], v[7]);
+    // final d delta (fp32, only for the dS_ref reduction) and dv = -d delta  (delta = pred - v, rnn_memory.py:660)
+    if (P.dSref) {
+      float4* dst = reinterpret_cast<float4*>(P.ddel + gi);
+      dst[0] = make_float4(v[0], v[1], v[2], v[3]);
+      dst[1] = make_float4(v[4], v[5], v[6], v[7]);
+    }
     if (P.dv_) {
       __align__(16) __nv_bfloat162 hb[4];
 #pragma unroll
@@ -844,8 +852,8 @@ __global__ void __launch_bounds__(kT) k_bwd_finalize_tc(Params P) {
       if (r < TT) {
         const int64_t gi = ((int64_t)n * P.T + p) * P.dphi + c16 * 16;
         float w0[8], w1[8];
-        ld8f(P.dphiR + gi, w0);
-        ld8f(P.dphiR + gi + 8, w1);
+        ld8io(P.dpb, gi, 1, w0);
+        ld8io(P.dpb, gi + 8, 1, w1);
 #pragma unroll
         for (int k = 0; k < 8; ++k) { a[k] += w0[k]; a[8 + k] += w1[k]; }
         if (h >= 0) {
