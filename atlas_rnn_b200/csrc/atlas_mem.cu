@@ -47,7 +47,7 @@ struct Layout {
   size_t saved, fwd, bwd;
   size_t st, delta, ST, cs, phik, phiq, dlb, stb, srb;         // in saved
   size_t adj, acs, dpsi, ddel, dphiR, hdd, hdp, du, hdu;       // in bwd scratch
-  size_t xq, xf, xs, gt, adjb, ddb, dpb;                        // in bwd scratch (tensor-core path)
+  size_t xq, xf, xs, gt, adjb, ddb, dpb, dpsib;                 // in bwd scratch (tensor-core path)
 };
 
 Layout make_layout(const AtlasMemShape* s) {
@@ -89,6 +89,7 @@ Layout make_layout(const AtlasMemShape* s) {
     L.adjb = put(N * nch * 2 * (size_t)tc::kTileBytes);
     L.ddb = put(N * T * s->d_v * 2);
     L.dpb = put(N * T * s->d_phi * 2);
+    L.dpsib = put(N * T * s->d_phi * 2);
   }
   L.bwd = o;
   return L;
@@ -244,6 +245,7 @@ Params make_params(const AtlasMemShape* s, const Layout& L, const AtlasMemFwd* f
       P.adjb = (unsigned char*)(sc + L.adjb);
       P.ddb = (__nv_bfloat16*)(sc + L.ddb);
       P.dpb = (__nv_bfloat16*)(sc + L.dpb);
+      P.dpsib = (__nv_bfloat16*)(sc + L.dpsib);
     }
   }
   P.apply_mask = 1;
@@ -412,8 +414,8 @@ int run_bwd_finish(const AtlasMemShape* s, const Params& P, cudaStream_t st) {
   if (int v = launch_scan(false, P, 0, st)) return v;
   if (tc_groups(s) & 8) {
     const dim3 g(P.nch, P.N);
+    LAUNCH_T(KID_BWD_KEYS_TC, tc::k_bwd_keys_tc, g, tc::kT, m.tc_b6, st, P);  // d psi part I5 first
     LAUNCH_T(KID_BWD_STATE_TC, tc::k_bwd_state_tc, g, tc::kT, m.tc_b4, st, P);
-    LAUNCH_T(KID_BWD_KEYS_TC, tc::k_bwd_keys_tc, g, tc::kT, m.tc_b6, st, P);
     if (P.e > 1 && (P.buf || P.dbuf)) LAUNCH(KID_BWD_BUF_TC, tc::k_bwd_buf_tc, dim3(1, P.N), m.buf_b, st, P);
     LAUNCH_T(KID_BWD_GATES_TC, tc::k_bwd_gates_tc, g, tc::kT, m.tc_b6, st, P);
   } else {

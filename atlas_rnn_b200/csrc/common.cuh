@@ -50,6 +50,7 @@ struct Params {
   void* gt;             // [N][nch] 128x128 bf16 Gram blocks (core-matrix tile layout)
   __nv_bfloat16* ddb;   // [N][T][dv]   d delta of each chunk's own keys (bf16 hand-off to finalize)
   __nv_bfloat16* dpb;   // [N][T][dphi] d phi of each chunk's own keys (bf16 hand-off to finalize)
+  __nv_bfloat16* dpsib; // [N][T][dphi] d psi (tensor-core path: keys part, then + state part)
   int apply_mask;
   // sequence-parallel segment outputs
   float *seg_coef, *seg_dS, *seg_dZ;

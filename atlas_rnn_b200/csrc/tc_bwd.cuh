@@ -157,7 +157,8 @@ __global__ void __launch_bounds__(kT) k_bwd_chunk_tc(Params P) {
 
 // ===========================================================================
 // state side: G_S = Psi S_in^T, G_Z = Psi Z_in^T (-> X[D_q][S_in], X[D_q][Z_in]),
-// H_S = dY S_in, H_Z = dY Z_in (-> d psi = sS H_S + sZ H_Z, written with '='),
+// H_S = dY S_in, H_Z = dY Z_in (-> d psi = I5 + sS H_S + sZ H_Z, I5 from k_bwd_keys_tc
+// which runs first; d psi leaves as bf16),
 // and the four Gram scalars <F_S|F_Z, S_in|Z_in> from the staged tiles while
 // the MMAs run.
 // ===========================================================================
@@ -233,13 +234,24 @@ __global__ void __launch_bounds__(kT) k_bwd_state_tc(Params P) {
       if ((tid & 31) == 0) red[k * (kT / 32) + (tid >> 5)] = t;
     }
   }
+  // d psi part I5 of this thread's row (k_bwd_keys_tc), fetched while the MMAs run
+  const int64_t grow = (int64_t)n * P.T + cx.t0 + row;
+  uint4 i5v[kCPW][2];
+#pragma unroll
+  for (int h = 0; h < kCPW; ++h) {
+    i5v[h][0] = i5v[h][1] = make_uint4(0u, 0u, 0u, 0u);
+    if (row < L) {
+      const uint4* src = reinterpret_cast<const uint4*>(P.dpsib + grow * P.dphi + (wg * kCPW + h) * 16);
+      i5v[h][0] = src[0];
+      i5v[h][1] = src[1];
+    }
+  }
   mma_wait(sy);
   pc.mark(34);
   {
     const int q = row;
     float xs = 0.f, xz = 0.f;
     const float ss = q < L ? sS[q] : 0.f, sz = q < L ? sZ[q] : 0.f;
-    const int64_t grow = (int64_t)n * P.T + cx.t0 + q;
 #pragma unroll
     for (int h = 0; h < kCPW; ++h) {
       const int c16 = wg * kCPW + h;
@@ -257,10 +269,15 @@ __global__ void __launch_bounds__(kT) k_bwd_state_tc(Params P) {
           xs += gs[i] * y0[i] + gs[8 + i] * y1[i];
           xz += gz[i] * y0[i] + gz[8 + i] * y1[i];
         }
-        float d[16];
+        float d[16], i0[8], i1[8];
+        unpack_unit(i5v[h][0], i0);
+        unpack_unit(i5v[h][1], i1);
 #pragma unroll
-        for (int i = 0; i < 16; ++i) d[i] = ss * hs[i] + sz * hz[i];
-        st16f(P.dpsi + grow * P.dphi + c16 * 16, d);
+        for (int i = 0; i < 8; ++i) {
+          d[i] = ss * hs[i] + sz * hz[i] + i0[i];
+          d[8 + i] = ss * hs[8 + i] + sz * hz[8 + i] + i1[i];
+        }
+        st16bf(P.dpsib + grow * P.dphi + c16 * 16, d);
       }
     }
     part[(wg * 2 + 0) * kR + q] = xs;
@@ -305,7 +322,7 @@ __device__ __forceinline__ void key_adj_weights(const Params& P, const Ctx& cx, 
 //   phase 2  A1 = dY delta^T, A2 = Psi Phi^T -> G = A1 o A2 (scratch), M3 = cS o A1,
 //            M1 = cS o A2
 //   phase 3  d delta += M1 dY, d phi += M3^T Psi (accumulating in TMEM), I5 = M3 Phi
-//   out      d delta, d phi written once (own keys / halo partials); d psi += I5
+//   out      d delta, d phi written once (own keys / halo partials); d psi = I5 (bf16)
 // The window-summed adjoint weight of key j for token q, sum_i W(i, j) eZ_{i+1}[q],
 // equals the forward coefficient cS_q[j] (both are
 // -sum_{n<q} prod_{l=n+1}^{q-1} alpha_l eta_n sum_{m<=n} prod_{l=m+1}^{n} beta_l W(m, j)),
@@ -459,7 +476,7 @@ __global__ void __launch_bounds__(kT) k_bwd_keys_tc(Params P) {
     __nv_bfloat16* dpo = P.dpb + ((int64_t)n * P.T + (own ? p : 0)) * P.dphi;
     float* ddh = P.hdd + (cid * e1 + (r < e - 1 ? r : 0)) * P.dv;
     float* dph = P.hdp + (cid * e1 + (r < e - 1 ? r : 0)) * P.dphi;
-    float* dq = P.dpsi + ((int64_t)n * P.T + cx.t0 + (r < L ? r : 0)) * P.dphi;
+    __nv_bfloat16* dq = P.dpsib + ((int64_t)n * P.T + cx.t0 + (r < L ? r : 0)) * P.dphi;
     for (int h = 0; h < kCPW; ++h) {
       const int c16 = wg * kCPW + h;
       float a[16], b[16], i5[16];
@@ -474,10 +491,7 @@ __global__ void __launch_bounds__(kT) k_bwd_keys_tc(Params P) {
         st16f(ddh + c16 * 16, a);
         st16f(dph + c16 * 16, b);
       }
-      if (r < L)
-#pragma unroll
-        for (int k = 0; k < 16; k += 4)  // onto the state part k_bwd_state_tc wrote
-          atomicAdd(reinterpret_cast<float4*>(dq + c16 * 16 + k), make_float4(i5[k], i5[k + 1], i5[k + 2], i5[k + 3]));
+      if (r < L) st16bf(dq + c16 * 16, i5);  // k_bwd_state_tc adds the state part
     }
   }
   pc.mark(10);
@@ -729,7 +743,10 @@ __global__ void __launch_bounds__(kThreads) k_bwd_buf_tc(Params P) {
               [&](int m, int c) { return bufn[(int64_t)c * dphi + m]; }));
     // d psi_i += sum_jb cS_i[jb] Buf_jb^T dy_i
     bgemm(stage, L, dphi,
-          [&](int i, int m, float acc) { P.dpsi[((int64_t)n * P.T + i) * dphi + m] += acc; },
+          [&](int i, int m, float acc) {
+            __nv_bfloat16* d = P.dpsib + ((int64_t)n * P.T + i) * dphi + m;
+            *d = __float2bfloat16_rn(__bfloat162float(*d) + acc);
+          },
           seg(e1 * dv,
               [&](int i, int kk) { return cSb[i * e1 + kk / dv] * dy[i * dv + kk % dv]; },
               [&](int kk, int m) { return bufn[(int64_t)kk * dphi + m]; }));
@@ -820,7 +837,7 @@ __global__ void __launch_bounds__(kT) k_bwd_finalize_tc(Params P) {
       const int r = x / (P.dphi / 8), c0 = (x % (P.dphi / 8)) * 8;
       const int64_t gi = ((int64_t)n * P.T + p0 + r) * P.dphi + c0;
       float g[8], q[8];
-      ld8f(P.dpsi + gi, g);
+      ld8io(P.dpsib, gi, 1, g);
       ld8io(P.q, gi, P.bf, q);
       __align__(16) __nv_bfloat162 hb[4];
 #pragma unroll
@@ -828,6 +845,16 @@ __global__ void __launch_bounds__(kT) k_bwd_finalize_tc(Params P) {
         hb[k] = __floats2bfloat162_rn(g[2 * k] * fmap_elem_grad(q[2 * k], P.fmode, P.fdeg),
                                       g[2 * k + 1] * fmap_elem_grad(q[2 * k + 1], P.fmode, P.fdeg));
       *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(P.dq_) + gi) = *reinterpret_cast<uint4*>(hb);
+    }
+  if (P.fmode == ATLAS_FMAP_TENSOR && P.dq_)  // the feature-map backward reads d psi as fp32
+    for (int x = tid; x < TT * (P.dphi / 8); x += kT) {
+      const int r = x / (P.dphi / 8), c0 = (x % (P.dphi / 8)) * 8;
+      const int64_t gi = ((int64_t)n * P.T + p0 + r) * P.dphi + c0;
+      float g[8];
+      ld8io(P.dpsib, gi, 1, g);
+      float4* d = reinterpret_cast<float4*>(P.dpsi + gi);
+      d[0] = make_float4(g[0], g[1], g[2], g[3]);
+      d[1] = make_float4(g[4], g[5], g[6], g[7]);
     }
   if (P.gmode == ATLAS_GATE_TOKEN && P.dgate)
     for (int r = tid; r < TT; r += kT) {

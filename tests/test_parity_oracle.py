@@ -124,6 +124,7 @@ CASES_TC = [
     W("tc_omega_e16_token", 200, d=128, e=16, gate="token", dtype=torch.bfloat16),
     W("tc_nomom_e2", 130, d=128, e=2, gate="token", mom=False, dtype=torch.bfloat16),
     W("tc_short", 5, d=128, e=3, gate="token", dtype=torch.bfloat16),
+    W("tc_tensor_fmap", 150, d=8, dphi=128, dv=128, e=3, gate="token", fm="tensor", deg=2, dtype=torch.bfloat16),
 ]
 
 
