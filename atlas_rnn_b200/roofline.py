@@ -73,3 +73,41 @@ def kernel_flops(name: str, w: Workload, C: int) -> float:
             raise KeyError(name)
         total += 2.0 * fma
     return total * w.N
+
+
+def kernel_bytes(name: str, w: Workload, C: int) -> float:
+    """Compulsory HBM bytes of one launch of a tensor-core kernel (bf16 io,
+    d_phi = d_v = 128): every operand it must read once and every result it must
+    write, per chunk of L tokens with K = L + e - 1 keys, without re-reads and
+    without padding rows. A row of a [*, 128] bf16 matrix is 256 B, a 128 x 128
+    bf16 tile 32 KB; per-token gates are (3 + n_u) bf16 values (n_u = 1 or e)."""
+    e = w.window
+    row, tile = 2.0 * w.d_v, 2.0 * w.d_v * w.d_phi
+    ng = 3 + (1 if w.gate == "token" else (e if w.gate == "window" else 0))
+    total = 0.0
+    if name == "k_bwd_finalize_tc":  # per 128-token tile
+        for t0 in range(0, w.T, 128):
+            TT = min(128, w.T - t0)
+            # reads d delta, d phi (bf16 hand-off), d psi, q, k; writes dv, dq, dk
+            total += 8 * TT * row + 2 * (e - 1) * 2 * row
+        return total * w.N
+    for t0 in range(0, w.T, C):
+        L = min(C, w.T - t0)
+        K = L + e - 1
+        gates = 2.0 * ng * L
+        if name == "k_fwd_chunk_tc":    # k, v rows in; delta rows, two increment tiles out
+            b = 2 * K * row + L * row + 2 * tile
+        elif name == "k_fwd_out_tc":    # q, k, delta rows and the two state tiles in; y out
+            b = L * row + 2 * K * row + 2 * tile + L * row
+        elif name == "k_bwd_chunk_tc":  # q, dy rows in; two adjoint increment tiles out
+            b = 2 * L * row + 2 * tile
+        elif name == "k_bwd_state_tc":  # q, dy rows, state and adjoint tiles in; d psi read and written
+            b = 2 * L * row + 4 * tile + 2 * L * row
+        elif name == "k_bwd_keys_tc":   # k, delta, q, dy rows and adjoint tiles in; G, d delta, d phi, d psi out
+            b = 2 * K * row + 2 * L * row + 2 * tile + tile + 2 * L * row + 4 * (e - 1) * row + L * row
+        elif name == "k_bwd_gates_tc":  # Gram block and pieces in; gate gradients out
+            b = tile + 2 * 1024 + gates
+        else:
+            raise KeyError(name)
+        total += b + gates
+    return total * w.N

@@ -240,7 +240,7 @@ def traffic_from_profiles(kernel: str, workload: str):
 def run_ours(args, w):
     import torch.distributed as dist
     from atlas_rnn_b200 import _lib
-    from atlas_rnn_b200.roofline import kernel_flops, step_bytes_per_token, step_flops_per_token
+    from atlas_rnn_b200.roofline import kernel_bytes, kernel_flops, step_bytes_per_token, step_flops_per_token
 
     ws, rank, local = dist_env()
     torch.cuda.set_device(local)
@@ -343,18 +343,35 @@ def run_ours(args, w):
     if os.path.exists(ppath):
         peaks = json.load(open(ppath))
     peak_tf = peaks.get("bf16_tflops", 1590.0)
+    peak_bw = peaks.get("hbm_gbs", 6650.0)
+    chunk = int(kernel_cfg_chunk(w))
     try:
-        alg_flops = kernel_flops(top_name, w, int(kernel_cfg_chunk(w)))
+        alg_flops = kernel_flops(top_name, w, chunk)
     except KeyError:
         alg_flops = None
+    try:
+        alg_bytes = kernel_bytes(top_name, w, chunk)
+    except KeyError:
+        alg_bytes = None
     avg_ms = top_ms / max(top_n, 1)
-    achieved = alg_flops / (avg_ms / 1000.0) / 1e12 if alg_flops else None
-    roofline = {"kernel": top_name, "bound": "tensor", "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
-                "frac": (achieved / peak_tf) if achieved else None,
-                "peak_source": "MEASURED_PEAKS.json bf16_tflops (burst)" if peaks else "fallback 1590",
-                "traffic": traffic_from_profiles(top_name, w.name), "launch_ms": avg_ms,
-                "algorithmic_flops_per_launch": alg_flops,
-                "kernel_share": top_ms / sum(v[0] for v in kern.values())}
+    # the kernel's own roofline: the larger of (compulsory bytes / HBM peak) and (flops / tensor peak)
+    t_hbm = alg_bytes / (peak_bw * 1e9) if alg_bytes else 0.0
+    t_tc = alg_flops / (peak_tf * 1e12) if alg_flops else 0.0
+    src = "MEASURED_PEAKS.json" if peaks else "fallback"
+    tflops = alg_flops / (avg_ms / 1000.0) / 1e12 if alg_flops else None
+    gbs = alg_bytes / (avg_ms / 1000.0) / 1e9 if alg_bytes else None
+    traffic = traffic_from_profiles(top_name, w.name)
+    if t_hbm >= t_tc and gbs is not None:
+        roofline = {"kernel": top_name, "bound": "hbm", "achieved": gbs, "peak": peak_bw, "unit": "GB/s",
+                    "frac": gbs / peak_bw, "peak_source": f"{src} hbm_gbs", "traffic": traffic,
+                    "algorithmic_bytes_per_launch": alg_bytes, "tensor_tflops": tflops,
+                    "tensor_frac": (tflops / peak_tf) if tflops else None}
+    else:
+        roofline = {"kernel": top_name, "bound": "tensor", "achieved": tflops, "peak": peak_tf, "unit": "TFLOP/s",
+                    "frac": (tflops / peak_tf) if tflops else None, "peak_source": f"{src} bf16_tflops (burst)",
+                    "traffic": traffic, "hbm_gbs": gbs}
+    roofline.update({"launch_ms": avg_ms, "algorithmic_flops_per_launch": alg_flops,
+                     "kernel_share": top_ms / sum(v[0] for v in kern.values())})
     Ff, Fb = step_flops_per_token(w)
     Bf, Bb = step_bytes_per_token(w)
     tok_heads = w.N * w.T
