@@ -121,7 +121,9 @@ Smem smem_sizes(const AtlasMemShape* s, int C) {
   m.tc_f3 = 6 * (size_t)tc::kTileBytes + 4 * (size_t)(tctx + 3 * 132);
   m.buf_y = 4 * (size_t)(ctx + r4(C * (e > 1 ? e - 1 : 1)) + r4(C * dphi) + kStageFloats);
   m.tc_b1 = 3 * (size_t)tc::kTileBytes + 4 * (size_t)(tctx + 6 * 132);
-  m.tc_b4 = 6 * (size_t)tc::kTileBytes + 4 * (size_t)(tctx + 3 * 132 + 4 * (tc::kT / 32) + 2 * tc::kWG * tc::kR);
+  m.tc_b4 = 6 * (size_t)tc::kTileBytes +
+            4 * (size_t)(tctx + 6 * 132 + 2 * 2 * tc::kR + 4 + tc::kR + 4 * (tc::kT / 32) +
+                         tc::kGateParts * (tc::kWG - 1) * tc::kR);
   m.tc_b6 = 6 * (size_t)tc::kTileBytes +
             4 * (size_t)(tctx + 6 * 132 + 4 * tc::kR + 4 + tc::kR + tc::kGateParts * (tc::kWG - 1) * tc::kR);
   m.buf_b = 4 * (size_t)(ctx + r4(C * dphi) + r4(C * dv) + 3 * r4(C * (e > 1 ? e - 1 : 1)) + 3 * r4(C + 1) + 32 +
@@ -150,9 +152,9 @@ int ensure_attrs() {
                       (const void*)k_bwd_bufout,  (const void*)k_fmap_tensor_fwd, (const void*)k_fmap_tensor_bwd,
                       (const void*)k_fwd_scan<1>, (const void*)k_fwd_scan<4>, (const void*)k_bwd_scan<1>,
                       (const void*)k_bwd_scan<4>, (const void*)tc::k_fwd_chunk_tc, (const void*)tc::k_fwd_out_tc,
-                      (const void*)tc::k_fwd_buf_y, (const void*)tc::k_bwd_chunk_tc, (const void*)tc::k_bwd_state_tc,
+                      (const void*)tc::k_fwd_buf_y, (const void*)tc::k_bwd_chunk_tc, (const void*)tc::k_bwd_state_gates_tc,
                       (const void*)tc::k_bwd_buf_tc,
-                      (const void*)tc::k_bwd_gates_tc, (const void*)tc::k_bwd_finalize_tc, (const void*)tc::k_bwd_dsref_tc, (const void*)tc::k_bwd_keys_tc,
+                      (const void*)tc::k_bwd_finalize_tc, (const void*)tc::k_bwd_dsref_tc, (const void*)tc::k_bwd_keys_tc,
                       (const void*)tc::k_fwd_scan_tc, (const void*)tc::k_bwd_scan_tc};
   for (const void* k : ks) {
     cudaFuncAttributes fa;
@@ -256,12 +258,12 @@ Params make_params(const AtlasMemShape* s, const Layout& L, const AtlasMemFwd* f
 enum KernelId {
   KID_FMAP_FWD, KID_FWD_CHUNK, KID_FWD_SCAN, KID_FWD_OUT, KID_BUF_OUT, KID_BWD_CHUNK, KID_BWD_SCAN,
   KID_BWD_GRADS, KID_BWD_BUFOUT, KID_BWD_FINAL, KID_BWD_DSREF, KID_FMAP_BWD, KID_FWD_CHUNK_TC, KID_FWD_OUT_TC, KID_FWD_BUF_Y,
-  KID_BWD_CHUNK_TC, KID_BWD_STATE_TC, KID_BWD_BUF_TC, KID_BWD_GATES_TC, KID_BWD_FINAL_TC, KID_BWD_DSREF_TC, KID_BWD_KEYS_TC, KID_SREF_TILE, KID_COUNT
+  KID_BWD_CHUNK_TC, KID_BWD_STATE_GATES_TC, KID_BWD_BUF_TC, KID_BWD_FINAL_TC, KID_BWD_DSREF_TC, KID_BWD_KEYS_TC, KID_SREF_TILE, KID_COUNT
 };
 const char* const kKernelNames[KID_COUNT] = {
   "k_fmap_tensor_fwd", "k_fwd_chunk", "k_fwd_scan", "k_fwd_out", "k_buf_out", "k_bwd_chunk", "k_bwd_scan",
   "k_bwd_grads", "k_bwd_bufout", "k_bwd_finalize", "k_bwd_dsref", "k_fmap_tensor_bwd", "k_fwd_chunk_tc", "k_fwd_out_tc", "k_fwd_buf_y",
-  "k_bwd_chunk_tc", "k_bwd_state_tc", "k_bwd_buf_tc", "k_bwd_gates_tc", "k_bwd_finalize_tc", "k_bwd_dsref_tc", "k_bwd_keys_tc", "k_sref_tile"};
+  "k_bwd_chunk_tc", "k_bwd_state_gates_tc", "k_bwd_buf_tc", "k_bwd_finalize_tc", "k_bwd_dsref_tc", "k_bwd_keys_tc", "k_sref_tile"};
 
 constexpr int kMaxTimed = 8192;
 struct Prof {
@@ -414,10 +416,11 @@ int run_bwd_finish(const AtlasMemShape* s, const Params& P, cudaStream_t st) {
   if (int v = launch_scan(false, P, 0, st)) return v;
   if (tc_groups(s) & 8) {
     const dim3 g(P.nch, P.N);
-    LAUNCH_T(KID_BWD_KEYS_TC, tc::k_bwd_keys_tc, g, tc::kT, m.tc_b6, st, P);  // d psi part I5 first
-    LAUNCH_T(KID_BWD_STATE_TC, tc::k_bwd_state_tc, g, tc::kT, m.tc_b4, st, P);
+    // keys (d psi part I5, G, xf), the carried-buffer terms of chunk 0 (G columns, xf, d psi),
+    // then the state side and the gate gradients (d psi completed)
+    LAUNCH_T(KID_BWD_KEYS_TC, tc::k_bwd_keys_tc, g, tc::kT, m.tc_b6, st, P);
     if (P.e > 1 && (P.buf || P.dbuf)) LAUNCH(KID_BWD_BUF_TC, tc::k_bwd_buf_tc, dim3(1, P.N), m.buf_b, st, P);
-    LAUNCH_T(KID_BWD_GATES_TC, tc::k_bwd_gates_tc, g, tc::kT, m.tc_b6, st, P);
+    LAUNCH_T(KID_BWD_STATE_GATES_TC, tc::k_bwd_state_gates_tc, g, tc::kT, m.tc_b4, st, P);
   } else {
     LAUNCH(KID_BWD_GRADS, k_bwd_grads, dim3(P.nch, P.N), m.b3, st, P);
   }

@@ -2,17 +2,18 @@
 // k_bwd_chunk + k_bwd_grads (chunk_kernels.cuh) produce, split by operand set
 // so that each kernel keeps at most six 32 KB operand tiles in shared memory:
 //
-//   k_bwd_chunk_tc  adjoint increments dShat, dZhat of a chunk        tiles dY*eS, dY*eZ, Psi
-//   k_bwd_state_tc  Psi S_in^T, dY S_in (and Z_in): the Gram entries  tiles Psi, dY, S_in, Z_in
-//                   <dy_q psi_q^T, S_in>, and d psi's state part
-//   k_bwd_keys_tc   Phi F^T, delta F (Gram entries <F, R_j>, d delta   tiles Phi, delta, F_S|Psi,
-//                   and d phi through F, the four <F, S> dots), then   F_Z|dY, M1, M3
-//                   A1 = dY delta^T, A2 = Psi Phi^T, the Gram block
-//                   G = A1 o A2 and the intra-chunk terms
-//   k_bwd_gates_tc  d alpha, d eta, d beta and the window-gate        tiles G, cS, cZ, cZ+, eS+, eZ+
-//                   gradients as bilinear forms of the Gram matrix
-// Gram pieces travel between kernels through the backward scratch:
-//   xq[N][nch][128][2], xf[N][nch][128][2], xs[N][nch][4], G tiles [N][nch][32 KB].
+//   k_bwd_chunk_tc        adjoint increments dShat, dZhat of a chunk   tiles dY*eS, dY*eZ, Psi
+//   k_bwd_keys_tc         Phi F^T, delta F (Gram entries <F, R_j>,     tiles Phi, delta, F_S|Psi,
+//                         d delta and d phi through F), then            F_Z|dY, cS|M3, M1
+//                         A1 = dY delta^T, A2 = Psi Phi^T, the Gram
+//                         block G = A1 o A2 and the intra-chunk terms
+//   k_bwd_state_gates_tc  Psi S_in^T, dY S_in (and Z_in): the Gram     tiles Psi, dY, S_in, Z_in,
+//                         entries <dy_q psi_q^T, S_in>, d psi, the      F_S, F_Z, then cS, G, cZ,
+//                         four <F, S> dots; then d alpha, d eta,        cZ+, eS+, eZ+
+//                         d beta and the window-gate gradients as
+//                         bilinear forms of the Gram matrix
+// Gram pieces travel between the two through the backward scratch:
+//   xf[N][nch][128][2], G tiles [N][nch][32 KB].
 #pragma once
 #include "tc_fwd.cuh"
 
@@ -153,152 +154,6 @@ __global__ void __launch_bounds__(kT) k_bwd_chunk_tc(Params P) {
   }
   tc_teardown(tm, 256);  pc.mark(52);
 
-}
-
-// ===========================================================================
-// state side: G_S = Psi S_in^T, G_Z = Psi Z_in^T (-> X[D_q][S_in], X[D_q][Z_in]),
-// H_S = dY S_in, H_Z = dY Z_in (-> d psi = I5 + sS H_S + sZ H_Z, I5 from k_bwd_keys_tc
-// which runs first; d psi leaves as bf16),
-// and the four Gram scalars <F_S|F_Z, S_in|Z_in> from the staged tiles while
-// the MMAs run.
-// ===========================================================================
-__global__ void __launch_bounds__(kT) k_bwd_state_tc(Params P) {
-  PhaseClock pc;
-  extern __shared__ __align__(1024) unsigned char sm[];
-  unsigned char* tPsi = sm;
-  unsigned char* tY = sm + kTileBytes;
-  unsigned char* tSin = sm + 2 * kTileBytes;
-  unsigned char* tZin = sm + 3 * kTileBytes;
-  unsigned char* tFS = sm + 4 * kTileBytes;
-  unsigned char* tFZ = sm + 5 * kTileBytes;
-  SmemAlloc sa{reinterpret_cast<float*>(sm + 6 * kTileBytes), 0};
-  __shared__ uint64_t mbar;
-  __shared__ uint32_t tbase;
-  Ctx cx;
-  load_ctx(P, sa, cx, kT);
-  float* sS = sa.take(kR + 1);
-  float* sZ = sa.take(kR + 1);
-  float* zZ = sa.take(kR + 1);
-  float* red = sa.take(4 * (kT / 32));
-  float* part = sa.take(2 * kWG * kR);  // [warpgroup][2][row] partial dot products
-  const int n = cx.n, L = cx.L, tid = threadIdx.x, row = row_of(), wg = wg_of();
-  Sync sy{&mbar, &tbase, 0, nullptr};
-  const uint32_t tm = tc_setup(sy);
-  const int64_t cid = chunk_id(P, cx);
-  const unsigned char* Sin = P.stb + cid * 2 * kTileBytes;
-  const unsigned char* FS = P.adjb + cid * 2 * kTileBytes;
-  async_rows_psi(P, cx, tPsi);
-  async_rows_dy(P, cx, tY);
-  async_copy_tile(tSin, Sin);
-  async_copy_tile(tZin, Sin + kTileBytes);
-  async_copy_tile(tFS, FS);
-  async_copy_tile(tFZ, FS + kTileBytes);
-  __syncthreads();
-  pc.mark(32);
-  if (tid < 32) fwd_scalars_warp(cx, sS, sZ, zZ);
-  async_wait();
-  __syncthreads();
-  phi_xform(P, tPsi);
-  pc.mark(33);
-  smem_to_tc();
-  if (tid == 0) {
-    mma_chain(tm, op(tPsi, kD, 0), op(tSin, kD, 0), 8, kD, false);
-    mma_chain(tm + 128, op(tPsi, kD, 0), op(tZin, kD, 0), 8, kD, false);
-    mma_chain(tm + 256, op(tY, kD, 0), op(tSin, kD, 1), 8, kD, false);
-    mma_chain(tm + 384, op(tY, kD, 0), op(tZin, kD, 1), 8, kD, false);
-  }
-  {  // <F_S|F_Z, S_in|Z_in>: elementwise over the raw tiles (same layout for all four)
-    float s00 = 0.f, s01 = 0.f, s10 = 0.f, s11 = 0.f;
-    for (int u = tid; u < kTileBytes / 16; u += kT) {
-      const uint4 a = reinterpret_cast<const uint4*>(tFS)[u], b = reinterpret_cast<const uint4*>(tFZ)[u];
-      const uint4 c = reinterpret_cast<const uint4*>(tSin)[u], d = reinterpret_cast<const uint4*>(tZin)[u];
-      const __nv_bfloat162* fa = reinterpret_cast<const __nv_bfloat162*>(&a);
-      const __nv_bfloat162* fb = reinterpret_cast<const __nv_bfloat162*>(&b);
-      const __nv_bfloat162* fc = reinterpret_cast<const __nv_bfloat162*>(&c);
-      const __nv_bfloat162* fd = reinterpret_cast<const __nv_bfloat162*>(&d);
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const float2 fs = __bfloat1622float2(fa[k]), fz = __bfloat1622float2(fb[k]);
-        const float2 si = __bfloat1622float2(fc[k]), zi = __bfloat1622float2(fd[k]);
-        s00 += fs.x * si.x + fs.y * si.y;
-        s01 += fs.x * zi.x + fs.y * zi.y;
-        s10 += fz.x * si.x + fz.y * si.y;
-        s11 += fz.x * zi.x + fz.y * zi.y;
-      }
-    }
-    const float v[4] = {s00, s01, s10, s11};
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      float t = v[k];
-      for (int off = 16; off > 0; off >>= 1) t += __shfl_xor_sync(0xffffffffu, t, off);
-      if ((tid & 31) == 0) red[k * (kT / 32) + (tid >> 5)] = t;
-    }
-  }
-  // d psi part I5 of this thread's row (k_bwd_keys_tc), fetched while the MMAs run
-  const int64_t grow = (int64_t)n * P.T + cx.t0 + row;
-  uint4 i5v[kCPW][2];
-#pragma unroll
-  for (int h = 0; h < kCPW; ++h) {
-    i5v[h][0] = i5v[h][1] = make_uint4(0u, 0u, 0u, 0u);
-    if (row < L) {
-      const uint4* src = reinterpret_cast<const uint4*>(P.dpsib + grow * P.dphi + (wg * kCPW + h) * 16);
-      i5v[h][0] = src[0];
-      i5v[h][1] = src[1];
-    }
-  }
-  mma_wait(sy);
-  pc.mark(34);
-  {
-    const int q = row;
-    float xs = 0.f, xz = 0.f;
-    const float ss = q < L ? sS[q] : 0.f, sz = q < L ? sZ[q] : 0.f;
-#pragma unroll
-    for (int h = 0; h < kCPW; ++h) {
-      const int c16 = wg * kCPW + h;
-      float gs[16], gz[16], hs[16], hz[16], y0[8], y1[8];
-      umma::tmem_ld16(lane_addr(tm, c16 * 16), gs);
-      umma::tmem_ld16(lane_addr(tm, 128 + c16 * 16), gz);
-      umma::tmem_ld16(lane_addr(tm, 256 + c16 * 16), hs);
-      umma::tmem_ld16(lane_addr(tm, 384 + c16 * 16), hz);
-      umma::tmem_ld_wait();
-      if (q < L) {
-        load_unit(tY, q, 2 * c16, kD, y0);
-        load_unit(tY, q, 2 * c16 + 1, kD, y1);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          xs += gs[i] * y0[i] + gs[8 + i] * y1[i];
-          xz += gz[i] * y0[i] + gz[8 + i] * y1[i];
-        }
-        float d[16], i0[8], i1[8];
-        unpack_unit(i5v[h][0], i0);
-        unpack_unit(i5v[h][1], i1);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          d[i] = ss * hs[i] + sz * hz[i] + i0[i];
-          d[8 + i] = ss * hs[8 + i] + sz * hz[8 + i] + i1[i];
-        }
-        st16bf(P.dpsib + grow * P.dphi + c16 * 16, d);
-      }
-    }
-    part[(wg * 2 + 0) * kR + q] = xs;
-    part[(wg * 2 + 1) * kR + q] = xz;
-  }
-  __syncthreads();
-  pc.mark(35);
-  if (wg == 0) {
-    const int q = row;
-    float* xq = P.xq + (cid * kR + q) * 2;
-    float a = 0.f, b = 0.f;
-    for (int g = 0; g < kWG; ++g) { a += part[(2 * g) * kR + q]; b += part[(2 * g + 1) * kR + q]; }
-    xq[0] = q < L ? a : 0.f;
-    xq[1] = q < L ? b : 0.f;
-  } else if (wg == 1 && row < 4) {
-    float t = 0.f;
-    for (int w = 0; w < kT / 32; ++w) t += red[row * (kT / 32) + w];
-    P.xs[cid * 4 + row] = t;
-  }
-  pc.mark(36);
-  tc_teardown(tm);
 }
 
 // Window-summed adjoint scalars of key j: wZS_j = sum_i W(i,j) hZS_{i+1}, wZZ likewise.
@@ -491,7 +346,7 @@ __global__ void __launch_bounds__(kT) k_bwd_keys_tc(Params P) {
         st16f(ddh + c16 * 16, a);
         st16f(dph + c16 * 16, b);
       }
-      if (r < L) st16bf(dq + c16 * 16, i5);  // k_bwd_state_tc adds the state part
+      if (r < L) st16bf(dq + c16 * 16, i5);  // k_bwd_state_gates_tc adds the state part
     }
   }
   pc.mark(10);
@@ -499,30 +354,58 @@ __global__ void __launch_bounds__(kT) k_bwd_keys_tc(Params P) {
 }
 
 // ===========================================================================
-// gate gradients from the Gram matrix (token i of the chunk):
-//   d alpha_i = <Shat_i, S_{i-1}>, d eta_i = -<Shat_i, Z_i>, d beta_i = <Zhat_i, Z_{i-1}>,
-//   dW(i, j) = <Zhat_i, R_j>.
-// The G block enters through W_a = C_S G^T, W_e = C_Z+ G^T, W_b = C_Z G^T and
-// E_Z+ G (tensor cores); the F / S_in / Z_in rows and columns of the Gram
-// matrix are folded in on CUDA cores.
+// state side and gate gradients in one kernel.
+//   state  G_S = Psi S_in^T, G_Z = Psi Z_in^T (-> X[D_q][S_in], X[D_q][Z_in]),
+//          H_S = dY S_in, H_Z = dY Z_in (-> d psi = I5 + sS H_S + sZ H_Z; I5 from
+//          k_bwd_keys_tc, which runs first; d psi leaves as bf16), and the four Gram
+//          scalars <F_S|F_Z, S_in|Z_in> from the staged tiles while the MMAs run;
+//   gates  d alpha, d eta, d beta and the window-gate gradients as bilinear forms
+//          of the Gram matrix: W_a = C_S G^T, W_e = C_Z+ G^T, W_b = C_Z G^T and
+//          E_Z+ G on tensor cores, the F / S_in / Z_in rows and columns of the Gram
+//          matrix folded in on CUDA cores.
+// Once the state MMAs and the dots are done, five of the six tiles take the
+// coefficient tiles of the gate gradients (warpgroups 0 and 1 build them)
+// while warpgroups 2 and 3 run the state epilogue; the Gram block G then
+// replaces dY. X[D_q][S_in|Z_in] and the four scalars stay on chip.
 // ===========================================================================
 constexpr int kGateParts = 10;
-__global__ void __launch_bounds__(kT) k_bwd_gates_tc(Params P) {
+__device__ __forceinline__ void wg_sync(int id) {  // named barrier of one warpgroup
+  asm volatile("bar.sync %0, 128;\n" ::"r"(id) : "memory");
+}
+__device__ __forceinline__ void pair_sync() {  // named barrier of warpgroups 2 and 3
+  asm volatile("bar.sync 4, 256;\n" ::: "memory");
+}
+__global__ void __launch_bounds__(kT) k_bwd_state_gates_tc(Params P) {
   PhaseClock pc;
   extern __shared__ __align__(1024) unsigned char sm[];
-  unsigned char* tG = sm;
-  unsigned char* tCS = sm + kTileBytes;       // cS_i[j]     (state before token i)
-  unsigned char* tCZp = sm + 2 * kTileBytes;  // cZ_i[j]
-  unsigned char* tCZn = sm + 3 * kTileBytes;  // cZ_{i+1}[j] (state after token i)
-  unsigned char* tES = sm + 4 * kTileBytes;   // eS_{i+1}[q]
-  unsigned char* tEZ = sm + 5 * kTileBytes;   // eZ_{i+1}[q]
+  unsigned char* tPsi = sm;
+  unsigned char* tY = sm + kTileBytes;
+  unsigned char* tSin = sm + 2 * kTileBytes;
+  unsigned char* tZin = sm + 3 * kTileBytes;
+  unsigned char* tFS = sm + 4 * kTileBytes;
+  unsigned char* tFZ = sm + 5 * kTileBytes;
+  unsigned char* tCS = tPsi;   // cS_i[j]      (state before token i)
+  unsigned char* tG = tY;      // Gram block
+  unsigned char* tCZp = tSin;  // cZ_i[j]
+  unsigned char* tCZn = tZin;  // cZ_{i+1}[j]  (state after token i)
+  unsigned char* tES = tFS;    // eS_{i+1}[q]
+  unsigned char* tEZ = tFZ;    // eZ_{i+1}[q]
   SmemAlloc sa{reinterpret_cast<float*>(sm + 6 * kTileBytes), 0};
   __shared__ uint64_t mbar;
   __shared__ uint32_t tbase;
   Ctx cx;
   ctx_geom(P, cx);
   const int64_t cid = chunk_id(P, cx);
-  async_copy_tile(tG, reinterpret_cast<const unsigned char*>(P.gt) + cid * kTileBytes);
+  {  // every operand tile in flight before anything else
+    const unsigned char* Sin = P.stb + cid * 2 * kTileBytes;
+    const unsigned char* FS = P.adjb + cid * 2 * kTileBytes;
+    async_rows_psi(P, cx, tPsi);
+    async_rows_dy(P, cx, tY);
+    async_copy_tile(tSin, Sin);
+    async_copy_tile(tZin, Sin + kTileBytes);
+    async_copy_tile(tFS, FS);
+    async_copy_tile(tFZ, FS + kTileBytes);
+  }
   load_ctx(P, sa, cx, kT);
   float* sS = sa.take(kR + 1);
   float* sZ = sa.take(kR + 1);
@@ -534,45 +417,139 @@ __global__ void __launch_bounds__(kT) k_bwd_gates_tc(Params P) {
   float* xf = sa.take(2 * kR);
   float* xs = sa.take(4);
   float* duj = sa.take(kR);
-  float* part = sa.take(kGateParts * (kWG - 1) * kR);  // partial sums of warpgroups 1..
-
+  float* red = sa.take(4 * (kT / 32));
+  float* part = sa.take(kGateParts * (kWG - 1) * kR);  // state: xq partials; gates: partial sums of warpgroups 1..
   const int n = cx.n, K = cx.K, L = cx.L, tid = threadIdx.x, e = P.e, row = row_of(), wg = wg_of();
-  if (tid < 2 * kR / 4) {
-    cp16(xq + 4 * tid, P.xq + cid * 2 * kR + 4 * tid, true);
-    cp16(xf + 4 * tid, P.xf + cid * 2 * kR + 4 * tid, true);
-  } else if (tid == 2 * kR / 4) {
-    cp16(xs, P.xs + cid * 4, true);
-  }
+  if (tid < 2 * kR / 4) cp16(xf + 4 * tid, P.xf + cid * 2 * kR + 4 * tid, true);
   if (tid < kR) duj[tid] = 0.f;
-  zero_tile(tCS);
-  zero_tile(tCZp);
-  zero_tile(tCZn);
-  zero_tile(tES);
-  zero_tile(tEZ);
   Sync sy{&mbar, &tbase, 0, nullptr};
   const uint32_t tm = tc_setup(sy);  // (its barrier also publishes the gates)
-  pc.mark(24);
-  if (wg == 0) {
-    const int j = row;  // forward coefficients of key j (column j of tCS, tCZp, tCZn; tiles zero-filled)
+  pc.mark(32);
+  if (tid < 32) fwd_scalars_warp(cx, sS, sZ, zZ);
+  else if (tid < 64) adj_scalars_warp(cx, hS, hZS, hZZ);
+  async_wait();
+  __syncthreads();
+  phi_xform(P, tPsi);
+  pc.mark(33);
+  smem_to_tc();
+  if (tid == 0) {
+    mma_chain(tm, op(tPsi, kD, 0), op(tSin, kD, 0), 8, kD, false);
+    mma_chain(tm + 128, op(tPsi, kD, 0), op(tZin, kD, 0), 8, kD, false);
+    mma_chain(tm + 256, op(tY, kD, 0), op(tSin, kD, 1), 8, kD, false);
+    mma_chain(tm + 384, op(tY, kD, 0), op(tZin, kD, 1), 8, kD, false);
+  }
+  {  // <F_S|F_Z, S_in|Z_in>: elementwise over the raw tiles (same layout for all four)
+    float s00 = 0.f, s01 = 0.f, s10 = 0.f, s11 = 0.f;
+    for (int u = tid; u < kTileBytes / 16; u += kT) {
+      const uint4 a = reinterpret_cast<const uint4*>(tFS)[u], b = reinterpret_cast<const uint4*>(tFZ)[u];
+      const uint4 c = reinterpret_cast<const uint4*>(tSin)[u], d = reinterpret_cast<const uint4*>(tZin)[u];
+      const __nv_bfloat162* fa = reinterpret_cast<const __nv_bfloat162*>(&a);
+      const __nv_bfloat162* fb = reinterpret_cast<const __nv_bfloat162*>(&b);
+      const __nv_bfloat162* fc = reinterpret_cast<const __nv_bfloat162*>(&c);
+      const __nv_bfloat162* fd = reinterpret_cast<const __nv_bfloat162*>(&d);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 fs = __bfloat1622float2(fa[k]), fz = __bfloat1622float2(fb[k]);
+        const float2 si = __bfloat1622float2(fc[k]), zi = __bfloat1622float2(fd[k]);
+        s00 += fs.x * si.x + fs.y * si.y;
+        s01 += fs.x * zi.x + fs.y * zi.y;
+        s10 += fz.x * si.x + fz.y * si.y;
+        s11 += fz.x * zi.x + fz.y * zi.y;
+      }
+    }
+    const float v[4] = {s00, s01, s10, s11};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      float t = v[k];
+      for (int off = 16; off > 0; off >>= 1) t += __shfl_xor_sync(0xffffffffu, t, off);
+      if ((tid & 31) == 0) red[k * (kT / 32) + (tid >> 5)] = t;
+    }
+  }
+  // d psi part I5 of this thread's row for the state epilogue of warpgroups 2, 3
+  // (column groups 4 (wg - 2) .. + 3), fetched while the MMAs run
+  const int64_t grow = (int64_t)n * P.T + cx.t0 + row;
+  uint4 i5v[4][2];
+#pragma unroll
+  for (int h = 0; h < 4; ++h) {
+    i5v[h][0] = i5v[h][1] = make_uint4(0u, 0u, 0u, 0u);
+    if (wg >= 2 && row < L) {
+      const uint4* src = reinterpret_cast<const uint4*>(P.dpsib + grow * P.dphi + ((wg - 2) * 4 + h) * 16);
+      i5v[h][0] = src[0];
+      i5v[h][1] = src[1];
+    }
+  }
+  mma_wait(sy);
+  __syncthreads();  // the state MMAs and the dots are done with Psi, S_in, Z_in, F_S, F_Z
+  pc.mark(34);
+  if (wg == 0) {  // forward coefficients of key j (columns of tCS, tCZp, tCZn)
+    zero_tile_wg(tCS);
+    zero_tile_wg(tCZp);
+    zero_tile_wg(tCZn);
+    wg_sync(2);
+    const int j = row;
     fwd_column_z(P, cx, j, [&](int i, float cs, float cz, float czn) {
       st_bf(tCS, i, j, cs);
       st_bf(tCZp, i, j, cz);
       st_bf(tCZn, i, j, czn);
     });
-  } else if (wg == 1) {
-    const int q = row;  // adjoint coefficients of token q (column q of tES, tEZ): rows i <- eS_{i+1}, eZ_{i+1}
+  } else if (wg == 1) {  // adjoint coefficients of token q (columns of tES, tEZ): rows i <- eS_{i+1}, eZ_{i+1}
+    zero_tile_wg(tES);
+    zero_tile_wg(tEZ);
+    wg_sync(3);
+    const int q = row;
     adj_column_z(cx, q, [&](int i, float es, float ez) {
       st_bf(tES, i, q, es);
       st_bf(tEZ, i, q, ez);
     });
-  } else if (wg == 2 && row < 32) {
-    fwd_scalars_warp(cx, sS, sZ, zZ);
-  } else if (wg == 3 && row < 32) {
-    adj_scalars_warp(cx, hS, hZS, hZZ);
+  } else {  // state epilogue (warpgroups 2, 3): d psi, X[D_q][S_in|Z_in]
+    const int q = row;
+    float a = 0.f, b = 0.f;
+    const float ss = q < L ? sS[q] : 0.f, sz = q < L ? sZ[q] : 0.f;
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      const int c16 = (wg - 2) * 4 + h;
+      float gs[16], gz[16], hs[16], hz[16], y0[8], y1[8];
+      umma::tmem_ld16(lane_addr(tm, c16 * 16), gs);
+      umma::tmem_ld16(lane_addr(tm, 128 + c16 * 16), gz);
+      umma::tmem_ld16(lane_addr(tm, 256 + c16 * 16), hs);
+      umma::tmem_ld16(lane_addr(tm, 384 + c16 * 16), hz);
+      umma::tmem_ld_wait();
+      if (q < L) {
+        load_unit(tY, q, 2 * c16, kD, y0);
+        load_unit(tY, q, 2 * c16 + 1, kD, y1);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          a += gs[i] * y0[i] + gs[8 + i] * y1[i];
+          b += gz[i] * y0[i] + gz[8 + i] * y1[i];
+        }
+        float d[16], i0[8], i1[8];
+        unpack_unit(i5v[h][0], i0);
+        unpack_unit(i5v[h][1], i1);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          d[i] = ss * hs[i] + sz * hz[i] + i0[i];
+          d[8 + i] = ss * hs[8 + i] + sz * hz[8 + i] + i1[i];
+        }
+        st16bf(P.dpsib + grow * P.dphi + c16 * 16, d);
+      }
+    }
+    part[((wg - 2) * 2 + 0) * kR + q] = a;
+    part[((wg - 2) * 2 + 1) * kR + q] = b;
+    umma::fence_before();
+    pair_sync();  // both halves of X[D_q] in part; dY no longer read
+    if (wg == 2) {
+      xq[2 * q] = q < L ? part[q] + part[2 * kR + q] : 0.f;
+      xq[2 * q + 1] = q < L ? part[kR + q] + part[3 * kR + q] : 0.f;
+    } else if (row < 4) {
+      float t = 0.f;
+      for (int w = 0; w < kT / 32; ++w) t += red[row * (kT / 32) + w];
+      xs[row] = t;
+    }
+    async_copy_tile(tG, reinterpret_cast<const unsigned char*>(P.gt) + cid * kTileBytes, 256, 256);
+    async_wait();
   }
-  async_wait();
-  pc.mark(25);
-  smem_to_tc();
+  pc.mark(35);
+  smem_to_tc();  // coefficient tiles, G, xq, xs ready; the state accumulators are read
   if (tid == 0) {
     mma_chain(tm, op(tCS, kR, 0), op(tG, kR, 0), 8, kR, false);         // W_a[i][q]
     mma_chain(tm + 128, op(tCZn, kR, 0), op(tG, kR, 0), 8, kR, false);  // W_e[i][q]
@@ -580,7 +557,7 @@ __global__ void __launch_bounds__(kT) k_bwd_gates_tc(Params P) {
     mma_chain(tm + 384, op(tEZ, kR, 0), op(tG, kR, 1), 8, kR, false);   // E_Z+ G [i][j]
   }
   mma_wait(sy);
-  pc.mark(26);
+  pc.mark(36);
   const int i = row;
   float acc[kGateParts];
 #pragma unroll
@@ -621,7 +598,6 @@ __global__ void __launch_bounds__(kT) k_bwd_gates_tc(Params P) {
   if (wg >= 1)
 #pragma unroll
     for (int k = 0; k < kGateParts; ++k) part[((wg - 1) * kGateParts + k) * kR + i] = acc[k];
-  pc.mark(27);
   // window weights dW(i, j) = hZS_{i+1} X[F_S][R_j] + hZZ_{i+1} X[F_Z][R_j] + (E_Z+ G)[i][j]
   if (P.gmode != ATLAS_GATE_NONE) {
     const int rb = (threadIdx.x >> 5) & 3;  // this warp's rows [32 rb, 32 rb + 32)
@@ -646,7 +622,6 @@ __global__ void __launch_bounds__(kT) k_bwd_gates_tc(Params P) {
     }
   }
   __syncthreads();
-  pc.mark(28);
   if (wg == 0 && i < L) {
     for (int g = 1; g < kWG; ++g)
 #pragma unroll
@@ -665,13 +640,13 @@ __global__ void __launch_bounds__(kT) k_bwd_gates_tc(Params P) {
     if (j < K && p >= cx.t0) P.du[(int64_t)n * P.T + p] = duj[j];
     else if (j < K && p >= 0) P.hdu[cid * (e - 1) + j] = duj[j];
   }
-  tc_teardown(tm);  pc.mark(29);
-
+  pc.mark(37);
+  tc_teardown(tm);
 }
 
 // ===========================================================================
 // chunk 0 with a carried omega buffer (dense entries Buf_jb, jb < e-1), after
-// k_bwd_keys_tc and before k_bwd_gates_tc: the Gram columns of the buffer
+// k_bwd_keys_tc and before k_bwd_state_gates_tc: the Gram columns of the buffer
 // entries (X[F][Buf], G[q][Buf] = dy_q . Buf psi_q), their d psi terms, and the
 // buffer's own gradient dBuf_jb = wZS F_S + wZZ F_Z + sum_q wE_jb[q] dy_q psi_q^T.
 // Block GEMMs on CUDA cores, one CTA of kThreads per unit.

@@ -201,6 +201,12 @@ __device__ __forceinline__ void adj_scalars_warp(const Ctx& cx, float* hS, float
   __syncwarp();
 }
 
+// Zero a tile with the 128 threads of the calling warpgroup.
+__device__ __forceinline__ void zero_tile_wg(unsigned char* tile) {
+  for (int u = threadIdx.x & 127; u < kTileBytes / 16; u += 128)
+    reinterpret_cast<uint4*>(tile)[u] = make_uint4(0u, 0u, 0u, 0u);
+}
+
 // Unit u of a 128 x C tile (cpr = C / 8 units per row) in shared-memory address
 // order: unit_off(r, cb, C) == 16 u, so consecutive threads touch consecutive
 // 16-byte units (no bank conflicts), and a warp covers 8 rows x 4 column blocks

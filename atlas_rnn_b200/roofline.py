@@ -59,13 +59,11 @@ def kernel_flops(name: str, w: Workload, C: int) -> float:
             fma = L * K * dp + 2 * L * dp * dv + L * K * dv
         elif name == "k_bwd_chunk_tc":
             fma = 2 * dv * L * dp
-        elif name == "k_bwd_state_tc":
-            fma = 2 * L * dp * dv + 2 * L * dv * dp
+        elif name == "k_bwd_state_gates_tc":
+            fma = 2 * L * dp * dv + 2 * L * dv * dp + 4 * L * K * L
         elif name == "k_bwd_keys_tc":
             fma = (2 * K * dp * dv + 2 * K * dv * dp + 4 * dv * dp
                    + L * K * dv + L * K * dp + K * L * dv + K * L * dp + L * K * dp)
-        elif name == "k_bwd_gates_tc":
-            fma = 4 * L * K * L
         elif name == "k_bwd_grads":
             fma = (L * K * dv + L * K * dp + L * 2 * dv * dp + 2 * K * dp * dv + 3 * (L + 2) * (K + 2) * L
                    + L * K * (L + 2) + K * L * dv + K * dp * (2 * dv + L) + L * dp * (2 * dv + K) + 4 * dv * dp)
@@ -101,12 +99,10 @@ def kernel_bytes(name: str, w: Workload, C: int) -> float:
             b = L * row + 2 * K * row + 2 * tile + L * row
         elif name == "k_bwd_chunk_tc":  # q, dy rows in; two adjoint increment tiles out
             b = 2 * L * row + 2 * tile
-        elif name == "k_bwd_state_tc":  # q, dy rows, state and adjoint tiles in; d psi read and written
-            b = 2 * L * row + 4 * tile + 2 * L * row
+        elif name == "k_bwd_state_gates_tc":  # q, dy rows, state / adjoint tiles, d psi, G in; d psi, gate grads out
+            b = 2 * L * row + 4 * tile + 2 * L * row + tile + 2 * 1024 + gates
         elif name == "k_bwd_keys_tc":   # k, delta, q, dy rows and adjoint tiles in; G, d delta, d phi, d psi out
             b = 2 * K * row + 2 * L * row + 2 * tile + tile + 2 * L * row + 4 * (e - 1) * row + L * row
-        elif name == "k_bwd_gates_tc":  # Gram block and pieces in; gate gradients out
-            b = tile + 2 * 1024 + gates
         else:
             raise KeyError(name)
         total += b + gates
