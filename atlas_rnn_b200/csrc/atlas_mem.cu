@@ -123,7 +123,7 @@ Smem smem_sizes(const AtlasMemShape* s, int C) {
   m.tc_b1 = 3 * (size_t)tc::kTileBytes + 4 * (size_t)(tctx + 6 * 132);
   m.tc_b4 = 6 * (size_t)tc::kTileBytes +
             4 * (size_t)(tctx + 6 * 132 + 2 * 2 * tc::kR + 4 + tc::kR + 4 * (tc::kT / 32) +
-                         tc::kGateParts * (tc::kWG - 1) * tc::kR);
+                         tc::kGateParts * (tc::kWG - 1) * tc::kR + 2 * tc::kR);
   m.tc_b6 = 6 * (size_t)tc::kTileBytes +
             4 * (size_t)(tctx + 6 * 132 + 4 * tc::kR + 4 + tc::kR + tc::kGateParts * (tc::kWG - 1) * tc::kR);
   m.buf_b = 4 * (size_t)(ctx + r4(C * dphi) + r4(C * dv) + 3 * r4(C * (e > 1 ? e - 1 : 1)) + 3 * r4(C + 1) + 32 +

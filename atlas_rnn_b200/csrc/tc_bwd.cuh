@@ -9,9 +9,10 @@
 //                         block G = A1 o A2 and the intra-chunk terms
 //   k_bwd_state_gates_tc  Psi S_in^T, dY S_in (and Z_in): the Gram     tiles Psi, dY, S_in, Z_in,
 //                         entries <dy_q psi_q^T, S_in>, d psi, the      F_S, F_Z, then cS, G, cZ,
-//                         four <F, S> dots; then d alpha, d eta,        cZ+, eS+, eZ+
+//                         four <F, S> dots; then d alpha, d eta,        eS+, eZ+
 //                         d beta and the window-gate gradients as
-//                         bilinear forms of the Gram matrix
+//                         bilinear forms of the Gram matrix (W_e[i] =
+//                         W_b[i + 1], so no cZ+ tile)
 // Gram pieces travel between the two through the backward scratch:
 //   xf[N][nch][128][2], G tiles [N][nch][32 KB].
 #pragma once
@@ -360,8 +361,8 @@ __global__ void __launch_bounds__(kT) k_bwd_keys_tc(Params P) {
 //          k_bwd_keys_tc, which runs first; d psi leaves as bf16), and the four Gram
 //          scalars <F_S|F_Z, S_in|Z_in> from the staged tiles while the MMAs run;
 //   gates  d alpha, d eta, d beta and the window-gate gradients as bilinear forms
-//          of the Gram matrix: W_a = C_S G^T, W_e = C_Z+ G^T, W_b = C_Z G^T and
-//          E_Z+ G on tensor cores, the F / S_in / Z_in rows and columns of the Gram
+//          of the Gram matrix: W_a = C_S G^T, W_b = C_Z G^T (W_e = C_Z+ G^T is W_b
+//          shifted by one row) and E_Z+ G on tensor cores, the F / S_in / Z_in rows and columns of the Gram
 //          matrix folded in on CUDA cores.
 // Once the state MMAs and the dots are done, five of the six tiles take the
 // coefficient tiles of the gate gradients (warpgroups 0 and 1 build them)
@@ -385,9 +386,8 @@ __global__ void __launch_bounds__(kT) k_bwd_state_gates_tc(Params P) {
   unsigned char* tFS = sm + 4 * kTileBytes;
   unsigned char* tFZ = sm + 5 * kTileBytes;
   unsigned char* tCS = tPsi;   // cS_i[j]      (state before token i)
-  unsigned char* tG = tY;      // Gram block
-  unsigned char* tCZp = tSin;  // cZ_i[j]
-  unsigned char* tCZn = tZin;  // cZ_{i+1}[j]  (state after token i)
+  unsigned char* tG = tZin;    // Gram block (Z_in is free after the state MMAs)
+  unsigned char* tCZp = tSin;  // cZ_i[j], rows 0..L (row L: after the last token)
   unsigned char* tES = tFS;    // eS_{i+1}[q]
   unsigned char* tEZ = tFZ;    // eZ_{i+1}[q]
   SmemAlloc sa{reinterpret_cast<float*>(sm + 6 * kTileBytes), 0};
@@ -419,6 +419,7 @@ __global__ void __launch_bounds__(kT) k_bwd_state_gates_tc(Params P) {
   float* duj = sa.take(kR);
   float* red = sa.take(4 * (kT / 32));
   float* part = sa.take(kGateParts * (kWG - 1) * kR);  // state: xq partials; gates: partial sums of warpgroups 1..
+  float* sh0 = sa.take(2 * kR);                        // warpgroup 0's row-shifted gate sums
   const int n = cx.n, K = cx.K, L = cx.L, tid = threadIdx.x, e = P.e, row = row_of(), wg = wg_of();
   if (tid < 2 * kR / 4) cp16(xf + 4 * tid, P.xf + cid * 2 * kR + 4 * tid, true);
   if (tid < kR) duj[tid] = 0.f;
@@ -481,17 +482,17 @@ __global__ void __launch_bounds__(kT) k_bwd_state_gates_tc(Params P) {
   mma_wait(sy);
   __syncthreads();  // the state MMAs and the dots are done with Psi, S_in, Z_in, F_S, F_Z
   pc.mark(34);
-  if (wg == 0) {  // forward coefficients of key j (columns of tCS, tCZp, tCZn)
+  if (wg == 0) {  // forward coefficients of key j (columns of tCS, tCZp)
     zero_tile_wg(tCS);
     zero_tile_wg(tCZp);
-    zero_tile_wg(tCZn);
     wg_sync(2);
     const int j = row;
     fwd_column_z(P, cx, j, [&](int i, float cs, float cz, float czn) {
       st_bf(tCS, i, j, cs);
       st_bf(tCZp, i, j, cz);
-      st_bf(tCZn, i, j, czn);
+      if (i == L - 1) st_bf(tCZp, L, j, czn);
     });
+    if (row == 0) pc.lap(24);
   } else if (wg == 1) {  // adjoint coefficients of token q (columns of tES, tEZ): rows i <- eS_{i+1}, eZ_{i+1}
     zero_tile_wg(tES);
     zero_tile_wg(tEZ);
@@ -501,7 +502,9 @@ __global__ void __launch_bounds__(kT) k_bwd_state_gates_tc(Params P) {
       st_bf(tES, i, q, es);
       st_bf(tEZ, i, q, ez);
     });
-  } else {  // state epilogue (warpgroups 2, 3): d psi, X[D_q][S_in|Z_in]
+    if (row == 0) pc.lap(25);
+  } else {  // state epilogue (warpgroups 2, 3): d psi, X[D_q][S_in|Z_in]; the Gram block arrives meanwhile
+    async_copy_tile(tG, reinterpret_cast<const unsigned char*>(P.gt) + cid * kTileBytes, 256, 256);
     const int q = row;
     float a = 0.f, b = 0.f;
     const float ss = q < L ? sS[q] : 0.f, sz = q < L ? sZ[q] : 0.f;
@@ -545,14 +548,14 @@ __global__ void __launch_bounds__(kT) k_bwd_state_gates_tc(Params P) {
       for (int w = 0; w < kT / 32; ++w) t += red[row * (kT / 32) + w];
       xs[row] = t;
     }
-    async_copy_tile(tG, reinterpret_cast<const unsigned char*>(P.gt) + cid * kTileBytes, 256, 256);
+    if (tid == 256) pc.lap(26);
     async_wait();
+    if (tid == 256) pc.lap(27);
   }
   pc.mark(35);
   smem_to_tc();  // coefficient tiles, G, xq, xs ready; the state accumulators are read
   if (tid == 0) {
     mma_chain(tm, op(tCS, kR, 0), op(tG, kR, 0), 8, kR, false);         // W_a[i][q]
-    mma_chain(tm + 128, op(tCZn, kR, 0), op(tG, kR, 0), 8, kR, false);  // W_e[i][q]
     mma_chain(tm + 256, op(tCZp, kR, 0), op(tG, kR, 0), 8, kR, false);  // W_b[i][q]
     mma_chain(tm + 384, op(tEZ, kR, 0), op(tG, kR, 1), 8, kR, false);   // E_Z+ G [i][j]
   }
@@ -565,39 +568,45 @@ __global__ void __launch_bounds__(kT) k_bwd_state_gates_tc(Params P) {
 #pragma unroll
   for (int h4 = 0; h4 < kCPW; ++h4) {
     const int c16 = wg * kCPW + h4;
-    float A[16], E[16], B[16];
+    float A[16], B[16];
     umma::tmem_ld16(lane_addr(tm, c16 * 16), A);
-    umma::tmem_ld16(lane_addr(tm, 128 + c16 * 16), E);
     umma::tmem_ld16(lane_addr(tm, 256 + c16 * 16), B);
     umma::tmem_ld_wait();
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const int cb = 2 * c16 + h;
-      float cs8[8], czn8[8], czp8[8], es8[8], ez8[8];
+      float cs8[8], czp8[8], es8[8], ez8[8], esm[8];
       load_unit(tCS, i, cb, kR, cs8);
-      load_unit(tCZn, i, cb, kR, czn8);
       load_unit(tCZp, i, cb, kR, czp8);
       load_unit(tES, i, cb, kR, es8);
       load_unit(tEZ, i, cb, kR, ez8);
+      load_unit(tES, i > 0 ? i - 1 : 0, cb, kR, esm);  // row i - 1, for the shifted W_e term
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
         const int x = cb * 8 + k;  // key j (for c*) or token q (for e*)
         acc[0] += xf[2 * x] * cs8[k];        // F_S . cS_i
-        acc[1] += xf[2 * x] * czn8[k];       // F_S . cZ_{i+1}
         acc[2] += xf[2 * x] * czp8[k];       // F_S . cZ_i
         acc[3] += xf[2 * x + 1] * czp8[k];   // F_Z . cZ_i
         acc[4] += xq[2 * x] * es8[k];        // eS_{i+1} . X[D][S_in]
         acc[5] += xq[2 * x + 1] * es8[k];    // eS_{i+1} . X[D][Z_in]
         acc[6] += xq[2 * x + 1] * ez8[k];    // eZ_{i+1} . X[D][Z_in]
         acc[7] += es8[k] * A[8 * h + k];
-        acc[8] += es8[k] * E[8 * h + k];
+        acc[8] += esm[k] * B[8 * h + k];     // eS_i . W_b[i] = row i - 1's eS_{i'+1} . W_e[i']
         acc[9] += ez8[k] * B[8 * h + k];
       }
     }
   }
-  if (wg >= 1)
+  // W_e[i] = W_b[i + 1] and cZ_{i+1} = cZ_i of row i + 1: the terms acc[1] = F_S . cZ_{i+1} and
+  // acc[8] = eS_{i+1} . W_e[i] of row i are acc[2] and the shifted product of row i + 1.
+  acc[1] = acc[2];
+  if (i == 0) acc[8] = 0.f;
+  if (wg >= 1) {
 #pragma unroll
     for (int k = 0; k < kGateParts; ++k) part[((wg - 1) * kGateParts + k) * kR + i] = acc[k];
+  } else {
+    sh0[i] = acc[1];
+    sh0[kR + i] = acc[8];
+  }
   // window weights dW(i, j) = hZS_{i+1} X[F_S][R_j] + hZZ_{i+1} X[F_Z][R_j] + (E_Z+ G)[i][j]
   if (P.gmode != ATLAS_GATE_NONE) {
     const int rb = (threadIdx.x >> 5) & 3;  // this warp's rows [32 rb, 32 rb + 32)
@@ -623,9 +632,11 @@ __global__ void __launch_bounds__(kT) k_bwd_state_gates_tc(Params P) {
   }
   __syncthreads();
   if (wg == 0 && i < L) {
+    acc[1] = sh0[i + 1];
+    acc[8] = sh0[kR + i + 1];
     for (int g = 1; g < kWG; ++g)
 #pragma unroll
-      for (int k = 0; k < kGateParts; ++k) acc[k] += part[((g - 1) * kGateParts + k) * kR + i];
+      for (int k = 0; k < kGateParts; ++k) acc[k] += part[((g - 1) * kGateParts + k) * kR + i + (k == 1 || k == 8 ? 1 : 0)];
     const float da = hS[i + 1] * (xs[0] * sS[i] + xs[1] * sZ[i] + acc[0]) + (acc[4] * sS[i] + acc[5] * sZ[i] + acc[7]);
     const float de = -(hS[i + 1] * (xs[1] * zZ[i + 1] + acc[1]) + (acc[5] * zZ[i + 1] + acc[8]));
     const float db = hZS[i + 1] * (xs[1] * zZ[i] + acc[2]) + hZZ[i + 1] * (xs[3] * zZ[i] + acc[3]) +
