@@ -72,6 +72,8 @@ def lib():
         L.atlas_mem_forward_noalloc.argtypes = [P(Shape), P(Fwd), _vp]
         L.atlas_mem_forward_noalloc.restype = ctypes.c_int
         L.atlas_mem_noalloc_scratch_bytes.restype = ctypes.c_size_t
+        L.atlas_mem_decode_step.argtypes = [P(Shape), P(Fwd), _vp]
+        L.atlas_mem_decode_step.restype = ctypes.c_int
         L.atlas_mem_selftest_umma.argtypes = [_vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                               ctypes.c_int, _vp, _vp]
         L.atlas_mem_selftest_umma.restype = ctypes.c_int

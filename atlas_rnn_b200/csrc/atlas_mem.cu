@@ -9,6 +9,7 @@
 #include "chunk_kernels.cuh"
 #include "tc_bwd.cuh"
 #include "tc_scan.cuh"
+#include "decode.cuh"
 #include "umma_selftest.cuh"
 
 using namespace atlas;
@@ -227,16 +228,18 @@ Params make_params(const AtlasMemShape* s, const Layout& L, const AtlasMemFwd* f
     P.dbuf = s->window > 1 ? b->dbuf_in : nullptr;
   }
   char* sv = (char*)const_cast<void*>(saved);
-  const bool tcm = tc_groups(s) == kTcAll;
-  P.st = (float*)(sv + L.st); P.ST = (float*)(sv + L.ST);
-  P.delta = tcm ? nullptr : (float*)(sv + L.delta);
-  P.dlb = tcm ? (__nv_bfloat16*)(sv + L.dlb) : nullptr;
-  P.stb = tcm ? (unsigned char*)(sv + L.stb) : nullptr;
-  P.srb = tcm ? (unsigned char*)(sv + L.srb) : nullptr;
-  P.inc_bf16 = tcm ? 1 : 0;
-  P.cs = (float*)(sv + L.cs);
-  P.phik = s->fmap_mode == ATLAS_FMAP_TENSOR ? (float*)(sv + L.phik) : nullptr;
-  P.phiq = s->fmap_mode == ATLAS_FMAP_TENSOR ? (float*)(sv + L.phiq) : nullptr;
+  if (sv) {
+    const bool tcm = tc_groups(s) == kTcAll;
+    P.st = (float*)(sv + L.st); P.ST = (float*)(sv + L.ST);
+    P.delta = tcm ? nullptr : (float*)(sv + L.delta);
+    P.dlb = tcm ? (__nv_bfloat16*)(sv + L.dlb) : nullptr;
+    P.stb = tcm ? (unsigned char*)(sv + L.stb) : nullptr;
+    P.srb = tcm ? (unsigned char*)(sv + L.srb) : nullptr;
+    P.inc_bf16 = tcm ? 1 : 0;
+    P.cs = (float*)(sv + L.cs);
+    P.phik = s->fmap_mode == ATLAS_FMAP_TENSOR ? (float*)(sv + L.phik) : nullptr;
+    P.phiq = s->fmap_mode == ATLAS_FMAP_TENSOR ? (float*)(sv + L.phiq) : nullptr;
+  }
   if (scratch) {
     char* sc = (char*)scratch;
     P.adj = (float*)(sc + L.adj); P.acs = (float*)(sc + L.acs); P.dpsi = (float*)(sc + L.dpsi);
@@ -258,12 +261,12 @@ Params make_params(const AtlasMemShape* s, const Layout& L, const AtlasMemFwd* f
 enum KernelId {
   KID_FMAP_FWD, KID_FWD_CHUNK, KID_FWD_SCAN, KID_FWD_OUT, KID_BUF_OUT, KID_BWD_CHUNK, KID_BWD_SCAN,
   KID_BWD_GRADS, KID_BWD_BUFOUT, KID_BWD_FINAL, KID_BWD_DSREF, KID_FMAP_BWD, KID_FWD_CHUNK_TC, KID_FWD_OUT_TC, KID_FWD_BUF_Y,
-  KID_BWD_CHUNK_TC, KID_BWD_STATE_GATES_TC, KID_BWD_BUF_TC, KID_BWD_FINAL_TC, KID_BWD_DSREF_TC, KID_BWD_KEYS_TC, KID_SREF_TILE, KID_COUNT
+  KID_BWD_CHUNK_TC, KID_BWD_STATE_GATES_TC, KID_BWD_BUF_TC, KID_BWD_FINAL_TC, KID_BWD_DSREF_TC, KID_BWD_KEYS_TC, KID_SREF_TILE, KID_DECODE, KID_COUNT
 };
 const char* const kKernelNames[KID_COUNT] = {
   "k_fmap_tensor_fwd", "k_fwd_chunk", "k_fwd_scan", "k_fwd_out", "k_buf_out", "k_bwd_chunk", "k_bwd_scan",
   "k_bwd_grads", "k_bwd_bufout", "k_bwd_finalize", "k_bwd_dsref", "k_fmap_tensor_bwd", "k_fwd_chunk_tc", "k_fwd_out_tc", "k_fwd_buf_y",
-  "k_bwd_chunk_tc", "k_bwd_state_gates_tc", "k_bwd_buf_tc", "k_bwd_finalize_tc", "k_bwd_dsref_tc", "k_bwd_keys_tc", "k_sref_tile"};
+  "k_bwd_chunk_tc", "k_bwd_state_gates_tc", "k_bwd_buf_tc", "k_bwd_finalize_tc", "k_bwd_dsref_tc", "k_bwd_keys_tc", "k_sref_tile", "k_decode_step"};
 
 constexpr int kMaxTimed = 8192;
 struct Prof {
@@ -575,6 +578,21 @@ int atlas_mem_backward(const AtlasMemShape* shape, const AtlasMemFwd* fwd, const
   cudaStream_t st = (cudaStream_t)stream;
   if ((v = run_bwd_local(shape, P, st))) return v;
   return run_bwd_finish(shape, P, st);
+}
+
+int atlas_mem_decode_step(const AtlasMemShape* shape, const AtlasMemFwd* fwd, void* stream) {
+  int v;
+  if ((v = validate_shape(shape))) return v;
+  if (shape->T != 1 || shape->fmap_mode == ATLAS_FMAP_TENSOR || shape->d_phi > 256 || shape->d_v > 256)
+    return ATLAS_ERR_UNSUPPORTED;
+  if ((v = validate_fwd(shape, fwd, true))) return v;
+  if (shape->window > 1 && (!fwd->buf_out || fwd->buf_out == fwd->buf_in)) return ATLAS_ERR_INVALID_ARG;
+  const Layout L = make_layout(shape);
+  const Params P = make_params(shape, L, fwd, nullptr, nullptr, nullptr);
+  cudaStream_t st = (cudaStream_t)stream;
+  LAUNCH(KID_DECODE, k_decode_step, dim3((unsigned)((shape->d_v + kDecodeRows - 1) / kDecodeRows), (unsigned)shape->N),
+         0, st, P);
+  return ATLAS_OK;
 }
 
 int atlas_mem_forward_local(const AtlasMemShape* shape, const AtlasMemFwd* fwd, void* saved, size_t saved_bytes,

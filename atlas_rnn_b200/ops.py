@@ -113,6 +113,35 @@ def _io(t: Tensor | None, dtype) -> Tensor | None:
     return None if t is None else t.to(dtype).contiguous()
 
 
+def decode_supported(spec: Spec, d_k: int, d_phi: int, d_v: int) -> bool:
+    """Shapes atlas_mem_decode_step handles (T = 1, no tensor feature map, heads up to 256)."""
+    return spec.fmap_mode != "tensor" and d_phi <= 256 and d_v <= 256
+
+
+def decode_step(spec: Spec, k, q, v, lr, decay, beta, gate, S_ref, S0, Z0, buf, proj):
+    """One token (T = 1) through atlas_mem_decode_step: inference only, no autograd
+    graph, no workspaces. Operands as for MemoryRecurrenceFn (io dtype for k..gate,
+    fp32 states)."""
+    dev = k.device
+    N, T, _ = k.shape
+    d_phi, d_v = S_ref.shape[-1], v.shape[-1]
+    shape = _shape(spec, k, v, d_phi)
+    y = torch.empty(N, T, d_v, dtype=k.dtype, device=dev)
+    S_end = torch.empty(N, d_v, d_phi, dtype=torch.float32, device=dev)
+    Z_end = torch.empty_like(S_end) if spec.momentum else S_end.new_empty(0)
+    e = spec.window
+    buf_out = (torch.empty(N, e - 1, d_v, d_phi, dtype=torch.float32, device=dev) if e > 1
+               else S_end.new_empty(0))
+    p = _lib.ptr
+    fwd = _lib.Fwd(k=p(k), q=p(q), v=p(v), lr=p(lr), decay=p(decay), beta=p(beta), gate=p(gate),
+                   S_ref=p(S_ref), S0=p(S0), Z0=p(Z0), buf_in=p(buf), proj=p(proj), y=p(y),
+                   S_end=p(S_end), Z_end=p(Z_end) if spec.momentum else None,
+                   buf_out=p(buf_out) if e > 1 else None)
+    _lib.check(_lib.lib().atlas_mem_decode_step(ctypes.byref(shape), ctypes.byref(fwd), _stream(dev)),
+               "decode_step")
+    return y, S_end, Z_end, buf_out
+
+
 def memory_recurrence(k: Tensor, q: Tensor, v: Tensor, lr: Tensor, decay: Tensor,
                       beta: Tensor | None = None, gate: Tensor | None = None, *, S_ref: Tensor,
                       S0: Tensor, Z0: Tensor | None = None, omega_buffer: Tensor | None = None,
@@ -126,6 +155,8 @@ def memory_recurrence(k: Tensor, q: Tensor, v: Tensor, lr: Tensor, decay: Tensor
     S_ref, S0, Z0 [N,d_v,d_phi]; omega_buffer [N,e-1,d_v,d_phi].
     Returns (y [N,T,d_v], S_end (clamped to +-100), Z_end or None, new omega buffer or None).
     io tensors run in bfloat16 when k is bfloat16, else float32; states in float32.
+    A single token (T = 1) with no autograd graph to record runs as one decode
+    kernel (atlas_mem_decode_step) unless the tensor feature map is on.
     """
     if not k.is_cuda:
         raise RuntimeError("atlas_rnn_b200.memory_recurrence: tensors must be on a CUDA device "
@@ -145,9 +176,14 @@ def memory_recurrence(k: Tensor, q: Tensor, v: Tensor, lr: Tensor, decay: Tensor
     Z0c = f32(Z0) if momentum else None
     buf = f32(omega_buffer) if window > 1 else None
     projc = f32(proj) if spec.fmap_mode == "tensor" else None
-    y, S_end, Z_end, buf_out = MemoryRecurrenceFn.apply(
-        spec, _io(k, io), _io(q, io), _io(v, io), _io(lr, io), _io(decay, io), _io(beta, io),
-        _io(gate, io), f32(S_ref), f32(S0), Z0c, buf, projc)
+    args = (_io(k, io), _io(q, io), _io(v, io), _io(lr, io), _io(decay, io), _io(beta, io), _io(gate, io),
+            f32(S_ref), f32(S0), Z0c, buf, projc)
+    needs_grad = torch.is_grad_enabled() and any(
+        t is not None and t.requires_grad for t in (k, q, v, lr, decay, beta, gate, S_ref, S0, Z0, omega_buffer))
+    if k.shape[1] == 1 and not needs_grad and decode_supported(spec, k.shape[-1], S_ref.shape[-1], v.shape[-1]):
+        y, S_end, Z_end, buf_out = decode_step(spec, *args)
+    else:
+        y, S_end, Z_end, buf_out = MemoryRecurrenceFn.apply(spec, *args)
     S_end = S_end.to(state_dtype)
     Z_end = Z_end.to(state_dtype) if momentum else None
     buf_out = buf_out.to(state_dtype) if window > 1 else None

@@ -162,6 +162,21 @@ int atlas_mem_forward_noalloc(const AtlasMemShape* shape, const AtlasMemFwd* fwd
 /* Size in bytes of the fixed scratch array used by atlas_mem_forward_noalloc. */
 size_t atlas_mem_noalloc_scratch_bytes(void);
 
+/* One decoding step (shape->T == 1) without workspaces: the token's memory
+ * update and read-out in a single streaming kernel, for inference loops that
+ * call the cell one token at a time with the state carried (the reference's
+ * generate, rnn_transformer.py:864-904, through OmegaRNNMemoryCell.forward with
+ * seq_len 1; semantics rnn_memory.py:655-730 at T = 1):
+ *   delta = S_ref phi(k) - v,  g = window sum over [buf_in, delta phi(k)^T],
+ *   Z_end = beta Z0 + g,  S_end = clamp(alpha S0 - eta Z_end, -100, 100)
+ *   (without momentum S_end = clamp(alpha S0 - eta g)),  y = S0 phi(q),
+ *   buf_out = buf_in shifted by one entry with delta phi(k)^T appended.
+ * Same operands and results as atlas_mem_forward with T = 1; no backward can
+ * follow. d_phi, d_v <= 256; the tensor feature map is not handled
+ * (ATLAS_ERR_UNSUPPORTED: use atlas_mem_forward). buf_out must not alias
+ * buf_in. Allocates nothing. */
+int atlas_mem_decode_step(const AtlasMemShape* shape, const AtlasMemFwd* fwd, void* stream);
+
 /* Backward pass (AtlasOmegaFunction.backward, atlas_omega_autograd.py:155-204;
  * gradients of the PyTorch path's autograd). `fwd` must hold the same
  * forward operands (outputs may be NULL) and `saved` the forward's workspace. */
