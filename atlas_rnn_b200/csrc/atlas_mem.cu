@@ -590,8 +590,13 @@ int atlas_mem_decode_step(const AtlasMemShape* shape, const AtlasMemFwd* fwd, vo
   const Layout L = make_layout(shape);
   const Params P = make_params(shape, L, fwd, nullptr, nullptr, nullptr);
   cudaStream_t st = (cudaStream_t)stream;
-  LAUNCH(KID_DECODE, k_decode_step, dim3((unsigned)((shape->d_v + kDecodeRows - 1) / kDecodeRows), (unsigned)shape->N),
-         0, st, P);
+  const dim3 grid((unsigned)((shape->d_v + kDecodeRows - 1) / kDecodeRows), (unsigned)shape->N);
+  auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  const bool vec = shape->d_phi % 4 == 0 && al16(fwd->S_ref) && al16(fwd->S0) && al16(fwd->S_end) &&
+                   (!fwd->Z0 || al16(fwd->Z0)) && (!fwd->Z_end || al16(fwd->Z_end)) &&
+                   (!fwd->buf_in || al16(fwd->buf_in)) && (!fwd->buf_out || al16(fwd->buf_out));
+  if (vec) LAUNCH(KID_DECODE, k_decode_step4, grid, 0, st, P);
+  else LAUNCH(KID_DECODE, k_decode_step, grid, 0, st, P);
   return ATLAS_OK;
 }
 
