@@ -2,12 +2,14 @@
 
 Public API mirrors atlas_pytorch/rnn_memory.py (RNNMemoryCell, OmegaRNNMemoryCell,
 RNNMemory, OmegaRNNMemory, RNNMemState, state_detach, PolynomialFeatureMap) plus the
-functional ``memory_recurrence`` and the multi-GPU helpers in ``parallel``.
+functional ``memory_recurrence``, the GPU drop-in for the third-party
+``assoc_scan.AssocScan`` (``AssocScan``, ``assoc_scan``) and the multi-GPU helpers in ``parallel``.
 """
 from .ops import memory_recurrence, MemoryRecurrenceFn
+from .scan import AssocScan, assoc_scan
 from .rnn_memory import (RNNMemState, state_detach, PolynomialFeatureMap, MultiheadRMSNorm,
                          RNNMemoryCell, OmegaRNNMemoryCell, RNNMemory, OmegaRNNMemory)
 
-__all__ = ["memory_recurrence", "MemoryRecurrenceFn", "RNNMemState", "state_detach",
+__all__ = ["memory_recurrence", "MemoryRecurrenceFn", "AssocScan", "assoc_scan", "RNNMemState", "state_detach",
            "PolynomialFeatureMap", "MultiheadRMSNorm", "RNNMemoryCell", "OmegaRNNMemoryCell",
            "RNNMemory", "OmegaRNNMemory"]

@@ -74,6 +74,10 @@ def lib():
         L.atlas_mem_noalloc_scratch_bytes.restype = ctypes.c_size_t
         L.atlas_mem_decode_step.argtypes = [P(Shape), P(Fwd), _vp]
         L.atlas_mem_decode_step.restype = ctypes.c_int
+        L.atlas_scan_forward.argtypes = [_vp, _vp, _vp, _vp, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int, ctypes.c_int, _vp]
+        L.atlas_scan_forward.restype = ctypes.c_int
+        L.atlas_scan_backward.argtypes = [_vp, _vp, _vp, _vp, _vp, _vp, _vp, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int, ctypes.c_int, _vp]
+        L.atlas_scan_backward.restype = ctypes.c_int
         L.atlas_mem_selftest_umma.argtypes = [_vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                               ctypes.c_int, _vp, _vp]
         L.atlas_mem_selftest_umma.restype = ctypes.c_int

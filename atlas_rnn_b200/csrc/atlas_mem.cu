@@ -10,6 +10,7 @@
 #include "tc_bwd.cuh"
 #include "tc_scan.cuh"
 #include "decode.cuh"
+#include "scan_op.cuh"
 #include "umma_selftest.cuh"
 
 using namespace atlas;
@@ -261,12 +262,12 @@ Params make_params(const AtlasMemShape* s, const Layout& L, const AtlasMemFwd* f
 enum KernelId {
   KID_FMAP_FWD, KID_FWD_CHUNK, KID_FWD_SCAN, KID_FWD_OUT, KID_BUF_OUT, KID_BWD_CHUNK, KID_BWD_SCAN,
   KID_BWD_GRADS, KID_BWD_BUFOUT, KID_BWD_FINAL, KID_BWD_DSREF, KID_FMAP_BWD, KID_FWD_CHUNK_TC, KID_FWD_OUT_TC, KID_FWD_BUF_Y,
-  KID_BWD_CHUNK_TC, KID_BWD_STATE_GATES_TC, KID_BWD_BUF_TC, KID_BWD_FINAL_TC, KID_BWD_DSREF_TC, KID_BWD_KEYS_TC, KID_SREF_TILE, KID_DECODE, KID_COUNT
+  KID_BWD_CHUNK_TC, KID_BWD_STATE_GATES_TC, KID_BWD_BUF_TC, KID_BWD_FINAL_TC, KID_BWD_DSREF_TC, KID_BWD_KEYS_TC, KID_SREF_TILE, KID_DECODE, KID_SCAN_OP_FWD, KID_SCAN_OP_BWD, KID_COUNT
 };
 const char* const kKernelNames[KID_COUNT] = {
   "k_fmap_tensor_fwd", "k_fwd_chunk", "k_fwd_scan", "k_fwd_out", "k_buf_out", "k_bwd_chunk", "k_bwd_scan",
   "k_bwd_grads", "k_bwd_bufout", "k_bwd_finalize", "k_bwd_dsref", "k_fmap_tensor_bwd", "k_fwd_chunk_tc", "k_fwd_out_tc", "k_fwd_buf_y",
-  "k_bwd_chunk_tc", "k_bwd_state_gates_tc", "k_bwd_buf_tc", "k_bwd_finalize_tc", "k_bwd_dsref_tc", "k_bwd_keys_tc", "k_sref_tile", "k_decode_step"};
+  "k_bwd_chunk_tc", "k_bwd_state_gates_tc", "k_bwd_buf_tc", "k_bwd_finalize_tc", "k_bwd_dsref_tc", "k_bwd_keys_tc", "k_sref_tile", "k_decode_step", "k_scan_op_fwd", "k_scan_op_bwd"};
 
 constexpr int kMaxTimed = 8192;
 struct Prof {
@@ -597,6 +598,47 @@ int atlas_mem_decode_step(const AtlasMemShape* shape, const AtlasMemFwd* fwd, vo
                    (!fwd->buf_in || al16(fwd->buf_in)) && (!fwd->buf_out || al16(fwd->buf_out));
   if (vec) LAUNCH(KID_DECODE, k_decode_step4, grid, 0, st, P);
   else LAUNCH(KID_DECODE, k_decode_step, grid, 0, st, P);
+  return ATLAS_OK;
+}
+
+int atlas_scan_forward(const float* gates, const void* inputs, const float* prev, void* out, int64_t B, int64_t T,
+                       int64_t D, int dtype_io, int remove_prev, void* stream) {
+  if (!gates || !inputs || !out || B < 1 || T < 1 || D < 1) return ATLAS_ERR_INVALID_ARG;
+  if (dtype_io != ATLAS_F32 && dtype_io != ATLAS_BF16) return ATLAS_ERR_INVALID_ARG;
+  const int off = (prev && !remove_prev) ? 1 : 0;
+  cudaStream_t st = (cudaStream_t)stream;
+  const unsigned gx = (unsigned)((D + kScanOpThreads - 1) / kScanOpThreads);
+  for (int64_t b0 = 0; b0 < B; b0 += 65535) {
+    const dim3 grid(gx, (unsigned)std::min<int64_t>(65535, B - b0));
+    if (dtype_io == ATLAS_F32)
+      LAUNCH_T(KID_SCAN_OP_FWD, k_scan_op_fwd<float>, grid, kScanOpThreads, 0, st, gates, (const float*)inputs, prev,
+               (float*)out, T, D, off, b0);
+    else
+      LAUNCH_T(KID_SCAN_OP_FWD, k_scan_op_fwd<__nv_bfloat16>, grid, kScanOpThreads, 0, st, gates,
+               (const __nv_bfloat16*)inputs, prev, (__nv_bfloat16*)out, T, D, off, b0);
+  }
+  return ATLAS_OK;
+}
+
+int atlas_scan_backward(const float* gates, const void* out, const float* prev, const void* dout, float* d_gates,
+                        void* d_inputs, float* d_prev, int64_t B, int64_t T, int64_t D, int dtype_io,
+                        int remove_prev, void* stream) {
+  if (!gates || !out || !dout || !d_gates || !d_inputs || B < 1 || T < 1 || D < 1) return ATLAS_ERR_INVALID_ARG;
+  if (dtype_io != ATLAS_F32 && dtype_io != ATLAS_BF16) return ATLAS_ERR_INVALID_ARG;
+  const int off = (prev && !remove_prev) ? 1 : 0;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (cudaMemsetAsync(d_gates, 0, (size_t)B * T * sizeof(float), st) != cudaSuccess) return ATLAS_ERR_LAUNCH;
+  const unsigned gx = (unsigned)((D + kScanOpThreads - 1) / kScanOpThreads);
+  for (int64_t b0 = 0; b0 < B; b0 += 65535) {
+    const dim3 grid(gx, (unsigned)std::min<int64_t>(65535, B - b0));
+    if (dtype_io == ATLAS_F32)
+      LAUNCH_T(KID_SCAN_OP_BWD, k_scan_op_bwd<float>, grid, kScanOpThreads, 0, st, gates, (const float*)out, prev,
+               (const float*)dout, d_gates, (float*)d_inputs, d_prev, T, D, off, b0);
+    else
+      LAUNCH_T(KID_SCAN_OP_BWD, k_scan_op_bwd<__nv_bfloat16>, grid, kScanOpThreads, 0, st, gates,
+               (const __nv_bfloat16*)out, prev, (const __nv_bfloat16*)dout, d_gates, (__nv_bfloat16*)d_inputs,
+               d_prev, T, D, off, b0);
+  }
   return ATLAS_OK;
 }
 

@@ -243,6 +243,24 @@ long long atlas_mem_launch_count(void);
 int atlas_mem_kernel_count(void);
 const char* atlas_mem_kernel_name(int kernel_id);
 
+/* ---- scalar-gated scan (drop-in for assoc_scan.AssocScan) -----------------
+ * The reference's legacy OmegaNeuralMemory (omega.py:262-315) and the Titans
+ * paths call the third-party AssocScan as AssocScan()(gates, inputs, prev=...,
+ * remove_prev=...) (rnn_memory.py:34,189,363-379; omega.py:315): over dim 1,
+ *   h_t = gates[b,t] * h_{t-1} + inputs[b,t,...],  h_0 = prev[b,...] (or 0),
+ * outputs h_1..h_T, with prev prepended (T + 1 outputs) when remove_prev is
+ * false. gates [B,T] fp32; inputs / outputs [B,T,D] (trailing dims flattened)
+ * in fp32 or bf16 (dtype_io), fp32 accumulation; prev [B,D] fp32 or NULL. */
+int atlas_scan_forward(const float* gates, const void* inputs, const float* prev, void* out, int64_t B,
+                       int64_t T, int64_t D, int dtype_io, int remove_prev, void* stream);
+/* Backward of atlas_scan_forward. out is the forward output (with prev
+ * prepended when remove_prev was false), dout its gradient (same layout and
+ * dtype). d_gates [B,T] fp32 (required; it is accumulated over D, zeroed
+ * here), d_inputs [B,T,D] in dtype_io, d_prev [B,D] fp32 or NULL. */
+int atlas_scan_backward(const float* gates, const void* out, const float* prev, const void* dout,
+                        float* d_gates, void* d_inputs, float* d_prev, int64_t B, int64_t T, int64_t D,
+                        int dtype_io, int remove_prev, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

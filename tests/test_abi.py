@@ -65,3 +65,11 @@ def test_no_cpu_fallback():
     with pytest.raises(RuntimeError, match="CUDA"):
         memory_recurrence(x, x, x, torch.rand(1, 4), torch.rand(1, 4), S_ref=torch.zeros(1, 8, 8),
                           S0=torch.zeros(1, 8, 8))
+
+
+def test_scan_has_no_cpu_path():
+    """The AssocScan drop-in runs only on the GPU kernels (no silent CPU fallback)."""
+    import torch
+    from atlas_rnn_b200 import AssocScan
+    with pytest.raises(RuntimeError):
+        AssocScan()(torch.ones(1, 2), torch.ones(1, 2, 3))
