@@ -23,28 +23,6 @@ namespace tc {
 
 __device__ __forceinline__ int64_t chunk_id(const Params& P, const Ctx& cx) { return (int64_t)cx.n * P.nch + cx.c; }
 
-// Token rows of dy (zero for rows >= L), optionally scaled per row.
-template <class Scale>
-__device__ __forceinline__ void fill_rows_dy(const Params& P, const Ctx& cx, unsigned char* tile, Scale sc,
-                                             int first = 0, int count = kT) {
-  fill_tile(tile, kD, [&](int r, int c0, float(&v)[8]) {
-    if (r < cx.L) {
-      ld8io(P.dy, ((int64_t)cx.n * P.T + cx.t0 + r) * P.dv + c0, P.bf, v);
-      const float s = sc(r);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) v[i] *= s;
-    } else {
-      zero8(v);
-    }
-  }, first, count);
-}
-__device__ __forceinline__ void fill_keys_delta(const Params& P, const Ctx& cx, unsigned char* tile, int first = 0,
-                                                int count = kT) {
-  fill_rows_raw(tile, [&](int r) -> const __nv_bfloat16* {
-    const int p = cx.kp0 + r;
-    return (r < cx.K && p >= 0) ? P.dlb + ((int64_t)cx.n * P.T + p) * P.dv : nullptr;
-  }, first, count);
-}
 
 // Scalars of the adjoint transform of the chunk (rows r = 0..L) computed by one thread.
 __device__ __forceinline__ void adj_scalars(const Ctx& cx, float* hS, float* hZS, float* hZZ) {
@@ -57,17 +35,6 @@ __device__ __forceinline__ void adj_scalars(const Ctx& cx, float* hS, float* hZS
     hzz = cx.be[r] * hzz;
     hzs = cx.be[r] * hzs - eta * hs;
     hS[r] = hs; hZS[r] = hzs; hZZ[r] = hzz;
-  }
-}
-// Scalars of the forward chunk transform (rows r = 0..L) computed by one thread.
-__device__ __forceinline__ void fwd_scalars(const Ctx& cx, float* sS, float* sZ, float* zZ) {
-  float s = 1.f, sz = 0.f, z = 1.f;
-  sS[0] = s; sZ[0] = sz; zZ[0] = z;
-  for (int i = 0; i < cx.L; ++i) {
-    z = cx.be[i] * z;
-    s = cx.al[i] * s;
-    sz = cx.al[i] * sz - cx.et[i] * z;
-    sS[i + 1] = s; sZ[i + 1] = sz; zZ[i + 1] = z;
   }
 }
 

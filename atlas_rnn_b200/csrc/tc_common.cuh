@@ -246,54 +246,6 @@ __device__ __forceinline__ void fill_tile(unsigned char* tile, int C, F src, int
     }
   }
 }
-// Copy a 32 KB tile that is already in the core-matrix layout (raw 16-byte units).
-__device__ __forceinline__ void copy_tile(unsigned char* tile, const unsigned char* src, int first = 0,
-                                          int count = kT) {
-  constexpr int kBatch = 8, kUnits = kTileBytes / 16;
-  const int me = (int)threadIdx.x - first;
-  if (me < 0 || me >= count) return;
-  const uint4* s4 = reinterpret_cast<const uint4*>(src);
-  uint4* d4 = reinterpret_cast<uint4*>(tile);
-  for (int base = me; base < kUnits; base += count * kBatch) {
-    uint4 v[kBatch];
-#pragma unroll
-    for (int k = 0; k < kBatch; ++k) {
-      const int u = base + k * count;
-      if (u < kUnits) v[k] = s4[u];
-    }
-#pragma unroll
-    for (int k = 0; k < kBatch; ++k) {
-      const int u = base + k * count;
-      if (u < kUnits) d4[u] = v[k];
-    }
-  }
-}
-// Rows of a bf16 row-major [*, 128] matrix into a tile: rowp(r) is the row, or
-// nullptr for a zero row; 16-byte units are copied unchanged.
-template <class F>
-__device__ __forceinline__ void fill_rows_raw(unsigned char* tile, F rowp, int first = 0, int count = kT) {
-  constexpr int kBatch = 8, kUnits = kTileBytes / 16, kCpr = kD / 8;
-  const int me = (int)threadIdx.x - first;
-  if (me < 0 || me >= count) return;
-  for (int base = me; base < kUnits; base += count * kBatch) {
-    uint4 v[kBatch];
-#pragma unroll
-    for (int k = 0; k < kBatch; ++k) {
-      const int u = base + k * count;
-      if (u < kUnits) {
-        int r, cb;
-        unit_rc(u, kCpr, r, cb);
-        const __nv_bfloat16* row = rowp(r);
-        v[k] = row ? reinterpret_cast<const uint4*>(row)[cb] : make_uint4(0u, 0u, 0u, 0u);
-      }
-    }
-#pragma unroll
-    for (int k = 0; k < kBatch; ++k) {
-      const int u = base + k * count;
-      if (u < kUnits) *reinterpret_cast<uint4*>(tile + 16 * u) = v[k];
-    }
-  }
-}
 // ---------------------------------------------------------------------------
 // Asynchronous tile loads (cp.async, 16 bytes, L2 only). Every thread issues
 // its copies without waiting, so a whole tile set is in flight at once; a zero

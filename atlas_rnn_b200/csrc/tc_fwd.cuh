@@ -13,39 +13,16 @@ __host__ __device__ __forceinline__ int ctx_floats(int C, int e) {
   return 3 * r4(C) + r4(C + e) + r4(C * e);
 }
 
-// Forward coefficients of key j token by token (the recurrence of fwd_coefs),
-// with the gates of 8 tokens loaded ahead of the dependent arithmetic.
-// emit(i, cS before token i, cZ before token i, cZ after token i), i = 0..L-1.
-template <class F>
-__device__ __forceinline__ void fwd_column(const Params& P, const Ctx& cx, int j, F emit) {
-  float cs = 0.f, cz = 0.f;
-  for (int i0 = 0; i0 < cx.L; i0 += 8) {
-    float al[8], et[8], be[8], w[8];
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const int i = min(i0 + k, cx.L - 1);
-      al[k] = cx.al[i]; et[k] = cx.et[i]; be[k] = cx.be[i];
-      w[k] = wgt(P, cx, i, j);
-    }
-#pragma unroll
-    for (int k = 0; k < 8; ++k)
-      if (i0 + k < cx.L) {
-        const float czn = be[k] * cz + w[k];
-        emit(i0 + k, cs, cz, czn);
-        cz = czn;
-        cs = al[k] * cs - et[k] * cz;
-      }
-  }
-}
 __device__ __forceinline__ void zero_tile(unsigned char* tile) {
   for (int u = threadIdx.x; u < kTileBytes / 16; u += blockDim.x)
     reinterpret_cast<uint4*>(tile)[u] = make_uint4(0u, 0u, 0u, 0u);
 }
-// fwd_column without the structurally zero rows: key j has no coefficient before
-// its first window token j - e + 1, receives window weights up to token j and
-// then evolves homogeneously, so only tokens [max(0, j - e + 1), L) are emitted
-// (the caller zero-fills the tile rows beforehand) and the weight lookup runs
-// for at most e of them. Same emit(i, cS before i, cZ before i, cZ after i).
+// Forward coefficients of key j token by token (the recurrence of fwd_coefs,
+// chunk_kernels.cuh): emit(i, cS before token i, cZ before token i, cZ after
+// token i). Key j has no coefficient before its first window token j - e + 1,
+// receives window weights up to token j and then evolves homogeneously, so only
+// tokens [max(0, j - e + 1), L) are emitted (the caller zero-fills the tile rows
+// beforehand) and the weight lookup runs for at most e of them.
 template <class F>
 __device__ __forceinline__ void fwd_column_z(const Params& P, const Ctx& cx, int j, F emit) {
   const int L = cx.L;
@@ -77,9 +54,9 @@ __device__ __forceinline__ void fwd_column_z(const Params& P, const Ctx& cx, int
     cs = cx.al[i] * cs - cx.et[i] * cz;
   }
 }
-// adj_column without the structurally zero rows: token q's adjoint coefficients
-// vanish for rows i >= q, so only rows [0, q) are emitted (descending; the
-// caller zero-fills the tile). Same emit(i, eS_{i+1}[q], eZ_{i+1}[q]).
+// Adjoint coefficients of token q (the recurrence of adj_coefs, chunk_kernels.cuh):
+// emit(i, eS_{i+1}[q], eZ_{i+1}[q]) for i descending. They vanish for rows
+// i >= q, so only rows [0, q) are emitted (the caller zero-fills the tile).
 // With es_end / ez_end given, the values after token 0 (eS_0[q], eZ_0[q]) are returned there.
 template <class F>
 __device__ __forceinline__ void adj_column_z(const Ctx& cx, int q, F emit, float* es_end = nullptr,
@@ -116,33 +93,6 @@ __device__ __forceinline__ void adj_column_z(const Ctx& cx, int q, F emit, float
   if (ez_end) *ez_end = ez;
 }
 
-// Adjoint coefficients of token q (the recurrence of adj_coefs), 8 tokens per
-// gate batch. emit(i, eS_{i+1}[q], eZ_{i+1}[q]) for i = L-1 down to 0.
-// With es_end / ez_end given, the values after token 0 (eS_0[q], eZ_0[q]) are returned there.
-template <class F>
-__device__ __forceinline__ void adj_column(const Ctx& cx, int q, F emit, float* es_end = nullptr,
-                                           float* ez_end = nullptr) {
-  float es = 0.f, ez = 0.f;
-  for (int i0 = cx.L - 1; i0 >= 0; i0 -= 8) {
-    float al[8], be[8], etm[8];
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const int i = max(i0 - k, 0);
-      al[k] = cx.al[i]; be[k] = cx.be[i];
-      etm[k] = i >= 1 ? cx.et[i - 1] : 0.f;
-    }
-#pragma unroll
-    for (int k = 0; k < 8; ++k)
-      if (i0 - k >= 0) {
-        const int i = i0 - k;
-        emit(i, es, ez);
-        es = al[k] * es + (q == i ? 1.f : 0.f);
-        ez = be[k] * ez - etm[k] * es;
-      }
-  }
-  if (es_end) *es_end = es;
-  if (ez_end) *ez_end = ez;
-}
 __device__ __forceinline__ void st_bf(unsigned char* tile, int r, int c, float v) {
   *reinterpret_cast<__nv_bfloat16*>(tile + umma::elem_off(r, c, kR)) = __float2bfloat16_rn(v);
 }
@@ -210,10 +160,6 @@ __device__ __forceinline__ void async_rows_dy(const Params& P, const Ctx& cx, un
 // Named barrier over warpgroups 1..kWG-1 (the loaders while warpgroup 0 is busy).
 __device__ __forceinline__ void loaders_sync() { asm volatile("bar.sync 1, %0;\n" ::"n"(kT - 128) : "memory"); }
 
-// A dense fp32 [128 x 128] row-major matrix into a tile.
-__device__ __forceinline__ void fill_dense(unsigned char* tile, const float* M, int first = 0, int count = kT) {
-  fill_tile(tile, kD, [&](int r, int c0, float(&v)[8]) { ld8f(M + r * kD + c0, v); }, first, count);
-}
 
 // S_ref of every unit as one bf16 operand tile (core-matrix layout), once per
 // call: the chunk kernels then copy it raw. Grid (N), 256 threads.
