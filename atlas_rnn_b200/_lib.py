@@ -78,6 +78,10 @@ def lib():
         L.atlas_scan_forward.restype = ctypes.c_int
         L.atlas_scan_backward.argtypes = [_vp, _vp, _vp, _vp, _vp, _vp, _vp, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int, ctypes.c_int, _vp]
         L.atlas_scan_backward.restype = ctypes.c_int
+        L.atlas_mem_compose_carries.argtypes = [_vp, ctypes.c_int64, ctypes.c_int, ctypes.c_int, ctypes.c_int64,
+                                                ctypes.c_int64, ctypes.c_int, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+                                                _vp, _vp]
+        L.atlas_mem_compose_carries.restype = ctypes.c_int
         L.atlas_mem_selftest_umma.argtypes = [_vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                               ctypes.c_int, _vp, _vp]
         L.atlas_mem_selftest_umma.restype = ctypes.c_int

@@ -11,6 +11,7 @@
 #include "tc_scan.cuh"
 #include "decode.cuh"
 #include "scan_op.cuh"
+#include "carry.cuh"
 #include "umma_selftest.cuh"
 
 using namespace atlas;
@@ -157,7 +158,9 @@ int ensure_attrs() {
                       (const void*)tc::k_fwd_buf_y, (const void*)tc::k_bwd_chunk_tc, (const void*)tc::k_bwd_state_gates_tc,
                       (const void*)tc::k_bwd_buf_tc,
                       (const void*)tc::k_bwd_finalize_tc, (const void*)tc::k_bwd_dsref_tc, (const void*)tc::k_bwd_keys_tc,
-                      (const void*)tc::k_fwd_scan_tc, (const void*)tc::k_bwd_scan_tc};
+                      (const void*)tc::k_fwd_scan_tc<1>, (const void*)tc::k_fwd_scan_tc<2>,
+                      (const void*)tc::k_fwd_scan_tc<4>, (const void*)tc::k_bwd_scan_tc<1>,
+                      (const void*)tc::k_bwd_scan_tc<2>, (const void*)tc::k_bwd_scan_tc<4>};
   for (const void* k : ks) {
     cudaFuncAttributes fa;
     if (cudaFuncGetAttributes(&fa, k) != cudaSuccess) return ATLAS_ERR_LAUNCH;
@@ -262,12 +265,12 @@ Params make_params(const AtlasMemShape* s, const Layout& L, const AtlasMemFwd* f
 enum KernelId {
   KID_FMAP_FWD, KID_FWD_CHUNK, KID_FWD_SCAN, KID_FWD_OUT, KID_BUF_OUT, KID_BWD_CHUNK, KID_BWD_SCAN,
   KID_BWD_GRADS, KID_BWD_BUFOUT, KID_BWD_FINAL, KID_BWD_DSREF, KID_FMAP_BWD, KID_FWD_CHUNK_TC, KID_FWD_OUT_TC, KID_FWD_BUF_Y,
-  KID_BWD_CHUNK_TC, KID_BWD_STATE_GATES_TC, KID_BWD_BUF_TC, KID_BWD_FINAL_TC, KID_BWD_DSREF_TC, KID_BWD_KEYS_TC, KID_SREF_TILE, KID_DECODE, KID_SCAN_OP_FWD, KID_SCAN_OP_BWD, KID_COUNT
+  KID_BWD_CHUNK_TC, KID_BWD_STATE_GATES_TC, KID_BWD_BUF_TC, KID_BWD_FINAL_TC, KID_BWD_DSREF_TC, KID_BWD_KEYS_TC, KID_SREF_TILE, KID_DECODE, KID_SCAN_OP_FWD, KID_SCAN_OP_BWD, KID_CARRY, KID_COUNT
 };
 const char* const kKernelNames[KID_COUNT] = {
   "k_fmap_tensor_fwd", "k_fwd_chunk", "k_fwd_scan", "k_fwd_out", "k_buf_out", "k_bwd_chunk", "k_bwd_scan",
   "k_bwd_grads", "k_bwd_bufout", "k_bwd_finalize", "k_bwd_dsref", "k_fmap_tensor_bwd", "k_fwd_chunk_tc", "k_fwd_out_tc", "k_fwd_buf_y",
-  "k_bwd_chunk_tc", "k_bwd_state_gates_tc", "k_bwd_buf_tc", "k_bwd_finalize_tc", "k_bwd_dsref_tc", "k_bwd_keys_tc", "k_sref_tile", "k_decode_step", "k_scan_op_fwd", "k_scan_op_bwd"};
+  "k_bwd_chunk_tc", "k_bwd_state_gates_tc", "k_bwd_buf_tc", "k_bwd_finalize_tc", "k_bwd_dsref_tc", "k_bwd_keys_tc", "k_sref_tile", "k_decode_step", "k_scan_op_fwd", "k_scan_op_bwd", "k_compose_carries"};
 
 constexpr int kMaxTimed = 8192;
 struct Prof {
@@ -347,23 +350,37 @@ int sm_count() {
   return cached[dev];
 }
 
-// One resident wave of tc::k_{fwd,bwd}_scan_tc (kScanF groups of 8 elements per thread, rounds beyond that).
-int launch_scan_tc(bool fwd, const Params& P, cudaStream_t st) {
+// One resident wave of tc::k_{fwd,bwd}_scan_tc: F groups of 8 elements per thread, F the smallest of
+// 1, 2, 4 that covers the units (rounds of F = 4 beyond that).
+template <int F>
+int launch_scan_tc_f(bool fwd, const Params& P, int dry, int rounds, int threads, cudaStream_t st) {
   const int grid = sm_count();
-  const int64_t G = (int64_t)grid * tc::kScanThreads, total = (int64_t)P.N * tc::kOct;
-  const int rounds = (int)((total + G * tc::kScanF - 1) / (G * tc::kScanF));
   for (int r = 0; r < rounds; ++r) {
-    if (fwd) LAUNCH_T(KID_FWD_SCAN, tc::k_fwd_scan_tc, dim3(grid), tc::kScanThreads, tc::kScanRingBytes, st, P, r);
-    else LAUNCH_T(KID_BWD_SCAN, tc::k_bwd_scan_tc, dim3(grid), tc::kScanThreads, tc::kScanRingBytes, st, P, r);
+    if (fwd)
+      LAUNCH_T(KID_FWD_SCAN, tc::k_fwd_scan_tc<F>, dim3(grid), threads, tc::kScanRingBytes, st, P, r, dry);
+    else
+      LAUNCH_T(KID_BWD_SCAN, tc::k_bwd_scan_tc<F>, dim3(grid), threads, tc::kScanRingBytes, st, P, r, dry);
   }
   return ATLAS_OK;
+}
+int launch_scan_tc(bool fwd, const Params& P, int dry, cudaStream_t st) {
+  const int64_t sms = sm_count(), G = sms * tc::kScanThreads, total = (int64_t)P.N * tc::kOct;
+  const int64_t per = (total + G - 1) / G;  // groups per thread at full CTAs
+  const int F = per <= 1 ? 1 : (per <= 2 ? 2 : 4);
+  // threads per CTA: the fewest warps that still cover one round of F groups per thread on every SM
+  const int64_t need = (total + F * sms - 1) / (F * sms);
+  const int threads = per > 4 ? tc::kScanThreads : (int)std::min<int64_t>(tc::kScanThreads, (need + 31) / 32 * 32);
+  if (F == 1) return launch_scan_tc_f<1>(fwd, P, dry, 1, threads, st);
+  if (F == 2) return launch_scan_tc_f<2>(fwd, P, dry, 1, threads, st);
+  return launch_scan_tc_f<4>(fwd, P, dry, (int)((per + 3) / 4), threads, st);
 }
 
 int launch_scan(bool fwd, const Params& P, int dry, cudaStream_t st) {
   const int64_t D2 = (int64_t)P.dv * P.dphi;
-  if (!dry && P.inc_bf16 && (fwd ? P.stb != nullptr : P.adjb != nullptr) && P.dv == tc::kD && P.dphi == tc::kD &&
-      (int64_t)P.N * tc::kOct < ((int64_t)1 << 31) && std::getenv("ATLAS_MEM_SCAN_GENERIC") == nullptr)
-    return launch_scan_tc(fwd, P, st);
+  if (P.inc_bf16 && (dry || (fwd ? P.stb != nullptr : P.adjb != nullptr)) && P.dv == tc::kD &&
+      P.dphi == tc::kD && (int64_t)P.N * tc::kOct < ((int64_t)1 << 31) &&
+      std::getenv("ATLAS_MEM_SCAN_GENERIC") == nullptr)
+    return launch_scan_tc(fwd, P, dry, st);
   const size_t smem = (size_t)P.nch * sizeof(float4);
   const bool v4 = (D2 % 4) == 0;
   const int64_t units = v4 ? D2 / 4 : D2;
@@ -639,6 +656,20 @@ int atlas_scan_backward(const float* gates, const void* out, const float* prev, 
                (const __nv_bfloat16*)out, prev, (const __nv_bfloat16*)dout, d_gates, (__nv_bfloat16*)d_inputs,
                d_prev, T, D, off, b0);
   }
+  return ATLAS_OK;
+}
+
+int atlas_mem_compose_carries(const float* seg, int64_t record_len, int world, int rank, int64_t N, int64_t d2,
+                              int backward, const float* S0, const float* Z0, const float* S_T, float* in_S,
+                              float* in_Z, float* out_S, float* out_S_clamped, float* out_Z, void* stream) {
+  const int64_t coef_len = (N * 3 + 3) / 4 * 4;
+  if (!seg || world < 1 || rank < 0 || rank >= world || N < 1 || d2 < 1 || record_len < coef_len + 2 * N * d2)
+    return ATLAS_ERR_INVALID_ARG;
+  CarryArgs A{seg, record_len, coef_len, N * d2, world, rank, (int)N, backward ? 1 : 0, d2,
+              S0, Z0, backward ? S_T : nullptr, in_S, in_Z, out_S, backward ? nullptr : out_S_clamped, out_Z};
+  cudaStream_t st = (cudaStream_t)stream;
+  const int64_t blocks = std::min<int64_t>((A.ND2 + kThreads - 1) / kThreads, (int64_t)sm_count() * 8);
+  LAUNCH(KID_CARRY, k_compose_carries, dim3((unsigned)blocks), 0, st, A);
   return ATLAS_OK;
 }
 

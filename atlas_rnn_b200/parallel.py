@@ -91,10 +91,20 @@ class Segment:
                         S0=p(S0) if S0 is not None else p(self.S_ref), Z0=p(Z0), buf_in=None, proj=None,
                         y=p(y), S_end=p(S_end), Z_end=p(Z_end), buf_out=None)
 
+    def record_len(self) -> int:
+        """Floats in one packed segment-transform record: coef [N,3] (padded to a
+        multiple of 4), dS [N,d_v,d_phi], dZ [N,d_v,d_phi]."""
+        return (self.N * 3 + 3) // 4 * 4 + 2 * self.N * self.d_v * self.d_phi
+
     def _seg_bufs(self):
-        coef = torch.empty(self.N, 3, device=self.dev)
-        dS = torch.empty(self.N, self.d_v, self.d_phi, device=self.dev)
-        return coef, dS, torch.empty_like(dS)
+        """A packed record and its three views, so one collective moves all of it."""
+        rec = torch.empty(self.record_len(), device=self.dev)
+        cl, nd2 = (self.N * 3 + 3) // 4 * 4, self.N * self.d_v * self.d_phi
+        coef = rec[:self.N * 3].view(self.N, 3)
+        dS = rec[cl:cl + nd2].view(self.N, self.d_v, self.d_phi)
+        dZ = rec[cl + nd2:cl + 2 * nd2].view(self.N, self.d_v, self.d_phi)
+        self.record = rec
+        return coef, dS, dZ
 
     def forward_local(self):
         coef, dS, dZ = self._seg_bufs()
@@ -153,10 +163,32 @@ class Segment:
         return g
 
 
-def _gather(t: Tensor, group) -> list[Tensor]:
-    out = [torch.empty_like(t) for _ in range(dist.get_world_size(group))]
-    dist.all_gather(out, t.contiguous(), group=group)
+def _gather_records(seg: Segment, group) -> Tensor:
+    """All ranks' packed segment-transform records, [world, record_len], in one all-gather."""
+    P = dist.get_world_size(group)
+    out = torch.empty(P, seg.record.numel(), device=seg.dev)
+    dist.all_gather_into_tensor(out, seg.record, group=group)
     return out
+
+
+def compose_carries_device(seg: Segment, records: Tensor, rank: int, backward: bool, S0, Z0, S_T=None,
+                           clamped: bool = False):
+    """The carry composition of compose_forward_carries / compose_backward_carries as one
+    kernel (atlas_mem_compose_carries) over the gathered records.
+    Returns (in_S, in_Z, out_S, out_S_clamped or None, out_Z)."""
+    N, d2 = seg.N, seg.d_v * seg.d_phi
+    shp = (N, seg.d_v, seg.d_phi)
+    new = lambda: torch.empty(shp, device=seg.dev)
+    in_S, in_Z, out_S, out_Z = new(), new(), new(), new()
+    out_Sc = new() if clamped else None
+    p = _lib.ptr
+    c = lambda t: None if t is None else t.contiguous()
+    S0, Z0, S_T = c(S0), c(Z0), c(S_T)
+    _lib.check(_lib.lib().atlas_mem_compose_carries(p(records), records.shape[1], records.shape[0], rank, N, d2,
+                                                    int(backward), p(S0), p(Z0), p(S_T), p(in_S), p(in_Z),
+                                                    p(out_S), p(out_Sc), p(out_Z), _stream(seg.dev)),
+               "compose_carries")
+    return in_S, in_Z, out_S, out_Sc, out_Z
 
 
 class SeqParallelMemoryFn(torch.autograd.Function):
@@ -165,37 +197,34 @@ class SeqParallelMemoryFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, spec: Spec, group, k, q, v, lr, decay, beta, S_ref, S0, Z0):
         seg = Segment(spec, k, q, v, lr, decay, beta, S_ref)
-        coef, dS, dZ = seg.forward_local()
-        Z0e = Z0 if Z0 is not None else torch.zeros_like(S0)
-        coefs, dSs, dZs = _gather(coef, group), _gather(dS, group), _gather(dZ, group)
-        carries, (S_T, Z_T) = compose_forward_carries(coefs, dSs, dZs, S0, Z0e)
+        seg.forward_local()
         r = dist.get_rank(group)
-        S_in, Z_in = carries[r]
+        records = _gather_records(seg, group)
+        S_in, Z_in, S_T, S_end, Z_T = compose_carries_device(seg, records, r, False, S0, Z0, clamped=True)
         y, _, _ = seg.forward_finish(S_in, Z_in if spec.momentum else None)
         ctx.seg, ctx.group, ctx.spec, ctx.S_T = seg, group, spec, S_T
         ctx.set_materialize_grads(False)
-        S_end = S_T.clamp(-100, 100)                 # rnn_memory.py:701
         Z_end = Z_T if spec.momentum else S_T.new_empty(0)
         return y, S_end, Z_end
 
     @staticmethod
     def backward(ctx, dy, dS_end, dZ_end):
         seg, group, spec = ctx.seg, ctx.group, ctx.spec
-        r, P = dist.get_rank(group), dist.get_world_size(group)
+        r = dist.get_rank(group)
         if dy is None:
             dy = torch.zeros(seg.N, seg.T, seg.d_v, dtype=seg.k.dtype, device=seg.dev)
         dy = dy.contiguous()
-        coef, dFS, dFZ = seg.backward_local(dy)
-        coefs, dFSs, dFZs = _gather(coef, group), _gather(dFS, group), _gather(dFZ, group)
+        seg.backward_local(dy)
+        records = _gather_records(seg, group)
         # every rank returned the same S_end / Z_end: their upstream gradients add up
-        # copies: the all-reduce below must not modify the caller's gradient tensors
-        FS_end = torch.zeros_like(ctx.S_T) if dS_end is None else dS_end.float().clone()
-        FZ_end = torch.zeros_like(ctx.S_T) if (dZ_end is None or dZ_end.numel() == 0) else dZ_end.float().clone()
-        dist.all_reduce(FS_end, group=group)
-        dist.all_reduce(FZ_end, group=group)
-        FS_end = FS_end * ((ctx.S_T >= -100) & (ctx.S_T <= 100))  # clamp gradient
-        incoming, (dS0, dZ0) = compose_backward_carries(coefs, dFSs, dFZs, FS_end, FZ_end)
-        FS, FZ = incoming[r]
+        # (one all-reduce of both; a fresh buffer, so the caller's tensors stay as they are)
+        ends = torch.zeros((2,) + tuple(ctx.S_T.shape), device=seg.dev)
+        if dS_end is not None:
+            ends[0].copy_(dS_end)
+        if dZ_end is not None and dZ_end.numel() != 0:
+            ends[1].copy_(dZ_end)
+        dist.all_reduce(ends, group=group)
+        FS, FZ, dS0, _, dZ0 = compose_carries_device(seg, records, r, True, ends[0], ends[1], S_T=ctx.S_T)
         flags = ctx.needs_input_grad  # (spec, group, k, q, v, lr, decay, beta, S_ref, S0, Z0)
         need = {n for n, f in zip(("k", "q", "v", "lr", "decay", "beta", "S_ref"), flags[2:9]) if f}
         g = seg.backward_finish(dy, FS, FZ if spec.momentum else None, apply_mask=False, need=need)

@@ -220,6 +220,22 @@ int atlas_mem_backward_finish(const AtlasMemShape* shape, const AtlasMemFwd* fwd
                               void* scratch, size_t scratch_bytes, int apply_clamp_mask,
                               void* stream);
 
+/* Composes the gathered segment transforms of all `world` ranks (the host-side
+ * step of the carry exchange, done on the device in one pass). seg is
+ * [world][record_len] floats; a rank's record is coef [N,3] padded to a
+ * multiple of 4 floats, then dS [N,d2], then dZ [N,d2] (the buffers
+ * *_local fill). Forward (backward = 0): S0 / Z0 (Z0 may be NULL = 0) through
+ * ranks 0..world-1; in_S / in_Z receive the carry entering `rank`, out_S the
+ * unclamped S_T, out_S_clamped clamp(S_T, -100, 100), out_Z Z_T. Backward:
+ * S0 / Z0 are the summed dS_end / dZ_end (NULL = 0), dS_end masked where S_T
+ * (NULL = no mask) lies outside [-100, 100], composed through ranks
+ * world-1..0; in_* receive the adjoint arriving at the end of `rank`'s
+ * segment, out_S / out_Z the adjoint at the sequence start (dS0 / dZ0).
+ * Any output may be NULL. */
+int atlas_mem_compose_carries(const float* seg, int64_t record_len, int world, int rank, int64_t N, int64_t d2,
+                              int backward, const float* S0, const float* Z0, const float* S_T, float* in_S,
+                              float* in_Z, float* out_S, float* out_S_clamped, float* out_Z, void* stream);
+
 /* Device self-check of the tensor-core (tcgen05) GEMM building block used by
  * the fused kernels: D[128,N] = A[128,K] * B^T with A given as [128][K]
  * (a_mn_major = 0) or [K][128] (1), B as [N][K] (b_mn_major = 0) or [K][N] (1);
