@@ -1,7 +1,9 @@
 """atlas_rnn_b200: B200-native memory-update hot path of Atlas-RNN.
 
 Public API mirrors atlas_pytorch/rnn_memory.py (RNNMemoryCell, OmegaRNNMemoryCell,
-RNNMemory, OmegaRNNMemory, RNNMemState, state_detach, PolynomialFeatureMap) plus the
+RNNMemory, OmegaRNNMemory, RNNMemState, state_detach, PolynomialFeatureMap), the LMM
+language model of atlas_pytorch/rnn_transformer.py (RNNMemoryTransformer with
+block_type 'lmm', LMMBlock, LongTermMemoryModel), plus the
 functional ``memory_recurrence``, the GPU drop-in for the third-party
 ``assoc_scan.AssocScan`` (``AssocScan``, ``assoc_scan``) and the multi-GPU helpers in ``parallel``.
 """
@@ -9,7 +11,8 @@ from .ops import memory_recurrence, MemoryRecurrenceFn
 from .scan import AssocScan, assoc_scan
 from .rnn_memory import (RNNMemState, state_detach, PolynomialFeatureMap, MultiheadRMSNorm,
                          RNNMemoryCell, OmegaRNNMemoryCell, RNNMemory, OmegaRNNMemory)
+from .rnn_transformer import LMMBlock, LongTermMemoryModel, RNNMemoryTransformer
 
 __all__ = ["memory_recurrence", "MemoryRecurrenceFn", "AssocScan", "assoc_scan", "RNNMemState", "state_detach",
            "PolynomialFeatureMap", "MultiheadRMSNorm", "RNNMemoryCell", "OmegaRNNMemoryCell",
-           "RNNMemory", "OmegaRNNMemory"]
+           "RNNMemory", "OmegaRNNMemory", "LMMBlock", "LongTermMemoryModel", "RNNMemoryTransformer"]

@@ -13,6 +13,9 @@ data-path collective); timing is the max over ranks of CUDA-event time.
 the CPU restatement in oracle/ (materialised [N,T,d,d] einsums and log-depth
 scalar scans, autograd backward), on a bounded slice of the same workload,
 scaled to the whole workload. Under torchrun only rank 0 runs it.
+
+``--config 3`` times the LMM language model instead (one training step of the
+12-layer model of the benchmark config: loss, backward, AdamW; bf16 autocast).
 """
 from __future__ import annotations
 
@@ -445,6 +448,109 @@ def kernel_cfg_chunk(w):
     return 32 if w.window - 1 <= 32 else w.window - 1
 
 
+LM_C3 = dict(num_tokens=256, dim=768, depth=12, block_type="lmm", heads=12, dim_head=64, ff_mult=4,
+             omega_window=8, use_omega_gate=True, use_momentum=True, poly_mode="elementwise", poly_degree=2,
+             qkv_conv_kernel=4)
+LM_C3_BATCH, LM_C3_SEQ = 16, 8192
+
+
+def run_lm(args):
+    """Config 3: one training step (next-token loss, backward, AdamW) of the 12-layer LMM
+    language model (RNNMemoryTransformer, block_type 'lmm'; SwiGLU hidden 2048) on synthetic
+    byte tokens under bf16 autocast, random-init weights. N > 1: the global batch is split
+    over the ranks (data parallel, gradients all-reduced by DistributedDataParallel)."""
+    import torch.distributed as dist
+    from atlas_rnn_b200 import RNNMemoryTransformer, _lib
+
+    ws, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    B = (args.B or LM_C3_BATCH) // ws
+    T = args.T or LM_C3_SEQ
+    torch.manual_seed(0)
+    model = RNNMemoryTransformer(**LM_C3).to(dev)
+    with torch.no_grad():  # N(0, 0.02) weights as the benchmark config states
+        for name, p in model.named_parameters():
+            if p.dim() > 1:
+                p.normal_(0.0, 0.02)
+    net = torch.nn.parallel.DistributedDataParallel(model, device_ids=[local]) if ws > 1 else model
+    opt = torch.optim.AdamW(model.parameters(), lr=1e-4, fused=True)
+    g = torch.Generator(device=dev).manual_seed(1234 + rank)
+    tokens = torch.randint(0, 256, (B, T + 1), device=dev, generator=g)
+    host_tokens = tokens.cpu().pin_memory()
+    loss_host = torch.empty((), dtype=torch.float32).pin_memory()
+
+    def step(tok):
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            loss = net(tok, return_loss=True)
+        opt.zero_grad(set_to_none=True)
+        loss.backward()
+        opt.step()
+        return loss
+
+    def barrier():
+        if ws > 1:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize(dev)
+
+    for _ in range(args.warmup):
+        step(tokens)
+    barrier()
+    st = torch.cuda.current_stream(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    props = torch.cuda.get_device_properties(dev)
+    ids = [("GPU-" + str(props.uuid)) if getattr(props, "uuid", None) is not None else str(local)]
+    if ws > 1:
+        gathered = [None] * ws
+        dist.all_gather_object(gathered, ids[0])
+        ids = gathered
+    launches0 = _lib.launch_count()
+    with ClockSampler(ids, rank) as clk:
+        barrier()
+        clk.mark_start()
+        ev0.record(st)
+        for _ in range(args.steps):
+            step(tokens)
+        ev1.record(st)
+        barrier()
+        clk.mark_end()
+    ms = ev0.elapsed_time(ev1)
+    launches = _lib.launch_count() - launches0
+    # end to end: tokens from pinned host memory, loss back to the host, every step
+    barrier()
+    ev0.record(st)
+    for _ in range(args.steps):
+        loss = step(host_tokens.to(dev, non_blocking=True))
+        loss_host.copy_(loss.detach().float(), non_blocking=True)
+    ev1.record(st)
+    barrier()
+    e2e_ms = ev0.elapsed_time(ev1)
+    if ws > 1:
+        t = torch.tensor([ms, e2e_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, e2e_ms = t.tolist()
+    tok = ws * B * T * args.steps
+    if rank == 0:
+        line = {
+            "metric": "LM training tokens/sec", "value": tok / (ms / 1000.0), "unit": UNIT, "n_gpus": ws,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic byte tokens (uniform 0..255), random-init N(0, 0.02) weights",
+            "config": {"workload": "lmm_lm_c3", "global_batch": B * ws, "seq_len": T, **LM_C3,
+                       "parallelism": f"data-parallel x{ws}", "l2": "activations exceed L2"},
+            "e2e": {"value": tok / (e2e_ms / 1000.0), "unit": UNIT,
+                    "h2d_bytes_per_step": host_tokens.numel() * host_tokens.element_size(), "d2h_bytes_per_step": 4},
+            "gpu_launches": launches, "loss": float(loss_host), "clocks": clk.summary(),
+            "peak_mem_gb": torch.cuda.max_memory_allocated(dev) / 1e9,
+        }
+        print(json.dumps(line), flush=True)
+    if ws > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -460,6 +566,13 @@ def main():
     args = ap.parse_args()
     global WITH_BUFFER
     WITH_BUFFER = args.with_buffer
+    if args.config == 3:
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "the reference LM runs its memory cells in "
+                              "materialised [B,H,T,d,d] torch einsums; config 3 does not fit one GPU that way"}))
+            return
+        run_lm(args)
+        return
     w = CONFIGS[args.config]
     if args.T or args.B:
         w = shrink(w, B=args.B, T=args.T)

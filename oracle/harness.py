@@ -13,6 +13,7 @@ gate sub-modules are replaced so that the cell's own ``_forward_impl``
 * ``to_out``         -> Identity
 * ``phi``            -> the reference's own PolynomialFeatureMap with a given proj
 
+``load_reference_rnn_transformer`` loads the reference LM module on top of it.
 Used only by ``tests/golden/make_golden.py`` where the reference sources exist;
 the generated fixtures travel, the reference does not.
 """
@@ -36,6 +37,30 @@ def load_reference_rnn_memory(reference_root: str):
         sys.modules["assoc_scan"] = mod
     path = f"{reference_root}/atlas_pytorch/rnn_memory.py"
     spec = importlib.util.spec_from_file_location("_reference_rnn_memory", path)
+    module = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(module)
+    return module
+
+
+def load_reference_rnn_transformer(reference_root: str, rm):
+    """Import the reference rnn_transformer.py by path on top of `rm` (the loaded
+    rnn_memory module). Its attention dependencies (rotary_embedding_torch,
+    x_transformers) are absent here; they are only used by the attention block types,
+    so they are registered as empty placeholders for the import."""
+    for name, attr in (("rotary_embedding_torch", "RotaryEmbedding"), ("x_transformers", None),
+                       ("x_transformers.attend", "Attend")):
+        if name not in sys.modules:
+            mod = types.ModuleType(name)
+            if attr:
+                setattr(mod, attr, type(attr, (nn.Module,), {}))
+            sys.modules[name] = mod
+    if "atlas_pytorch" not in sys.modules:
+        pkg = types.ModuleType("atlas_pytorch")
+        pkg.__path__ = []
+        sys.modules["atlas_pytorch"] = pkg
+    sys.modules["atlas_pytorch.rnn_memory"] = rm
+    path = f"{reference_root}/atlas_pytorch/rnn_transformer.py"
+    spec = importlib.util.spec_from_file_location("_reference_rnn_transformer", path)
     module = importlib.util.module_from_spec(spec)
     spec.loader.exec_module(module)
     return module

@@ -11,6 +11,9 @@ Two kinds of fixture:
 * ``core_*.npz``   -- the recurrence at the q/k/v/gates boundary (harness), N = B*H
 * ``module_*.npz`` -- a whole reference cell (projections, convs, norms, gates) with
                       its state_dict, input x and outputs / x.grad.
+* ``lm_*.npz``     -- the reference LMM language model (RNNMemoryTransformer,
+                      block_type 'lmm'): state_dict, tokens, loss, logits, every
+                      parameter gradient, and the logits of one-token cached steps.
 """
 from __future__ import annotations
 
@@ -152,6 +155,47 @@ def make_module(rm, name, cls, kw, B, T, state_kind, seed):
     np.savez_compressed(os.path.join(HERE, name + ".npz"), **rec)
 
 
+LM_CASES = {
+    # name: (RNNMemoryTransformer kwargs, B, T, decode steps)
+    "lm_lmm_omega_e3_elem": (dict(num_tokens=256, dim=32, depth=2, block_type="lmm", heads=2, dim_head=16,
+                                  omega_window=3, use_omega_gate=True, poly_mode="elementwise", poly_degree=2,
+                                  qkv_conv_kernel=4), 2, 23, 5),
+    "lm_lmm_titans": (dict(num_tokens=256, dim=24, depth=2, block_type="lmm", heads=3, dim_head=8,
+                           use_momentum=True, qkv_conv_kernel=None), 1, 17, 4),
+}
+
+
+def make_lm(rt, name, kw, B, T, steps, seed):
+    """The reference LM (rnn_transformer.py:720-862): next-token loss, logits and every
+    parameter gradient; then `steps` one-token calls carrying the memory states (the
+    cached path of generate, :880-886) on fixed tokens, with their logits."""
+    torch.manual_seed(seed)
+    m = rt.RNNMemoryTransformer(**kw).to(DT)
+    with torch.no_grad():  # non-default gate heads so every gate varies per token
+        for blk in m.layers:
+            for head in ("to_lr", "to_decay", "to_momentum", "to_omega_gate"):
+                mod = getattr(blk.memory, head, None)
+                if mod is not None:
+                    mod[0].weight.normal_(0, 0.2)
+    tokens = torch.randint(0, kw["num_tokens"], (B, T))
+    loss, logits, states, _ = m(tokens, return_loss=True, return_cache=True)
+    loss.backward()
+    rec = {"tokens": tokens.numpy(), "loss": np.array(loss.item()), "logits": logits.detach().numpy()}
+    for key, p in m.named_parameters():
+        rec["grad." + key] = p.grad.numpy()
+    for key, t in m.state_dict().items():
+        rec["sd." + key] = t.numpy()
+    step_tokens = torch.randint(0, kw["num_tokens"], (steps, B, 1))
+    with torch.no_grad():
+        st, outs = None, []
+        for s in range(steps):
+            lg, st, _ = m(step_tokens[s], mem_states=st, return_cache=True)
+            outs.append(lg.numpy())
+    rec["step_tokens"] = step_tokens.numpy()
+    rec["step_logits"] = np.stack(outs)
+    np.savez_compressed(os.path.join(HERE, name + ".npz"), **rec)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("ATLAS_RNN_REFERENCE"), required=False)
@@ -164,6 +208,10 @@ def main():
         print("wrote", name)
     for i, (name, (cls, kw, B, T, sk)) in enumerate(MODULE_CASES.items()):
         make_module(rm, name, cls, kw, B, T, sk, seed=200 + i)
+        print("wrote", name)
+    rt = harness.load_reference_rnn_transformer(args.reference, rm)
+    for i, (name, (kw, B, T, steps)) in enumerate(LM_CASES.items()):
+        make_lm(rt, name, kw, B, T, steps, seed=300 + i)
         print("wrote", name)
 
 
