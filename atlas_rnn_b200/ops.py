@@ -11,9 +11,11 @@ passes pointers.
 from __future__ import annotations
 
 import ctypes
+import os
 from dataclasses import dataclass
 
 import torch
+import torch.nn.functional as F
 from torch import Tensor
 
 from . import _lib
@@ -142,6 +144,33 @@ def decode_step(spec: Spec, k, q, v, lr, decay, beta, gate, S_ref, S0, Z0, buf, 
     return y, S_end, Z_end, buf_out
 
 
+TC_D = 128  # state side of the tensor-core kernels
+
+
+def _pad_to_tc(spec: Spec, io, d_k: int, d_phi: int, d_v: int) -> bool:
+    """bf16 heads narrower than the tensor-core kernels' 128 x 128 state run those kernels
+    on zero-padded heads (feature map off or elementwise, so d_phi = d_k). Exact: with
+    zero-padded phi(k), phi(q), v, S_ref, S0, Z0 and buffer, the padded rows of delta are
+    S_ref[pad] phi - 0 = 0 and every padded column is multiplied by phi[pad] = 0, so the
+    padded part of every state stays zero and the outputs are the unpadded ones.
+    ATLAS_MEM_PAD128=0 keeps such heads on the CUDA-core kernels."""
+    if io != torch.bfloat16 or spec.fmap_mode == "tensor" or spec.window > 16:
+        return False
+    if not (d_phi == d_k and d_phi < TC_D and d_v <= TC_D):
+        return False
+    return os.environ.get("ATLAS_MEM_PAD128", "1") != "0" and os.environ.get("ATLAS_MEM_TC", "1") != "0"
+
+
+def _padded_call(spec: Spec, d_v: int, d_phi: int, k, q, v, lr, decay, beta, gate, S_ref, S0, Z0, buf, proj):
+    pk, pv = TC_D - d_phi, TC_D - d_v
+    vec = lambda t, p: F.pad(t, (0, p))                       # [.., d] -> [.., 128]
+    mat = lambda t: None if t is None else F.pad(t, (0, pk, 0, pv))  # [.., d_v, d_phi] -> [.., 128, 128]
+    y, S_end, Z_end, buf_out = MemoryRecurrenceFn.apply(spec, vec(k, pk), vec(q, pk), vec(v, pv), lr, decay,
+                                                        beta, gate, mat(S_ref), mat(S0), mat(Z0), mat(buf), proj)
+    cut = lambda t: t[..., :d_v, :d_phi] if t is not None and t.numel() else t
+    return y[..., :d_v], cut(S_end), cut(Z_end), cut(buf_out)
+
+
 def memory_recurrence(k: Tensor, q: Tensor, v: Tensor, lr: Tensor, decay: Tensor,
                       beta: Tensor | None = None, gate: Tensor | None = None, *, S_ref: Tensor,
                       S0: Tensor, Z0: Tensor | None = None, omega_buffer: Tensor | None = None,
@@ -154,7 +183,8 @@ def memory_recurrence(k: Tensor, q: Tensor, v: Tensor, lr: Tensor, decay: Tensor
     'window', per-position window weights U[t, j] on the term of token t-j);
     S_ref, S0, Z0 [N,d_v,d_phi]; omega_buffer [N,e-1,d_v,d_phi].
     Returns (y [N,T,d_v], S_end (clamped to +-100), Z_end or None, new omega buffer or None).
-    io tensors run in bfloat16 when k is bfloat16, else float32; states in float32.
+    io tensors run in bfloat16 when k is bfloat16 or bf16 autocast is on (as autocast runs the
+    reference's einsums), else float32; states in float32.
     A single token (T = 1) with no autograd graph to record runs as one decode
     kernel (atlas_mem_decode_step) unless the tensor feature map is on.
     """
@@ -162,6 +192,8 @@ def memory_recurrence(k: Tensor, q: Tensor, v: Tensor, lr: Tensor, decay: Tensor
         raise RuntimeError("atlas_rnn_b200.memory_recurrence: tensors must be on a CUDA device "
                            "(the library has no CPU path)")
     io = torch.bfloat16 if k.dtype == torch.bfloat16 else torch.float32
+    if torch.is_autocast_enabled("cuda") and torch.get_autocast_dtype("cuda") == torch.bfloat16:
+        io = torch.bfloat16  # a matmul-like op under bf16 autocast: bf16 operands, fp32 state and accumulation
     if gate is None:
         gm = _lib.GATE_NONE
     elif gate_mode == "window" or (gate_mode is None and gate.dim() == 3):
@@ -182,6 +214,8 @@ def memory_recurrence(k: Tensor, q: Tensor, v: Tensor, lr: Tensor, decay: Tensor
         t is not None and t.requires_grad for t in (k, q, v, lr, decay, beta, gate, S_ref, S0, Z0, omega_buffer))
     if k.shape[1] == 1 and not needs_grad and decode_supported(spec, k.shape[-1], S_ref.shape[-1], v.shape[-1]):
         y, S_end, Z_end, buf_out = decode_step(spec, *args)
+    elif _pad_to_tc(spec, io, k.shape[-1], S_ref.shape[-1], v.shape[-1]):
+        y, S_end, Z_end, buf_out = _padded_call(spec, v.shape[-1], S_ref.shape[-1], *args)
     else:
         y, S_end, Z_end, buf_out = MemoryRecurrenceFn.apply(spec, *args)
     S_end = S_end.to(state_dtype)

@@ -91,8 +91,28 @@ def test_fp32_separate_sref(native_lib, w):
 @pytest.mark.parametrize("w", [W("bf16_titans", 130, d=64, dtype=torch.bfloat16),
                                W("bf16_omega_window", 99, d=64, e=4, gate="window", fm="elementwise", deg=2,
                                  dtype=torch.bfloat16)], ids=lambda w: w.name)
-def test_bf16_vs_oracle(native_lib, w):
+@pytest.mark.parametrize("pad", ["1", "0"], ids=["padded_tc", "cuda_cores"])
+def test_bf16_vs_oracle(native_lib, monkeypatch, w, pad):
+    """bf16 heads under 128 run the tensor-core kernels zero-padded (default) or the
+    CUDA-core kernels (ATLAS_MEM_PAD128=0)."""
+    monkeypatch.setenv("ATLAS_MEM_PAD128", pad)
     run_case(w)
+
+
+# bf16 heads narrower than 128 on the zero-padded tensor-core path
+CASES_PAD = [
+    W("pad_c3_like_e8_token_elem", 300, d=64, e=8, gate="token", fm="elementwise", deg=2, dtype=torch.bfloat16,
+      N=(2, 3)),
+    W("pad_titans_d32_nomom", 140, d=32, mom=False, dtype=torch.bfloat16),
+    W("pad_rect_dv48_dphi32", 133, d=32, dv=48, e=3, gate="token", dtype=torch.bfloat16),
+    W("pad_e16_window_d64", 200, d=64, e=16, gate="window", dtype=torch.bfloat16),
+    W("pad_short_t3", 3, d=64, e=4, gate="token", dtype=torch.bfloat16),
+]
+
+
+@pytest.mark.parametrize("w", CASES_PAD, ids=lambda w: w.name)
+def test_bf16_padded_tensor_core_path(native_lib, w):
+    run_case(w, state_scale=0.1)
 
 
 def test_config0_full(native_lib):
