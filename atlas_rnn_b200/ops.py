@@ -171,11 +171,30 @@ def _padded_call(spec: Spec, d_v: int, d_phi: int, k, q, v, lr, decay, beta, gat
     return y[..., :d_v], cut(S_end), cut(Z_end), cut(buf_out)
 
 
+def _chunk_ref_mode(k, q, v, lr, decay, beta, gate, *, S0, Z0, omega_buffer, window, gate_mode, fmap_mode,
+                    fmap_degree, proj, chunk, ref_chunk):
+    """ref_mode 'chunk' as consecutive calls whose reference state is their own start state."""
+    if not ref_chunk or ref_chunk < 1:
+        raise ValueError("ref_mode='chunk' needs ref_chunk >= 1 (tokens per reference state)")
+    T = k.shape[1]
+    S, Z, buf, ys = S0, Z0, omega_buffer, []
+    cut = lambda t, lo, hi: None if t is None else t[:, lo:hi]
+    for lo in range(0, T, ref_chunk):
+        hi = min(T, lo + ref_chunk)
+        y, S, Z, buf = memory_recurrence(cut(k, lo, hi), cut(q, lo, hi), cut(v, lo, hi), cut(lr, lo, hi),
+                                         cut(decay, lo, hi), cut(beta, lo, hi), cut(gate, lo, hi), S_ref=S, S0=S,
+                                         Z0=Z, omega_buffer=buf, window=window, gate_mode=gate_mode,
+                                         fmap_mode=fmap_mode, fmap_degree=fmap_degree, proj=proj, chunk=chunk)
+        ys.append(y)
+    return torch.cat(ys, dim=1), S, Z, buf
+
+
 def memory_recurrence(k: Tensor, q: Tensor, v: Tensor, lr: Tensor, decay: Tensor,
                       beta: Tensor | None = None, gate: Tensor | None = None, *, S_ref: Tensor,
                       S0: Tensor, Z0: Tensor | None = None, omega_buffer: Tensor | None = None,
                       window: int = 1, gate_mode: str | None = None, fmap_mode: str = "off",
-                      fmap_degree: int = 1, proj: Tensor | None = None, chunk: int = 0):
+                      fmap_degree: int = 1, proj: Tensor | None = None, chunk: int = 0,
+                      ref_mode: str = "call", ref_chunk: int | None = None):
     """Memory recurrence over N = batch*heads units.
 
     k, q [N,T,d_k]; v [N,T,d_v]; lr (eta), decay (alpha), beta [N,T]; gate [N,T]
@@ -187,7 +206,18 @@ def memory_recurrence(k: Tensor, q: Tensor, v: Tensor, lr: Tensor, decay: Tensor
     reference's einsums), else float32; states in float32.
     A single token (T = 1) with no autograd graph to record runs as one decode
     kernel (atlas_mem_decode_step) unless the tensor feature map is on.
+    ref_mode 'call' (default, the reference's semantics): every token's delta uses S_ref.
+    ref_mode 'chunk': the chunk-start state is the reference state -- the sequence runs as
+    consecutive calls of ref_chunk tokens, each with S_ref = S0 = the state (clamped to
+    +-100) the call before returned, carrying Z and the omega buffer; S_ref is then unused.
+    That is the reference cell called once per chunk in a loop (tests/test_rnn_all.py:804-825).
     """
+    if ref_mode == "chunk":
+        return _chunk_ref_mode(k, q, v, lr, decay, beta, gate, S0=S0, Z0=Z0, omega_buffer=omega_buffer,
+                               window=window, gate_mode=gate_mode, fmap_mode=fmap_mode, fmap_degree=fmap_degree,
+                               proj=proj, chunk=chunk, ref_chunk=ref_chunk)
+    if ref_mode != "call":
+        raise ValueError(f"ref_mode must be 'call' or 'chunk', not {ref_mode!r}")
     if not k.is_cuda:
         raise RuntimeError("atlas_rnn_b200.memory_recurrence: tensors must be on a CUDA device "
                            "(the library has no CPU path)")
