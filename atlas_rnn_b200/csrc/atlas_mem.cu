@@ -12,6 +12,7 @@
 #include "decode.cuh"
 #include "scan_op.cuh"
 #include "carry.cuh"
+#include "dwconv.cuh"
 #include "umma_selftest.cuh"
 
 using namespace atlas;
@@ -265,12 +266,12 @@ Params make_params(const AtlasMemShape* s, const Layout& L, const AtlasMemFwd* f
 enum KernelId {
   KID_FMAP_FWD, KID_FWD_CHUNK, KID_FWD_SCAN, KID_FWD_OUT, KID_BUF_OUT, KID_BWD_CHUNK, KID_BWD_SCAN,
   KID_BWD_GRADS, KID_BWD_BUFOUT, KID_BWD_FINAL, KID_BWD_DSREF, KID_FMAP_BWD, KID_FWD_CHUNK_TC, KID_FWD_OUT_TC, KID_FWD_BUF_Y,
-  KID_BWD_CHUNK_TC, KID_BWD_STATE_GATES_TC, KID_BWD_BUF_TC, KID_BWD_FINAL_TC, KID_BWD_DSREF_TC, KID_BWD_KEYS_TC, KID_SREF_TILE, KID_DECODE, KID_SCAN_OP_FWD, KID_SCAN_OP_BWD, KID_CARRY, KID_COUNT
+  KID_BWD_CHUNK_TC, KID_BWD_STATE_GATES_TC, KID_BWD_BUF_TC, KID_BWD_FINAL_TC, KID_BWD_DSREF_TC, KID_BWD_KEYS_TC, KID_SREF_TILE, KID_DECODE, KID_SCAN_OP_FWD, KID_SCAN_OP_BWD, KID_CARRY, KID_DWCONV_FWD, KID_DWCONV_BWD, KID_COUNT
 };
 const char* const kKernelNames[KID_COUNT] = {
   "k_fmap_tensor_fwd", "k_fwd_chunk", "k_fwd_scan", "k_fwd_out", "k_buf_out", "k_bwd_chunk", "k_bwd_scan",
   "k_bwd_grads", "k_bwd_bufout", "k_bwd_finalize", "k_bwd_dsref", "k_fmap_tensor_bwd", "k_fwd_chunk_tc", "k_fwd_out_tc", "k_fwd_buf_y",
-  "k_bwd_chunk_tc", "k_bwd_state_gates_tc", "k_bwd_buf_tc", "k_bwd_finalize_tc", "k_bwd_dsref_tc", "k_bwd_keys_tc", "k_sref_tile", "k_decode_step", "k_scan_op_fwd", "k_scan_op_bwd", "k_compose_carries"};
+  "k_bwd_chunk_tc", "k_bwd_state_gates_tc", "k_bwd_buf_tc", "k_bwd_finalize_tc", "k_bwd_dsref_tc", "k_bwd_keys_tc", "k_sref_tile", "k_decode_step", "k_scan_op_fwd", "k_scan_op_bwd", "k_compose_carries", "k_dwconv3_fwd", "k_dwconv3_bwd"};
 
 constexpr int kMaxTimed = 8192;
 struct Prof {
@@ -507,6 +508,57 @@ int check_ws(const Layout& L, const void* saved, size_t saved_bytes, const void*
 
 }  // namespace
 
+// ---- q/k/v depthwise convolutions (dwconv.cuh) ----
+template <int K, class X, class Y>
+int dwconv_fwd_t(const void* x, const float* wq, const float* wk, const float* wv, void* yq, void* yk, void* yv,
+                 int64_t B, int64_t T, int64_t C, cudaStream_t st) {
+  const dim3 grid((unsigned)((C + kConvThreads - 1) / kConvThreads), (unsigned)((T + kConvRun - 1) / kConvRun),
+                  (unsigned)B);
+  LAUNCH_T(KID_DWCONV_FWD, (k_dwconv3_fwd<K, X, Y>), grid, kConvThreads, 0, st, (const X*)x, wq, wk, wv, (Y*)yq,
+           (Y*)yk, (Y*)yv, T, C);
+  return ATLAS_OK;
+}
+template <int K, class X, class Y>
+int dwconv_bwd_t(const void* x, const float* wq, const float* wk, const float* wv, const void* dq, const void* dk,
+                 const void* dv, void* dx, float* dw, int64_t B, int64_t T, int64_t C, cudaStream_t st) {
+  const dim3 grid((unsigned)((C + kConvThreads - 1) / kConvThreads), (unsigned)((T + kConvRun - 1) / kConvRun),
+                  (unsigned)B);
+  LAUNCH_T(KID_DWCONV_BWD, (k_dwconv3_bwd<K, X, Y>), grid, kConvThreads, 0, st, (const X*)x, wq, wk, wv,
+           (const Y*)dq, (const Y*)dk, (const Y*)dv, (X*)dx, dw, T, C);
+  return ATLAS_OK;
+}
+template <class X, class Y>
+int dwconv_dispatch(bool fwd, int K, const void* x, const float* wq, const float* wk, const float* wv, void* a,
+                    void* b, void* c, const void* dq, const void* dk, const void* dv, float* dw, int64_t B,
+                    int64_t T, int64_t C, cudaStream_t st) {
+#define ATLAS_DWCONV_CASE(KK)                                                                   \
+  case KK:                                                                                      \
+    return fwd ? dwconv_fwd_t<KK, X, Y>(x, wq, wk, wv, a, b, c, B, T, C, st)                    \
+               : dwconv_bwd_t<KK, X, Y>(x, wq, wk, wv, dq, dk, dv, a, dw, B, T, C, st);
+  switch (K) {
+    ATLAS_DWCONV_CASE(2)
+    ATLAS_DWCONV_CASE(3)
+    ATLAS_DWCONV_CASE(4)
+    ATLAS_DWCONV_CASE(5)
+    ATLAS_DWCONV_CASE(6)
+    ATLAS_DWCONV_CASE(7)
+    ATLAS_DWCONV_CASE(8)
+    default:
+      return ATLAS_ERR_INVALID_ARG;
+  }
+#undef ATLAS_DWCONV_CASE
+}
+int dwconv_types(bool fwd, int K, int dtype_x, int dtype_y, const void* x, const float* wq, const float* wk,
+                 const float* wv, void* a, void* b, void* c, const void* dq, const void* dk, const void* dv,
+                 float* dw, int64_t B, int64_t T, int64_t C, cudaStream_t st) {
+  const bool xb = dtype_x == ATLAS_BF16, yb = dtype_y == ATLAS_BF16;
+  if (xb && yb) return dwconv_dispatch<__nv_bfloat16, __nv_bfloat16>(fwd, K, x, wq, wk, wv, a, b, c, dq, dk, dv, dw, B, T, C, st);
+  if (xb) return dwconv_dispatch<__nv_bfloat16, float>(fwd, K, x, wq, wk, wv, a, b, c, dq, dk, dv, dw, B, T, C, st);
+  if (yb) return dwconv_dispatch<float, __nv_bfloat16>(fwd, K, x, wq, wk, wv, a, b, c, dq, dk, dv, dw, B, T, C, st);
+  return dwconv_dispatch<float, float>(fwd, K, x, wq, wk, wv, a, b, c, dq, dk, dv, dw, B, T, C, st);
+}
+bool dtype_ok(int d) { return d == ATLAS_F32 || d == ATLAS_BF16; }
+
 extern "C" {
 
 int atlas_mem_abi_version(void) { return ATLAS_MEM_ABI_VERSION; }
@@ -671,6 +723,29 @@ int atlas_mem_compose_carries(const float* seg, int64_t record_len, int world, i
   const int64_t blocks = std::min<int64_t>((A.ND2 + kThreads - 1) / kThreads, (int64_t)sm_count() * 8);
   LAUNCH(KID_CARRY, k_compose_carries, dim3((unsigned)blocks), 0, st, A);
   return ATLAS_OK;
+}
+
+int atlas_dwconv3_forward(const void* x, int dtype_x, const float* w_q, const float* w_k, const float* w_v, int K,
+                          void* y_q, void* y_k, void* y_v, int dtype_y, int64_t B, int64_t T, int64_t C,
+                          void* stream) {
+  if (!x || !w_q || !w_k || !w_v || !y_q || !y_k || !y_v || B < 1 || T < 1 || C < 1 || B > 65535 ||
+      !dtype_ok(dtype_x) || !dtype_ok(dtype_y) || K < 2 || K > kConvMaxK || (T + kConvRun - 1) / kConvRun > 65535)
+    return ATLAS_ERR_INVALID_ARG;
+  return dwconv_types(true, K, dtype_x, dtype_y, x, w_q, w_k, w_v, y_q, y_k, y_v, nullptr, nullptr, nullptr,
+                      nullptr, B, T, C, (cudaStream_t)stream);
+}
+
+int atlas_dwconv3_backward(const void* x, int dtype_x, const float* w_q, const float* w_k, const float* w_v, int K,
+                           const void* dy_q, const void* dy_k, const void* dy_v, int dtype_y, void* dx,
+                           float* dw, int64_t B, int64_t T, int64_t C, void* stream) {
+  if (!x || !w_q || !w_k || !w_v || !dy_q || !dy_k || !dy_v || !dx || !dw || B < 1 || T < 1 || C < 1 ||
+      B > 65535 || !dtype_ok(dtype_x) || !dtype_ok(dtype_y) || K < 2 || K > kConvMaxK ||
+      (T + kConvRun - 1) / kConvRun > 65535)
+    return ATLAS_ERR_INVALID_ARG;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (cudaMemsetAsync(dw, 0, (size_t)3 * C * K * sizeof(float), st) != cudaSuccess) return ATLAS_ERR_LAUNCH;
+  return dwconv_types(false, K, dtype_x, dtype_y, x, w_q, w_k, w_v, dx, nullptr, nullptr, dy_q, dy_k, dy_v, dw,
+                      B, T, C, st);
 }
 
 int atlas_mem_forward_local(const AtlasMemShape* shape, const AtlasMemFwd* fwd, void* saved, size_t saved_bytes,

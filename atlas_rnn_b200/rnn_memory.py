@@ -22,6 +22,7 @@ import torch.nn.functional as F
 from torch import Tensor, nn
 from torch.nn import Conv1d, Linear, Module, Parameter
 
+from .conv import qkv_depthwise_conv
 from .ops import memory_recurrence
 
 
@@ -158,11 +159,13 @@ class _MemoryCellBase(Module):
             state = self.init_state(batch, x.device, x.dtype)
         x_act = self.activation(self.pre_norm(x))
         q_in = k_in = v_in = x_act
-        if exists(self.q_conv):
+        if exists(self.q_conv) and self.qkv_conv_kernel <= 8:
+            # the three depthwise convs in one GPU pass (first T outputs, as the reference keeps)
+            q_in, k_in, v_in = qkv_depthwise_conv(x_act, self.q_conv.weight, self.k_conv.weight,
+                                                  self.v_conv.weight)
+        elif exists(self.q_conv):  # kernel sizes above 8: torch's Conv1d on the same device
             q_in = self.q_conv(q_in.transpose(1, 2)).transpose(1, 2)
-        if exists(self.k_conv):
             k_in = self.k_conv(k_in.transpose(1, 2)).transpose(1, 2)
-        if exists(self.v_conv):
             v_in = self.v_conv(v_in.transpose(1, 2)).transpose(1, 2)
         tile = self.scan_chunk_len
         if exists(tile) and seq_len > tile:

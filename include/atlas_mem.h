@@ -236,6 +236,22 @@ int atlas_mem_compose_carries(const float* seg, int64_t record_len, int world, i
                               int backward, const float* S0, const float* Z0, const float* S_T, float* in_S,
                               float* in_Z, float* out_S, float* out_S_clamped, float* out_Z, void* stream);
 
+/* The three depthwise convolutions in front of q, k and v in the memory cells
+ * (rnn_memory.py:196-202,334-340: Conv1d(C, C, K, padding=K/2, groups=C,
+ * bias=False) over the sequence, first T outputs kept), in one pass over x in
+ * its [B, T, C] layout: y_m[b,t,c] = sum_j w_m[c,j] x[b, t+j-K/2, c] (zero
+ * outside the sequence) for m = q, k, v. w_* are fp32 [C, K] (the Conv1d weight
+ * [C, 1, K]); x in dtype_x, outputs in dtype_y (ATLAS_F32 / ATLAS_BF16);
+ * fp32 accumulation. 2 <= K <= 8, B <= 65535. */
+int atlas_dwconv3_forward(const void* x, int dtype_x, const float* w_q, const float* w_k, const float* w_v, int K,
+                          void* y_q, void* y_k, void* y_v, int dtype_y, int64_t B, int64_t T, int64_t C,
+                          void* stream);
+/* Its backward: dx (dtype_x, [B, T, C]; the sum over the three convolutions)
+ * and dw fp32 [3, C, K] (q, k, v weight gradients; zeroed here, then summed). */
+int atlas_dwconv3_backward(const void* x, int dtype_x, const float* w_q, const float* w_k, const float* w_v, int K,
+                           const void* dy_q, const void* dy_k, const void* dy_v, int dtype_y, void* dx,
+                           float* dw, int64_t B, int64_t T, int64_t C, void* stream);
+
 /* Device self-check of the tensor-core (tcgen05) GEMM building block used by
  * the fused kernels: D[128,N] = A[128,K] * B^T with A given as [128][K]
  * (a_mn_major = 0) or [K][128] (1), B as [N][K] (b_mn_major = 0) or [K][N] (1);
