@@ -89,6 +89,12 @@ def lib():
                                              ctypes.c_int, _vp, _vp, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
                                              _vp]
         L.atlas_dwconv3_backward.restype = ctypes.c_int
+        L.atlas_head_prep_forward.argtypes = [_vp, ctypes.c_int, _vp, _vp, ctypes.c_int, ctypes.c_int64,
+                                              ctypes.c_int64, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp]
+        L.atlas_head_prep_forward.restype = ctypes.c_int
+        L.atlas_head_prep_backward.argtypes = [_vp, ctypes.c_int, _vp, _vp, ctypes.c_int, _vp, _vp, ctypes.c_int64,
+                                               ctypes.c_int64, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp]
+        L.atlas_head_prep_backward.restype = ctypes.c_int
         L.atlas_mem_selftest_umma.argtypes = [_vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                               ctypes.c_int, _vp, _vp]
         L.atlas_mem_selftest_umma.restype = ctypes.c_int

@@ -13,6 +13,7 @@
 #include "scan_op.cuh"
 #include "carry.cuh"
 #include "dwconv.cuh"
+#include "headprep.cuh"
 #include "umma_selftest.cuh"
 
 using namespace atlas;
@@ -266,12 +267,12 @@ Params make_params(const AtlasMemShape* s, const Layout& L, const AtlasMemFwd* f
 enum KernelId {
   KID_FMAP_FWD, KID_FWD_CHUNK, KID_FWD_SCAN, KID_FWD_OUT, KID_BUF_OUT, KID_BWD_CHUNK, KID_BWD_SCAN,
   KID_BWD_GRADS, KID_BWD_BUFOUT, KID_BWD_FINAL, KID_BWD_DSREF, KID_FMAP_BWD, KID_FWD_CHUNK_TC, KID_FWD_OUT_TC, KID_FWD_BUF_Y,
-  KID_BWD_CHUNK_TC, KID_BWD_STATE_GATES_TC, KID_BWD_BUF_TC, KID_BWD_FINAL_TC, KID_BWD_DSREF_TC, KID_BWD_KEYS_TC, KID_SREF_TILE, KID_DECODE, KID_SCAN_OP_FWD, KID_SCAN_OP_BWD, KID_CARRY, KID_DWCONV_FWD, KID_DWCONV_BWD, KID_COUNT
+  KID_BWD_CHUNK_TC, KID_BWD_STATE_GATES_TC, KID_BWD_BUF_TC, KID_BWD_FINAL_TC, KID_BWD_DSREF_TC, KID_BWD_KEYS_TC, KID_SREF_TILE, KID_DECODE, KID_SCAN_OP_FWD, KID_SCAN_OP_BWD, KID_CARRY, KID_DWCONV_FWD, KID_DWCONV_BWD, KID_HEADPREP_FWD, KID_HEADPREP_BWD, KID_COUNT
 };
 const char* const kKernelNames[KID_COUNT] = {
   "k_fmap_tensor_fwd", "k_fwd_chunk", "k_fwd_scan", "k_fwd_out", "k_buf_out", "k_bwd_chunk", "k_bwd_scan",
   "k_bwd_grads", "k_bwd_bufout", "k_bwd_finalize", "k_bwd_dsref", "k_fmap_tensor_bwd", "k_fwd_chunk_tc", "k_fwd_out_tc", "k_fwd_buf_y",
-  "k_bwd_chunk_tc", "k_bwd_state_gates_tc", "k_bwd_buf_tc", "k_bwd_finalize_tc", "k_bwd_dsref_tc", "k_bwd_keys_tc", "k_sref_tile", "k_decode_step", "k_scan_op_fwd", "k_scan_op_bwd", "k_compose_carries", "k_dwconv3_fwd", "k_dwconv3_bwd"};
+  "k_bwd_chunk_tc", "k_bwd_state_gates_tc", "k_bwd_buf_tc", "k_bwd_finalize_tc", "k_bwd_dsref_tc", "k_bwd_keys_tc", "k_sref_tile", "k_decode_step", "k_scan_op_fwd", "k_scan_op_bwd", "k_compose_carries", "k_dwconv3_fwd", "k_dwconv3_bwd", "k_head_prep_fwd", "k_head_prep_bwd"};
 
 constexpr int kMaxTimed = 8192;
 struct Prof {
@@ -559,6 +560,40 @@ int dwconv_types(bool fwd, int K, int dtype_x, int dtype_y, const void* x, const
 }
 bool dtype_ok(int d) { return d == ATLAS_F32 || d == ATLAS_BF16; }
 
+// ---- head preparation (headprep.cuh) ----
+template <int PER, class I, class O>
+int head_prep_t(bool fwd, const void* t, const float* gamma, void* o, const void* g, void* dt, float* dgamma,
+                int64_t B, int64_t T, int H, int Dp, cudaStream_t st) {
+  const int64_t BT = B * T;
+  const dim3 grid((unsigned)H, (unsigned)((BT + kHpRows - 1) / kHpRows));
+  if (fwd)
+    LAUNCH_T(KID_HEADPREP_FWD, (k_head_prep_fwd<PER, I, O>), grid, kHpWarps * 32, 0, st, (const I*)t, gamma, (O*)o,
+             BT, T, H, Dp);
+  else
+    LAUNCH_T(KID_HEADPREP_BWD, (k_head_prep_bwd<PER, I, O>), grid, kHpWarps * 32, 0, st, (const I*)t, gamma,
+             (const O*)g, (I*)dt, dgamma, BT, T, H, Dp);
+  return ATLAS_OK;
+}
+template <class I, class O>
+int head_prep_d(bool fwd, int d, const void* t, const float* gamma, void* o, const void* g, void* dt, float* dgamma,
+                int64_t B, int64_t T, int H, int Dp, cudaStream_t st) {
+  switch (d) {
+    case 32: return head_prep_t<1, I, O>(fwd, t, gamma, o, g, dt, dgamma, B, T, H, Dp, st);
+    case 64: return head_prep_t<2, I, O>(fwd, t, gamma, o, g, dt, dgamma, B, T, H, Dp, st);
+    case 96: return head_prep_t<3, I, O>(fwd, t, gamma, o, g, dt, dgamma, B, T, H, Dp, st);
+    case 128: return head_prep_t<4, I, O>(fwd, t, gamma, o, g, dt, dgamma, B, T, H, Dp, st);
+    default: return ATLAS_ERR_INVALID_ARG;
+  }
+}
+int head_prep(bool fwd, int dtype_in, int dtype_out, int d, const void* t, const float* gamma, void* o,
+              const void* g, void* dt, float* dgamma, int64_t B, int64_t T, int H, int Dp, cudaStream_t st) {
+  const bool ib = dtype_in == ATLAS_BF16, ob = dtype_out == ATLAS_BF16;
+  if (ib && ob) return head_prep_d<__nv_bfloat16, __nv_bfloat16>(fwd, d, t, gamma, o, g, dt, dgamma, B, T, H, Dp, st);
+  if (ib) return head_prep_d<__nv_bfloat16, float>(fwd, d, t, gamma, o, g, dt, dgamma, B, T, H, Dp, st);
+  if (ob) return head_prep_d<float, __nv_bfloat16>(fwd, d, t, gamma, o, g, dt, dgamma, B, T, H, Dp, st);
+  return head_prep_d<float, float>(fwd, d, t, gamma, o, g, dt, dgamma, B, T, H, Dp, st);
+}
+
 extern "C" {
 
 int atlas_mem_abi_version(void) { return ATLAS_MEM_ABI_VERSION; }
@@ -746,6 +781,28 @@ int atlas_dwconv3_backward(const void* x, int dtype_x, const float* w_q, const f
   if (cudaMemsetAsync(dw, 0, (size_t)3 * C * K * sizeof(float), st) != cudaSuccess) return ATLAS_ERR_LAUNCH;
   return dwconv_types(false, K, dtype_x, dtype_y, x, w_q, w_k, w_v, dx, nullptr, nullptr, dy_q, dy_k, dy_v, dw,
                       B, T, C, st);
+}
+
+int atlas_head_prep_forward(const void* t, int dtype_in, const float* gamma, void* out, int dtype_out, int64_t B,
+                            int64_t T, int H, int d, int d_out, void* stream) {
+  if (!t || !out || B < 1 || T < 1 || H < 1 || H > 65535 || d_out < d || !dtype_ok(dtype_in) ||
+      !dtype_ok(dtype_out) || (B * T + kHpRows - 1) / kHpRows > 65535)
+    return ATLAS_ERR_INVALID_ARG;
+  return head_prep(true, dtype_in, dtype_out, d, t, gamma, out, nullptr, nullptr, nullptr, B, T, H, d_out,
+                   (cudaStream_t)stream);
+}
+
+int atlas_head_prep_backward(const void* t, int dtype_in, const float* gamma, const void* grad_out, int dtype_out,
+                             void* grad_t, float* grad_gamma, int64_t B, int64_t T, int H, int d, int d_out,
+                             void* stream) {
+  if (!t || !grad_out || !grad_t || B < 1 || T < 1 || H < 1 || H > 65535 || d_out < d || !dtype_ok(dtype_in) ||
+      !dtype_ok(dtype_out) || (B * T + kHpRows - 1) / kHpRows > 65535 || (grad_gamma && !gamma))
+    return ATLAS_ERR_INVALID_ARG;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (grad_gamma && cudaMemsetAsync(grad_gamma, 0, (size_t)H * d * sizeof(float), st) != cudaSuccess)
+    return ATLAS_ERR_LAUNCH;
+  return head_prep(false, dtype_in, dtype_out, d, t, gamma, nullptr, grad_out, grad_t, grad_gamma, B, T, H, d_out,
+                   st);
 }
 
 int atlas_mem_forward_local(const AtlasMemShape* shape, const AtlasMemFwd* fwd, void* saved, size_t saved_bytes,

@@ -161,9 +161,10 @@ def _pad_to_tc(spec: Spec, io, d_k: int, d_phi: int, d_v: int) -> bool:
     return os.environ.get("ATLAS_MEM_PAD128", "1") != "0" and os.environ.get("ATLAS_MEM_TC", "1") != "0"
 
 
-def _padded_call(spec: Spec, d_v: int, d_phi: int, k, q, v, lr, decay, beta, gate, S_ref, S0, Z0, buf, proj):
+def _padded_call(spec: Spec, d_v: int, d_phi: int, k, q, v, lr, decay, beta, gate, S_ref, S0, Z0, buf, proj,
+                 vectors_padded: bool = False):
     pk, pv = TC_D - d_phi, TC_D - d_v
-    vec = lambda t, p: F.pad(t, (0, p))                       # [.., d] -> [.., 128]
+    vec = (lambda t, p: t) if vectors_padded else (lambda t, p: F.pad(t, (0, p)))  # [.., d] -> [.., 128]
     mat = lambda t: None if t is None else F.pad(t, (0, pk, 0, pv))  # [.., d_v, d_phi] -> [.., 128, 128]
     y, S_end, Z_end, buf_out = MemoryRecurrenceFn.apply(spec, vec(k, pk), vec(q, pk), vec(v, pv), lr, decay,
                                                         beta, gate, mat(S_ref), mat(S0), mat(Z0), mat(buf), proj)
@@ -194,7 +195,7 @@ def memory_recurrence(k: Tensor, q: Tensor, v: Tensor, lr: Tensor, decay: Tensor
                       S0: Tensor, Z0: Tensor | None = None, omega_buffer: Tensor | None = None,
                       window: int = 1, gate_mode: str | None = None, fmap_mode: str = "off",
                       fmap_degree: int = 1, proj: Tensor | None = None, chunk: int = 0,
-                      ref_mode: str = "call", ref_chunk: int | None = None):
+                      ref_mode: str = "call", ref_chunk: int | None = None, heads_padded_from: tuple | None = None):
     """Memory recurrence over N = batch*heads units.
 
     k, q [N,T,d_k]; v [N,T,d_v]; lr (eta), decay (alpha), beta [N,T]; gate [N,T]
@@ -211,6 +212,8 @@ def memory_recurrence(k: Tensor, q: Tensor, v: Tensor, lr: Tensor, decay: Tensor
     consecutive calls of ref_chunk tokens, each with S_ref = S0 = the state (clamped to
     +-100) the call before returned, carrying Z and the omega buffer; S_ref is then unused.
     That is the reference cell called once per chunk in a loop (tests/test_rnn_all.py:804-825).
+    heads_padded_from=(d_v, d_phi): k, q, v arrive zero-padded to 128 columns (``head_prep``)
+    for states of d_v x d_phi; the states are padded here and the outputs cut back.
     """
     if ref_mode == "chunk":
         return _chunk_ref_mode(k, q, v, lr, decay, beta, gate, S0=S0, Z0=Z0, omega_buffer=omega_buffer,
@@ -242,8 +245,12 @@ def memory_recurrence(k: Tensor, q: Tensor, v: Tensor, lr: Tensor, decay: Tensor
             f32(S_ref), f32(S0), Z0c, buf, projc)
     needs_grad = torch.is_grad_enabled() and any(
         t is not None and t.requires_grad for t in (k, q, v, lr, decay, beta, gate, S_ref, S0, Z0, omega_buffer))
-    if k.shape[1] == 1 and not needs_grad and decode_supported(spec, k.shape[-1], S_ref.shape[-1], v.shape[-1]):
+    if (heads_padded_from is None and k.shape[1] == 1 and not needs_grad
+            and decode_supported(spec, k.shape[-1], S_ref.shape[-1], v.shape[-1])):
         y, S_end, Z_end, buf_out = decode_step(spec, *args)
+    elif heads_padded_from is not None:  # k, q, v already zero-padded to 128 columns (head_prep)
+        y, S_end, Z_end, buf_out = _padded_call(spec, heads_padded_from[0], heads_padded_from[1], *args,
+                                                vectors_padded=True)
     elif _pad_to_tc(spec, io, k.shape[-1], S_ref.shape[-1], v.shape[-1]):
         y, S_end, Z_end, buf_out = _padded_call(spec, v.shape[-1], S_ref.shape[-1], *args)
     else:

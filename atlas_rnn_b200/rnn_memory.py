@@ -14,6 +14,7 @@ single backend and no CPU path.
 from __future__ import annotations
 
 import math
+import os
 from functools import partial
 from typing import NamedTuple
 
@@ -23,7 +24,8 @@ from torch import Tensor, nn
 from torch.nn import Conv1d, Linear, Module, Parameter
 
 from .conv import qkv_depthwise_conv
-from .ops import memory_recurrence
+from .headprep import HEAD_DIMS, head_prep
+from .ops import TC_D, memory_recurrence
 
 
 def exists(v):
@@ -133,6 +135,20 @@ class _MemoryCellBase(Module):
         self.phi = PolynomialFeatureMap(dim_head, poly_degree, poly_mode)
         self.register_buffer("_dummy", torch.zeros(1))
 
+    def _head_prep_ok(self, proj_q: Tensor, seq_len: int) -> bool:
+        """bf16 operands (bf16 inputs or bf16 autocast) on the tensor-core kernels: q, k, v go
+        through head_prep (ATLAS_MEM_HEADPREP=0 turns it off)."""
+        if not proj_q.is_cuda or seq_len < 2 or os.environ.get("ATLAS_MEM_HEADPREP", "1") == "0":
+            return False
+        bf16 = proj_q.dtype == torch.bfloat16 or (torch.is_autocast_enabled("cuda")
+                                                   and torch.get_autocast_dtype("cuda") == torch.bfloat16)
+        mode = self.phi.mode if self.phi.degree > 1 else "off"
+        if not bf16 or mode == "tensor" or self.omega_window > 16 or self.dim_head not in HEAD_DIMS:
+            return False
+        if os.environ.get("ATLAS_MEM_TC", "1") == "0":
+            return False
+        return self.dim_head == TC_D or os.environ.get("ATLAS_MEM_PAD128", "1") != "0"
+
     # [b, n, (h d)] -> [b, h, n, d]
     def split_heads(self, t: Tensor) -> Tensor:
         b, n, hd = t.shape
@@ -155,7 +171,8 @@ class _MemoryCellBase(Module):
 
     def forward(self, x: Tensor, state: RNNMemState | None = None):
         batch, seq_len, _ = x.shape
-        if not exists(state):
+        fresh = not exists(state)  # init_state's omega buffer is all zero: the kernels skip it
+        if fresh:
             state = self.init_state(batch, x.device, x.dtype)
         x_act = self.activation(self.pre_norm(x))
         q_in = k_in = v_in = x_act
@@ -174,31 +191,45 @@ class _MemoryCellBase(Module):
             for lo in range(0, seq_len, tile):
                 hi = min(seq_len, lo + tile)
                 out, cur = self._forward_impl(x_act[:, lo:hi], q_in[:, lo:hi], k_in[:, lo:hi],
-                                              v_in[:, lo:hi], cur, S_ref=S_ref)
+                                              v_in[:, lo:hi], cur, S_ref=S_ref, zero_buffer=fresh and lo == 0)
                 outs.append(out)
             return torch.cat(outs, dim=1), cur
-        return self._forward_impl(x_act, q_in, k_in, v_in, state, S_ref=state.S)
+        return self._forward_impl(x_act, q_in, k_in, v_in, state, S_ref=state.S, zero_buffer=fresh)
 
-    def _forward_impl(self, x_act, q_in, k_in, v_in, state: RNNMemState, *, S_ref: Tensor):
+    def _forward_impl(self, x_act, q_in, k_in, v_in, state: RNNMemState, *, S_ref: Tensor,
+                      zero_buffer: bool = False):
         batch, seq_len, _ = x_act.shape
-        q = self.split_heads(self.to_q(q_in))[:, :, :seq_len]
-        k = self.split_heads(self.to_k(k_in))[:, :, :seq_len]
-        v = self.split_heads(self.to_v(v_in))[:, :, :seq_len]
-        q, k = self.q_norm(q), self.k_norm(k)
+        pq, pk, pv = self.to_q(q_in), self.to_k(k_in), self.to_v(v_in)
         bh = batch * self.heads
         flat = lambda t: t.reshape(bh, seq_len, t.shape[-1])
+        padded_from = None
+        if self._head_prep_ok(pq, seq_len):
+            # split, per-head norm, cast and zero-pad to 128 columns in one pass per tensor
+            cut = lambda t: t if t.shape[1] == seq_len else t[:, :seq_len].contiguous()
+            gain = lambda norm: norm.gamma if isinstance(norm, MultiheadRMSNorm) else None
+            d = self.dim_head
+            k = head_prep(cut(pk), gain(self.k_norm), self.heads, TC_D, torch.bfloat16)
+            q = head_prep(cut(pq), gain(self.q_norm), self.heads, TC_D, torch.bfloat16)
+            v = head_prep(cut(pv), None, self.heads, TC_D, torch.bfloat16)
+            padded_from, flat = (d, d), (lambda t: t)
+        else:
+            q = self.split_heads(pq)[:, :, :seq_len]
+            k = self.split_heads(pk)[:, :, :seq_len]
+            v = self.split_heads(pv)[:, :, :seq_len]
+            q, k = self.q_norm(q), self.k_norm(k)
         heads_first = lambda g: g.transpose(1, 2).reshape(bh, seq_len)   # 'b n h -> (b h) n'
         lr = heads_first(self.to_lr(x_act))
         decay = heads_first(self.to_decay(x_act))
         beta = heads_first(self.to_momentum(x_act)) if self.use_momentum else None
         gate = heads_first(self.to_omega_gate(x_act)) if self.use_omega_gate else None
         e = self.omega_window
-        buf = state.omega_buffer if e > 1 else None
+        # no buffer = zero history (the same result; the buffer kernels do not run)
+        buf = state.omega_buffer if e > 1 and not zero_buffer else None
         y, S_end, Z_end, new_buf = memory_recurrence(
             flat(k), flat(q), flat(v), lr, decay, beta, gate, S_ref=S_ref, S0=state.S,
             Z0=state.Z if self.use_momentum else None, omega_buffer=buf, window=e,
             gate_mode="token", fmap_mode=self.phi.mode, fmap_degree=self.phi.degree,
-            proj=getattr(self.phi, "proj", None))
+            proj=getattr(self.phi, "proj", None), heads_padded_from=padded_from)
         y = y.to(x_act.dtype).view(batch, self.heads, seq_len, -1)
         out = self.to_out(self.merge_heads(y))
         nxt = RNNMemState(seq_index=state.seq_index + seq_len, S=S_end, Z=Z_end,

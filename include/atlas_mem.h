@@ -252,6 +252,20 @@ int atlas_dwconv3_backward(const void* x, int dtype_x, const float* w_q, const f
                            const void* dy_q, const void* dy_k, const void* dy_v, int dtype_y, void* dx,
                            float* dw, int64_t B, int64_t T, int64_t C, void* stream);
 
+/* Head preparation of the memory cells: the projection output t [B, T, H*d]
+ * is split into heads, RMS-normalised per head with gain gamma [H, d] when
+ * gamma is given (MultiheadRMSNorm, rnn_memory.py:139-147: x / max(||x|| d^-1/2,
+ * 1e-8) * gamma[h]) and written as out [B*H, T, d_out] with zero columns
+ * d..d_out-1. d in {32, 64, 96, 128}; dtypes ATLAS_F32 / ATLAS_BF16. */
+int atlas_head_prep_forward(const void* t, int dtype_in, const float* gamma, void* out, int dtype_out, int64_t B,
+                            int64_t T, int H, int d, int d_out, void* stream);
+/* Its backward: grad_t [B, T, H*d] (dtype_in) from grad_out [B*H, T, d_out]
+ * (its first d columns), and grad_gamma [H, d] fp32 (zeroed here; may be NULL;
+ * needs gamma). */
+int atlas_head_prep_backward(const void* t, int dtype_in, const float* gamma, const void* grad_out, int dtype_out,
+                             void* grad_t, float* grad_gamma, int64_t B, int64_t T, int H, int d, int d_out,
+                             void* stream);
+
 /* Device self-check of the tensor-core (tcgen05) GEMM building block used by
  * the fused kernels: D[128,N] = A[128,K] * B^T with A given as [128][K]
  * (a_mn_major = 0) or [K][128] (1), B as [N][K] (b_mn_major = 0) or [K][N] (1);
