@@ -328,20 +328,49 @@ def run_ours(args, w):
     h2d = sum(t.numel() * t.element_size() for t in host.values())
     d2h = y_host.numel() * y_host.element_size()
 
-    def e2e_step():
-        d = {n: (host[n].to(dev, non_blocking=True) if n in host else None) for n in names + ("dy",)}
-        for n in names:
-            if d[n] is not None:
-                d[n].requires_grad_(True)
-        y = step(inp, w, d)
-        y_host.copy_(y.detach(), non_blocking=True)
+    # pipelined as a deployment runs it: step i + 1's inputs copy in on a copy stream while step i
+    # computes (two device buffers), and y goes back on a third stream; every step's copies are
+    # inside the timed region
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    dbuf = [{n: torch.empty_like(host[n], device=dev) for n in host} for _ in range(2)]
+    yh = [y_host, torch.empty_like(y_host).pin_memory()]
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_used = [torch.cuda.Event() for _ in range(2)]
+    ev_y = [torch.cuda.Event() for _ in range(2)]
+    for e in ev_used:
+        e.record(st)
 
-    for _ in range(max(1, args.warmup // 2)):
-        e2e_step()
+    def issue_copy(i):
+        j = i % 2
+        with torch.cuda.stream(s_in):
+            s_in.wait_event(ev_used[j])  # the compute that read this buffer two steps ago is done
+            for n in host:
+                dbuf[j][n].copy_(host[n], non_blocking=True)
+            ev_in[j].record(s_in)
+
+    def e2e_run(n_steps):
+        issue_copy(0)
+        for i in range(n_steps):
+            j = i % 2
+            st.wait_event(ev_in[j])
+            if i + 1 < n_steps:
+                issue_copy(i + 1)
+            d = {n: (dbuf[j][n].detach().requires_grad_(n in names) if n in host else None)
+                 for n in names + ("dy",)}
+            y = step(inp, w, d)
+            ev_used[j].record(st)
+            ev_y[j].record(st)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(ev_y[j])
+                yh[j].copy_(y.detach(), non_blocking=True)
+                y.record_stream(s_out)
+        st.wait_stream(s_out)
+
+    e2e_run(max(2, args.warmup // 2))
     barrier()
     ev0.record(st)
-    for _ in range(args.steps):
-        e2e_step()
+    s_in.wait_event(ev0)  # the first copy is inside the timed region
+    e2e_run(args.steps)
     ev1.record(st)
     barrier()
     e2e_ms = max_over_ranks(ev0.elapsed_time(ev1))
@@ -521,8 +550,10 @@ def run_lm(args):
     # end to end: tokens from pinned host memory, loss back to the host, every step
     barrier()
     ev0.record(st)
+    tok_dev = torch.empty_like(tokens)  # one preallocated device buffer: no allocation inside the region
     for _ in range(args.steps):
-        loss = step(host_tokens.to(dev, non_blocking=True))
+        tok_dev.copy_(host_tokens, non_blocking=True)
+        loss = step(tok_dev)
         loss_host.copy_(loss.detach().float(), non_blocking=True)
     ev1.record(st)
     barrier()
@@ -532,6 +563,13 @@ def run_lm(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms, e2e_ms = t.tolist()
     tok = ws * B * T * args.steps
+    if args.torch_profile and rank == 0:  # per-kernel table of one more step (after the timed ones)
+        from torch.profiler import ProfilerActivity, profile
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            step(tokens)
+            torch.cuda.synchronize(dev)
+        print(prof.key_averages().table(sort_by="cuda_time_total", row_limit=30, max_name_column_width=70),
+              file=sys.stderr, flush=True)
     if rank == 0:
         line = {
             "metric": "LM training tokens/sec", "value": tok / (ms / 1000.0), "unit": UNIT, "n_gpus": ws,
@@ -563,6 +601,8 @@ def main():
     ap.add_argument("--T", type=int, default=None, help="override tokens (for profiling small cases)")
     ap.add_argument("--B", type=int, default=None)
     ap.add_argument("--with-buffer", action="store_true", help="pass the zero omega buffer explicitly")
+    ap.add_argument("--torch-profile", action="store_true",
+                    help="config 3: print torch.profiler's per-kernel table of one extra step to stderr")
     args = ap.parse_args()
     global WITH_BUFFER
     WITH_BUFFER = args.with_buffer
