@@ -11,8 +11,12 @@
   The transforms compose associatively -- the split-scan identity of the
   reference (tests/test_titans.py:680-707) -- so ranks all-gather them over NCCL
   and each composes the ones before it (forward) or after it (backward) into
-  its carry. S_ref is the call-start state of the whole sequence on every rank
-  (rnn_memory.py:284,298); its gradient is summed over ranks. Window e = 1 only
+  its carry. The transforms travel as one packed record per rank in a single
+  all-gather, and the composition runs on the device (``compose_carries_device``
+  over ``atlas_mem_compose_carries``); ``compose_forward_carries`` /
+  ``compose_backward_carries`` state the same composition in torch ops and are
+  what the kernel is tested against. S_ref is the call-start state of the whole
+  sequence on every rank (rnn_memory.py:284,298); its gradient is summed over ranks. Window e = 1 only
   (a wider window would need an (e-1)-token halo from the previous rank).
 """
 from __future__ import annotations
@@ -34,7 +38,7 @@ def shard_units(N: int, rank: int, world: int) -> slice:
 
 
 # ---------------------------------------------------------------------------
-# transform composition (pure torch; the host side of the carry exchange)
+# transform composition in torch ops (the specification of atlas_mem_compose_carries)
 # ---------------------------------------------------------------------------
 def _c(coef, i):
     return coef[:, i, None, None]
