@@ -218,10 +218,16 @@ class _MemoryCellBase(Module):
             v = self.split_heads(pv)[:, :, :seq_len]
             q, k = self.q_norm(q), self.k_norm(k)
         heads_first = lambda g: g.transpose(1, 2).reshape(bh, seq_len)   # 'b n h -> (b h) n'
-        lr = heads_first(self.to_lr(x_act))
-        decay = heads_first(self.to_decay(x_act))
-        beta = heads_first(self.to_momentum(x_act)) if self.use_momentum else None
-        gate = heads_first(self.to_omega_gate(x_act)) if self.use_omega_gate else None
+        # the gate heads (Linear(dim, heads) + sigmoid each) as one projection: x_act is read,
+        # cast and back-propagated once instead of once per head
+        heads = [self.to_lr, self.to_decay] + ([self.to_momentum] if self.use_momentum else []) + \
+            ([self.to_omega_gate] if self.use_omega_gate else [])
+        w = torch.cat([h[0].weight for h in heads])
+        b = torch.cat([h[0].bias for h in heads])
+        gates = F.linear(x_act, w, b).sigmoid().split(self.heads, dim=-1)
+        lr, decay = heads_first(gates[0]), heads_first(gates[1])
+        beta = heads_first(gates[2]) if self.use_momentum else None
+        gate = heads_first(gates[-1]) if self.use_omega_gate else None
         e = self.omega_window
         # no buffer = zero history (the same result; the buffer kernels do not run)
         buf = state.omega_buffer if e > 1 and not zero_buffer else None
@@ -230,7 +236,10 @@ class _MemoryCellBase(Module):
             Z0=state.Z if self.use_momentum else None, omega_buffer=buf, window=e,
             gate_mode="token", fmap_mode=self.phi.mode, fmap_degree=self.phi.degree,
             proj=getattr(self.phi, "proj", None), heads_padded_from=padded_from)
-        y = y.to(x_act.dtype).view(batch, self.heads, seq_len, -1)
+        if not (y.dtype == torch.bfloat16 and torch.is_autocast_enabled("cuda")
+                and torch.get_autocast_dtype("cuda") == torch.bfloat16):
+            y = y.to(x_act.dtype)  # (under bf16 autocast to_out takes bf16: the round trip is skipped)
+        y = y.view(batch, self.heads, seq_len, -1)
         out = self.to_out(self.merge_heads(y))
         nxt = RNNMemState(seq_index=state.seq_index + seq_len, S=S_end, Z=Z_end,
                           omega_buffer=new_buf if e > 1 else None)
