@@ -46,6 +46,10 @@ CONFIGS = {
                 torch.bfloat16, 128),
     4: Workload("omega_rnn_tensor_c4", 4, 8, 16384, 64, 256, 128, 16, "token", "tensor", 2, True,
                 torch.bfloat16, 64),
+    # not a benchmark config: the one shape the reference's own CUDA kernels run (window 16, head 64,
+    # bf16, per-token omega gate), for timing those kernels beside ours (bench.py --impl reference-cuda)
+    5: Workload("omega16_d64_refkernel", 8, 16, 4096, 64, 64, 64, 16, "token", "off", 1, True,
+                torch.bfloat16, 0),
 }
 
 

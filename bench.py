@@ -477,6 +477,53 @@ def kernel_cfg_chunk(w):
     return 32 if w.window - 1 <= 32 else w.window - 1
 
 
+def run_reference_cuda(args, w):
+    """The reference's own Omega-16 CUDA kernels (atlas_pytorch/cuda, built from its sources into
+    oracle/_ref by oracle/ref_cuda.py) on the workload they support, fwd+bwd as the reference's
+    autograd wrapper runs them; rank 0 only. Also reports how far their y is from ours."""
+    ws, rank, local = dist_env()
+    if rank != 0:
+        return
+    if not (w.window == 16 and w.d_k == w.d_phi == w.d_v == 64 and w.gate == "token" and w.fmap_mode == "off"
+            and w.dtype == torch.bfloat16 and w.momentum):
+        print(json.dumps({"impl": "reference-cuda", "unavailable": "the reference's CUDA kernels run only "
+                          "window 16, head 64, bf16, per-token gate, momentum (use --config 5)"}))
+        return
+    from oracle import ref_cuda
+    try:
+        ext = ref_cuda.load()
+    except Exception as ex:  # not built here
+        print(json.dumps({"impl": "reference-cuda", "unavailable": str(ex)}))
+        return
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    inp = make_inputs(w, seed=0, device=dev, state_scale=0.1)
+    b16 = lambda t: t.to(torch.bfloat16).contiguous()
+    args_ref = [b16(inp[n]) for n in ("k", "q", "v")] + [b16(inp["S0"])] + \
+        [b16(inp[n]) for n in ("lr", "decay", "beta", "gate")] + [b16(inp["S0"]), b16(inp["Z0"]), b16(inp["dy"])]
+    for _ in range(args.warmup):
+        ref_cuda.forward_backward(ext, *args_ref)
+    torch.cuda.synchronize(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(args.steps):
+        (y_ref, _, _), _ = ref_cuda.forward_backward(ext, *args_ref)
+    ev1.record()
+    torch.cuda.synchronize(dev)
+    ms = ev0.elapsed_time(ev1) / args.steps
+    from atlas_rnn_b200 import memory_recurrence
+    with torch.no_grad():
+        y_ours = memory_recurrence(inp["k"], inp["q"], inp["v"], inp["lr"], inp["decay"], inp["beta"], inp["gate"],
+                                   S_ref=inp["S0"], S0=inp["S0"], Z0=inp["Z0"], window=16, gate_mode="token")[0]
+    diff = ((y_ref.float() - y_ours.float()).norm() / y_ours.float().norm()).item()
+    print(json.dumps({"impl": "reference-cuda", "metric": METRIC, "value": w.B * w.T / (ms / 1000.0), "unit": UNIT,
+                      "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+                      "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
+                      "config": {"workload": w.name, "B": w.B, "H": w.H, "T": w.T, "d": 64, "window": 16},
+                      "kernels": "reference atlas_omega.cu forward_exact_kernel + backward_exact_kernel (sm_100a)",
+                      "y_rel_l2_vs_ours": diff}), flush=True)
+
+
 LM_C3 = dict(num_tokens=256, dim=768, depth=12, block_type="lmm", heads=12, dim_head=64, ff_mult=4,
              omega_window=8, use_omega_gate=True, use_momentum=True, poly_mode="elementwise", poly_degree=2,
              qkv_conv_kernel=4)
@@ -595,7 +642,7 @@ def main():
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--config", type=int, default=1)
-    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference", "reference-cuda"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--T", type=int, default=None, help="override tokens (for profiling small cases)")
@@ -616,7 +663,9 @@ def main():
     w = CONFIGS[args.config]
     if args.T or args.B:
         w = shrink(w, B=args.B, T=args.T)
-    if args.impl == "reference":
+    if args.impl == "reference-cuda":
+        run_reference_cuda(args, w)
+    elif args.impl == "reference":
         run_reference(args, w)
     else:
         run_ours(args, w)
