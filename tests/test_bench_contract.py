@@ -1,0 +1,31 @@
+"""CPU: bench.py's reference arm prints the one JSON line of the benchmark contract
+(runs the oracle port on the host cores; a few seconds)."""
+import json
+import os
+import subprocess
+import sys
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def run(*args):
+    out = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), *args], capture_output=True, text=True,
+                         timeout=300, cwd=ROOT)
+    assert out.returncode == 0, out.stderr[-2000:]
+    lines = [l for l in out.stdout.splitlines() if l.startswith("{")]
+    assert len(lines) == 1, out.stdout
+    return json.loads(lines[0])
+
+
+def test_reference_arm_line():
+    d = run("--impl", "reference", "--steps", "1", "--warmup", "3")
+    assert d["impl"] == "reference" and d["metric"] == "memory-layer fwd+bwd tokens/sec" and d["unit"] == "tokens/s"
+    assert d["value"] > 0 and d["higher_is_better"] is True and d["steps"] == 1 and d["warmup"] == 3
+    assert d["cpu_baseline"]["kind"] == "port" and d["cpu_baseline"]["value"] == d["value"]
+    assert d["e2e"] == {"value": d["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+    assert d["config"]["workload"] == "omega_rnn_c1"
+
+
+def test_reference_cuda_arm_refuses_other_shapes():
+    d = run("--impl", "reference-cuda", "--config", "1", "--steps", "1", "--warmup", "3")
+    assert d["impl"] == "reference-cuda" and "unavailable" in d
