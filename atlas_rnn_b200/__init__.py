@@ -8,11 +8,12 @@ functional ``memory_recurrence``, the GPU drop-in for the third-party
 ``assoc_scan.AssocScan`` (``AssocScan``, ``assoc_scan``) and the multi-GPU helpers in ``parallel``.
 """
 from .ops import memory_recurrence, MemoryRecurrenceFn
+from ._lib import check_device_status
 from .scan import AssocScan, assoc_scan
 from .rnn_memory import (RNNMemState, state_detach, PolynomialFeatureMap, MultiheadRMSNorm,
                          RNNMemoryCell, OmegaRNNMemoryCell, RNNMemory, OmegaRNNMemory)
 from .rnn_transformer import LMMBlock, LongTermMemoryModel, RNNMemoryTransformer
 
-__all__ = ["memory_recurrence", "MemoryRecurrenceFn", "AssocScan", "assoc_scan", "RNNMemState", "state_detach",
+__all__ = ["memory_recurrence", "MemoryRecurrenceFn", "check_device_status", "AssocScan", "assoc_scan", "RNNMemState", "state_detach",
            "PolynomialFeatureMap", "MultiheadRMSNorm", "RNNMemoryCell", "OmegaRNNMemoryCell",
            "RNNMemory", "OmegaRNNMemory", "LMMBlock", "LongTermMemoryModel", "RNNMemoryTransformer"]

@@ -30,12 +30,13 @@ _vp = ctypes.c_void_p
 
 class Fwd(ctypes.Structure):
     _fields_ = [(n, _vp) for n in ("k", "q", "v", "lr", "decay", "beta", "gate", "S_ref", "S0", "Z0",
-                                   "buf_in", "proj", "y", "S_end", "Z_end", "buf_out")]
+                                   "buf_in", "proj", "y", "S_end", "Z_end", "buf_out", "status")]
 
 
 class Bwd(ctypes.Structure):
     _fields_ = [(n, _vp) for n in ("dy", "dS_end", "dZ_end", "dbuf_out", "dk", "dq", "dv", "dlr",
-                                   "ddecay", "dbeta", "dgate", "dS_ref", "dS0", "dZ0", "dbuf_in")]
+                                   "ddecay", "dbeta", "dgate", "dS_ref", "dS0", "dZ0", "dbuf_in",
+                                   "status")]
 
 
 _lib = None
@@ -98,6 +99,10 @@ def lib():
         L.atlas_mem_selftest_umma.argtypes = [_vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                               ctypes.c_int, _vp, _vp]
         L.atlas_mem_selftest_umma.restype = ctypes.c_int
+        L.atlas_mem_read_status.argtypes = [_vp, _vp]
+        L.atlas_mem_read_status.restype = ctypes.c_int
+        L.atlas_mem_selftest_wait_timeout.argtypes = [_vp, ctypes.c_int, _vp]
+        L.atlas_mem_selftest_wait_timeout.restype = ctypes.c_int
         L.atlas_mem_profile_enable.argtypes = [ctypes.c_int]
         L.atlas_mem_profile_read.argtypes = [ctypes.c_int, P(ctypes.c_double), P(ctypes.c_longlong)]
         L.atlas_mem_launch_count.restype = ctypes.c_longlong
@@ -128,6 +133,37 @@ def workspace_sizes(shape: Shape):
     check(lib().atlas_mem_workspace_size(ctypes.byref(shape), ctypes.byref(s), ctypes.byref(f),
                                          ctypes.byref(b)), "workspace_size")
     return s.value, f.value, b.value
+
+
+_status_words = {}
+
+
+def status_word(device):
+    """The per-device int32 status word this package hands to every call
+    (``status`` in the Fwd / Bwd structs). Kernels set it when a bounded wait
+    for tensor-core work runs out; ``check_device_status`` reads it."""
+    import torch
+    idx = torch.device(device).index
+    idx = torch.cuda.current_device() if idx is None else idx
+    w = _status_words.get(idx)
+    if w is None:
+        w = torch.zeros(1, dtype=torch.int32, device=f"cuda:{idx}")
+        _status_words[idx] = w
+    return w
+
+
+def check_device_status(device=None, reset: bool = True):
+    """Synchronise the current stream of ``device``, read its status word and
+    raise RuntimeError (ATLAS_ERR_DEVICE) if a kernel reported a timed-out
+    wait since the last check. The word is cleared afterwards unless
+    ``reset`` is False."""
+    import torch
+    w = status_word(device if device is not None else torch.device("cuda"))
+    stream = ctypes.c_void_p(torch.cuda.current_stream(w.device).cuda_stream)
+    code = lib().atlas_mem_read_status(ptr(w), stream)
+    if code != 0 and reset:
+        w.zero_()
+    check(code, "device status")
 
 
 def profile_enable(on: bool):

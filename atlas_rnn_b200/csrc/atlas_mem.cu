@@ -224,6 +224,7 @@ Params make_params(const AtlasMemShape* s, const Layout& L, const AtlasMemFwd* f
     P.gate = f->gate; P.Sref = f->S_ref; P.S0 = f->S0; P.Z0 = s->momentum ? f->Z0 : nullptr;
     P.buf = s->window > 1 ? f->buf_in : nullptr; P.proj = f->proj;
     P.y = f->y; P.S_end = f->S_end; P.Z_end = s->momentum ? f->Z_end : nullptr; P.buf_out = f->buf_out;
+    P.status = f->status;
   }
   if (b) {
     P.dy = b->dy; P.dS_end = b->dS_end; P.dZ_end = s->momentum ? b->dZ_end : nullptr;
@@ -232,6 +233,7 @@ Params make_params(const AtlasMemShape* s, const Layout& L, const AtlasMemFwd* f
     P.dbeta = s->momentum ? b->dbeta : nullptr; P.dgate = s->gate_mode != ATLAS_GATE_NONE ? b->dgate : nullptr;
     P.dSref = b->dS_ref; P.dS0 = b->dS0; P.dZ0 = s->momentum ? b->dZ0 : nullptr;
     P.dbuf = s->window > 1 ? b->dbuf_in : nullptr;
+    P.status = b->status;
   }
   char* sv = (char*)const_cast<void*>(saved);
   if (sv) {
@@ -481,22 +483,23 @@ int run_bwd_finish(const AtlasMemShape* s, const Params& P, cudaStream_t st) {
 // device array, so every GPU that loads this library holds it until exit.
 constexpr size_t kNoAllocScratchBytes = (size_t)32 << 20;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
-std::mutex g_noalloc_mu;
-void* g_noalloc_addr[64];
 
 // Device address of the array on the current device. Host code cannot use the
 // symbol itself (it names a host-side stand-in), so the address is looked up
-// once per device with that device current and cached.
-int noalloc_scratch(void** out) {
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return ATLAS_ERR_LAUNCH;
-  std::lock_guard<std::mutex> lk(g_noalloc_mu);
-  if (!g_noalloc_addr[dev]) {
-    void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) return ATLAS_ERR_LAUNCH;
-    g_noalloc_addr[dev] = p;
+// with that device current. It is looked up on every call rather than cached:
+// after a context reset the module is loaded again and the array can move.
+// The first lookup on a device loads the module there, which is not allowed
+// while a stream is being captured; that case gets its own error code.
+int noalloc_scratch(cudaStream_t st, void** out) {
+  void* p = nullptr;
+  if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) {
+    (void)cudaGetLastError();
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(st, &cs) == cudaSuccess && cs != cudaStreamCaptureStatusNone)
+      return ATLAS_ERR_NOALLOC_CAPTURE;
+    return ATLAS_ERR_LAUNCH;
   }
-  *out = g_noalloc_addr[dev];
+  *out = p;
   return ATLAS_OK;
 }
 
@@ -594,6 +597,17 @@ int head_prep(bool fwd, int dtype_in, int dtype_out, int d, const void* t, const
   return head_prep_d<float, float>(fwd, d, t, gamma, o, g, dt, dgamma, B, T, H, Dp, st);
 }
 
+// A barrier nothing arrives on, waited on through the tensor-core kernels'
+// bounded wait-and-report path (atlas_mem_selftest_wait_timeout).
+__global__ void __launch_bounds__(tc::kT) k_wait_timeout_selftest(int* status, int polls) {
+  __shared__ uint64_t mbar;
+  if (threadIdx.x == 0) umma::mbar_init(&mbar, 1);
+  umma::fence_before();
+  __syncthreads();
+  tc::Sync sy{&mbar, nullptr, 0, status};
+  (void)tc::sync_wait(sy, polls);
+}
+
 extern "C" {
 
 int atlas_mem_abi_version(void) { return ATLAS_MEM_ABI_VERSION; }
@@ -608,6 +622,9 @@ const char* atlas_mem_error_string(int code) {
     case ATLAS_ERR_DEVICE: return "device-side status reported a fault";
     case ATLAS_ERR_NOALLOC_TOO_LARGE:
       return "shape needs more scratch than the fixed no-alloc array holds (see atlas_mem_noalloc_scratch_bytes)";
+    case ATLAS_ERR_NOALLOC_CAPTURE:
+      return "no-alloc scratch lookup failed during stream capture: make the first no-alloc call on this "
+             "device before capturing";
     default: return "unknown error";
   }
 }
@@ -644,7 +661,7 @@ int atlas_mem_forward_noalloc(const AtlasMemShape* shape, const AtlasMemFwd* fwd
   const Layout L = make_layout(shape);
   if (L.saved > kNoAllocScratchBytes) return ATLAS_ERR_NOALLOC_TOO_LARGE;
   void* scratch = nullptr;
-  if ((v = noalloc_scratch(&scratch))) return v;
+  if ((v = noalloc_scratch((cudaStream_t)stream, &scratch))) return v;
   if ((v = ensure_attrs())) return v;
   // Every scratch word the forward reads is written earlier in the same call,
   // so nothing has to be cleared between calls.
@@ -880,6 +897,21 @@ int atlas_mem_selftest_umma(const void* A, const void* B, float* D, int N, int K
     return ATLAS_ERR_LAUNCH;
   k_umma_selftest<<<1, 128, smem, (cudaStream_t)stream>>>((const __nv_bfloat16*)A, (const __nv_bfloat16*)B, D, N, K,
                                                           a_mn_major, b_mn_major, status);
+  LAUNCH_CHECK();
+  return ATLAS_OK;
+}
+
+int atlas_mem_read_status(const int* status, void* stream) {
+  if (!status) return ATLAS_ERR_INVALID_ARG;
+  if (cudaStreamSynchronize((cudaStream_t)stream) != cudaSuccess) return ATLAS_ERR_LAUNCH;
+  int h = 0;
+  if (cudaMemcpy(&h, status, sizeof(int), cudaMemcpyDefault) != cudaSuccess) return ATLAS_ERR_LAUNCH;
+  return h ? ATLAS_ERR_DEVICE : ATLAS_OK;
+}
+
+int atlas_mem_selftest_wait_timeout(int* status, int polls, void* stream) {
+  if (!status || polls < 1 || polls > (1 << 20)) return ATLAS_ERR_INVALID_ARG;
+  k_wait_timeout_selftest<<<1, tc::kT, 0, (cudaStream_t)stream>>>(status, polls);
   LAUNCH_CHECK();
   return ATLAS_OK;
 }

@@ -54,6 +54,8 @@ struct Params {
   int apply_mask;
   // sequence-parallel segment outputs
   float *seg_coef, *seg_dS, *seg_dZ;
+  // caller's device status word (NULL = none): bounded waits that ran out
+  int* status;
 };
 
 __device__ __forceinline__ float ldio(const void* p, int64_t i, int bf) {

@@ -63,7 +63,7 @@ __global__ void __launch_bounds__(kT) k_bwd_chunk_tc(Params P) {
   float* hZS = sa.take(kR + 1);
   float* hZZ = sa.take(kR + 1);
   const int L = cx.L, tid = threadIdx.x, row = row_of(), wg = wg_of();
-  Sync sy{&mbar, &tbase, 0, nullptr};
+  Sync sy{&mbar, &tbase, 0, P.status};
   const uint32_t tm = tc_setup(sy, 256);
   pc.mark(48);
   // adjoint weights of token q at the chunk input: eS_0[q], eZ_0[q] equal the
@@ -104,7 +104,7 @@ __global__ void __launch_bounds__(kT) k_bwd_chunk_tc(Params P) {
     mma_chain(tm, op(tYS, kD, 1), op(tPsi, kD, 1), 8, kD, false);
     mma_chain(tm + 128, op(tYZ, kD, 1), op(tPsi, kD, 1), 8, kD, false);
   }
-  mma_wait(sy);
+  ATLAS_MMA_WAIT_OR_LEAVE(sy, tm, 256);
   pc.mark(51);
   {
     const int64_t D2 = (int64_t)kD * kD;
@@ -171,7 +171,7 @@ __global__ void __launch_bounds__(kT) k_bwd_keys_tc(Params P) {
   float* hZZ = sa.take(kR + 1);
   float* part = sa.take(2 * kWG * kR);
   const int n = cx.n, K = cx.K, L = cx.L, tid = threadIdx.x, e = P.e, row = row_of(), wg = wg_of();
-  Sync sy{&mbar, &tbase, 0, nullptr};
+  Sync sy{&mbar, &tbase, 0, P.status};
   const uint32_t tm = tc_setup(sy);
   const int64_t cid = chunk_id(P, cx);
   const unsigned char* FS = P.adjb + cid * 2 * kTileBytes;
@@ -202,7 +202,7 @@ __global__ void __launch_bounds__(kT) k_bwd_keys_tc(Params P) {
     mma_chain(tm + 256, op(tDl, kD, 0), op(tFS, kD, 1), 8, kD, false);  // Q1
     mma_chain(tm + 384, op(tDl, kD, 0), op(tFZ, kD, 1), 8, kD, false);  // Q2
   }
-  mma_wait(sy);
+  ATLAS_MMA_WAIT_OR_LEAVE(sy, tm, 512);
   pc.mark(4);
   async_rows_psi(P, cx, tFS);  // F tiles are free once the phase-1 MMAs are done
   async_rows_dy(P, cx, tFZ);
@@ -252,7 +252,7 @@ __global__ void __launch_bounds__(kT) k_bwd_keys_tc(Params P) {
     mma_chain(tm + 128, op(tFZ, kD, 0), op(tDl, kD, 0), 8, kR, false);   // A1[q][j] = dY delta^T
     mma_chain(tm + 384, op(tFS, kD, 0), op(tPhi, kD, 0), 8, kR, false);  // A2[q][j] = Psi Phi^T
   }
-  mma_wait(sy);
+  ATLAS_MMA_WAIT_OR_LEAVE(sy, tm, 512);
   pc.mark(7);
   {  // phase-2 epilogue, row q: G, M3 = cS o A1, M1 = cS o A2
     const int q = row;
@@ -288,7 +288,7 @@ __global__ void __launch_bounds__(kT) k_bwd_keys_tc(Params P) {
     mma_chain(tm + 256, op(tM3, kR, 1), op(tFS, kD, 1), 8, kD, true);    // d phi   += M2 Psi (M2 = M3)
     mma_chain(tm + 128, op(tM3, kR, 0), op(tPhi, kD, 1), 8, kD, false);  // I5 = M3 Phi
   }
-  mma_wait(sy);
+  ATLAS_MMA_WAIT_OR_LEAVE(sy, tm, 512);
   pc.mark(9);
   {
     const int r = row, p = cx.kp0 + r;
@@ -390,7 +390,7 @@ __global__ void __launch_bounds__(kT) k_bwd_state_gates_tc(Params P) {
   const int n = cx.n, K = cx.K, L = cx.L, tid = threadIdx.x, e = P.e, row = row_of(), wg = wg_of();
   if (tid < 2 * kR / 4) cp16(xf + 4 * tid, P.xf + cid * 2 * kR + 4 * tid, true);
   if (tid < kR) duj[tid] = 0.f;
-  Sync sy{&mbar, &tbase, 0, nullptr};
+  Sync sy{&mbar, &tbase, 0, P.status};
   const uint32_t tm = tc_setup(sy);  // (its barrier also publishes the gates)
   pc.mark(32);
   if (tid < 32) fwd_scalars_warp(cx, sS, sZ, zZ);
@@ -446,7 +446,7 @@ __global__ void __launch_bounds__(kT) k_bwd_state_gates_tc(Params P) {
       i5v[h][1] = src[1];
     }
   }
-  mma_wait(sy);
+  ATLAS_MMA_WAIT_OR_LEAVE(sy, tm, 512);
   __syncthreads();  // the state MMAs and the dots are done with Psi, S_in, Z_in, F_S, F_Z
   pc.mark(34);
   if (wg == 0) {  // forward coefficients of key j (columns of tCS, tCZp)
@@ -526,7 +526,7 @@ __global__ void __launch_bounds__(kT) k_bwd_state_gates_tc(Params P) {
     mma_chain(tm + 256, op(tCZp, kR, 0), op(tG, kR, 0), 8, kR, false);  // W_b[i][q]
     mma_chain(tm + 384, op(tEZ, kR, 0), op(tG, kR, 1), 8, kR, false);   // E_Z+ G [i][j]
   }
-  mma_wait(sy);
+  ATLAS_MMA_WAIT_OR_LEAVE(sy, tm, 512);
   pc.mark(36);
   const int i = row;
   float acc[kGateParts];
@@ -745,7 +745,7 @@ __global__ void __launch_bounds__(kT) k_bwd_finalize_tc(Params P) {
   const int n = blockIdx.y, p0 = blockIdx.x * kR, e = P.e, tid = threadIdx.x, row = row_of(), wg = wg_of();
   const int TT = min(kR, P.T - p0);
   async_copy_tile(tSR, P.srb + (int64_t)n * kTileBytes);
-  Sync sy{&mbar, &tbase, 0, nullptr};
+  Sync sy{&mbar, &tbase, 0, P.status};
   const uint32_t tm = tc_setup(sy, 128);
   const int e1 = e > 1 ? e - 1 : 1;
   // halo slot of token p in the next chunk (keys of chunk c+1 start at t0(c+1)-(e-1))
@@ -818,7 +818,7 @@ __global__ void __launch_bounds__(kT) k_bwd_finalize_tc(Params P) {
       stio(P.dgate, (int64_t)n * P.T + p, d, P.bf);
     }
   pc.mark(57);
-  mma_wait(sy);
+  ATLAS_MMA_WAIT_OR_LEAVE(sy, tm, 128);
   pc.mark(58);
   {
     const int r = row, p = p0 + r;
@@ -877,7 +877,7 @@ __global__ void __launch_bounds__(kT) k_bwd_dsref_tc(Params P, int tiles_per_cta
   const int n = blockIdx.y, tid = threadIdx.x, row = row_of(), wg = wg_of();
   const int ntiles = (P.T + kR - 1) / kR;
   const int tb = blockIdx.x * tiles_per_cta, te = min(ntiles, tb + tiles_per_cta);
-  Sync sy{&mbar, &tbase, 0, nullptr};
+  Sync sy{&mbar, &tbase, 0, P.status};
   const uint32_t tm = tc_setup(sy, 128);
   for (int t = tb; t < te; ++t) {
     const int p0 = t * kR, TT = min(kR, P.T - p0);
@@ -891,7 +891,7 @@ __global__ void __launch_bounds__(kT) k_bwd_dsref_tc(Params P, int tiles_per_cta
     });
     smem_to_tc();
     if (tid == 0) mma_chain(tm, op(tDD, kD, 1), op(tPh, kD, 1), 8, kD, t > tb);
-    mma_wait(sy);  // the tiles are refilled next iteration
+    ATLAS_MMA_WAIT_OR_LEAVE(sy, tm, 128);  // the tiles are refilled next iteration
   }
   if (te > tb) {
     float* dst = P.dSref + ((int64_t)n * kD + row) * kD;

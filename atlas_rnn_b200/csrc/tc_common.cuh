@@ -43,6 +43,9 @@ __device__ __forceinline__ void mma_chain(uint32_t d_tmem, Op A, Op B, int kstep
 }
 
 // Per-CTA tensor-core state: TMEM base, one mbarrier and its phase, a status word.
+// Code a kernel writes to the caller's status word when a bounded wait ran out.
+constexpr int kDevStatMmaTimeout = 1;
+
 struct Sync {
   uint64_t* mbar;
   uint32_t* tbase;
@@ -73,13 +76,30 @@ __device__ __forceinline__ void smem_to_tc() {
   umma::fence_after();
 }
 
-// Thread 0 commits the MMAs issued so far; everybody waits for them (bounded).
-__device__ __forceinline__ void mma_wait(Sync& s) {
-  if (threadIdx.x == 0) umma::commit(s.mbar);
-  const bool ok = umma::mbar_wait(s.mbar, s.phase);
-  if (!ok && s.status) atomicExch(s.status, 1);
+// Bounded wait of every thread of the CTA on the barrier's current phase.
+// Returns true (the same value in every thread) when the phase completed.
+// When any thread's wait ran out, thread 0 records kDevStatMmaTimeout in the
+// status word (if one was given), the threads that gave up wait once more,
+// again bounded, so that tensor-core work still in flight can drain, and every
+// thread gets false: the caller must skip its TMEM reads, release TMEM and
+// return. All threads of the CTA must call it at the same point.
+__device__ __forceinline__ bool sync_wait(Sync& s, long long polls = (1ll << 22)) {
+  const bool ok = umma::mbar_wait(s.mbar, s.phase, polls);
+  if (__syncthreads_or(!ok)) {
+    if (threadIdx.x == 0 && s.status) atomicExch(s.status, kDevStatMmaTimeout);
+    if (!ok) umma::mbar_wait(s.mbar, s.phase, polls);
+    return false;
+  }
   s.phase ^= 1u;
   umma::fence_after();
+  return true;
+}
+
+// Thread 0 commits the MMAs issued so far; everybody waits for them (bounded,
+// reported as in sync_wait).
+__device__ __forceinline__ bool mma_wait(Sync& s) {
+  if (threadIdx.x == 0) umma::commit(s.mbar);
+  return sync_wait(s);
 }
 
 // Release TMEM (all threads call; after the last TMEM access).
@@ -88,6 +108,18 @@ __device__ __forceinline__ void tc_teardown(uint32_t tm, uint32_t ncols = 512) {
   __syncthreads();
   if (threadIdx.x < 32) umma::tmem_dealloc(tm, ncols);
 }
+
+// In a tensor-core kernel: wait for the MMAs issued so far; if the bounded
+// wait ran out (reported in the status word), let this thread's cp.async
+// copies land, release the CTA's `ncols` TMEM columns and leave the kernel.
+#define ATLAS_MMA_WAIT_OR_LEAVE(sy, tm, ncols)             \
+  do {                                                      \
+    if (!mma_wait(sy)) {                                    \
+      asm volatile("cp.async.wait_all;\n" ::: "memory");   \
+      tc_teardown(tm, ncols);                               \
+      return;                                               \
+    }                                                       \
+  } while (0)
 
 // TMEM address of row (this thread's lane) and column `col`.
 __device__ __forceinline__ uint32_t lane_addr(uint32_t tm, int col) {

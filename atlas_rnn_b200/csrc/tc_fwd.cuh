@@ -201,7 +201,7 @@ __global__ void __launch_bounds__(kT) k_fwd_chunk_tc(Params P) {
   float* Bsuf = sa.take(kR);
   float* Hs = sa.take(kR);
   const int n = cx.n, c = cx.c, K = cx.K, L = cx.L, tid = threadIdx.x, row = row_of(), wg = wg_of();
-  Sync sy{&mbar, &tbase, 0, nullptr};
+  Sync sy{&mbar, &tbase, 0, P.status};
   const uint32_t tm = tc_setup(sy, 256);  // (its barrier also publishes the gates)
   pc.mark(40);
   // End coefficients of key j from suffix sequences of the chunk (no per-key chain):
@@ -251,7 +251,7 @@ __global__ void __launch_bounds__(kT) k_fwd_chunk_tc(Params P) {
 #pragma unroll
     for (int u = 0; u < kD / (8 * kWG); ++u) vrow[u] = src[u];
   }
-  mma_wait(sy);
+  ATLAS_MMA_WAIT_OR_LEAVE(sy, tm, 256);
   pc.mark(42);
   {
     const float ws = cSe[j], wz = cZe[j];
@@ -292,7 +292,7 @@ __global__ void __launch_bounds__(kT) k_fwd_chunk_tc(Params P) {
     mma_chain(tm + 128, op(tDS, kD, 1), op(tPhi, kD, 1), 8, kD, false);
     mma_chain(tm, op(tDZ, kD, 1), op(tPhi, kD, 1), 8, kD, false);  // over delta, already read
   }
-  mma_wait(sy);
+  ATLAS_MMA_WAIT_OR_LEAVE(sy, tm, 256);
   pc.mark(44);
   {  // increments: row = state row nn
     const int64_t D2 = (int64_t)kD * kD;
@@ -352,7 +352,7 @@ __global__ void __launch_bounds__(kT) k_fwd_out_tc(Params P) {
   float* sZv = sa.take(kR + 1);
   float* zZv = sa.take(kR + 1);
   const int n = cx.n, L = cx.L, tid = threadIdx.x, row = row_of(), wg = wg_of();
-  Sync sy{&mbar, &tbase, 0, nullptr};
+  Sync sy{&mbar, &tbase, 0, P.status};
   const uint32_t tm = tc_setup(sy);  // (its barrier also publishes the gates)
   pc.mark(16);
   if (wg == 0) {  // column j = row of tMs: cS of key j before each token i (tile zero-filled)
@@ -374,7 +374,7 @@ __global__ void __launch_bounds__(kT) k_fwd_out_tc(Params P) {
     mma_chain(tm + 128, op(tPsi, kD, 0), op(tSin, kD, 0), kD / 16, kD, false);    // Psi S_in^T
     mma_chain(tm + 256, op(tPsi, kD, 0), op(tZin, kD, 0), kD / 16, kD, false);    // Psi Z_in^T
   }
-  mma_wait(sy);
+  ATLAS_MMA_WAIT_OR_LEAVE(sy, tm, 512);
   pc.mark(19);
 #pragma unroll
   for (int h = 0; h < kCPW; ++h) {  // Ms = cS o A2 (row `row`, this warpgroup's columns)
@@ -392,7 +392,7 @@ __global__ void __launch_bounds__(kT) k_fwd_out_tc(Params P) {
   pc.mark(20);
   smem_to_tc();
   if (tid == 0) mma_chain(tm + 384, op(tMs, kR, 0), op(tDl, kD, 1), 8, kD, false);
-  mma_wait(sy);
+  ATLAS_MMA_WAIT_OR_LEAVE(sy, tm, 512);
   pc.mark(21);
   {
     const int i = row;

@@ -64,7 +64,7 @@ class MemoryRecurrenceFn(torch.autograd.Function):
         fwd = _lib.Fwd(k=p(k), q=p(q), v=p(v), lr=p(lr), decay=p(decay), beta=p(beta), gate=p(gate),
                        S_ref=p(S_ref), S0=p(S0), Z0=p(Z0), buf_in=p(buf), proj=p(proj), y=p(y),
                        S_end=p(S_end), Z_end=p(Z_end) if spec.momentum else None,
-                       buf_out=p(buf_out) if e > 1 else None)
+                       buf_out=p(buf_out) if e > 1 else None, status=p(_lib.status_word(dev)))
         _lib.check(_lib.lib().atlas_mem_forward(ctypes.byref(shape), ctypes.byref(fwd), p(saved),
                                                  saved.numel(), None, 0, _stream(dev)), "forward")
         ctx.spec, ctx.shape, ctx.bwd_bytes = spec, shape, bwd_b
@@ -100,10 +100,12 @@ class MemoryRecurrenceFn(torch.autograd.Function):
         scratch = torch.empty(max(ctx.bwd_bytes, 1), dtype=torch.uint8, device=dev)
         p = _lib.ptr
         fwd = _lib.Fwd(k=p(k), q=p(q), v=p(v), lr=p(lr), decay=p(decay), beta=p(beta), gate=p(gate),
-                       S_ref=p(S_ref), S0=p(S0), Z0=p(Z0), buf_in=p(buf), proj=p(proj))
+                       S_ref=p(S_ref), S0=p(S0), Z0=p(Z0), buf_in=p(buf), proj=p(proj),
+                       status=p(_lib.status_word(dev)))
         bwd = _lib.Bwd(dy=p(dy), dS_end=p(dS_end), dZ_end=p(dZ_end), dbuf_out=p(dbuf_out), dk=p(dk),
                        dq=p(dq), dv=p(dv), dlr=p(dlr), ddecay=p(ddecay), dbeta=p(dbeta), dgate=p(dgate),
-                       dS_ref=p(dS_ref), dS0=p(dS0), dZ0=p(dZ0), dbuf_in=p(dbuf))
+                       dS_ref=p(dS_ref), dS0=p(dS0), dZ0=p(dZ0), dbuf_in=p(dbuf),
+                       status=p(_lib.status_word(dev)))
         saved = ctx.saved_ws
         _lib.check(_lib.lib().atlas_mem_backward(ctypes.byref(shape), ctypes.byref(fwd), ctypes.byref(bwd),
                                                   p(saved), saved.numel(), p(scratch), scratch.numel(),

@@ -93,7 +93,8 @@ class Segment:
         return _lib.Fwd(k=p(self.k), q=p(self.q), v=p(self.v), lr=p(self.lr), decay=p(self.decay),
                         beta=p(self.beta), gate=None, S_ref=p(self.S_ref),
                         S0=p(S0) if S0 is not None else p(self.S_ref), Z0=p(Z0), buf_in=None, proj=None,
-                        y=p(y), S_end=p(S_end), Z_end=p(Z_end), buf_out=None)
+                        y=p(y), S_end=p(S_end), Z_end=p(Z_end), buf_out=None,
+                        status=p(_lib.status_word(self.dev)))
 
     def record_len(self) -> int:
         """Floats in one packed segment-transform record: coef [N,3] (padded to a
@@ -136,7 +137,7 @@ class Segment:
         return _lib.Bwd(dy=p(dy), dS_end=p(FS), dZ_end=p(FZ), dbuf_out=None, dk=p(g.get("k")), dq=p(g.get("q")),
                         dv=p(g.get("v")), dlr=p(g.get("lr")), ddecay=p(g.get("decay")), dbeta=p(g.get("beta")),
                         dgate=None, dS_ref=p(g.get("S_ref")), dS0=p(g.get("S0")), dZ0=p(g.get("Z0")),
-                        dbuf_in=None)
+                        dbuf_in=None, status=p(_lib.status_word(self.dev)))
 
     def backward_local(self, dy):
         self.scratch = torch.empty(max(self.bwd_bytes, 1), dtype=torch.uint8, device=self.dev)

@@ -83,29 +83,68 @@ def cpu_sample(w, n_units=1, t_tokens=512, min_seconds=10.0, max_reps=50):
     return tok_s, per, len(times), sample
 
 
+def reference_cuda_times(steps=5, warmup=2):
+    """The reference's own Omega-16 CUDA kernels (built from its sources into oracle/_ref by
+    oracle/ref_cuda.py) fwd+bwd on the shapes of its performance test, CUDA-event timed; or
+    the reason they cannot run here."""
+    if not torch.cuda.is_available():
+        return {"unavailable": "no CUDA device"}
+    from oracle import ref_cuda
+    try:
+        ext = ref_cuda.load()
+    except Exception as ex:
+        return {"unavailable": str(ex)}
+    dev = torch.device("cuda", torch.cuda.current_device())
+    out = {}
+    b16 = lambda t: t.to(torch.bfloat16).contiguous()
+    for wr in ref_kernel_workloads():
+        x = make_inputs(wr, seed=0, device=dev, state_scale=0.1)
+        a = [b16(x[n]) for n in ("k", "q", "v")] + [b16(x["S0"])] + \
+            [b16(x[n]) for n in ("lr", "decay", "beta", "gate")] + [b16(x["S0"]), b16(x["Z0"]), b16(x["dy"])]
+        m = timed_ms(lambda: ref_cuda.forward_backward(ext, *a), steps, warmup, dev,
+                     lambda: torch.cuda.synchronize(dev))
+        out[f"B{wr.B}_H{wr.H}_T{wr.T}"] = {"ms_per_step": m, "tokens_per_s": wr.B * wr.T / (m / 1000.0)}
+        del x, a
+    return {"kernels": "reference atlas_omega.cu forward_exact_kernel + backward_exact_kernel (sm_100a build)",
+            "times": out}
+
+
 def run_reference(args, w):
+    """The reference arm: the reference's algorithm (restated in oracle/, the reference being a
+    Python package that cannot travel) fwd+bwd on the host cores, rank 0 only. Each step is
+    ``REF_REPS`` repetitions of a bounded slice (1 unit x 512 tokens); ms_per_step is that
+    measured slice time, and value scales the slice's rate to the whole workload (the work is
+    linear in units and tokens), with the factor stated. At N = 1 the line also carries the
+    reference's own CUDA kernels timed on the shapes of its performance test."""
     ws, rank, _ = dist_env()
     if rank != 0:
         return
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    # warm-up then timed steps; each step is one bounded sample
+    REF_REPS = 5
     for _ in range(args.warmup):
         cpu_sample(w, min_seconds=0.0, max_reps=1)
-    vals, pers = [], []
+    pers, sample = [], ""
     for _ in range(args.steps):
-        v, per, _, sample = cpu_sample(w, min_seconds=0.0, max_reps=1)
-        vals.append(v)
+        _, per, _, sample = cpu_sample(w, min_seconds=0.0, max_reps=REF_REPS)
         pers.append(per)
-    value = statistics.median(vals)
+    per = statistics.median(pers)
+    n_units, t_tok = 1, min(512, w.T)
+    scale = (w.N / n_units) * (w.T / t_tok)
+    value = w.B * w.T / (per * scale)
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": 1000.0 * w.B * w.T / value, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": w.name, "B": w.B, "H": w.H, "T": w.T, "d_k": w.d_k, "d_v": w.d_v,
-                       "window": w.window},
+            "warmup": args.warmup, "ms_per_step": 1000.0 * per, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": config_dict(w, ws),
+            "slice": {"units": n_units, "tokens": t_tok, "reps_per_step": REF_REPS,
+                      "ms_per_rep_median": 1000.0 * per, "scale_to_workload": scale,
+                      "ms_per_workload_step_extrapolated": 1000.0 * per * scale,
+                      "note": "ms_per_step is the measured slice; value is its rate scaled to the workload"},
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
                              "sample": sample},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    if ws == 1 and args.config == 1 and not args.no_extra:
+        line["reference_kernel_shapes"] = reference_cuda_times()
     print(json.dumps(line), flush=True)
 
 
@@ -128,7 +167,9 @@ class ClockSampler:
         self.ids = gpu_ids
         self.rank = rank
         self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", "clocks.csv")
+        import tempfile
+        fd, self.path = tempfile.mkstemp(prefix="atlas_bench_clocks_", suffix=".csv")
+        os.close(fd)
         self.t0 = self.t1 = None
 
     def _rows(self):
@@ -178,6 +219,15 @@ class ClockSampler:
             self.f.close()
 
     def summary(self):
+        try:
+            return self._summary()
+        finally:
+            try:
+                os.unlink(self.path)
+            except OSError:
+                pass
+
+    def _summary(self):
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         allrows = self._rows()
@@ -241,6 +291,72 @@ def traffic_from_profiles(kernel: str, workload: str):
                 return None
     return None
 
+# shapes of the reference's own performance test (tests/test_atlas_performance.py:97-204):
+# head 64, window 16, bf16, per-token omega gate, momentum -- the only shape its CUDA kernels run
+REF_KERNEL_SHAPES = ((8, 14, 512), (4, 14, 16384))
+
+
+def ref_kernel_workloads():
+    return [shrink(CONFIGS[5], B=b, H=h, T=t) for b, h, t in REF_KERNEL_SHAPES]
+
+
+def timed_ms(fn, steps, warmup, dev, sync):
+    """CUDA-event time per call of fn() on the current stream, after warmup calls;
+    sync() brackets the region (barrier + synchronize)."""
+    for _ in range(warmup):
+        fn()
+    sync()
+    st = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(steps):
+        fn()
+    e1.record(st)
+    sync()
+    return e0.elapsed_time(e1) / steps
+
+
+def measure_extra(args, ws, rank, dev, sync, max_over_ranks):
+    """Numbers added to the default line: the long-context configuration (sequence-parallel
+    over the ranks at N > 1) fwd+bwd and forward only, and, at N = 1, this package on the
+    shapes of the reference's own CUDA-kernel performance test."""
+    out = {}
+    w2 = CONFIGS[2]
+    w = shard_workload(w2, ws)
+    inp = make_inputs(w, seed=100 + rank, device=dev)
+    step = step_seqpar if ws > 1 else step_api
+    names = ("k", "q", "v", "lr", "decay", "beta", "gate")
+
+    def leaves():
+        d = {n: (inp[n].detach().requires_grad_(True) if inp[n] is not None else None) for n in names}
+        d["dy"] = inp["dy"]
+        return d
+
+    steps = max(3, min(args.steps, 10))
+    ms = max_over_ranks(timed_ms(lambda: step(inp, w, leaves()), steps, 3, dev, sync))
+    with torch.no_grad():
+        fms = max_over_ranks(timed_ms(lambda: step(inp, w, leaves(), backward=False), steps, 3, dev, sync))
+    out["long_context"] = {"config": config_dict(w2, ws), "scaling": "strong", "steps": steps,
+                           "ms_per_step": ms, "value": w2.B * w2.T / (ms / 1000.0), "unit": UNIT,
+                           "forward_only": {"ms_per_step": fms, "value": w2.B * w2.T / (fms / 1000.0)}}
+    del inp
+    if ws == 1:
+        rk = {}
+        for wr in ref_kernel_workloads():
+            x = make_inputs(wr, seed=0, device=dev, state_scale=0.1)
+
+            def lv():
+                d = {n: (x[n].detach().requires_grad_(True) if x[n] is not None else None) for n in names}
+                d["dy"] = x["dy"]
+                return d
+            m = timed_ms(lambda: step_api(x, wr, lv()), 10, 3, dev, sync)
+            rk[f"B{wr.B}_H{wr.H}_T{wr.T}"] = {"ms_per_step": m, "tokens_per_s": wr.B * wr.T / (m / 1000.0)}
+        out["reference_kernel_shapes"] = {
+            "what": "this package fwd+bwd (bf16, head 64, window 16, token gate, momentum) on the shapes of the "
+                    "reference's CUDA-kernel performance test; the reference arm times its kernels on the same",
+            "ours": rk}
+    return out
+
 
 def run_ours(args, w):
     import torch.distributed as dist
@@ -253,13 +369,12 @@ def run_ours(args, w):
     if ws > 1:
         dist.init_process_group("nccl", device_id=dev)
     _lib.lib()
-    # long-context configs with window 1 run sequence-parallel across the ranks
-    # (strong scaling: the ranks share one sequence); the others run one copy
-    # of the configuration per rank (weak scaling)
+    # long-context configs with window 1 run sequence-parallel across the ranks (the ranks
+    # share one sequence); the others are sharded by batch*head units (each rank runs
+    # B/N of the batch). Both are strong scaling: the whole job is the configuration.
     seqpar = ws > 1 and w.window == 1 and w.gate == "none"
     w_full = w
-    if seqpar:
-        w = shrink(w, T=w.T // ws)
+    w = shard_workload(w, ws)
     step = step_seqpar if seqpar else step_api
     inp = make_inputs(w, seed=rank, device=dev)
     names = ("k", "q", "v", "lr", "decay", "beta", "gate")
@@ -432,6 +547,8 @@ def run_ours(args, w):
     step_roof_ms = max((Ff + Fb) * tok_heads / (peak_tf * 1e12),
                        (Bf + Bb) * tok_heads / (peaks.get("hbm_gbs", 6650.0) * 1e9)) * 1000.0
     clocks = clk.summary()
+    extra = measure_extra(args, ws, rank, dev, barrier, max_over_ranks) if args.config == 1 and not args.no_extra \
+        else {}
 
     if rank == 0:
         cpu = None
@@ -441,16 +558,11 @@ def run_ours(args, w):
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
-            "scaling": "strong" if seqpar else "weak",
+            "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16" if w.dtype == torch.bfloat16 else "f32",
             "data": "synthetic (seeded, benchmark-config distributions)",
-            "config": {"workload": w.name, "B": w.B, "H": w.H, "T": w_full.T, "d_k": w.d_k, "d_phi": w.d_phi,
-                       "d_v": w.d_v, "window": w.window, "gate": w.gate, "fmap": f"{w.fmap_mode}:{w.fmap_degree}",
-                       "momentum": w.momentum, "per_rank_units": w.N,
-                       "parallelism": (f"sequence-parallel x{ws} (T/{ws} per rank, NCCL carry exchange)" if seqpar
-                                       else f"bh-replica x{ws}"),
-                       "l2": "inputs exceed L2 (no flush needed)" if tok_heads * (2 * w.d_k + w.d_v) * w.dtype.itemsize > 126e6
-                       else "inputs fit L2"},
+            "config": config_dict(w_full, ws),
+            "per_rank": {"units": w.N, "tokens": w.T, "batch": w.B},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "forward_only": {"value": fwd_value, "unit": UNIT, "ms_per_step": fwd_ms / args.steps},
             "gpu_launches": launches,
@@ -461,11 +573,39 @@ def run_ours(args, w):
             "kernels_ms_per_step": {k: v[0] / prof_steps for k, v in kern.items() if v[1]},
             "clocks": clocks,
             "cpu_baseline": cpu,
+            **extra,
         }
         print(json.dumps(line), flush=True)
     if ws > 1:
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()
+
+
+def shard_workload(w, ws):
+    """This rank's part of the configuration at world size ws: a T / ws token slice of
+    the long-context (window 1, no gate) configurations, else B / ws of the batch
+    (batch*head units are independent; H / ws when B does not divide)."""
+    if ws == 1:
+        return w
+    if w.window == 1 and w.gate == "none":
+        assert w.T % ws == 0
+        return shrink(w, T=w.T // ws)
+    if w.B % ws == 0:
+        return shrink(w, B=w.B // ws)
+    assert w.H % ws == 0, "batch*head units do not divide over the ranks"
+    return shrink(w, H=w.H // ws)
+
+
+def config_dict(w, ws):
+    """The workload description both arms print (same keys and values)."""
+    seqpar = w.window == 1 and w.gate == "none"
+    tok_heads = w.N * w.T
+    return {"workload": w.name, "B": w.B, "H": w.H, "T": w.T, "d_k": w.d_k, "d_phi": w.d_phi, "d_v": w.d_v,
+            "window": w.window, "gate": w.gate, "fmap": f"{w.fmap_mode}:{w.fmap_degree}", "momentum": w.momentum,
+            "parallelism": (f"sequence-parallel x{ws} (T/{ws} per rank, NCCL carry exchange)" if seqpar and ws > 1
+                            else f"batch*head sharded x{ws}"),
+            "l2": ("inputs exceed L2 (no flush needed)" if tok_heads * (2 * w.d_k + w.d_v) * w.dtype.itemsize > 126e6
+                   else "inputs fit L2")}
 
 
 def kernel_cfg_chunk(w):
@@ -644,6 +784,8 @@ def main():
     ap.add_argument("--config", type=int, default=1)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference", "reference-cuda"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="skip the long-context and reference-kernel-shape numbers of the default line")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--T", type=int, default=None, help="override tokens (for profiling small cases)")
     ap.add_argument("--B", type=int, default=None)

@@ -45,7 +45,7 @@
 extern "C" {
 #endif
 
-#define ATLAS_MEM_ABI_VERSION 1
+#define ATLAS_MEM_ABI_VERSION 2
 
 enum AtlasFmapMode { ATLAS_FMAP_OFF = 0, ATLAS_FMAP_ELEMENTWISE = 1, ATLAS_FMAP_TENSOR = 2 };
 enum AtlasGateMode { ATLAS_GATE_NONE = 0, ATLAS_GATE_TOKEN = 1, ATLAS_GATE_WINDOW = 2 };
@@ -58,7 +58,8 @@ enum AtlasError {
   ATLAS_ERR_WORKSPACE = 3,     /* workspace pointer missing or too small          */
   ATLAS_ERR_LAUNCH = 4,        /* a kernel launch failed (cudaGetLastError)        */
   ATLAS_ERR_DEVICE = 5,        /* device-side status word reported a fault         */
-  ATLAS_ERR_NOALLOC_TOO_LARGE = 6 /* shape exceeds the fixed scratch of the no-alloc entry */
+  ATLAS_ERR_NOALLOC_TOO_LARGE = 6, /* shape exceeds the fixed scratch of the no-alloc entry */
+  ATLAS_ERR_NOALLOC_CAPTURE = 7    /* no-alloc scratch looked up for the first time inside a stream capture */
 };
 
 /* Shapes and modes of one call. Mirrors the constructor arguments of
@@ -98,6 +99,7 @@ typedef struct AtlasMemFwd {
   float* S_end;        /* [N,d_v,d_phi]                                         */
   float* Z_end;        /* [N,d_v,d_phi]                                         */
   float* buf_out;      /* [N,e-1,d_v,d_phi]                                     */
+  int* status;         /* optional device-visible status word, see below        */
 } AtlasMemFwd;
 
 /* Backward operands: upstream gradients in, input gradients out. Optional
@@ -119,7 +121,34 @@ typedef struct AtlasMemBwd {
   float* dS0;            /* [N,d_v,d_phi]                                       */
   float* dZ0;            /* [N,d_v,d_phi]                                       */
   float* dbuf_in;        /* [N,e-1,d_v,d_phi]                                   */
+  int* status;           /* optional device-visible status word, see below      */
 } AtlasMemBwd;
+
+/* Device status word (`status` in AtlasMemFwd / AtlasMemBwd; NULL = none).
+ * Every wait of a kernel for its tensor-core work is bounded. When one runs
+ * out, the kernel writes ATLAS_DEVSTAT_MMA_TIMEOUT to *status, lets its copies
+ * and tensor-core work in flight drain (again bounded), releases its tensor
+ * memory and returns without writing the rest of its results; the call's
+ * outputs are then invalid. The caller zeroes the word (device memory, or
+ * pinned host memory the device can reach) and reads it once the work has
+ * finished, for example with atlas_mem_read_status. The library never clears
+ * it, so one word can collect the status of many calls. */
+#define ATLAS_DEVSTAT_MMA_TIMEOUT 1
+
+/* Synchronises `stream`, reads *status (a device or device-visible pointer)
+ * and returns ATLAS_ERR_DEVICE if it is nonzero, ATLAS_OK otherwise
+ * (ATLAS_ERR_LAUNCH if the synchronisation or the read failed). The word is
+ * left as it is. No reference counterpart (the reference has no device-side
+ * error reporting). */
+int atlas_mem_read_status(const int* status, void* stream);
+
+/* Self test of the bounded-wait path: one CTA initialises a barrier that
+ * nothing ever arrives on and waits on it for `polls` polls through the same
+ * wait-and-report code the tensor-core kernels use, so *status receives
+ * ATLAS_DEVSTAT_MMA_TIMEOUT. No tensor-core work is issued and no tensor
+ * memory is held, so the timeout is harmless and the context stays usable.
+ * polls must be in [1, 1<<20]. No reference counterpart. */
+int atlas_mem_selftest_wait_timeout(int* status, int polls, void* stream);
 
 /* Library version / ABI check. */
 int atlas_mem_abi_version(void);
@@ -150,8 +179,11 @@ int atlas_mem_forward(const AtlasMemShape* shape, const AtlasMemFwd* fwd,
  *    until the process exits. Shapes whose forward workspace
  *    (atlas_mem_workspace_size's `saved`) exceeds it are rejected with
  *    ATLAS_ERR_NOALLOC_TOO_LARGE before anything is launched.
- *  - The first call on each device looks up the array's device address with
- *    that device current; make that first call before any stream capture.
+ *  - Every call looks up the array's device address with the current device
+ *    (nothing is cached, so a context reset is harmless). The first lookup on
+ *    a device loads the library's kernels there, which CUDA refuses inside a
+ *    stream capture: make the first call on each device before any capture
+ *    (a first call made during capture returns ATLAS_ERR_NOALLOC_CAPTURE).
  *  - All calls share the one array and it keeps the last call's contents:
  *    calls whose work overlaps on the GPU (other streams, other host threads)
  *    race with each other. Nothing in it needs to start at zero.

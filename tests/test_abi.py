@@ -27,7 +27,7 @@ def test_header_declares_entry_points():
 def test_library_exports_every_declared_symbol(native_lib):
     for name in declared_functions():
         assert hasattr(native_lib, name), name
-    assert native_lib.atlas_mem_abi_version() == 1
+    assert native_lib.atlas_mem_abi_version() == 2
     assert native_lib.atlas_mem_error_string(0) == b"ok"
 
 
@@ -40,6 +40,7 @@ def test_struct_layouts_match_header(native_lib):
 int main(void) {
   printf("%zu %zu %zu %zu %zu %zu\n", sizeof(AtlasMemShape), sizeof(AtlasMemFwd), sizeof(AtlasMemBwd),
          offsetof(AtlasMemShape, chunk), offsetof(AtlasMemFwd, buf_out), offsetof(AtlasMemBwd, dbuf_in));
+  printf("%zu %zu\n", offsetof(AtlasMemFwd, status), offsetof(AtlasMemBwd, status));
   return 0;
 }
 '''
@@ -50,12 +51,15 @@ int main(void) {
         subprocess.run(["gcc", "-I", os.path.dirname(HEADER), c, "-o", exe], check=True)
         got = [int(x) for x in subprocess.run([exe], capture_output=True, text=True).stdout.split()]
     exp = [ctypes.sizeof(_lib.Shape), ctypes.sizeof(_lib.Fwd), ctypes.sizeof(_lib.Bwd),
-           _lib.Shape.chunk.offset, _lib.Fwd.buf_out.offset, _lib.Bwd.dbuf_in.offset]
+           _lib.Shape.chunk.offset, _lib.Fwd.buf_out.offset, _lib.Bwd.dbuf_in.offset,
+           _lib.Fwd.status.offset, _lib.Bwd.status.offset]
     assert got == exp
 
 
 def test_null_arguments_rejected(native_lib):
     assert native_lib.atlas_mem_workspace_size(None, None, None, None) == 1
+    assert native_lib.atlas_mem_read_status(None, None) == 1
+    assert native_lib.atlas_mem_selftest_wait_timeout(None, 10, None) == 1
     assert native_lib.atlas_mem_forward(None, None, None, 0, None, 0, None) == 1
 
 

@@ -24,6 +24,14 @@ def test_reference_arm_line():
     assert d["cpu_baseline"]["kind"] == "port" and d["cpu_baseline"]["value"] == d["value"]
     assert d["e2e"] == {"value": d["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
     assert d["config"]["workload"] == "omega_rnn_c1"
+    assert d["slice"]["reps_per_step"] >= 5 and d["ms_per_step"] == d["slice"]["ms_per_rep_median"]
+    # the same config dict as our arm prints (bench.config_dict), so the driver can match the two
+    sys.path.insert(0, ROOT)
+    import bench
+    from atlas_rnn_b200.workloads import CONFIGS
+    assert d["config"] == json.loads(json.dumps(bench.config_dict(CONFIGS[1], 1)))
+    # no CUDA device here: the reference kernels' block says so
+    assert "unavailable" in d["reference_kernel_shapes"]
 
 
 def test_reference_cuda_arm_refuses_other_shapes():

@@ -122,3 +122,46 @@ def test_sequential_numpy_restatement_agrees(e, mom, gate):
     for x, y in zip(a, b):
         if x is not None:
             assert np.allclose(x.numpy(), y, atol=1e-10)
+
+
+# ---- streaming restatement for long sequences, pinned against the autograd oracle ---------
+@pytest.mark.parametrize("mom", [True, False])
+@pytest.mark.parametrize("saturate", [False, True])
+def test_streaming_oracle_matches_autograd(mom, saturate):
+    """oracle/streaming_ref.py (token-by-token forward, hand-derived reverse recurrence with
+    checkpointed segments) equals autograd of memory_ref.memory_layer, including the
+    clamp of S_end when |S_T| passes 100."""
+    from oracle import streaming_ref
+    g = torch.Generator().manual_seed(5)
+    N, T, d = 2, 150, 16
+    rn = lambda *s: torch.randn(*s, generator=g, dtype=torch.float64)
+    unit = lambda t: t / t.norm(dim=-1, keepdim=True)
+    k, q, v = unit(rn(N, T, d)), unit(rn(N, T, d)), unit(rn(N, T, d))
+    decay = torch.sigmoid(3 + 0.5 * rn(N, T))
+    if saturate:
+        decay = 0.999 + 0.001 * torch.rand(N, T, generator=g, dtype=torch.float64)
+    lr = 0.1 * torch.sigmoid(rn(N, T))
+    beta = torch.sigmoid(1 + 0.5 * rn(N, T)) if mom else None
+    scale = 150.0 if saturate else 0.1
+    S_ref, S0 = 0.1 * rn(N, d, d), scale * rn(N, d, d)
+    Z0 = 0.1 * rn(N, d, d) if mom else None
+    dy, dS, dZ = rn(N, T, d), rn(N, d, d), rn(N, d, d)
+    leaves = [t.clone().requires_grad_(True) if t is not None else None
+              for t in (k, q, v, lr, decay, beta, S_ref, S0, Z0)]
+    y, S_end, Z_end, _ = memory_ref.memory_layer(leaves[0], leaves[1], leaves[2], leaves[3], leaves[4],
+                                                 leaves[5], None, leaves[6], leaves[7], leaves[8], None)
+    outs, ups = [y, S_end], [dy, dS]
+    if mom:
+        outs.append(Z_end)
+        ups.append(dZ)
+    torch.autograd.backward(outs, ups)
+    ys, Ss, Zs, S_T, _ = streaming_ref.forward(k, q, v, lr, decay, beta, S_ref, S0, Z0)
+    if saturate:
+        assert (S_T.abs() > 100).float().mean() > 0.2
+    assert rel_l2(ys, y.detach()) < 1e-12 and rel_l2(Ss, S_end.detach()) < 1e-12
+    gr = streaming_ref.backward(k, q, v, lr, decay, beta, S_ref, S0, Z0, dy, dS, dZ if mom else None, seg=32)
+    names = ["k", "q", "v", "lr", "decay", "beta", "S_ref", "S0", "Z0"]
+    for name, leaf in zip(names, leaves):
+        if leaf is None:
+            continue
+        assert rel_l2(gr[name], leaf.grad) < 1e-10, name

@@ -13,9 +13,11 @@ from tests.helpers import TOL_BF16, TOL_F32, oracle_run, rel_l2
 pytestmark = pytest.mark.gpu
 
 
-def run_case(w: Workload, seed=0, state_scale=0.1, tol=None, separate_sref=False, chunk=0):
+def run_case(w: Workload, seed=0, state_scale=0.1, tol=None, separate_sref=False, chunk=0, mutate=None):
     tol = tol if tol is not None else (TOL_F32 if w.dtype == torch.float32 else TOL_BF16)
     inp = make_inputs(w, seed=seed, device="cuda", state_scale=state_scale)
+    if mutate is not None:
+        mutate(inp)
     g = torch.Generator().manual_seed(seed + 7)
     S_ref = (0.1 * torch.randn(w.N, w.d_v, w.d_phi, generator=g)).cuda() if separate_sref else None
     leaves = {n: (t.clone().requires_grad_(True) if t is not None else None) for n, t in inp.items()
@@ -122,8 +124,41 @@ def test_config0_full(native_lib):
 
 
 def test_config1_slice(native_lib):
-    """BASELINE config 1 (bf16, e=4, window gates, elementwise g=2) on a batch*head slice."""
+    """BASELINE config 1 (bf16, e=4, window gates, elementwise g=2) on a batch*head slice,
+    from a zero state (the benchmark's) and from a non-zero S0 / Z0 / omega buffer
+    (scale 0.1, as the reference's tests use: test_rnn_all.py:469-470,551-553)."""
     run_case(shrink(CONFIGS[1], B=1, H=2, T=1024), state_scale=0.0)
+    run_case(shrink(CONFIGS[1], B=1, H=2, T=4096), state_scale=0.1, seed=4)
+
+
+# ---- the clamp of S_end (rnn_memory.py:372-373,701-702) driven into saturation -------------
+def _saturate(inp):
+    """alpha close to 1 and |S0| of order 150, so a large share of S_T lies beyond +-100:
+    S_end is clamped there and its gradient is zero (torch.clamp's rule)."""
+    g = torch.Generator().manual_seed(99)
+    dec = inp["decay"]
+    inp["decay"] = (0.999 + 0.001 * torch.rand(dec.shape, generator=g)).to(dec.dtype).to(dec.device)
+    inp["S0"] = (1500.0 * inp["S0"]).contiguous()  # S0 was 0.1 N(0,1)
+    S_T_est = inp["S0"]
+    assert (S_T_est.abs() > 100).float().mean() > 0.3
+
+
+CASES_CLAMP = [
+    W("clamp_f32_e4_token", 90, e=4, gate="token"),
+    W("clamp_f32_nomom", 70, mom=False),
+    W("clamp_tc_e4_window_elem", 260, d=128, e=4, gate="window", fm="elementwise", deg=2, dtype=torch.bfloat16),
+    W("clamp_tc_nomom", 200, d=128, mom=False, dtype=torch.bfloat16),
+    W("clamp_padded_d64_e8", 150, d=64, e=8, gate="token", dtype=torch.bfloat16),
+]
+
+
+@pytest.mark.parametrize("w", CASES_CLAMP, ids=lambda w: w.name)
+def test_clamp_saturated(native_lib, w):
+    """S_end, Z_end and every input gradient against the oracle with the clamp active
+    (CUDA-core fp32 path, tensor-core bf16 path, padded tensor-core path). S_ref is a
+    separate state of the usual scale (0.1), so the deltas stay of order one and the
+    bf16 tolerance measures the clamp, not bf16 rounding of deltas of order 100."""
+    run_case(w, state_scale=0.1, mutate=_saturate, separate_sref=True)
 
 
 def test_config4_slice(native_lib):

@@ -93,3 +93,49 @@ def test_forward_noalloc_rejects_oversized_shape(native_lib):
     rc = native_lib.atlas_mem_forward_noalloc(ctypes.byref(shape), ctypes.byref(f), None)
     assert rc == 6
     assert b"no-alloc" in native_lib.atlas_mem_error_string(rc)
+
+
+def _tc_case(seed, N, T, e=4):
+    """bf16 io, d = 128, window gates, elementwise map: the shape the tensor-core kernels run."""
+    from atlas_rnn_b200 import _lib
+    from atlas_rnn_b200.workloads import Workload, make_inputs
+    w = Workload("noalloc_tc", 1, N, T, 128, 128, 128, e, "window", "elementwise", 2, True, torch.bfloat16, 0)
+    inp = make_inputs(w, seed=seed, device="cuda", state_scale=0.1)
+    x = {"k": inp["k"], "q": inp["q"], "v": inp["v"], "lr": inp["lr"], "decay": inp["decay"],
+         "beta": inp["beta"], "gate": inp["gate"], "S0": inp["S0"], "Z0": inp["Z0"], "buf": inp["omega_buffer"]}
+    shape = _lib.Shape(N=N, T=T, d_k=128, d_phi=128, d_v=128, window=e, fmap_mode=1, fmap_degree=2,
+                       gate_mode=_lib.GATE_WINDOW, momentum=1, dtype_io=_lib.BF16, chunk=0)
+    o = {"y": torch.empty(N, T, 128, device="cuda", dtype=torch.bfloat16),
+         "S_end": torch.empty(N, 128, 128, device="cuda"), "Z_end": torch.empty(N, 128, 128, device="cuda"),
+         "buf_out": torch.empty(N, e - 1, 128, 128, device="cuda")}
+    return inp, x, shape, o
+
+
+def test_forward_noalloc_tensor_core_path(native_lib):
+    """The tensor-core layout of the scratch (bf16 delta rows, state tiles, S_ref tile) run
+    through the fixed array: T is not a multiple of the chunk, the array holds another,
+    larger call's data before each checked call, and the results are compared with
+    atlas_mem_forward (caller workspace) and with the CPU oracle at the bf16 tolerance."""
+    from atlas_rnn_b200 import _lib
+    from tests.helpers import TOL_BF16, oracle_run
+    lib = native_lib
+    for seed in (1, 2):
+        # a larger call first, so the array is full of unrelated data
+        _, xb, sb, ob = _tc_case(seed + 10, N=6, T=900)
+        assert lib.atlas_mem_forward_noalloc(ctypes.byref(sb), ctypes.byref(_fwd_struct(xb, ob)), None) == 0
+        inp, x, shape, o = _tc_case(seed, N=2, T=300)
+        saved_b, _, _ = _lib.workspace_sizes(shape)
+        assert saved_b <= lib.atlas_mem_noalloc_scratch_bytes()
+        rc = lib.atlas_mem_forward_noalloc(ctypes.byref(shape), ctypes.byref(_fwd_struct(x, o)), None)
+        assert rc == 0, lib.atlas_mem_error_string(rc)
+        torch.cuda.synchronize()
+        ref = {n: torch.empty_like(t) for n, t in o.items()}
+        saved = torch.empty(saved_b, dtype=torch.uint8, device="cuda")
+        rc = lib.atlas_mem_forward(ctypes.byref(shape), ctypes.byref(_fwd_struct(x, ref)), _lib.ptr(saved),
+                                   saved.numel(), None, 0, None)
+        assert rc == 0
+        torch.cuda.synchronize()
+        out_ref, _ = oracle_run(inp, 4, "window", "elementwise", 2, grads=False)
+        for name in ("y", "S_end", "Z_end", "buf_out"):
+            assert rel_l2(o[name].float(), ref[name].float()) < TOL_F32, (seed, name)
+            assert rel_l2(o[name].float(), out_ref[name]) < TOL_BF16, (seed, name)
