@@ -1,6 +1,7 @@
 // C ABI of libatlas_mem.so: argument checks, workspace layout and the launch
 // sequences of the forward and backward passes. Declarations and the reference
 // interfaces they replace are in include/atlas_mem.h.
+#include <cudaTypedefs.h>
 #include <mutex>
 
 #include <algorithm>
@@ -503,6 +504,51 @@ int noalloc_scratch(cudaStream_t st, void** out) {
   return ATLAS_OK;
 }
 
+// ---- TMA descriptors of the bf16 row operands (tensor-core kernels) ----------
+PFN_cuTensorMapEncodeTiled_v12000 tma_encoder() {
+  static std::once_flag once;
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* f = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  });
+  return fn;
+}
+
+// A bf16 [N, T, 128] row-major array as the 4-D view (8 elements, T rows, 16
+// column blocks, N units): a box {8, 8, 16, 1} is one 8-row group of a tile in
+// the core-matrix layout, and rows outside [0, T) of a unit read as zeros.
+int encode_rows(CUtensorMap* m, const void* base, int64_t N, int64_t T) {
+  if (!base) return ATLAS_OK;
+  if (reinterpret_cast<uintptr_t>(base) % 16) return ATLAS_ERR_INVALID_ARG;
+  PFN_cuTensorMapEncodeTiled_v12000 enc = tma_encoder();
+  if (!enc) return ATLAS_ERR_LAUNCH;
+  const cuuint64_t dims[4] = {8, (cuuint64_t)T, (cuuint64_t)(tc::kD / 8), (cuuint64_t)N};
+  const cuuint64_t strides[3] = {(cuuint64_t)tc::kD * 2, 16, (cuuint64_t)T * tc::kD * 2};
+  const cuuint32_t box[4] = {8, 8, (cuuint32_t)(tc::kD / 8), 1};
+  const cuuint32_t es[4] = {1, 1, 1, 1};
+  const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, es,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? ATLAS_OK : ATLAS_ERR_LAUNCH;
+}
+
+// Descriptors for the operands the tensor-core kernels load by TMA.
+int encode_tma(Params& P, const AtlasMemShape* s) {
+  if (!tc_groups(s)) return ATLAS_OK;
+  int v;
+  if (P.fmode != ATLAS_FMAP_TENSOR) {
+    if ((v = encode_rows(&P.tm_q, P.q, P.N, P.T))) return v;
+    if ((v = encode_rows(&P.tm_k, P.k, P.N, P.T))) return v;
+  }
+  if ((v = encode_rows(&P.tm_dy, P.dy, P.N, P.T))) return v;
+  if ((v = encode_rows(&P.tm_dl, P.dlb, P.N, P.T))) return v;
+  return ATLAS_OK;
+}
+
 int check_ws(const Layout& L, const void* saved, size_t saved_bytes, const void* scratch, size_t scratch_bytes,
              bool need_scratch) {
   if (!saved || saved_bytes < L.saved) return ATLAS_ERR_WORKSPACE;
@@ -648,7 +694,8 @@ int atlas_mem_forward(const AtlasMemShape* shape, const AtlasMemFwd* fwd, void* 
   const Layout L = make_layout(shape);
   if ((v = check_ws(L, saved, saved_bytes, nullptr, 0, false))) return v;
   if ((v = ensure_attrs())) return v;
-  const Params P = make_params(shape, L, fwd, nullptr, saved, nullptr);
+  Params P = make_params(shape, L, fwd, nullptr, saved, nullptr);
+  if (int te = encode_tma(P, shape)) return te;
   cudaStream_t st = (cudaStream_t)stream;
   if ((v = run_fwd_local(shape, P, st))) return v;
   return run_fwd_finish(shape, P, st);
@@ -665,7 +712,8 @@ int atlas_mem_forward_noalloc(const AtlasMemShape* shape, const AtlasMemFwd* fwd
   if ((v = ensure_attrs())) return v;
   // Every scratch word the forward reads is written earlier in the same call,
   // so nothing has to be cleared between calls.
-  const Params P = make_params(shape, L, fwd, nullptr, scratch, nullptr);
+  Params P = make_params(shape, L, fwd, nullptr, scratch, nullptr);
+  if (int te = encode_tma(P, shape)) return te;
   cudaStream_t st = (cudaStream_t)stream;
   if ((v = run_fwd_local(shape, P, st))) return v;
   return run_fwd_finish(shape, P, st);
@@ -696,7 +744,8 @@ int atlas_mem_backward(const AtlasMemShape* shape, const AtlasMemFwd* fwd, const
   const Layout L = make_layout(shape);
   if ((v = check_ws(L, saved, saved_bytes, scratch, scratch_bytes, true))) return v;
   if ((v = ensure_attrs())) return v;
-  const Params P = make_params(shape, L, fwd, bwd, saved, scratch);
+  Params P = make_params(shape, L, fwd, bwd, saved, scratch);
+  if (int te = encode_tma(P, shape)) return te;
   cudaStream_t st = (cudaStream_t)stream;
   if ((v = run_bwd_local(shape, P, st))) return v;
   return run_bwd_finish(shape, P, st);
@@ -710,7 +759,8 @@ int atlas_mem_decode_step(const AtlasMemShape* shape, const AtlasMemFwd* fwd, vo
   if ((v = validate_fwd(shape, fwd, true))) return v;
   if (shape->window > 1 && (!fwd->buf_out || fwd->buf_out == fwd->buf_in)) return ATLAS_ERR_INVALID_ARG;
   const Layout L = make_layout(shape);
-  const Params P = make_params(shape, L, fwd, nullptr, nullptr, nullptr);
+  Params P = make_params(shape, L, fwd, nullptr, nullptr, nullptr);
+  if (int te = encode_tma(P, shape)) return te;
   cudaStream_t st = (cudaStream_t)stream;
   const dim3 grid((unsigned)((shape->d_v + kDecodeRows - 1) / kDecodeRows), (unsigned)shape->N);
   auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
@@ -834,6 +884,7 @@ int atlas_mem_forward_local(const AtlasMemShape* shape, const AtlasMemFwd* fwd, 
   if ((v = check_ws(L, saved, saved_bytes, nullptr, 0, false))) return v;
   if ((v = ensure_attrs())) return v;
   Params P = make_params(shape, L, fwd, nullptr, saved, nullptr);
+  if (int te = encode_tma(P, shape)) return te;
   P.seg_coef = seg_coef; P.seg_dS = seg_dS; P.seg_dZ = seg_dZ;
   cudaStream_t st = (cudaStream_t)stream;
   if ((v = run_fwd_local(shape, P, st))) return v;
@@ -850,7 +901,8 @@ int atlas_mem_forward_finish(const AtlasMemShape* shape, const AtlasMemFwd* fwd,
   const Layout L = make_layout(shape);
   if ((v = check_ws(L, saved, saved_bytes, nullptr, 0, false))) return v;
   if ((v = ensure_attrs())) return v;
-  const Params P = make_params(shape, L, fwd, nullptr, saved, nullptr);
+  Params P = make_params(shape, L, fwd, nullptr, saved, nullptr);
+  if (int te = encode_tma(P, shape)) return te;
   return run_fwd_finish(shape, P, (cudaStream_t)stream);
 }
 
@@ -865,6 +917,7 @@ int atlas_mem_backward_local(const AtlasMemShape* shape, const AtlasMemFwd* fwd,
   if ((v = check_ws(L, saved, saved_bytes, scratch, scratch_bytes, true))) return v;
   if ((v = ensure_attrs())) return v;
   Params P = make_params(shape, L, fwd, bwd, saved, scratch);
+  if (int te = encode_tma(P, shape)) return te;
   P.seg_coef = seg_coef; P.seg_dS = seg_dS; P.seg_dZ = seg_dZ;
   cudaStream_t st = (cudaStream_t)stream;
   if ((v = run_bwd_local(shape, P, st))) return v;
@@ -882,6 +935,7 @@ int atlas_mem_backward_finish(const AtlasMemShape* shape, const AtlasMemFwd* fwd
   if ((v = check_ws(L, saved, saved_bytes, scratch, scratch_bytes, true))) return v;
   if ((v = ensure_attrs())) return v;
   Params P = make_params(shape, L, fwd, bwd, saved, scratch);
+  if (int te = encode_tma(P, shape)) return te;
   P.apply_mask = apply_clamp_mask ? 1 : 0;
   return run_bwd_finish(shape, P, (cudaStream_t)stream);
 }

@@ -1,5 +1,6 @@
 // Shared device helpers for the memory-update kernels.
 #pragma once
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <stdint.h>
@@ -12,6 +13,14 @@ constexpr int kThreads = 256;  // every CTA of the SIMT path runs 256 threads
 
 // Everything a kernel needs, passed by value (well under the 4 KB limit).
 struct Params {
+  // tensor-core path: TMA descriptors of the bf16 row-major [N, T, 128] operands
+  // (q, k, dy, and the saved delta rows), viewed as 4-D (8 elements, T rows,
+  // 16 column blocks, N units) so that a box of 8 rows lands in the
+  // core-matrix tile layout; zero-filled outside each unit's rows
+  alignas(64) CUtensorMap tm_q;
+  alignas(64) CUtensorMap tm_k;
+  alignas(64) CUtensorMap tm_dy;
+  alignas(64) CUtensorMap tm_dl;
   // shape
   int N, T, dk, dphi, dv, e, fmode, fdeg, gmode, mom, bf, C, nch;
   // forward operands

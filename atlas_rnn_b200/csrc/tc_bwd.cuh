@@ -42,19 +42,22 @@ __device__ __forceinline__ void adj_scalars(const Ctx& cx, float* hS, float* hZS
 // adjoint increments at the chunk input from the chunk's own dy:
 //   dShat = dY^T diag(eS_0) Psi,  dZhat = dY^T diag(eZ_0) Psi
 // ===========================================================================
-__global__ void __launch_bounds__(kT) k_bwd_chunk_tc(Params P) {
+__global__ void __launch_bounds__(kT) k_bwd_chunk_tc(const __grid_constant__ Params P) {
   PhaseClock pc;
   extern __shared__ __align__(1024) unsigned char sm[];
   unsigned char* tYS = sm;
   unsigned char* tYZ = sm + kTileBytes;
   unsigned char* tPsi = sm + 2 * kTileBytes;
   SmemAlloc sa{reinterpret_cast<float*>(sm + 3 * kTileBytes), 0};
-  __shared__ uint64_t mbar;
+  __shared__ uint64_t mbar, lbar;
   __shared__ uint32_t tbase;
   Ctx cx;
   ctx_geom(P, cx);
-  async_rows_psi(P, cx, tPsi);
-  async_rows_dy(P, cx, tYS);
+  TmaBatch ld{&lbar, 0};
+  if (threadIdx.x == 0) tma_init(ld);
+  load_rows_psi(P, cx, tPsi, ld);
+  load_rows_dy(P, cx, tYS, ld);
+  if (threadIdx.x == 0) tma_commit(ld);
   load_ctx(P, sa, cx, kT);
   float* eS0 = sa.take(kR + 1);
   float* eZ0 = sa.take(kR + 1);
@@ -80,7 +83,9 @@ __global__ void __launch_bounds__(kT) k_bwd_chunk_tc(Params P) {
       o[0] = hS[0]; o[1] = hZS[0]; o[2] = hZZ[0]; o[3] = 0.f;
     }
   }
-  async_wait();
+  tma_wait(ld, P.status);
+  zero_rows_from(tPsi, L);
+  zero_rows_from(tYS, L);
   __syncthreads();
   pc.mark(49);
   {  // dY rows scaled by eS0 (in place) and by eZ0 (into tYZ); psi feature map
@@ -152,7 +157,7 @@ __device__ __forceinline__ void key_adj_weights(const Params& P, const Ctx& cx, 
 // so one coefficient tile (cS, built by warpgroup 0 while the operand tiles
 // arrive by cp.async) serves the adjoint weights as well, and M2 = wE o A1 = M3.
 // ===========================================================================
-__global__ void __launch_bounds__(kT) k_bwd_keys_tc(Params P) {
+__global__ void __launch_bounds__(kT) k_bwd_keys_tc(const __grid_constant__ Params P) {
   PhaseClock pc;
   extern __shared__ __align__(1024) unsigned char sm[];
   unsigned char* tPhi = sm;
@@ -162,9 +167,19 @@ __global__ void __launch_bounds__(kT) k_bwd_keys_tc(Params P) {
   unsigned char* tM3 = sm + 4 * kTileBytes;   // cS, later M3 (= M2)
   unsigned char* tM1 = sm + 5 * kTileBytes;   // M1
   SmemAlloc sa{reinterpret_cast<float*>(sm + 6 * kTileBytes), 0};
-  __shared__ uint64_t mbar;
+  __shared__ uint64_t mbar, lbar;
   __shared__ uint32_t tbase;
   Ctx cx;
+  ctx_geom(P, cx);
+  const int64_t cid = chunk_id(P, cx);
+  const unsigned char* FS = P.adjb + cid * 2 * kTileBytes;
+  TmaBatch ld{&lbar, 0};
+  if (threadIdx.x == 0) tma_init(ld);
+  load_keys_phi(P, cx, tPhi, ld);
+  load_keys_delta(P, cx, tDl, ld);
+  load_tile(tFS, FS, ld);
+  load_tile(tFZ, FS + kTileBytes, ld);
+  if (threadIdx.x == 0) tma_commit(ld);
   load_ctx(P, sa, cx, kT);
   float* hS = sa.take(kR + 1);
   float* hZS = sa.take(kR + 1);
@@ -173,12 +188,6 @@ __global__ void __launch_bounds__(kT) k_bwd_keys_tc(Params P) {
   const int n = cx.n, K = cx.K, L = cx.L, tid = threadIdx.x, e = P.e, row = row_of(), wg = wg_of();
   Sync sy{&mbar, &tbase, 0, P.status};
   const uint32_t tm = tc_setup(sy);
-  const int64_t cid = chunk_id(P, cx);
-  const unsigned char* FS = P.adjb + cid * 2 * kTileBytes;
-  async_keys_phi(P, cx, tPhi);
-  async_keys_delta(P, cx, tDl);
-  async_copy_tile(tFS, FS);
-  async_copy_tile(tFZ, FS + kTileBytes);
   zero_tile(tM3);
   __syncthreads();  // gates of load_ctx visible, tM3 zero
   pc.mark(0);
@@ -188,7 +197,7 @@ __global__ void __launch_bounds__(kT) k_bwd_keys_tc(Params P) {
   } else if (wg == 1 && row < 32) {
     adj_scalars_warp(cx, hS, hZS, hZZ);
   }
-  async_wait();
+  tma_wait(ld, P.status);
   if (wg > 0) {
     loaders_sync();
     phi_xform(P, tPhi, 128, kT - 128);
@@ -204,8 +213,9 @@ __global__ void __launch_bounds__(kT) k_bwd_keys_tc(Params P) {
   }
   ATLAS_MMA_WAIT_OR_LEAVE(sy, tm, 512);
   pc.mark(4);
-  async_rows_psi(P, cx, tFS);  // F tiles are free once the phase-1 MMAs are done
-  async_rows_dy(P, cx, tFZ);
+  load_rows_psi(P, cx, tFS, ld);  // F tiles are free once the phase-1 MMAs are done
+  load_rows_dy(P, cx, tFZ, ld);
+  if (threadIdx.x == 0) tma_commit(ld);
   {  // phase-1 epilogue, row j: X[F][R_j]; F parts of d delta / d phi back into TMEM
     const int j = row;
     float wzs, wzz;
@@ -236,7 +246,9 @@ __global__ void __launch_bounds__(kT) k_bwd_keys_tc(Params P) {
     part[(wg * 2 + 1) * kR + j] = xZ;
   }
   umma::fence_before();
-  async_wait();
+  tma_wait(ld, P.status);
+  zero_rows_from(tFS, L);
+  zero_rows_from(tFZ, L);
   __syncthreads();  // psi / dY rows landed; P2 / Q2 columns are free
   if (wg == 0) {
     float a = 0.f, b = 0.f;
@@ -343,7 +355,7 @@ __device__ __forceinline__ void wg_sync(int id) {  // named barrier of one warpg
 __device__ __forceinline__ void pair_sync() {  // named barrier of warpgroups 2 and 3
   asm volatile("bar.sync 4, 256;\n" ::: "memory");
 }
-__global__ void __launch_bounds__(kT) k_bwd_state_gates_tc(Params P) {
+__global__ void __launch_bounds__(kT) k_bwd_state_gates_tc(const __grid_constant__ Params P) {
   PhaseClock pc;
   extern __shared__ __align__(1024) unsigned char sm[];
   unsigned char* tPsi = sm;
@@ -358,20 +370,23 @@ __global__ void __launch_bounds__(kT) k_bwd_state_gates_tc(Params P) {
   unsigned char* tES = tFS;    // eS_{i+1}[q]
   unsigned char* tEZ = tFZ;    // eZ_{i+1}[q]
   SmemAlloc sa{reinterpret_cast<float*>(sm + 6 * kTileBytes), 0};
-  __shared__ uint64_t mbar;
+  __shared__ uint64_t mbar, lbar;
   __shared__ uint32_t tbase;
   Ctx cx;
   ctx_geom(P, cx);
   const int64_t cid = chunk_id(P, cx);
+  TmaBatch ld{&lbar, 0};
+  if (threadIdx.x == 0) tma_init(ld);
   {  // every operand tile in flight before anything else
     const unsigned char* Sin = P.stb + cid * 2 * kTileBytes;
     const unsigned char* FS = P.adjb + cid * 2 * kTileBytes;
-    async_rows_psi(P, cx, tPsi);
-    async_rows_dy(P, cx, tY);
-    async_copy_tile(tSin, Sin);
-    async_copy_tile(tZin, Sin + kTileBytes);
-    async_copy_tile(tFS, FS);
-    async_copy_tile(tFZ, FS + kTileBytes);
+    load_rows_psi(P, cx, tPsi, ld);
+    load_rows_dy(P, cx, tY, ld);
+    load_tile(tSin, Sin, ld);
+    load_tile(tZin, Sin + kTileBytes, ld);
+    load_tile(tFS, FS, ld);
+    load_tile(tFZ, FS + kTileBytes, ld);
+    if (threadIdx.x == 0) tma_commit(ld);
   }
   load_ctx(P, sa, cx, kT);
   float* sS = sa.take(kR + 1);
@@ -395,7 +410,10 @@ __global__ void __launch_bounds__(kT) k_bwd_state_gates_tc(Params P) {
   pc.mark(32);
   if (tid < 32) fwd_scalars_warp(cx, sS, sZ, zZ);
   else if (tid < 64) adj_scalars_warp(cx, hS, hZS, hZZ);
-  async_wait();
+  async_wait();  // xf
+  tma_wait(ld, P.status);
+  zero_rows_from(tPsi, L);
+  zero_rows_from(tY, L);
   __syncthreads();
   phi_xform(P, tPsi);
   pc.mark(33);
@@ -471,7 +489,10 @@ __global__ void __launch_bounds__(kT) k_bwd_state_gates_tc(Params P) {
     });
     if (row == 0) pc.lap(25);
   } else {  // state epilogue (warpgroups 2, 3): d psi, X[D_q][S_in|Z_in]; the Gram block arrives meanwhile
-    async_copy_tile(tG, reinterpret_cast<const unsigned char*>(P.gt) + cid * kTileBytes, 256, 256);
+    if (tid == 256) {
+      tma_tile(tG, reinterpret_cast<const unsigned char*>(P.gt) + cid * kTileBytes, ld.bar);
+      tma_commit(ld);
+    }
     const int q = row;
     float a = 0.f, b = 0.f;
     const float ss = q < L ? sS[q] : 0.f, sz = q < L ? sZ[q] : 0.f;
@@ -516,9 +537,10 @@ __global__ void __launch_bounds__(kT) k_bwd_state_gates_tc(Params P) {
       xs[row] = t;
     }
     if (tid == 256) pc.lap(26);
-    async_wait();
+    tma_wait(ld, P.status);
     if (tid == 256) pc.lap(27);
   }
+  if (tid == 0) tma_wait(ld, P.status);  // the Gram tile, before thread 0 issues the MMAs that read it
   pc.mark(35);
   smem_to_tc();  // coefficient tiles, G, xq, xs ready; the state accumulators are read
   if (tid == 0) {
@@ -735,16 +757,21 @@ __global__ void __launch_bounds__(kThreads) k_bwd_buf_tc(Params P) {
 //   dk = d phi * fmap'(k), dq = d psi * fmap'(q)
 // (tensor feature map: d phi is left in the scratch for its own backward).
 // ===========================================================================
-__global__ void __launch_bounds__(kT) k_bwd_finalize_tc(Params P) {
+__global__ void __launch_bounds__(kT) k_bwd_finalize_tc(const __grid_constant__ Params P) {
   PhaseClock pc;
   extern __shared__ __align__(1024) unsigned char sm[];
   unsigned char* tDD = sm;               // d delta rows (bf16)
   unsigned char* tSR = sm + kTileBytes;  // S_ref
-  __shared__ uint64_t mbar;
+  __shared__ uint64_t mbar, lbar;
   __shared__ uint32_t tbase;
   const int n = blockIdx.y, p0 = blockIdx.x * kR, e = P.e, tid = threadIdx.x, row = row_of(), wg = wg_of();
   const int TT = min(kR, P.T - p0);
-  async_copy_tile(tSR, P.srb + (int64_t)n * kTileBytes);
+  TmaBatch ld{&lbar, 0};
+  if (tid == 0) {
+    tma_init(ld);
+    tma_tile(tSR, P.srb + (int64_t)n * kTileBytes, ld.bar);
+    tma_commit(ld);
+  }
   Sync sy{&mbar, &tbase, 0, P.status};
   const uint32_t tm = tc_setup(sy, 128);
   const int e1 = e > 1 ? e - 1 : 1;
@@ -781,7 +808,7 @@ __global__ void __launch_bounds__(kT) k_bwd_finalize_tc(Params P) {
     }
   }, 0, kT, /*rowmajor=*/true);
   pc.mark(56);
-  async_wait();
+  if (tid == 0) tma_wait(ld, P.status);  // S_ref tile, read only by the MMA thread 0 issues
   smem_to_tc();
   if (tid == 0) mma_chain(tm, op(tDD, kD, 0), op(tSR, kD, 1), 8, kD, false);  // d delta S_ref
   // while the MMA runs: dq, and du in token-gate mode

@@ -334,6 +334,78 @@ __device__ __forceinline__ void xform_rows(unsigned char* tile, int rows, F f, i
   }
 }
 
+// ---------------------------------------------------------------------------
+// TMA tile loads. One thread issues them; they complete on a CTA mbarrier with
+// a transaction count (expect_tx per tile, one arrive per batch), and every
+// thread that reads the tiles waits on the barrier's phase.
+//  * rows of a bf16 [N, T, 128] operand: 16 cp.async.bulk.tensor loads of one
+//    8-row group each through the 4-D descriptor in Params (rows outside
+//    [0, T) of the unit arrive as zeros);
+//  * a 32 KB tile already in the core-matrix layout: one cp.async.bulk copy.
+// No multicast: every load reads this GPU's memory into this CTA only.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;\n" ::"r"(umma::smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(umma::smem_u32(bar)) : "memory");
+}
+// 128 rows [row0, row0 + 128) of unit n into `tile` (issuing thread only).
+__device__ __forceinline__ void tma_rows(const CUtensorMap* map, unsigned char* tile, int n, int row0,
+                                         uint64_t* bar) {
+  mbar_expect_tx(bar, kTileBytes);
+#pragma unroll 1
+  for (int g = 0; g < kR / 8; ++g) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4, %5}], [%6];\n" ::"r"(umma::smem_u32(tile + g * (kTileBytes / 16))),
+        "l"(map), "r"(0), "r"(row0 + 8 * g), "r"(0), "r"(n), "r"(umma::smem_u32(bar))
+        : "memory");
+  }
+}
+// A 32 KB core-matrix tile from global memory (16-byte aligned) into `tile` (issuing thread only).
+__device__ __forceinline__ void tma_tile(unsigned char* tile, const void* src, uint64_t* bar) {
+  mbar_expect_tx(bar, kTileBytes);
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+          umma::smem_u32(tile)),
+      "l"(src), "r"(kTileBytes), "r"(umma::smem_u32(bar))
+      : "memory");
+}
+// Loads in flight on one barrier.
+struct TmaBatch {
+  uint64_t* bar;
+  uint32_t phase;
+};
+__device__ __forceinline__ void tma_init(TmaBatch& b) {  // one thread, before the CTA barrier of tc_setup
+  umma::mbar_init(b.bar, 1);
+  b.phase = 0;
+}
+// The issuing thread closes the batch after its loads.
+__device__ __forceinline__ void tma_commit(TmaBatch& b) { mbar_arrive(b.bar); }
+// Bounded wait of the calling thread for the batch (every reader calls it). A
+// wait that runs out is recorded in the status word and waited once more, so
+// that no copy is left in flight into shared memory the CTA gives up.
+__device__ __forceinline__ void tma_wait(TmaBatch& b, int* status) {
+  if (!umma::mbar_wait(b.bar, b.phase)) {
+    if (status) atomicExch(status, kDevStatMmaTimeout);
+    umma::mbar_wait(b.bar, b.phase);
+  }
+  b.phase ^= 1u;
+}
+// Zero rows [from, 128) of a tile (the rows a 128-row TMA box brings in past the
+// chunk's last token); threads [first, first + count).
+__device__ __forceinline__ void zero_rows_from(unsigned char* tile, int from, int first = 0, int count = kT) {
+  const int me = (int)threadIdx.x - first;
+  if (me < 0 || me >= count || from >= kR) return;
+  const int units = (kR - from) * (kD / 8);
+  for (int x = me; x < units; x += count) {
+    const int r = from + x / (kD / 8), cb = x % (kD / 8);
+    *reinterpret_cast<uint4*>(tile + umma::unit_off(r, cb, kD)) = make_uint4(0u, 0u, 0u, 0u);
+  }
+}
+
 __device__ __forceinline__ float bf_at(const unsigned char* tile, int r, int c) {
   return __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(tile + umma::elem_off(r, c, kD)));
 }

@@ -157,6 +157,29 @@ __device__ __forceinline__ void async_rows_dy(const Params& P, const Ctx& cx, un
     return r < cx.L ? dy + ((int64_t)cx.n * P.T + cx.t0 + r) * P.dv : nullptr;
   }, P.dy, first, count);
 }
+// TMA forms (call from every thread; thread 0 issues, the batch's barrier
+// signals arrival). With the tensor feature map the fp32 phi rows are
+// converted synchronously by all threads instead.
+__device__ __forceinline__ void load_keys_phi(const Params& P, const Ctx& cx, unsigned char* tile, TmaBatch& b) {
+  if (P.fmode == ATLAS_FMAP_TENSOR) { fill_keys_phi(P, cx, tile); return; }
+  if (threadIdx.x == 0) tma_rows(&P.tm_k, tile, cx.n, cx.kp0, b.bar);
+}
+// Token rows of psi; rows >= L hold the next chunk's tokens until zero_rows_from(tile, L).
+__device__ __forceinline__ void load_rows_psi(const Params& P, const Ctx& cx, unsigned char* tile, TmaBatch& b) {
+  if (P.fmode == ATLAS_FMAP_TENSOR) { fill_rows_psi(P, cx, tile); return; }
+  if (threadIdx.x == 0) tma_rows(&P.tm_q, tile, cx.n, cx.t0, b.bar);
+}
+__device__ __forceinline__ void load_keys_delta(const Params& P, const Ctx& cx, unsigned char* tile, TmaBatch& b) {
+  if (threadIdx.x == 0) tma_rows(&P.tm_dl, tile, cx.n, cx.kp0, b.bar);
+}
+// Token rows of dy; rows >= L as for load_rows_psi.
+__device__ __forceinline__ void load_rows_dy(const Params& P, const Ctx& cx, unsigned char* tile, TmaBatch& b) {
+  if (threadIdx.x == 0) tma_rows(&P.tm_dy, tile, cx.n, cx.t0, b.bar);
+}
+__device__ __forceinline__ void load_tile(unsigned char* tile, const unsigned char* src, TmaBatch& b) {
+  if (threadIdx.x == 0) tma_tile(tile, src, b.bar);
+}
+
 // Named barrier over warpgroups 1..kWG-1 (the loaders while warpgroup 0 is busy).
 __device__ __forceinline__ void loaders_sync() { asm volatile("bar.sync 1, %0;\n" ::"n"(kT - 128) : "memory"); }
 
@@ -180,7 +203,7 @@ __global__ void __launch_bounds__(256) k_sref_tile(Params P) {
 //   delta[keys x d_v] = Phi[keys x d_phi] S_ref^T - V
 //   dS[d_v x d_phi]   = (diag(cS_end) delta)^T Phi,  dZ likewise with cZ_end
 // ===========================================================================
-__global__ void __launch_bounds__(kT) k_fwd_chunk_tc(Params P) {
+__global__ void __launch_bounds__(kT) k_fwd_chunk_tc(const __grid_constant__ Params P) {
   PhaseClock pc;
   extern __shared__ __align__(1024) unsigned char sm[];
   unsigned char* tPhi = sm;
@@ -188,12 +211,15 @@ __global__ void __launch_bounds__(kT) k_fwd_chunk_tc(Params P) {
   unsigned char* tDS = sm + 2 * kTileBytes;
   unsigned char* tDZ = tSref;
   SmemAlloc sa{reinterpret_cast<float*>(sm + 3 * kTileBytes), 0};
-  __shared__ uint64_t mbar;
+  __shared__ uint64_t mbar, lbar;
   __shared__ uint32_t tbase;
   Ctx cx;
   ctx_geom(P, cx);
-  async_keys_phi(P, cx, tPhi);
-  async_copy_tile(tSref, P.srb + (int64_t)cx.n * kTileBytes);
+  TmaBatch ld{&lbar, 0};
+  if (threadIdx.x == 0) tma_init(ld);
+  load_keys_phi(P, cx, tPhi, ld);
+  load_tile(tSref, P.srb + (int64_t)cx.n * kTileBytes, ld);
+  if (threadIdx.x == 0) tma_commit(ld);
   load_ctx(P, sa, cx, kT);
   float* cSe = sa.take(kR);
   float* cZe = sa.take(kR);
@@ -235,7 +261,7 @@ __global__ void __launch_bounds__(kT) k_fwd_chunk_tc(Params P) {
       o[0] = cx.al[0] * Asuf[0]; o[1] = -cx.be[0] * Hs[0]; o[2] = cx.be[0] * Bsuf[0]; o[3] = 0.f;
     }
   }
-  async_wait();
+  tma_wait(ld, P.status);
   __syncthreads();
   phi_xform(P, tPhi);
   pc.mark(41);
@@ -324,7 +350,7 @@ __global__ void __launch_bounds__(kT) k_fwd_chunk_tc(Params P) {
 //   y = (cS o Psi Phi^T) delta + diag(sS) Psi S_in^T + diag(sZ) Psi Z_in^T
 // (chunk 0 with a carried buffer adds its dense terms in k_fwd_buf_y).
 // ===========================================================================
-__global__ void __launch_bounds__(kT) k_fwd_out_tc(Params P) {
+__global__ void __launch_bounds__(kT) k_fwd_out_tc(const __grid_constant__ Params P) {
   PhaseClock pc;
   extern __shared__ __align__(1024) unsigned char sm[];
   unsigned char* tPsi = sm;
@@ -334,17 +360,20 @@ __global__ void __launch_bounds__(kT) k_fwd_out_tc(Params P) {
   unsigned char* tSin = sm + 4 * kTileBytes;
   unsigned char* tZin = sm + 5 * kTileBytes;
   SmemAlloc sa{reinterpret_cast<float*>(sm + 6 * kTileBytes), 0};
-  __shared__ uint64_t mbar;
+  __shared__ uint64_t mbar, lbar;
   __shared__ uint32_t tbase;
   Ctx cx;
   ctx_geom(P, cx);
+  TmaBatch ld{&lbar, 0};
+  if (threadIdx.x == 0) tma_init(ld);
   {  // every operand tile in flight before anything else
     const unsigned char* Sin = P.stb + ((int64_t)cx.n * P.nch + cx.c) * 2 * kTileBytes;
-    async_rows_psi(P, cx, tPsi);
-    async_keys_phi(P, cx, tPhi);
-    async_keys_delta(P, cx, tDl);
-    async_copy_tile(tSin, Sin);
-    async_copy_tile(tZin, Sin + kTileBytes);
+    load_rows_psi(P, cx, tPsi, ld);
+    load_keys_phi(P, cx, tPhi, ld);
+    load_keys_delta(P, cx, tDl, ld);
+    load_tile(tSin, Sin, ld);
+    load_tile(tZin, Sin + kTileBytes, ld);
+    if (threadIdx.x == 0) tma_commit(ld);
   }
   zero_tile(tMs);
   load_ctx(P, sa, cx, kT);
@@ -361,11 +390,14 @@ __global__ void __launch_bounds__(kT) k_fwd_out_tc(Params P) {
   } else if (wg == 1 && row < 32) {
     fwd_scalars_warp(cx, sSv, sZv, zZv);  // state-path scalars before token i
   }
-  async_wait();
   if (wg > 0) {
+    tma_wait(ld, P.status);
+    zero_rows_from(tPsi, L, 128, kT - 128);
     loaders_sync();
     phi_xform(P, tPsi, 128, kT - 128);
     phi_xform(P, tPhi, 128, kT - 128);
+  } else {
+    tma_wait(ld, P.status);  // the MMAs read what warpgroups 1.. did not touch too
   }
   pc.mark(17);
   smem_to_tc();
