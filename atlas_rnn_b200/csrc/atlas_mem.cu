@@ -10,6 +10,7 @@
 #include "chunk_kernels.cuh"
 #include "tc_bwd.cuh"
 #include "tc_scan.cuh"
+#include "tc_fmap.cuh"
 #include "decode.cuh"
 #include "scan_op.cuh"
 #include "carry.cuh"
@@ -39,6 +40,12 @@ int tc_groups(const AtlasMemShape* s) {
   return kTcAll;
 }
 
+// The tensor feature map runs on tensor cores (tc_fmap.cuh) for bf16 io and
+// the head sizes it handles; otherwise on CUDA cores (k_fmap_tensor_*).
+bool fmap_tc(const AtlasMemShape* s) {
+  return s->fmap_mode == ATLAS_FMAP_TENSOR && tc::fmap_tc_ok(s->d_k, s->d_phi, s->dtype_io == ATLAS_BF16);
+}
+
 // Tokens per chunk: the caller's choice, else 128 - e when every chunk kernel
 // runs on tensor cores (keys = chunk + e - 1 fill a 128-row tile), else the
 // CUDA-core kernels' 32.
@@ -51,7 +58,7 @@ int chunk_of(const AtlasMemShape* s) {
 struct Layout {
   int C, nch;
   size_t saved, fwd, bwd;
-  size_t st, delta, ST, cs, phik, phiq, dlb, stb, srb;         // in saved
+  size_t st, delta, ST, cs, phik, phiq, dlb, stb, srb, projb;  // in saved
   size_t adj, acs, dpsi, ddel, dphiR, hdd, hdp, du, hdu;       // in bwd scratch
   size_t xq, xf, xs, gt, adjb, ddb, dpb, dpsib;                 // in bwd scratch (tensor-core path)
 };
@@ -75,6 +82,7 @@ Layout make_layout(const AtlasMemShape* s) {
   L.cs = put(N * nch * 4 * 4);
   L.phik = tens ? put(N * T * s->d_phi * 4) : 0;
   L.phiq = tens ? put(N * T * s->d_phi * 4) : 0;
+  L.projb = fmap_tc(s) ? put((size_t)(s->d_k + 1) * tc::fm_chunk_bytes(s->d_k, s->d_phi)) : 0;
   L.saved = o;
   L.fwd = 0;
   o = 0;
@@ -163,7 +171,8 @@ int ensure_attrs() {
                       (const void*)tc::k_bwd_finalize_tc, (const void*)tc::k_bwd_dsref_tc, (const void*)tc::k_bwd_keys_tc,
                       (const void*)tc::k_fwd_scan_tc<1>, (const void*)tc::k_fwd_scan_tc<2>,
                       (const void*)tc::k_fwd_scan_tc<4>, (const void*)tc::k_bwd_scan_tc<1>,
-                      (const void*)tc::k_bwd_scan_tc<2>, (const void*)tc::k_bwd_scan_tc<4>};
+                      (const void*)tc::k_bwd_scan_tc<2>, (const void*)tc::k_bwd_scan_tc<4>,
+                      (const void*)tc::k_fmap_fwd_tc, (const void*)tc::k_fmap_bwd_tc};
   for (const void* k : ks) {
     cudaFuncAttributes fa;
     if (cudaFuncGetAttributes(&fa, k) != cudaSuccess) return ATLAS_ERR_LAUNCH;
@@ -248,6 +257,7 @@ Params make_params(const AtlasMemShape* s, const Layout& L, const AtlasMemFwd* f
     P.cs = (float*)(sv + L.cs);
     P.phik = s->fmap_mode == ATLAS_FMAP_TENSOR ? (float*)(sv + L.phik) : nullptr;
     P.phiq = s->fmap_mode == ATLAS_FMAP_TENSOR ? (float*)(sv + L.phiq) : nullptr;
+    P.projb = fmap_tc(s) ? (unsigned char*)(sv + L.projb) : nullptr;
   }
   if (scratch) {
     char* sc = (char*)scratch;
@@ -270,12 +280,12 @@ Params make_params(const AtlasMemShape* s, const Layout& L, const AtlasMemFwd* f
 enum KernelId {
   KID_FMAP_FWD, KID_FWD_CHUNK, KID_FWD_SCAN, KID_FWD_OUT, KID_BUF_OUT, KID_BWD_CHUNK, KID_BWD_SCAN,
   KID_BWD_GRADS, KID_BWD_BUFOUT, KID_BWD_FINAL, KID_BWD_DSREF, KID_FMAP_BWD, KID_FWD_CHUNK_TC, KID_FWD_OUT_TC, KID_FWD_BUF_Y,
-  KID_BWD_CHUNK_TC, KID_BWD_STATE_GATES_TC, KID_BWD_BUF_TC, KID_BWD_FINAL_TC, KID_BWD_DSREF_TC, KID_BWD_KEYS_TC, KID_SREF_TILE, KID_DECODE, KID_SCAN_OP_FWD, KID_SCAN_OP_BWD, KID_CARRY, KID_DWCONV_FWD, KID_DWCONV_BWD, KID_HEADPREP_FWD, KID_HEADPREP_BWD, KID_COUNT
+  KID_BWD_CHUNK_TC, KID_BWD_STATE_GATES_TC, KID_BWD_BUF_TC, KID_BWD_FINAL_TC, KID_BWD_DSREF_TC, KID_BWD_KEYS_TC, KID_SREF_TILE, KID_DECODE, KID_SCAN_OP_FWD, KID_SCAN_OP_BWD, KID_CARRY, KID_DWCONV_FWD, KID_DWCONV_BWD, KID_HEADPREP_FWD, KID_HEADPREP_BWD, KID_PROJ_TILES, KID_FMAP_FWD_TC, KID_FMAP_BWD_TC, KID_COUNT
 };
 const char* const kKernelNames[KID_COUNT] = {
   "k_fmap_tensor_fwd", "k_fwd_chunk", "k_fwd_scan", "k_fwd_out", "k_buf_out", "k_bwd_chunk", "k_bwd_scan",
   "k_bwd_grads", "k_bwd_bufout", "k_bwd_finalize", "k_bwd_dsref", "k_fmap_tensor_bwd", "k_fwd_chunk_tc", "k_fwd_out_tc", "k_fwd_buf_y",
-  "k_bwd_chunk_tc", "k_bwd_state_gates_tc", "k_bwd_buf_tc", "k_bwd_finalize_tc", "k_bwd_dsref_tc", "k_bwd_keys_tc", "k_sref_tile", "k_decode_step", "k_scan_op_fwd", "k_scan_op_bwd", "k_compose_carries", "k_dwconv3_fwd", "k_dwconv3_bwd", "k_head_prep_fwd", "k_head_prep_bwd"};
+  "k_bwd_chunk_tc", "k_bwd_state_gates_tc", "k_bwd_buf_tc", "k_bwd_finalize_tc", "k_bwd_dsref_tc", "k_bwd_keys_tc", "k_sref_tile", "k_decode_step", "k_scan_op_fwd", "k_scan_op_bwd", "k_compose_carries", "k_dwconv3_fwd", "k_dwconv3_bwd", "k_head_prep_fwd", "k_head_prep_bwd", "k_proj_tiles", "k_fmap_fwd_tc", "k_fmap_bwd_tc"};
 
 constexpr int kMaxTimed = 8192;
 struct Prof {
@@ -404,7 +414,13 @@ int run_fwd_local(const AtlasMemShape* s, const Params& P, cudaStream_t st) {
   const Smem m = smem_sizes(s, P.C);
   const dim3 gch(P.nch, P.N);
   if (P.fmode == ATLAS_FMAP_TENSOR) {
-    LAUNCH(KID_FMAP_FWD, k_fmap_tensor_fwd, dim3((P.T + kFmTile - 1) / kFmTile, P.N, 2), m.fmf, st, P);
+    if (fmap_tc(s)) {
+      LAUNCH(KID_PROJ_TILES, tc::k_proj_tiles, dim3(P.dk + 1), 0, st, P);
+      LAUNCH_T(KID_FMAP_FWD_TC, tc::k_fmap_fwd_tc, dim3((P.T + tc::kR - 1) / tc::kR, P.N, 2), tc::kFmT,
+               tc::fm_fwd_smem(P.dk, P.dphi), st, P);
+    } else {
+      LAUNCH(KID_FMAP_FWD, k_fmap_tensor_fwd, dim3((P.T + kFmTile - 1) / kFmTile, P.N, 2), m.fmf, st, P);
+    }
   }
   if (tc_groups(s) & 1) {
     LAUNCH(KID_SREF_TILE, tc::k_sref_tile, dim3(P.N), 0, st, P);
@@ -474,7 +490,11 @@ int run_bwd_finish(const AtlasMemShape* s, const Params& P, cudaStream_t st) {
     }
   }
   if (P.fmode == ATLAS_FMAP_TENSOR && (P.dk_ || P.dq_)) {
-    LAUNCH(KID_FMAP_BWD, k_fmap_tensor_bwd, dim3((P.T + kFmTile - 1) / kFmTile, P.N, 2), m.fmb, st, P);
+    if (fmap_tc(s))
+      LAUNCH_T(KID_FMAP_BWD_TC, tc::k_fmap_bwd_tc, dim3((P.T + tc::kR - 1) / tc::kR, P.N, 2), tc::kFbT,
+               tc::fm_bwd_smem(P.dk, P.dphi), st, P);
+    else
+      LAUNCH(KID_FMAP_BWD, k_fmap_tensor_bwd, dim3((P.T + kFmTile - 1) / kFmTile, P.N, 2), m.fmb, st, P);
   }
   return ATLAS_OK;
 }

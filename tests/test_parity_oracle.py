@@ -187,3 +187,19 @@ CASES_TC = [
 @pytest.mark.parametrize("state_scale", [0.0, 0.1])
 def test_bf16_tensor_core_path(native_lib, w, state_scale):
     run_case(w, state_scale=state_scale)
+
+
+# tensor feature map on tensor cores (bf16, d_k in {16, 32, 64}, d_phi up to 256): the
+# [x; vec(x x^T)] Proj GEMM of rnn_memory.py:125-130 and its backward
+CASES_FMAP_TC = [
+    W("fmap_tc_d16_phi128_tcrec", 300, d=16, dphi=128, dv=128, e=3, gate="token", fm="tensor", deg=2,
+      dtype=torch.bfloat16),
+    W("fmap_tc_d32_phi64", 200, d=32, dphi=64, dv=48, e=2, gate="window", fm="tensor", deg=2, dtype=torch.bfloat16),
+    W("fmap_tc_d64_phi256_e16", 260, d=64, dphi=256, dv=128, e=16, gate="token", fm="tensor", deg=2,
+      dtype=torch.bfloat16),
+]
+
+
+@pytest.mark.parametrize("w", CASES_FMAP_TC, ids=lambda w: w.name)
+def test_tensor_fmap_tensor_cores(native_lib, w):
+    run_case(w, state_scale=0.1)
