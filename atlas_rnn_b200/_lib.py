@@ -99,6 +99,13 @@ def lib():
         L.atlas_mem_selftest_umma.argtypes = [_vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                               ctypes.c_int, _vp, _vp]
         L.atlas_mem_selftest_umma.restype = ctypes.c_int
+        L.atlas_fmap_tensor_workspace.argtypes = [ctypes.c_int, ctypes.c_int]
+        L.atlas_fmap_tensor_workspace.restype = ctypes.c_size_t
+        L.atlas_fmap_tensor_forward.argtypes = [ctypes.c_int64, ctypes.c_int, ctypes.c_int, _vp, _vp, _vp, _vp, _vp, _vp]
+        L.atlas_fmap_tensor_forward.restype = ctypes.c_int
+        L.atlas_fmap_tensor_backward.argtypes = [ctypes.c_int64, ctypes.c_int, ctypes.c_int, _vp, _vp, _vp, _vp, _vp,
+                                                 _vp]
+        L.atlas_fmap_tensor_backward.restype = ctypes.c_int
         L.atlas_mem_read_status.argtypes = [_vp, _vp]
         L.atlas_mem_read_status.restype = ctypes.c_int
         L.atlas_mem_selftest_wait_timeout.argtypes = [_vp, ctypes.c_int, _vp]

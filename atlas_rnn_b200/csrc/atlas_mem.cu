@@ -975,6 +975,51 @@ int atlas_mem_selftest_umma(const void* A, const void* B, float* D, int N, int K
   return ATLAS_OK;
 }
 
+size_t atlas_fmap_tensor_workspace(int d_k, int d_phi) {
+  if (!tc::fmap_tc_ok(d_k, d_phi, 1)) return 0;
+  return (size_t)(d_k + 1) * tc::fm_chunk_bytes(d_k, d_phi);
+}
+
+namespace {
+Params fmap_params(int64_t rows, int d_k, int d_phi, const void* x, const float* proj, void* proj_tiles) {
+  Params P{};
+  P.N = 1; P.T = (int)rows; P.dk = d_k; P.dphi = d_phi; P.bf = 1; P.fmode = ATLAS_FMAP_TENSOR; P.fdeg = 2;
+  P.k = x; P.proj = proj; P.projb = (unsigned char*)proj_tiles; P.fm_bf16 = 1;
+  return P;
+}
+}  // namespace
+
+int atlas_fmap_tensor_forward(int64_t rows, int d_k, int d_phi, const void* x, const float* proj, void* proj_tiles,
+                              void* phi, int* status, void* stream) {
+  if (!x || !proj || !proj_tiles || !phi || rows < 1) return ATLAS_ERR_INVALID_ARG;
+  if (!tc::fmap_tc_ok(d_k, d_phi, 1) || rows > ((int64_t)1 << 30)) return ATLAS_ERR_UNSUPPORTED;
+  int v;
+  if ((v = ensure_attrs())) return v;
+  Params P = fmap_params(rows, d_k, d_phi, x, proj, proj_tiles);
+  P.phik = (float*)phi;
+  P.status = status;
+  cudaStream_t st = (cudaStream_t)stream;
+  LAUNCH(KID_PROJ_TILES, tc::k_proj_tiles, dim3(d_k + 1), 0, st, P);
+  LAUNCH_T(KID_FMAP_FWD_TC, tc::k_fmap_fwd_tc, dim3((unsigned)((rows + tc::kR - 1) / tc::kR), 1, 1), tc::kFmT,
+           tc::fm_fwd_smem(d_k, d_phi), st, P);
+  return ATLAS_OK;
+}
+
+int atlas_fmap_tensor_backward(int64_t rows, int d_k, int d_phi, const void* x, const void* proj_tiles,
+                               const void* dphi, void* dx, int* status, void* stream) {
+  if (!x || !proj_tiles || !dphi || !dx || rows < 1) return ATLAS_ERR_INVALID_ARG;
+  if (!tc::fmap_tc_ok(d_k, d_phi, 1) || rows > ((int64_t)1 << 30)) return ATLAS_ERR_UNSUPPORTED;
+  int v;
+  if ((v = ensure_attrs())) return v;
+  Params P = fmap_params(rows, d_k, d_phi, x, nullptr, const_cast<void*>(proj_tiles));
+  P.dphiR = (float*)const_cast<void*>(dphi);
+  P.dk_ = dx;
+  P.status = status;
+  LAUNCH_T(KID_FMAP_BWD_TC, tc::k_fmap_bwd_tc, dim3((unsigned)((rows + tc::kR - 1) / tc::kR), 1, 1), tc::kFbT,
+           tc::fm_bwd_smem(d_k, d_phi), (cudaStream_t)stream, P);
+  return ATLAS_OK;
+}
+
 int atlas_mem_read_status(const int* status, void* stream) {
   if (!status) return ATLAS_ERR_INVALID_ARG;
   if (cudaStreamSynchronize((cudaStream_t)stream) != cudaSuccess) return ATLAS_ERR_LAUNCH;

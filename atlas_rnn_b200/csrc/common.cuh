@@ -40,6 +40,7 @@ struct Params {
   float *cs;     // [N][nch][4] chunk transform scalars (a, b, c)
   float *phik, *phiq;  // [N][T][dphi] tensor feature map only
   unsigned char* projb;  // tensor feature map on tensor cores: Proj as dk + 1 bf16 tiles of dk x dphi
+  int fm_bf16;           // stand-alone feature map: phi out / d phi in as bf16 (else fp32)
   // backward scratch
   float *adj;    // [N][nch][2][dv][dphi]: adjoint deltas, then adjoint at chunk end
   float *acs;    // [N][nch][4]

@@ -156,12 +156,17 @@ __global__ void __launch_bounds__(kFmT) k_fmap_fwd_tc(Params P) {
   } else {
     // epilogue: warp w reads TMEM lanes 32 (w % 4).., warpgroup g columns [g dphi/2, (g+1) dphi/2)
     const int row = tid & 127, g = tid >> 7, half = dphi / 2;
-    float* dst = (isq ? P.phiq : P.phik) + ((int64_t)n * P.T + t0 + row) * dphi;
+    const int64_t off = ((int64_t)n * P.T + t0 + row) * dphi;
+    float* dst = (isq ? P.phiq : P.phik) + off;
+    __nv_bfloat16* dsth = reinterpret_cast<__nv_bfloat16*>(isq ? P.phiq : P.phik) + off;
     for (int c16 = g * half; c16 < (g + 1) * half; c16 += 16) {
       float a[16];
       umma::tmem_ld16(tm + ((uint32_t)((tid >> 5) & 3) * 32 << 16) + c16, a);
       umma::tmem_ld_wait();
-      if (row < TT) st16f(dst + c16, a);
+      if (row < TT) {
+        if (P.fm_bf16) st16bf(dsth + c16, a);
+        else st16f(dst + c16, a);
+      }
     }
   }
   umma::fence_before();
@@ -202,14 +207,16 @@ __global__ void __launch_bounds__(kFbT) k_fmap_bwd_tc(Params P) {
     umma::tmem_relinquish();
   }
   {  // d phi rows -> bf16 operand tile (rows past the unit's end are zero)
-    const float* g = (isq ? P.dpsi : P.dphiR) + ((int64_t)n * P.T + t0) * dphi;
+    const int64_t g0 = ((int64_t)n * P.T + t0) * dphi;
+    const float* g = (isq ? P.dpsi : P.dphiR) + g0;
     const int cpr = dphi / 8;
     for (int u = tid; u < kR * cpr; u += kFbT) {
       int r, cb;
       unit_rc(u, cpr, r, cb);
       float v[8];
-      if (r < TT) ld8f(g + (int64_t)r * dphi + cb * 8, v);
-      else zero8(v);
+      if (r >= TT) zero8(v);
+      else if (P.fm_bf16) ld8io(isq ? P.dpsi : P.dphiR, g0 + (int64_t)r * dphi + cb * 8, 1, v);
+      else ld8f(g + (int64_t)r * dphi + cb * 8, v);
       *reinterpret_cast<uint4*>(Ag + 16 * u) = pack_unit(v);
     }
   }

@@ -174,6 +174,81 @@ def _padded_call(spec: Spec, d_v: int, d_phi: int, k, q, v, lr, decay, beta, gat
     return y[..., :d_v], cut(S_end), cut(Z_end), cut(buf_out)
 
 
+class FmapTensorFn(torch.autograd.Function):
+    """phi = [x; vec(x x^T)] Proj (rnn_memory.py:125-130) for bf16 x [..., d_k] on the
+    tensor cores (atlas_fmap_tensor_forward / _backward); phi bf16 [..., d_phi]. Proj is
+    a fixed buffer (no gradient)."""
+
+    @staticmethod
+    def forward(ctx, x, proj):
+        d_k, d_phi = x.shape[-1], proj.shape[-1]
+        rows = x.numel() // d_k
+        L = _lib.lib()
+        tiles = torch.empty(L.atlas_fmap_tensor_workspace(d_k, d_phi), dtype=torch.uint8, device=x.device)
+        phi = torch.empty(*x.shape[:-1], d_phi, dtype=torch.bfloat16, device=x.device)
+        p = _lib.ptr
+        _lib.check(L.atlas_fmap_tensor_forward(rows, d_k, d_phi, p(x), p(proj), p(tiles), p(phi),
+                                               p(_lib.status_word(x.device)), _stream(x.device)), "fmap forward")
+        ctx.save_for_backward(x, tiles)
+        ctx.d_phi = d_phi
+        return phi
+
+    @staticmethod
+    def backward(ctx, dphi):
+        x, tiles = ctx.saved_tensors
+        d_k = x.shape[-1]
+        dphi = dphi.to(torch.bfloat16).contiguous()
+        dx = torch.empty_like(x)
+        p = _lib.ptr
+        _lib.check(_lib.lib().atlas_fmap_tensor_backward(x.numel() // d_k, d_k, ctx.d_phi, p(x), p(tiles),
+                                                         p(dphi), p(dx), p(_lib.status_word(x.device)),
+                                                         _stream(x.device)), "fmap backward")
+        return dx, None
+
+
+def _fmap_tc_ok(d_k: int, d_phi: int) -> bool:
+    return 16 <= d_k <= 64 and d_k % 16 == 0 and 16 <= d_phi <= 256 and d_phi % 16 == 0
+
+
+def _split_phi_call(k, q, v, lr, decay, beta, gate, S_ref, S0, Z0, buf, proj, *, window, gate_mode, fmap_degree,
+                    chunk):
+    """The tensor feature map with d_phi = H * 128 (256): phi(k), phi(q) on
+    the tensor cores, then the recurrence as H units of d_phi = 128 each. The state splits by
+    columns, S = [S_1 | .. | S_H], and every part evolves with the same gates and the same
+    delta_t = S_ref phi_t - v_t = sum_g S_ref,g phi_g,t - v_t, so part h is the d_phi = 128
+    recurrence with keys phi_h, queries psi_h, S_ref,h and values
+    v_h = v - sum_{g != h} phi_g S_ref,g^T (which reproduces delta exactly); y is the sum of
+    the parts' outputs (S_{t-1} psi_t = sum_h S_h,t-1 psi_h,t, the within-chunk terms too),
+    and S_end, Z_end and the omega buffer are the parts side by side. The H parts run as
+    H N units in one call of the tensor-core kernels; autograd carries the gradients through
+    the split, the value adjustment (one batched GEMM) and the feature map."""
+    N, T, _ = k.shape
+    d_phi = S_ref.shape[-1]
+    H = d_phi // TC_D
+    phik = FmapTensorFn.apply(k.contiguous(), proj)
+    phiq = FmapTensorFn.apply(q.contiguous(), proj)
+    parts = lambda t: [t[..., h * TC_D:(h + 1) * TC_D] for h in range(H)]
+    pk, pq, pr = parts(phik), parts(phiq), parts(S_ref)
+    preds = [torch.bmm(pk[h].float(), pr[h].transpose(1, 2)) for h in range(H)]  # phi_h S_ref,h^T, fp32
+    total = preds[0]
+    for h in range(1, H):
+        total = total + preds[h]
+    vf = v.float()
+    vs = [(vf - (total - preds[h])).to(v.dtype) for h in range(H)]
+    cat = lambda ts: None if ts is None else torch.cat(ts, dim=0).contiguous()
+    rep = lambda t: None if t is None else t.repeat(H, *([1] * (t.dim() - 1)))
+    colparts = lambda t: None if t is None else cat(parts(t))
+    y2, S2, Z2, b2 = memory_recurrence(cat(pk), cat(pq), cat(vs), rep(lr), rep(decay), rep(beta), rep(gate),
+                                       S_ref=cat(pr), S0=colparts(S0), Z0=colparts(Z0), omega_buffer=colparts(buf),
+                                       window=window, gate_mode=gate_mode, fmap_mode="off", fmap_degree=1,
+                                       chunk=chunk)
+    y = y2[:N]
+    for h in range(1, H):
+        y = y + y2[h * N:(h + 1) * N]
+    join = lambda t: None if t is None else torch.cat([t[h * N:(h + 1) * N] for h in range(H)], dim=-1)
+    return y, join(S2), join(Z2), join(b2)
+
+
 def _chunk_ref_mode(k, q, v, lr, decay, beta, gate, *, S0, Z0, omega_buffer, window, gate_mode, fmap_mode,
                     fmap_degree, proj, chunk, ref_chunk):
     """ref_mode 'chunk' as consecutive calls whose reference state is their own start state."""
@@ -229,6 +304,19 @@ def memory_recurrence(k: Tensor, q: Tensor, v: Tensor, lr: Tensor, decay: Tensor
     io = torch.bfloat16 if k.dtype == torch.bfloat16 else torch.float32
     if torch.is_autocast_enabled("cuda") and torch.get_autocast_dtype("cuda") == torch.bfloat16:
         io = torch.bfloat16  # a matmul-like op under bf16 autocast: bf16 operands, fp32 state and accumulation
+    d_phi = S_ref.shape[-1]
+    if (fmap_mode == "tensor" and fmap_degree > 1 and io == torch.bfloat16 and heads_padded_from is None
+            and d_phi > TC_D and d_phi % TC_D == 0 and v.shape[-1] <= TC_D and window <= 16
+            and _fmap_tc_ok(k.shape[-1], d_phi) and os.environ.get("ATLAS_MEM_TC", "1") != "0"):
+        f32 = lambda t: None if t is None else t.to(torch.float32)
+        y, S_end, Z_end, buf_out = _split_phi_call(
+            _io(k, io), _io(q, io), _io(v, io), _io(lr, io), _io(decay, io), _io(beta, io), _io(gate, io),
+            f32(S_ref), f32(S0), f32(Z0) if beta is not None else None, f32(omega_buffer) if window > 1 else None,
+            proj.to(torch.float32).contiguous(), window=window, gate_mode=gate_mode, fmap_degree=fmap_degree,
+            chunk=chunk)
+        S_end = S_end.to(S0.dtype)
+        Z_end = Z_end.to(S0.dtype) if beta is not None else None
+        return y, S_end, Z_end, buf_out
     if gate is None:
         gm = _lib.GATE_NONE
     elif gate_mode == "window" or (gate_mode is None and gate.dim() == 3):

@@ -124,6 +124,26 @@ typedef struct AtlasMemBwd {
   int* status;           /* optional device-visible status word, see below      */
 } AtlasMemBwd;
 
+/* ---- tensor feature map on its own (the 'tensor' mode of
+ * PolynomialFeatureMap, rnn_memory.py:106-111,125-130):
+ *   phi = [x ; vec(x x^T)] Proj,  x [rows, d_k] bf16, Proj [d_k + d_k^2, d_phi] fp32,
+ *   phi [rows, d_phi] bf16 out,
+ * on tensor cores without forming the d_k + d_k^2 wide rows. For bf16 io,
+ * d_k in {16, 32, 48, 64} and d_phi a multiple of 16 up to 256; other shapes
+ * return ATLAS_ERR_UNSUPPORTED (atlas_mem_forward still handles them in its
+ * own tensor-mode path). `proj_tiles` is a caller workspace of
+ * atlas_fmap_tensor_workspace(d_k, d_phi) bytes: the forward fills it with
+ * Proj in bf16 and the backward reads it, so it must stay untouched in
+ * between. The backward writes dx [rows, d_k] (bf16) from d phi [rows, d_phi]
+ * (bf16); Proj is a fixed buffer and gets no gradient. `status`: optional
+ * device status word, as below. The reference computes the same product with
+ * einsum + matmul in PolynomialFeatureMap.forward (rnn_memory.py:125-130). */
+size_t atlas_fmap_tensor_workspace(int d_k, int d_phi);
+int atlas_fmap_tensor_forward(int64_t rows, int d_k, int d_phi, const void* x, const float* proj,
+                              void* proj_tiles, void* phi, int* status, void* stream);
+int atlas_fmap_tensor_backward(int64_t rows, int d_k, int d_phi, const void* x, const void* proj_tiles,
+                               const void* dphi, void* dx, int* status, void* stream);
+
 /* Device status word (`status` in AtlasMemFwd / AtlasMemBwd; NULL = none).
  * Every wait of a kernel for its tensor-core work is bounded. When one runs
  * out, the kernel writes ATLAS_DEVSTAT_MMA_TIMEOUT to *status, lets its copies

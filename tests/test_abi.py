@@ -15,7 +15,7 @@ HEADER = os.path.join(ROOT, "include", "atlas_mem.h")
 
 def declared_functions():
     src = open(HEADER).read()
-    return sorted(set(re.findall(r"^\s*(?:int|const char\*|size_t|long long)\s+(atlas_mem_\w+)\s*\(", src, re.M)))
+    return sorted(set(re.findall(r"^\s*(?:int|const char\*|size_t|long long)\s+(atlas_\w+)\s*\(", src, re.M)))
 
 
 def test_header_declares_entry_points():

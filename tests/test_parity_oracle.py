@@ -197,6 +197,9 @@ CASES_FMAP_TC = [
     W("fmap_tc_d32_phi64", 200, d=32, dphi=64, dv=48, e=2, gate="window", fm="tensor", deg=2, dtype=torch.bfloat16),
     W("fmap_tc_d64_phi256_e16", 260, d=64, dphi=256, dv=128, e=16, gate="token", fm="tensor", deg=2,
       dtype=torch.bfloat16),
+    # d_phi = 256 with a narrower value head: the column parts run the zero-padded tensor-core path
+    W("fmap_tc_d32_phi256_dv64_window", 200, d=32, dphi=256, dv=64, e=4, gate="window", fm="tensor", deg=2,
+      dtype=torch.bfloat16),
 ]
 
 
