@@ -416,7 +416,7 @@ int run_fwd_local(const AtlasMemShape* s, const Params& P, cudaStream_t st) {
   if (P.fmode == ATLAS_FMAP_TENSOR) {
     if (fmap_tc(s)) {
       LAUNCH(KID_PROJ_TILES, tc::k_proj_tiles, dim3(P.dk + 1), 0, st, P);
-      LAUNCH_T(KID_FMAP_FWD_TC, tc::k_fmap_fwd_tc, dim3((P.T + tc::kR - 1) / tc::kR, P.N, 2), tc::kFmT,
+      LAUNCH_T(KID_FMAP_FWD_TC, tc::k_fmap_fwd_tc, dim3((P.T + tc::kFmRows - 1) / tc::kFmRows, P.N, 2), tc::kFmT,
                tc::fm_fwd_smem(P.dk, P.dphi), st, P);
     } else {
       LAUNCH(KID_FMAP_FWD, k_fmap_tensor_fwd, dim3((P.T + kFmTile - 1) / kFmTile, P.N, 2), m.fmf, st, P);
@@ -491,7 +491,7 @@ int run_bwd_finish(const AtlasMemShape* s, const Params& P, cudaStream_t st) {
   }
   if (P.fmode == ATLAS_FMAP_TENSOR && (P.dk_ || P.dq_)) {
     if (fmap_tc(s))
-      LAUNCH_T(KID_FMAP_BWD_TC, tc::k_fmap_bwd_tc, dim3((P.T + tc::kR - 1) / tc::kR, P.N, 2), tc::kFbT,
+      LAUNCH_T(KID_FMAP_BWD_TC, tc::k_fmap_bwd_tc, dim3((P.T + tc::kR - 1) / tc::kR, P.N, 2), tc::kFmT,
                tc::fm_bwd_smem(P.dk, P.dphi), st, P);
     else
       LAUNCH(KID_FMAP_BWD, k_fmap_tensor_bwd, dim3((P.T + kFmTile - 1) / kFmTile, P.N, 2), m.fmb, st, P);
@@ -1000,7 +1000,7 @@ int atlas_fmap_tensor_forward(int64_t rows, int d_k, int d_phi, const void* x, c
   P.status = status;
   cudaStream_t st = (cudaStream_t)stream;
   LAUNCH(KID_PROJ_TILES, tc::k_proj_tiles, dim3(d_k + 1), 0, st, P);
-  LAUNCH_T(KID_FMAP_FWD_TC, tc::k_fmap_fwd_tc, dim3((unsigned)((rows + tc::kR - 1) / tc::kR), 1, 1), tc::kFmT,
+  LAUNCH_T(KID_FMAP_FWD_TC, tc::k_fmap_fwd_tc, dim3((unsigned)((rows + tc::kFmRows - 1) / tc::kFmRows), 1, 1), tc::kFmT,
            tc::fm_fwd_smem(d_k, d_phi), st, P);
   return ATLAS_OK;
 }
@@ -1015,7 +1015,7 @@ int atlas_fmap_tensor_backward(int64_t rows, int d_k, int d_phi, const void* x, 
   P.dphiR = (float*)const_cast<void*>(dphi);
   P.dk_ = dx;
   P.status = status;
-  LAUNCH_T(KID_FMAP_BWD_TC, tc::k_fmap_bwd_tc, dim3((unsigned)((rows + tc::kR - 1) / tc::kR), 1, 1), tc::kFbT,
+  LAUNCH_T(KID_FMAP_BWD_TC, tc::k_fmap_bwd_tc, dim3((unsigned)((rows + tc::kR - 1) / tc::kR), 1, 1), tc::kFmT,
            tc::fm_bwd_smem(d_k, d_phi), (cudaStream_t)stream, P);
   return ATLAS_OK;
 }

@@ -22,8 +22,7 @@
 namespace atlas {
 namespace tc {
 
-constexpr int kFmT = 256;  // threads of the forward CTA (two warpgroups split the columns)
-constexpr int kFbT = 128;  // threads of the backward CTA (one token row each)
+constexpr int kFmT = 256;  // threads of the forward and backward CTAs (two warpgroups)
 
 // Shapes the tensor-core feature map handles: dk a multiple of 16 up to 64,
 // dphi a multiple of 16 up to 256, bf16 io.
@@ -32,13 +31,6 @@ __host__ __device__ __forceinline__ bool fmap_tc_ok(int dk, int dphi, int bf) {
 }
 __host__ __device__ __forceinline__ int fm_chunk_bytes(int dk, int dphi) { return dk * dphi * 2; }
 __host__ __device__ __forceinline__ int fm_a_bytes(int dk) { return kR * dk * 2; }
-__host__ __device__ __forceinline__ int fm_x_stride(int dk) { return dk + 4; }  // padded fp32 rows: no bank conflicts
-__host__ __device__ __forceinline__ size_t fm_fwd_smem(int dk, int dphi) {
-  return 3 * (size_t)fm_chunk_bytes(dk, dphi) + 2 * (size_t)fm_a_bytes(dk) + 4 * (size_t)kR * fm_x_stride(dk);
-}
-__host__ __device__ __forceinline__ size_t fm_bwd_smem(int dk, int dphi) {
-  return 3 * (size_t)fm_chunk_bytes(dk, dphi) + (size_t)kR * dphi * 2;
-}
 __host__ __device__ __forceinline__ uint32_t tmem_cols_for(int n) {
   uint32_t c = 32;
   while ((int)c < n) c <<= 1;
@@ -58,39 +50,71 @@ __global__ void __launch_bounds__(256) k_proj_tiles(Params P) {
   }
 }
 
-// phi of 128 tokens of one unit for keys (blockIdx.z = 0) or queries (1), fp32
-// out to P.phik / P.phiq. Grid (ceil(T / 128), N, 2), kFmT threads.
+// Bulk copy of `bytes` (a multiple of 16) from global into shared memory on barrier `bar`
+// (issuing thread; the barrier's arrival is the caller's).
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  mbar_expect_tx(bar, bytes);
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+                   umma::smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(umma::smem_u32(bar))
+               : "memory");
+}
+
+constexpr int kFmRows = 256;  // tokens per forward CTA: two 128-row MMAs share each Proj chunk
+__host__ __device__ __forceinline__ int fm_xh_stride(int dk) { return dk + 8; }  // bf16 x rows, padded
+__host__ __device__ __forceinline__ size_t fm_fwd_smem(int dk, int dphi) {
+  return 3 * (size_t)fm_chunk_bytes(dk, dphi) + 4 * (size_t)fm_a_bytes(dk) + 2 * (size_t)kFmRows * fm_xh_stride(dk);
+}
+// Backward: G Proj chunks per MMA (N = G dk <= 128), two B stages of G chunks, the d phi tile.
+__host__ __device__ __forceinline__ int fm_group(int dk) { return dk >= 48 ? 2 : 128 / dk; }
+__host__ __device__ __forceinline__ size_t fm_bwd_smem(int dk, int dphi) {
+  return 2 * (size_t)fm_group(dk) * fm_chunk_bytes(dk, dphi) + (size_t)kR * dphi * 2;
+}
+
+// phi of 256 tokens of one unit for keys (blockIdx.z = 0) or queries (1), out to
+// P.phik / P.phiq (fp32, or bf16 with P.fm_bf16). Grid (ceil(T / 256), N, 2), kFmT threads.
+// Per feature chunk c: both 128-token halves' operand tiles are generated (stage c & 1),
+// then two MMAs (accumulators at TMEM columns 0 and 256) read the same Proj chunk
+// (ring stage c % 3), so each Proj byte fetched from L2 serves 256 tokens.
 __global__ void __launch_bounds__(kFmT) k_fmap_fwd_tc(Params P) {
   extern __shared__ __align__(1024) unsigned char sm[];
-  const int dk = P.dk, dphi = P.dphi, n = blockIdx.y, isq = blockIdx.z, t0 = blockIdx.x * kR;
-  const int TT = min(kR, P.T - t0), tid = threadIdx.x, nch = dk + 1, xs_ld = fm_x_stride(dk);
+  const int dk = P.dk, dphi = P.dphi, n = blockIdx.y, isq = blockIdx.z, t0 = blockIdx.x * kFmRows;
+  const int TT = min(kFmRows, P.T - t0), tid = threadIdx.x, nch = dk + 1, xl = fm_xh_stride(dk);
   const int cb_bytes = fm_chunk_bytes(dk, dphi), a_bytes = fm_a_bytes(dk);
-  unsigned char* Bs = sm;                          // 3 stages of Proj chunks
-  unsigned char* As = sm + 3 * cb_bytes;           // 2 stages of generated feature chunks
-  float* xs = reinterpret_cast<float*>(As + 2 * a_bytes);  // [128][dk + 4] raw x
+  unsigned char* Bs = sm;                                     // 3 stages of Proj chunks
+  unsigned char* As = sm + 3 * cb_bytes;                      // 2 stages x 2 halves of feature chunks
+  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(As + 4 * a_bytes);  // [256][dk + 8] raw x
   __shared__ uint64_t bb[3], mb[2];
   __shared__ uint32_t tbase;
-  const uint32_t ncols = tmem_cols_for(dphi);
   if (tid == 0) {
     for (int i = 0; i < 3; ++i) umma::mbar_init(&bb[i], 1);
     for (int i = 0; i < 2; ++i) umma::mbar_init(&mb[i], 1);
-    for (int c = 0; c < 2 && c < nch; ++c) {  // Proj chunks 0, 1 in flight
-      mbar_expect_tx(&bb[c], cb_bytes);
-      asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
-                       umma::smem_u32(Bs + c * cb_bytes)),
-                   "l"(P.projb + (size_t)c * cb_bytes), "r"(cb_bytes), "r"(umma::smem_u32(&bb[c]))
-                   : "memory");
+    for (int c = 0; c < 3 && c < nch; ++c) {  // Proj chunks 0..2 in flight
+      bulk_g2s(Bs + c * cb_bytes, P.projb + (size_t)c * cb_bytes, cb_bytes, &bb[c]);
       mbar_arrive(&bb[c]);
     }
   }
   if (tid < 32) {
-    umma::tmem_alloc(&tbase, ncols);
+    umma::tmem_alloc(&tbase, 512);
     umma::tmem_relinquish();
   }
-  const void* src = isq ? P.q : P.k;
-  for (int x = tid; x < kR * dk; x += kFmT) {
-    const int r = x / dk, c = x % dk;
-    xs[r * xs_ld + c] = r < TT ? ldio(src, ((int64_t)n * P.T + t0 + r) * dk + c, P.bf) : 0.f;
+  {  // raw x rows (bf16; rows past the unit's end are zero)
+    const int cpr = dk / 8;
+    for (int u = tid; u < kFmRows * cpr; u += kFmT) {
+      const int r = u / cpr, cb = u % cpr;
+      uint4 v = make_uint4(0u, 0u, 0u, 0u);
+      if (r < TT) {
+        if (P.bf) {
+          v = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(isq ? P.q : P.k) +
+                                              ((int64_t)n * P.T + t0 + r) * dk + cb * 8);
+        } else {
+          float f[8];
+          ld8f(reinterpret_cast<const float*>(isq ? P.q : P.k) + ((int64_t)n * P.T + t0 + r) * dk + cb * 8, f);
+          v = pack_unit(f);
+        }
+      }
+      *reinterpret_cast<uint4*>(xs + r * xl + cb * 8) = v;
+    }
   }
   umma::fence_before();
   __syncthreads();
@@ -101,67 +125,61 @@ __global__ void __launch_bounds__(kFmT) k_fmap_fwd_tc(Params P) {
   bool ok = true;
   for (int c = 0; c < nch; ++c) {
     const int sa = c & 1, sb = c % 3;
-    if (c >= 2) {  // MMA c - 2 done: A stage sa and B stage (c + 1) % 3 are free
+    if (c >= 2) {  // MMAs of chunk c - 2 done: A stage sa and B stage (c + 1) % 3 are free
       ok = umma::mbar_wait(&mb[sa], ((c >> 1) + 1) & 1) && ok;
       umma::fence_after();
       if (tid == 0 && c + 1 < nch) {
         const int s1 = (c + 1) % 3;
-        mbar_expect_tx(&bb[s1], cb_bytes);
-        asm volatile(
-            "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
-                umma::smem_u32(Bs + s1 * cb_bytes)),
-            "l"(P.projb + (size_t)(c + 1) * cb_bytes), "r"(cb_bytes), "r"(umma::smem_u32(&bb[s1]))
-            : "memory");
+        bulk_g2s(Bs + s1 * cb_bytes, P.projb + (size_t)(c + 1) * cb_bytes, cb_bytes, &bb[s1]);
         mbar_arrive(&bb[s1]);
       }
-    } else if (c == 1 && tid == 0 && nch > 2) {
-      // stage 2 is untouched so far: chunk 2 can go in at once
-      mbar_expect_tx(&bb[2], cb_bytes);
-      asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
-                       umma::smem_u32(Bs + 2 * cb_bytes)),
-                   "l"(P.projb + (size_t)2 * cb_bytes), "r"(cb_bytes), "r"(umma::smem_u32(&bb[2]))
-                   : "memory");
-      mbar_arrive(&bb[2]);
     }
-    // feature chunk c: x itself (c = 0) or x_{c-1} * x
-    unsigned char* A = As + sa * a_bytes;
-    for (int u = tid; u < units; u += kFmT) {
+    // feature chunk c of both halves: x itself (c = 0) or x_{c-1} * x
+    unsigned char* A = As + sa * 2 * a_bytes;
+    for (int u = tid; u < 2 * units; u += kFmT) {
+      const int h = u >= units, uu = u - h * units;
       int r, cb;
-      unit_rc(u, cpr, r, cb);
-      const float* xr = xs + r * xs_ld;
-      const float4 lo = *reinterpret_cast<const float4*>(xr + cb * 8);
-      const float4 hi = *reinterpret_cast<const float4*>(xr + cb * 8 + 4);
-      const float s = c == 0 ? 1.f : xr[c - 1];
-      const float v[8] = {s * lo.x, s * lo.y, s * lo.z, s * lo.w, s * hi.x, s * hi.y, s * hi.z, s * hi.w};
-      *reinterpret_cast<uint4*>(A + 16 * u) = pack_unit(v);
+      unit_rc(uu, cpr, r, cb);
+      const __nv_bfloat16* xr = xs + (h * kR + r) * xl;
+      float v[8];
+      unpack_unit(*reinterpret_cast<const uint4*>(xr + cb * 8), v);
+      if (c > 0) {
+        const float s = __bfloat162float(xr[c - 1]);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] *= s;
+      }
+      *reinterpret_cast<uint4*>(A + h * a_bytes + 16 * uu) = pack_unit(v);
     }
     umma::fence_async_smem();
     umma::fence_before();
     __syncthreads();
     if (tid == 0) {
-      // chunks 0, 1 and 2 were issued before their stage was waited on; later ones in the loop above
       ok = umma::mbar_wait(&bb[sb], (c / 3) & 1) && ok;
       umma::fence_after();
-      const uint32_t a0 = umma::smem_u32(A), b0 = umma::smem_u32(Bs + sb * cb_bytes);
-      for (int s = 0; s < dk / 16; ++s)
-        umma::mma(tm, umma::desc_kmajor(a0, dk, s), umma::desc_mnmajor(b0, dphi, s), idesc, (c > 0 || s > 0) ? 1 : 0);
+      const uint32_t b0 = umma::smem_u32(Bs + sb * cb_bytes);
+      for (int h = 0; h < 2; ++h) {
+        const uint32_t a0 = umma::smem_u32(A + h * a_bytes);
+        for (int s = 0; s < dk / 16; ++s)
+          umma::mma(tm + h * 256, umma::desc_kmajor(a0, dk, s), umma::desc_mnmajor(b0, dphi, s), idesc,
+                    (c > 0 || s > 0) ? 1 : 0);
+      }
       umma::commit(&mb[sa]);
     }
   }
-  // the last MMA (chunk nch - 1, stage (nch - 1) & 1)
   ok = umma::mbar_wait(&mb[(nch - 1) & 1], ((nch - 1) >> 1) & 1) && ok;
   umma::fence_after();
   if (__syncthreads_or(!ok)) {
     if (tid == 0 && P.status) atomicExch(P.status, kDevStatMmaTimeout);
   } else {
-    // epilogue: warp w reads TMEM lanes 32 (w % 4).., warpgroup g columns [g dphi/2, (g+1) dphi/2)
-    const int row = tid & 127, g = tid >> 7, half = dphi / 2;
+    // warpgroup h stores the rows of half h (its warps read TMEM lanes 32 (w % 4)..)
+    const int h = tid >> 7, row = h * kR + (tid & 127);
     const int64_t off = ((int64_t)n * P.T + t0 + row) * dphi;
     float* dst = (isq ? P.phiq : P.phik) + off;
     __nv_bfloat16* dsth = reinterpret_cast<__nv_bfloat16*>(isq ? P.phiq : P.phik) + off;
-    for (int c16 = g * half; c16 < (g + 1) * half; c16 += 16) {
+    const uint32_t lane = (uint32_t)((tid >> 5) & 3) * 32 << 16;
+    for (int c16 = 0; c16 < dphi; c16 += 16) {
       float a[16];
-      umma::tmem_ld16(tm + ((uint32_t)((tid >> 5) & 3) * 32 << 16) + c16, a);
+      umma::tmem_ld16(tm + lane + h * 256 + c16, a);
       umma::tmem_ld_wait();
       if (row < TT) {
         if (P.fm_bf16) st16bf(dsth + c16, a);
@@ -171,134 +189,147 @@ __global__ void __launch_bounds__(kFmT) k_fmap_fwd_tc(Params P) {
   }
   umma::fence_before();
   __syncthreads();
-  if (tid < 32) umma::tmem_dealloc(tm, ncols);
+  if (tid < 32) umma::tmem_dealloc(tm, 512);
 }
 
-// dx of 128 tokens of one unit for keys (blockIdx.z = 0: d phi in P.dphiR, dk
-// out) or queries (1: d psi in P.dpsi, dq out). Grid (ceil(T / 128), N, 2), kFbT threads.
-__global__ void __launch_bounds__(kFbT) k_fmap_bwd_tc(Params P) {
+// dx of 128 tokens of one unit for keys (blockIdx.z = 0: d phi in P.dphiR, dk out) or
+// queries (1: d psi in P.dpsi, dq out); d phi fp32, or bf16 with P.fm_bf16.
+// Grid (ceil(T / 128), N, 2), kFmT threads. The feature chunks go G at a time
+// (N = G dk columns per MMA, two alternating accumulators, B ring of two stages);
+// warpgroup w folds chunks [w G/2, (w+1) G/2) of each group into its own copy of
+// dx, and the two copies are summed at the end.
+__global__ void __launch_bounds__(kFmT) k_fmap_bwd_tc(Params P) {
   extern __shared__ __align__(1024) unsigned char sm[];
   const int dk = P.dk, dphi = P.dphi, n = blockIdx.y, isq = blockIdx.z, t0 = blockIdx.x * kR;
   const int TT = min(kR, P.T - t0), tid = threadIdx.x, nch = dk + 1;
   void* out = isq ? P.dq_ : P.dk_;
   if (!out) return;
-  const int cb_bytes = fm_chunk_bytes(dk, dphi);
-  unsigned char* Bs = sm;                  // 3 stages of Proj chunks (used K-major: rows = dk, K = dphi)
-  unsigned char* Ag = sm + 3 * cb_bytes;   // d phi tile [128 x dphi] bf16
-  __shared__ uint64_t bb[3], mb[2];
+  const int G = fm_group(dk), NG = G * dk, ngr = (nch + G - 1) / G;
+  const int cb_bytes = fm_chunk_bytes(dk, dphi), gb_bytes = G * cb_bytes;
+  unsigned char* Bs = sm;                  // 2 stages of G Proj chunks (K-major: rows = G dk, K = dphi)
+  unsigned char* Ag = sm + 2 * gb_bytes;   // d phi tile [128 x dphi] bf16
+  __shared__ uint64_t bb[2], mb[2];
   __shared__ uint32_t tbase;
-  const uint32_t ncols = tmem_cols_for(2 * dk);
-  auto issue_b = [&](int c) {
-    const int s = c % 3;
-    mbar_expect_tx(&bb[s], cb_bytes);
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
-                     umma::smem_u32(Bs + s * cb_bytes)),
-                 "l"(P.projb + (size_t)c * cb_bytes), "r"(cb_bytes), "r"(umma::smem_u32(&bb[s]))
-                 : "memory");
-    mbar_arrive(&bb[s]);
-  };
+  // bytes of group g present in projb (the last group may hold fewer than G chunks)
+  auto group_bytes = [&](int g) { return (uint32_t)(min(G, nch - g * G) * cb_bytes); };
   if (tid == 0) {
-    for (int i = 0; i < 3; ++i) umma::mbar_init(&bb[i], 1);
-    for (int i = 0; i < 2; ++i) umma::mbar_init(&mb[i], 1);
-    for (int c = 0; c < 3 && c < nch; ++c) issue_b(c);
+    for (int i = 0; i < 2; ++i) { umma::mbar_init(&bb[i], 1); umma::mbar_init(&mb[i], 1); }
+    for (int g = 0; g < 2 && g < ngr; ++g) {
+      bulk_g2s(Bs + g * gb_bytes, P.projb + (size_t)g * gb_bytes, group_bytes(g), &bb[g]);
+      mbar_arrive(&bb[g]);
+    }
   }
   if (tid < 32) {
-    umma::tmem_alloc(&tbase, ncols);
+    umma::tmem_alloc(&tbase, 256);
     umma::tmem_relinquish();
   }
   {  // d phi rows -> bf16 operand tile (rows past the unit's end are zero)
     const int64_t g0 = ((int64_t)n * P.T + t0) * dphi;
-    const float* g = (isq ? P.dpsi : P.dphiR) + g0;
+    const void* gsrc = isq ? (const void*)P.dpsi : (const void*)P.dphiR;
     const int cpr = dphi / 8;
-    for (int u = tid; u < kR * cpr; u += kFbT) {
+    for (int u = tid; u < kR * cpr; u += kFmT) {
       int r, cb;
       unit_rc(u, cpr, r, cb);
       float v[8];
       if (r >= TT) zero8(v);
-      else if (P.fm_bf16) ld8io(isq ? P.dpsi : P.dphiR, g0 + (int64_t)r * dphi + cb * 8, 1, v);
-      else ld8f(g + (int64_t)r * dphi + cb * 8, v);
+      else if (P.fm_bf16) ld8io(gsrc, g0 + (int64_t)r * dphi + cb * 8, 1, v);
+      else ld8f(reinterpret_cast<const float*>(gsrc) + g0 + (int64_t)r * dphi + cb * 8, v);
       *reinterpret_cast<uint4*>(Ag + 16 * u) = pack_unit(v);
     }
   }
-  // this thread's token: x and dx in registers
-  const int row = tid;
+  // this thread's token (row) and its warpgroup's chunks: x and a dx copy in registers
+  const int row = tid & 127, wgp = tid >> 7, half = G / 2;
   float x[64], dx[64];
-  const void* src = isq ? P.q : P.k;
+  {
+    const void* src = isq ? P.q : P.k;
 #pragma unroll
-  for (int i = 0; i < 64; ++i) {
-    x[i] = (i < dk && row < TT) ? ldio(src, ((int64_t)n * P.T + t0 + row) * dk + i, P.bf) : 0.f;
-    dx[i] = 0.f;
+    for (int i = 0; i < 64; ++i) {
+      x[i] = (i < dk && row < TT) ? ldio(src, ((int64_t)n * P.T + t0 + row) * dk + i, P.bf) : 0.f;
+      dx[i] = 0.f;
+    }
   }
   umma::fence_async_smem();
   umma::fence_before();
   __syncthreads();
   umma::fence_after();
   const uint32_t tm = tbase;
-  const uint32_t idesc = umma::make_idesc(128, dk, 0, 0);
+  const uint32_t idesc = umma::make_idesc(128, NG, 0, 0);
   const uint32_t a0 = umma::smem_u32(Ag);
   const uint32_t lane = (uint32_t)((tid >> 5) & 3) * 32 << 16;
-  auto issue_mma = [&](int c) {  // thread 0: accumulator c & 1 <- d phi Proj_c^T
-    const int sb = c % 3;
-    bool w = umma::mbar_wait(&bb[sb], (c / 3) & 1);
+  bool ok = true;
+  auto issue_mma = [&](int g) {  // thread 0: accumulator g & 1 <- d phi [Proj chunks of group g]^T
+    const int sb = g & 1;
+    const bool w = umma::mbar_wait(&bb[sb], (g >> 1) & 1);
     umma::fence_after();
-    const uint32_t b0 = umma::smem_u32(Bs + sb * cb_bytes);
+    const uint32_t b0 = umma::smem_u32(Bs + sb * gb_bytes);
     for (int s = 0; s < dphi / 16; ++s)
-      umma::mma(tm + (c & 1) * dk, umma::desc_kmajor(a0, dphi, s), umma::desc_kmajor(b0, dphi, s), idesc,
+      umma::mma(tm + (g & 1) * 128, umma::desc_kmajor(a0, dphi, s), umma::desc_kmajor(b0, dphi, s), idesc,
                 s > 0 ? 1 : 0);
-    umma::commit(&mb[c & 1]);
+    umma::commit(&mb[g & 1]);
     return w;
   };
-  bool ok = true;
   if (tid == 0) ok = issue_mma(0) && ok;
-  for (int c = 0; c < nch; ++c) {
-    // accumulator c landed; the next chunk's MMA goes into the other accumulator meanwhile
-    ok = umma::mbar_wait(&mb[c & 1], (c >> 1) & 1) && ok;
+  for (int g = 0; g < ngr; ++g) {
+    ok = umma::mbar_wait(&mb[g & 1], (g >> 1) & 1) && ok;  // accumulator of group g landed
     umma::fence_after();
     if (tid == 0) {
-      if (c + 1 < nch) ok = issue_mma(c + 1) && ok;  // its B stage was loaded two chunks ago
+      // stage g & 1 was read by MMA g (done): group g + 2 goes in; MMA g + 1 reads the other stage
+      if (g + 2 < ngr) {
+        bulk_g2s(Bs + (g & 1) * gb_bytes, P.projb + (size_t)(g + 2) * gb_bytes, group_bytes(g + 2), &bb[g & 1]);
+        mbar_arrive(&bb[g & 1]);
+      }
+      if (g + 1 < ngr) ok = issue_mma(g + 1) && ok;
     }
-    // fold chunk c into dx (columns in groups of 16)
-    float xa = 0.f;
+    for (int i = 0; i < half; ++i) {
+      const int j = wgp * half + i, c = g * G + j;  // chunk of this warpgroup
+      if (c >= nch) break;
+      float xa = 0.f;
 #pragma unroll
-    for (int i = 0; i < 64; ++i) xa = (i == c - 1) ? x[i] : xa;
-    float dot = 0.f;
+      for (int q = 0; q < 64; ++q) xa = (q == c - 1) ? x[q] : xa;
+      float dot = 0.f;
 #pragma unroll
-    for (int g = 0; g < 4; ++g) {
-      if (g * 16 >= dk) break;
-      float a[16];
-      umma::tmem_ld16(tm + lane + (c & 1) * dk + g * 16, a);
-      umma::tmem_ld_wait();
+      for (int q16 = 0; q16 < 4; ++q16) {
+        if (q16 * 16 >= dk) break;
+        float a[16];
+        umma::tmem_ld16(tm + lane + (g & 1) * 128 + j * dk + q16 * 16, a);
+        umma::tmem_ld_wait();
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        if (c == 0) {
-          dx[g * 16 + i] += a[i];
-        } else {
-          dot += a[i] * x[g * 16 + i];
-          dx[g * 16 + i] += xa * a[i];
+        for (int q = 0; q < 16; ++q) {
+          if (c == 0) {
+            dx[q16 * 16 + q] += a[q];
+          } else {
+            dot += a[q] * x[q16 * 16 + q];
+            dx[q16 * 16 + q] += xa * a[q];
+          }
         }
       }
-    }
-    if (c > 0) {
+      if (c > 0) {
 #pragma unroll
-      for (int i = 0; i < 64; ++i) if (i == c - 1) dx[i] += dot;
+        for (int q = 0; q < 64; ++q) dx[q] += (q == c - 1) ? dot : 0.f;
+      }
     }
     umma::fence_before();
-    __syncthreads();  // accumulator c & 1 is read: MMA c + 2 may overwrite it; B stage c % 3 is free
-    if (tid == 0 && c + 3 < nch) {
-      // MMA c + 1 was issued above and reads stage (c + 1) % 3; stage c % 3 was read by MMA c (done)
-      issue_b(c + 3);
-    }
+    __syncthreads();  // accumulator g & 1 is read: MMA g + 2 may overwrite it
   }
   if (__syncthreads_or(!ok)) {
     if (tid == 0 && P.status) atomicExch(P.status, kDevStatMmaTimeout);
-  } else if (row < TT) {
+  } else {
+    // sum the two warpgroups' dx copies through shared memory (the B ring is no longer read)
+    float* red = reinterpret_cast<float*>(sm);
+    if (wgp == 1) {
 #pragma unroll
-    for (int i = 0; i < 64; ++i)
-      if (i < dk) stio(out, ((int64_t)n * P.T + t0 + row) * dk + i, dx[i], P.bf);
+      for (int q = 0; q < 64; ++q) red[q * kR + row] = dx[q];
+    }
+    __syncthreads();
+    if (wgp == 0 && row < TT) {
+#pragma unroll
+      for (int q = 0; q < 64; ++q)
+        if (q < dk) stio(out, ((int64_t)n * P.T + t0 + row) * dk + q, dx[q] + red[q * kR + row], P.bf);
+    }
   }
   umma::fence_before();
   __syncthreads();
-  if (tid < 32) umma::tmem_dealloc(tm, ncols);
+  if (tid < 32) umma::tmem_dealloc(tm, 256);
 }
 
 }  // namespace tc

@@ -43,6 +43,10 @@ def kernel_flops(name: str, w: Workload, C: int) -> float:
     the contractions the chunked decomposition has to do (multiply-adds x 2),
     without the padding of the 128-row tensor-core tiles."""
     e, dv, dp = w.window, w.d_v, w.d_phi
+    if name in ("k_fmap_fwd_tc", "k_fmap_bwd_tc"):
+        # one launch maps one of k / q (the stand-alone feature map the d_phi > 128 path calls):
+        # [x; vec(x x^T)] Proj, or its transpose product in the backward, per token
+        return 2.0 * (w.d_k + w.d_k * w.d_k) * dp * w.T * w.N
     total = 0.0
     for t0 in range(0, w.T, C):
         L = min(C, w.T - t0)
