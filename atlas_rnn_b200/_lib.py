@@ -106,6 +106,11 @@ def lib():
         L.atlas_fmap_tensor_backward.argtypes = [ctypes.c_int64, ctypes.c_int, ctypes.c_int, _vp, _vp, _vp, _vp, _vp,
                                                  _vp]
         L.atlas_fmap_tensor_backward.restype = ctypes.c_int
+        i64, ci = ctypes.c_int64, ctypes.c_int
+        L.atlas_omega_store_forward.argtypes = [_vp] * 11 + [i64, i64, i64, ci, ci, _vp]
+        L.atlas_omega_store_forward.restype = ctypes.c_int
+        L.atlas_omega_store_backward.argtypes = [_vp] * 18 + [i64, i64, i64, ci, ci, _vp]
+        L.atlas_omega_store_backward.restype = ctypes.c_int
         L.atlas_mem_read_status.argtypes = [_vp, _vp]
         L.atlas_mem_read_status.restype = ctypes.c_int
         L.atlas_mem_selftest_wait_timeout.argtypes = [_vp, ctypes.c_int, _vp]

@@ -13,6 +13,7 @@
 #include "tc_fmap.cuh"
 #include "decode.cuh"
 #include "scan_op.cuh"
+#include "omega_store.cuh"
 #include "carry.cuh"
 #include "dwconv.cuh"
 #include "headprep.cuh"
@@ -280,12 +281,12 @@ Params make_params(const AtlasMemShape* s, const Layout& L, const AtlasMemFwd* f
 enum KernelId {
   KID_FMAP_FWD, KID_FWD_CHUNK, KID_FWD_SCAN, KID_FWD_OUT, KID_BUF_OUT, KID_BWD_CHUNK, KID_BWD_SCAN,
   KID_BWD_GRADS, KID_BWD_BUFOUT, KID_BWD_FINAL, KID_BWD_DSREF, KID_FMAP_BWD, KID_FWD_CHUNK_TC, KID_FWD_OUT_TC, KID_FWD_BUF_Y,
-  KID_BWD_CHUNK_TC, KID_BWD_STATE_GATES_TC, KID_BWD_BUF_TC, KID_BWD_FINAL_TC, KID_BWD_DSREF_TC, KID_BWD_KEYS_TC, KID_SREF_TILE, KID_DECODE, KID_SCAN_OP_FWD, KID_SCAN_OP_BWD, KID_CARRY, KID_DWCONV_FWD, KID_DWCONV_BWD, KID_HEADPREP_FWD, KID_HEADPREP_BWD, KID_PROJ_TILES, KID_FMAP_FWD_TC, KID_FMAP_BWD_TC, KID_COUNT
+  KID_BWD_CHUNK_TC, KID_BWD_STATE_GATES_TC, KID_BWD_BUF_TC, KID_BWD_FINAL_TC, KID_BWD_DSREF_TC, KID_BWD_KEYS_TC, KID_SREF_TILE, KID_DECODE, KID_SCAN_OP_FWD, KID_SCAN_OP_BWD, KID_CARRY, KID_DWCONV_FWD, KID_DWCONV_BWD, KID_HEADPREP_FWD, KID_HEADPREP_BWD, KID_PROJ_TILES, KID_FMAP_FWD_TC, KID_FMAP_BWD_TC, KID_OMEGA_STORE_FWD, KID_OMEGA_STORE_BWD, KID_COUNT
 };
 const char* const kKernelNames[KID_COUNT] = {
   "k_fmap_tensor_fwd", "k_fwd_chunk", "k_fwd_scan", "k_fwd_out", "k_buf_out", "k_bwd_chunk", "k_bwd_scan",
   "k_bwd_grads", "k_bwd_bufout", "k_bwd_finalize", "k_bwd_dsref", "k_fmap_tensor_bwd", "k_fwd_chunk_tc", "k_fwd_out_tc", "k_fwd_buf_y",
-  "k_bwd_chunk_tc", "k_bwd_state_gates_tc", "k_bwd_buf_tc", "k_bwd_finalize_tc", "k_bwd_dsref_tc", "k_bwd_keys_tc", "k_sref_tile", "k_decode_step", "k_scan_op_fwd", "k_scan_op_bwd", "k_compose_carries", "k_dwconv3_fwd", "k_dwconv3_bwd", "k_head_prep_fwd", "k_head_prep_bwd", "k_proj_tiles", "k_fmap_fwd_tc", "k_fmap_bwd_tc"};
+  "k_bwd_chunk_tc", "k_bwd_state_gates_tc", "k_bwd_buf_tc", "k_bwd_finalize_tc", "k_bwd_dsref_tc", "k_bwd_keys_tc", "k_sref_tile", "k_decode_step", "k_scan_op_fwd", "k_scan_op_bwd", "k_compose_carries", "k_dwconv3_fwd", "k_dwconv3_bwd", "k_head_prep_fwd", "k_head_prep_bwd", "k_proj_tiles", "k_fmap_fwd_tc", "k_fmap_bwd_tc", "k_omega_store_fwd", "k_omega_store_bwd"};
 
 constexpr int kMaxTimed = 8192;
 struct Prof {
@@ -808,6 +809,53 @@ int atlas_scan_forward(const float* gates, const void* inputs, const float* prev
       LAUNCH_T(KID_SCAN_OP_FWD, k_scan_op_fwd<__nv_bfloat16>, grid, kScanOpThreads, 0, st, gates,
                (const __nv_bfloat16*)inputs, prev, (__nv_bfloat16*)out, T, D, off, b0);
   }
+  return ATLAS_OK;
+}
+
+int atlas_omega_store_forward(const float* beta, const void* surprise, const float* last_momentum, const float* gate,
+                              const float* buf_in, const float* keep, const float* last_update, void* out,
+                              float* momentum_all, float* momentum_last, float* buf_out, int64_t B, int64_t T,
+                              int64_t D, int window, int dtype_io, void* stream) {
+  if (!surprise || !keep || !out || B < 1 || T < 1 || D < 1 || window < 1) return ATLAS_ERR_INVALID_ARG;
+  if (dtype_io != ATLAS_F32 && dtype_io != ATLAS_BF16) return ATLAS_ERR_INVALID_ARG;
+  if (window > kOmegaMaxWindow || B > 65535) return ATLAS_ERR_UNSUPPORTED;
+  if (window > 1 && !buf_out) return ATLAS_ERR_INVALID_ARG;
+  OmegaStoreArgs A{};
+  A.beta = beta; A.u = gate; A.a = keep; A.s = surprise; A.m0 = last_momentum; A.buf = window > 1 ? buf_in : nullptr;
+  A.h0 = last_update; A.out = out; A.m_all = beta ? momentum_all : nullptr; A.m_last = momentum_last;
+  A.buf_out = window > 1 ? buf_out : nullptr; A.B = B; A.T = T; A.D = D; A.e = window; A.off = last_update ? 1 : 0;
+  const dim3 grid((unsigned)((D + kScanOpThreads - 1) / kScanOpThreads), (unsigned)B);
+  cudaStream_t st = (cudaStream_t)stream;
+  if (dtype_io == ATLAS_F32) LAUNCH_T(KID_OMEGA_STORE_FWD, k_omega_store_fwd<float>, grid, kScanOpThreads, 0, st, A);
+  else LAUNCH_T(KID_OMEGA_STORE_FWD, k_omega_store_fwd<__nv_bfloat16>, grid, kScanOpThreads, 0, st, A);
+  return ATLAS_OK;
+}
+
+int atlas_omega_store_backward(const float* beta, const void* surprise, const float* last_momentum, const float* gate,
+                               const float* keep, const float* last_update, const void* out,
+                               const float* momentum_all, const void* d_out, const float* d_momentum_last,
+                               const float* d_buf_out, void* d_surprise, float* d_beta, float* d_gate, float* d_keep,
+                               float* d_last_momentum, float* d_last_update, float* d_buf_in, int64_t B, int64_t T,
+                               int64_t D, int window, int dtype_io, void* stream) {
+  if (!surprise || !keep || !out || !d_out || !d_surprise || !d_keep || B < 1 || T < 1 || D < 1 || window < 1)
+    return ATLAS_ERR_INVALID_ARG;
+  if (dtype_io != ATLAS_F32 && dtype_io != ATLAS_BF16) return ATLAS_ERR_INVALID_ARG;
+  if (window > kOmegaMaxWindow || B > 65535) return ATLAS_ERR_UNSUPPORTED;
+  if ((beta && (!momentum_all || !d_beta)) || (gate && !d_gate)) return ATLAS_ERR_INVALID_ARG;
+  OmegaStoreArgs A{};
+  A.beta = beta; A.u = gate; A.a = keep; A.s = surprise; A.m0 = last_momentum; A.h0 = last_update; A.out = (void*)out;
+  A.m_all = (float*)momentum_all; A.dout = d_out; A.dm_last = d_momentum_last;
+  A.dbuf_out = window > 1 ? d_buf_out : nullptr; A.ds = d_surprise; A.dbeta = d_beta; A.du = d_gate; A.da = d_keep;
+  A.dm0 = d_last_momentum; A.dh0 = d_last_update; A.dbuf = window > 1 ? d_buf_in : nullptr;
+  A.B = B; A.T = T; A.D = D; A.e = window; A.off = last_update ? 1 : 0;
+  cudaStream_t st = (cudaStream_t)stream;
+  const size_t bt = (size_t)B * T * sizeof(float);
+  if (cudaMemsetAsync(d_keep, 0, bt, st) != cudaSuccess) return ATLAS_ERR_LAUNCH;
+  if (beta && cudaMemsetAsync(d_beta, 0, bt, st) != cudaSuccess) return ATLAS_ERR_LAUNCH;
+  if (gate && cudaMemsetAsync(d_gate, 0, bt, st) != cudaSuccess) return ATLAS_ERR_LAUNCH;
+  const dim3 grid((unsigned)((D + kScanOpThreads - 1) / kScanOpThreads), (unsigned)B);
+  if (dtype_io == ATLAS_F32) LAUNCH_T(KID_OMEGA_STORE_BWD, k_omega_store_bwd<float>, grid, kScanOpThreads, 0, st, A);
+  else LAUNCH_T(KID_OMEGA_STORE_BWD, k_omega_store_bwd<__nv_bfloat16>, grid, kScanOpThreads, 0, st, A);
   return ATLAS_OK;
 }
 

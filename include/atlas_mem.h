@@ -359,6 +359,37 @@ int atlas_scan_backward(const float* gates, const void* out, const float* prev, 
                         float* d_gates, void* d_inputs, float* d_prev, int64_t B, int64_t T, int64_t D,
                         int dtype_io, int remove_prev, void* stream);
 
+/* ---- legacy OmegaNeuralMemory per-parameter update (omega.py:262-315) ----
+ * One fused pass over surprises s [B,T,D] (B = batch*heads, T = chunks, D =
+ * the parameter's elements flattened), replacing the momentum assoc_scan
+ * (omega.py:262-268), the omega gate (:276-283), the window sum with the
+ * carried __omega_buf (:285-298, _sliding_sum_along_n :24-33) and the decay
+ * assoc_scan with remove_prev=False (:315):
+ *   m_t = beta_t m_{t-1} + s_t  (m_0 = last_momentum; beta NULL: m_t = s_t)
+ *   g_t = gate_t m_t            (gate NULL: g_t = m_t)
+ *   w_t = sum_{j<window} g_{t-j}, g_{-1}.. from buf_in [B,window-1,D] (NULL = zeros)
+ *   h_t = keep_t h_{t-1} + w_t  (keep = 1 - decay_factor; h_0 = last_update)
+ * out [B,T+1,D] = h_0..h_T when last_update is given, else [B,T,D] = h_1..h_T;
+ * momentum_last [B,D] = m_T (may be NULL); buf_out [B,window-1,D] = the last
+ * window-1 entries of [buf_in; g]; momentum_all [B,T,D] fp32 keeps m for the
+ * backward (needed there when beta is given). Scalars [B,T] fp32, states fp32,
+ * s / out / d_out / d_surprise in dtype_io. window <= 16, B <= 65535. */
+int atlas_omega_store_forward(const float* beta, const void* surprise, const float* last_momentum,
+                              const float* gate, const float* buf_in, const float* keep,
+                              const float* last_update, void* out, float* momentum_all,
+                              float* momentum_last, float* buf_out, int64_t B, int64_t T, int64_t D,
+                              int window, int dtype_io, void* stream);
+/* Backward of atlas_omega_store_forward: d_out like out; d_momentum_last,
+ * d_buf_out optional upstream gradients. d_beta, d_gate, d_keep [B,T] are
+ * zeroed here and accumulated over D; d_last_momentum, d_last_update [B,D] and
+ * d_buf_in [B,window-1,D] may be NULL. */
+int atlas_omega_store_backward(const float* beta, const void* surprise, const float* last_momentum,
+                               const float* gate, const float* keep, const float* last_update, const void* out,
+                               const float* momentum_all, const void* d_out, const float* d_momentum_last,
+                               const float* d_buf_out, void* d_surprise, float* d_beta, float* d_gate,
+                               float* d_keep, float* d_last_momentum, float* d_last_update, float* d_buf_in,
+                               int64_t B, int64_t T, int64_t D, int window, int dtype_io, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

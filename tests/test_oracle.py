@@ -165,3 +165,36 @@ def test_streaming_oracle_matches_autograd(mom, saturate):
         if leaf is None:
             continue
         assert rel_l2(gr[name], leaf.grad) < 1e-10, name
+
+
+# ---- legacy OmegaNeuralMemory window: the reference's known answers (tests/test_atlas.py:147-169) ----
+def test_legacy_sliding_sum_known_answers():
+    from oracle.legacy_omega_ref import sliding_sum_along_n
+    x = torch.tensor([[[1., 2.], [3., 4.], [5., 6.], [7., 8.]],
+                      [[2., 1.], [4., 3.], [6., 5.], [8., 7.]]])
+    assert torch.equal(sliding_sum_along_n(x, 1), x)
+    assert torch.equal(sliding_sum_along_n(x, 2), torch.tensor([[[1., 2.], [4., 6.], [8., 10.], [12., 14.]],
+                                                                [[2., 1.], [6., 4.], [10., 8.], [14., 12.]]]))
+    assert torch.equal(sliding_sum_along_n(x, 3), torch.tensor([[[1., 2.], [4., 6.], [9., 12.], [15., 18.]],
+                                                                [[2., 1.], [6., 4.], [12., 9.], [18., 15.]]]))
+
+
+def test_legacy_omega_update_matches_sequential():
+    """The restated omega.py:262-315 chain against a token-by-token loop of the same recurrences."""
+    from oracle.legacy_omega_ref import omega_param_update
+    g = torch.Generator().manual_seed(3)
+    B, n, e = 3, 9, 4
+    s = torch.randn(B, n, 2, 3, generator=g, dtype=torch.float64)
+    beta, gate, decay = (torch.rand(B, n, generator=g, dtype=torch.float64) for _ in range(3))
+    m0, h0 = torch.randn(B, 2, 3, generator=g, dtype=torch.float64), torch.randn(B, 2, 3, generator=g,
+                                                                                  dtype=torch.float64)
+    buf = torch.randn(B, e - 1, 2, 3, generator=g, dtype=torch.float64)
+    upd, m_last, nb = omega_param_update(s, decay, h0, beta, m0, gate, buf, window=e)
+    m, h, hist, outs = m0.clone(), h0.clone(), [buf[:, i] for i in range(e - 1)], [h0]
+    for t in range(n):
+        m = beta[:, t, None, None] * m + s[:, t]
+        hist.append(gate[:, t, None, None] * m)
+        h = (1 - decay[:, t, None, None]) * h + sum(hist[-e:])
+        outs.append(h)
+    assert torch.allclose(upd, torch.stack(outs, 1)) and torch.allclose(m_last, m)
+    assert torch.allclose(nb, torch.stack(hist[-(e - 1):], 1))
