@@ -435,7 +435,8 @@ int run_fwd_finish(const AtlasMemShape* s, const Params& P, cudaStream_t st) {
   const Smem m = smem_sizes(s, P.C);
   if (int v = launch_scan(true, P, 0, st)) return v;
   if (tc_groups(s) & 2) {
-    LAUNCH_T(KID_FWD_OUT_TC, tc::k_fwd_out_tc, dim3(P.nch, P.N), tc::kT, m.tc_f3, st, P);
+    LAUNCH_T(KID_FWD_OUT_TC, tc::k_fwd_out_tc, dim3((unsigned)std::min(P.nch * P.N, sm_count())), tc::kT, m.tc_f3,
+             st, P);
     if (P.buf && P.e > 1)
       LAUNCH(KID_FWD_BUF_Y, tc::k_fwd_buf_y, dim3((P.dv + 63) / 64, P.N), m.buf_y, st, P);
   } else {

@@ -29,9 +29,23 @@ __device__ __forceinline__ void ctx_geom(const Params& P, Ctx& cx, int chunk = -
   cx.K = cx.L + P.e - 1;
   cx.kp0 = cx.t0 - (P.e - 1);
 }
+// Geometry of chunk c of unit n (persistent kernels that walk several chunks).
+__device__ __forceinline__ void ctx_at(const Params& P, Ctx& cx, int n, int c) {
+  cx.n = n;
+  cx.c = c;
+  cx.t0 = c * P.C;
+  cx.L = min(P.C, P.T - cx.t0);
+  cx.K = cx.L + P.e - 1;
+  cx.kp0 = cx.t0 - (P.e - 1);
+}
+__device__ __forceinline__ void load_ctx_gates(const Params& P, SmemAlloc& sa, Ctx& cx, int nthreads);
 __device__ __forceinline__ void load_ctx(const Params& P, SmemAlloc& sa, Ctx& cx, int nthreads = kThreads,
                                          int chunk = -1) {
   ctx_geom(P, cx, chunk);
+  load_ctx_gates(P, sa, cx, nthreads);
+}
+// The gates of the chunk cx already describes (ctx_geom / ctx_at) into shared memory.
+__device__ __forceinline__ void load_ctx_gates(const Params& P, SmemAlloc& sa, Ctx& cx, int nthreads) {
   cx.al = sa.take(P.C);
   cx.et = sa.take(P.C);
   cx.be = sa.take(P.C);

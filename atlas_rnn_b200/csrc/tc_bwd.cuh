@@ -307,11 +307,10 @@ __global__ void __launch_bounds__(kT) k_bwd_keys_tc(const __grid_constant__ Para
     const bool own = r < K && p >= cx.t0, halo = r < K && p >= 0 && p < cx.t0;
     const int e1 = e > 1 ? e - 1 : 1;
     // own keys: bf16 hand-off to finalize; halo keys (of the previous chunk's tokens): fp32 partials
-    __nv_bfloat16* ddo = P.ddb + ((int64_t)n * P.T + (own ? p : 0)) * P.dv;
-    __nv_bfloat16* dpo = P.dpb + ((int64_t)n * P.T + (own ? p : 0)) * P.dphi;
+    // (the MMAs are done with every tile: own rows are staged in tPhi / tDl / tM1 and
+    // leave row-contiguous below)
     float* ddh = P.hdd + (cid * e1 + (r < e - 1 ? r : 0)) * P.dv;
     float* dph = P.hdp + (cid * e1 + (r < e - 1 ? r : 0)) * P.dphi;
-    __nv_bfloat16* dq = P.dpsib + ((int64_t)n * P.T + cx.t0 + (r < L ? r : 0)) * P.dphi;
     for (int h = 0; h < kCPW; ++h) {
       const int c16 = wg * kCPW + h;
       float a[16], b[16], i5[16];
@@ -320,14 +319,22 @@ __global__ void __launch_bounds__(kT) k_bwd_keys_tc(const __grid_constant__ Para
       umma::tmem_ld16(lane_addr(tm, 128 + c16 * 16), i5);
       umma::tmem_ld_wait();
       if (own) {
-        st16bf(ddo + c16 * 16, a);
-        st16bf(dpo + c16 * 16, b);
+        stage16(tPhi, r, c16, a);
+        stage16(tDl, r, c16, b);
       } else if (halo) {
         st16f(ddh + c16 * 16, a);
         st16f(dph + c16 * 16, b);
       }
-      if (r < L) st16bf(dq + c16 * 16, i5);  // k_bwd_state_gates_tc adds the state part
+      if (r < L) stage16(tM1, r, c16, i5);  // k_bwd_state_gates_tc adds the state part
     }
+  }
+  __syncthreads();
+  {
+    const int64_t base = (int64_t)n * P.T;
+    auto own_row = [&](int r) { return r < K && cx.kp0 + r >= cx.t0; };
+    store_rows_from_tile(tPhi, [&](int r) { return own_row(r) ? P.ddb + (base + cx.kp0 + r) * P.dv : nullptr; });
+    store_rows_from_tile(tDl, [&](int r) { return own_row(r) ? P.dpb + (base + cx.kp0 + r) * P.dphi : nullptr; });
+    store_rows_from_tile(tM1, [&](int r) { return r < L ? P.dpsib + (base + cx.t0 + r) * P.dphi : nullptr; });
   }
   pc.mark(10);
   tc_teardown(tm);

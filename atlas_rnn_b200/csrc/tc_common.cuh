@@ -406,6 +406,26 @@ __device__ __forceinline__ void zero_rows_from(unsigned char* tile, int from, in
   }
 }
 
+// Rows of a 128 x 128 bf16 tile (core-matrix layout) out to global memory:
+// dst(r) is the global row of tile row r, or nullptr to skip it. Units go in
+// shared-memory order (unit_rc), so the reads are conflict-free and a warp
+// writes 8 rows x 64 contiguous bytes -- whole 32-byte sectors, where a
+// thread-per-row epilogue writes 16 bytes of 32 different rows per store.
+template <class F>
+__device__ __forceinline__ void store_rows_from_tile(const unsigned char* tile, F dst) {
+  for (int u = threadIdx.x; u < kTileBytes / 16; u += kT) {
+    int r, cb;
+    unit_rc(u, kD / 8, r, cb);
+    __nv_bfloat16* row = dst(r);
+    if (row) *reinterpret_cast<uint4*>(row + cb * 8) = reinterpret_cast<const uint4*>(tile)[u];
+  }
+}
+// 16 accumulator values of row r, columns [16 c16, 16 c16 + 16), into a bf16 tile.
+__device__ __forceinline__ void stage16(unsigned char* tile, int r, int c16, float (&v)[16]) {
+  store_unit(tile, r, 2 * c16, kD, *reinterpret_cast<float(*)[8]>(v));
+  store_unit(tile, r, 2 * c16 + 1, kD, *reinterpret_cast<float(*)[8]>(v + 8));
+}
+
 __device__ __forceinline__ float bf_at(const unsigned char* tile, int r, int c) {
   return __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(tile + umma::elem_off(r, c, kD)));
 }

@@ -350,6 +350,10 @@ __global__ void __launch_bounds__(kT) k_fwd_chunk_tc(const __grid_constant__ Par
 //   y = (cS o Psi Phi^T) delta + diag(sS) Psi S_in^T + diag(sZ) Psi Z_in^T
 // (chunk 0 with a carried buffer adds its dense terms in k_fwd_buf_y).
 // ===========================================================================
+// Persistent: each CTA walks chunks it = blockIdx.x, + gridDim.x, ... (chunk
+// fastest, then unit). The next chunk's operand tiles arrive by TMA while the
+// current one finishes: Psi, Phi, S_in, Z_in as soon as the first MMAs have read
+// them, delta once the last MMA has.
 __global__ void __launch_bounds__(kT) k_fwd_out_tc(const __grid_constant__ Params P) {
   PhaseClock pc;
   extern __shared__ __align__(1024) unsigned char sm[];
@@ -359,92 +363,124 @@ __global__ void __launch_bounds__(kT) k_fwd_out_tc(const __grid_constant__ Param
   unsigned char* tMs = sm + 3 * kTileBytes;
   unsigned char* tSin = sm + 4 * kTileBytes;
   unsigned char* tZin = sm + 5 * kTileBytes;
-  SmemAlloc sa{reinterpret_cast<float*>(sm + 6 * kTileBytes), 0};
-  __shared__ uint64_t mbar, lbar;
+  __shared__ uint64_t mbar, lbarA, lbarB;
   __shared__ uint32_t tbase;
-  Ctx cx;
-  ctx_geom(P, cx);
-  TmaBatch ld{&lbar, 0};
-  if (threadIdx.x == 0) tma_init(ld);
-  {  // every operand tile in flight before anything else
-    const unsigned char* Sin = P.stb + ((int64_t)cx.n * P.nch + cx.c) * 2 * kTileBytes;
-    load_rows_psi(P, cx, tPsi, ld);
-    load_keys_phi(P, cx, tPhi, ld);
-    load_keys_delta(P, cx, tDl, ld);
-    load_tile(tSin, Sin, ld);
-    load_tile(tZin, Sin + kTileBytes, ld);
-    if (threadIdx.x == 0) tma_commit(ld);
-  }
-  zero_tile(tMs);
-  load_ctx(P, sa, cx, kT);
-  float* sSv = sa.take(kR + 1);
-  float* sZv = sa.take(kR + 1);
-  float* zZv = sa.take(kR + 1);
-  const int n = cx.n, L = cx.L, tid = threadIdx.x, row = row_of(), wg = wg_of();
-  Sync sy{&mbar, &tbase, 0, P.status};
-  const uint32_t tm = tc_setup(sy);  // (its barrier also publishes the gates)
-  pc.mark(16);
-  if (wg == 0) {  // column j = row of tMs: cS of key j before each token i (tile zero-filled)
-    const int j = row;
-    fwd_column_z(P, cx, j, [&](int i, float cs, float, float) { st_bf(tMs, i, j, cs); });
-  } else if (wg == 1 && row < 32) {
-    fwd_scalars_warp(cx, sSv, sZv, zZv);  // state-path scalars before token i
-  }
-  if (wg > 0) {
-    tma_wait(ld, P.status);
-    zero_rows_from(tPsi, L, 128, kT - 128);
-    loaders_sync();
-    phi_xform(P, tPsi, 128, kT - 128);
-    phi_xform(P, tPhi, 128, kT - 128);
-  } else {
-    tma_wait(ld, P.status);  // the MMAs read what warpgroups 1.. did not touch too
-  }
-  pc.mark(17);
-  smem_to_tc();
+  const int tid = threadIdx.x, row = row_of(), wg = wg_of();
+  const int items = P.N * P.nch;
+  const bool tens = P.fmode == ATLAS_FMAP_TENSOR;
+  TmaBatch ldA{&lbarA, 0}, ldB{&lbarB, 0};
+  // thread 0: operand loads of item `it` (Psi, Phi, S_in, Z_in on A; delta on B)
+  auto issue_A = [&](int it) {
+    Ctx g;
+    ctx_at(P, g, it / P.nch, it % P.nch);
+    if (!tens) {
+      tma_rows(&P.tm_q, tPsi, g.n, g.t0, ldA.bar);
+      tma_rows(&P.tm_k, tPhi, g.n, g.kp0, ldA.bar);
+    }
+    const unsigned char* Sin = P.stb + ((int64_t)g.n * P.nch + g.c) * 2 * kTileBytes;
+    tma_tile(tSin, Sin, ldA.bar);
+    tma_tile(tZin, Sin + kTileBytes, ldA.bar);
+    tma_commit(ldA);
+  };
+  auto issue_B = [&](int it) {
+    Ctx g;
+    ctx_at(P, g, it / P.nch, it % P.nch);
+    tma_rows(&P.tm_dl, tDl, g.n, g.kp0, ldB.bar);
+    tma_commit(ldB);
+  };
   if (tid == 0) {
-    mma_chain(tm, op(tPsi, kD, 0), op(tPhi, kD, 0), kD / 16, kR, false);          // A2 = Psi Phi^T
-    mma_chain(tm + 128, op(tPsi, kD, 0), op(tSin, kD, 0), kD / 16, kD, false);    // Psi S_in^T
-    mma_chain(tm + 256, op(tPsi, kD, 0), op(tZin, kD, 0), kD / 16, kD, false);    // Psi Z_in^T
-  }
-  ATLAS_MMA_WAIT_OR_LEAVE(sy, tm, 512);
-  pc.mark(19);
-#pragma unroll
-  for (int h = 0; h < kCPW; ++h) {  // Ms = cS o A2 (row `row`, this warpgroup's columns)
-    const int c16 = wg * kCPW + h;
-    float a[16], m0[8], m1[8];
-    umma::tmem_ld16(lane_addr(tm, c16 * 16), a);
-    umma::tmem_ld_wait();
-    load_unit(tMs, row, 2 * c16, kR, m0);
-    load_unit(tMs, row, 2 * c16 + 1, kR, m1);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) { m0[i] *= a[i]; m1[i] *= a[8 + i]; }
-    store_unit(tMs, row, 2 * c16, kR, m0);
-    store_unit(tMs, row, 2 * c16 + 1, kR, m1);
-  }
-  pc.mark(20);
-  smem_to_tc();
-  if (tid == 0) mma_chain(tm + 384, op(tMs, kR, 0), op(tDl, kD, 1), 8, kD, false);
-  ATLAS_MMA_WAIT_OR_LEAVE(sy, tm, 512);
-  pc.mark(21);
-  {
-    const int i = row;
-    const float ss = i < L ? sSv[i] : 0.f, sz = i < L ? sZv[i] : 0.f;
-#pragma unroll
-    for (int h = 0; h < kCPW; ++h) {
-      const int c16 = wg * kCPW + h;
-      float yi[16], ps[16], pz[16];
-      umma::tmem_ld16(lane_addr(tm, 384 + c16 * 16), yi);
-      umma::tmem_ld16(lane_addr(tm, 128 + c16 * 16), ps);
-      umma::tmem_ld16(lane_addr(tm, 256 + c16 * 16), pz);
-      umma::tmem_ld_wait();
-      if (i < L) {
-#pragma unroll
-        for (int k = 0; k < 16; ++k) yi[k] += ss * ps[k] + sz * pz[k];
-        st16bf(reinterpret_cast<__nv_bfloat16*>(P.y) + ((int64_t)n * P.T + cx.t0 + i) * P.dv + c16 * 16, yi);
-      }
+    tma_init(ldA);
+    tma_init(ldB);
+    if ((int)blockIdx.x < items) {
+      issue_A(blockIdx.x);
+      issue_B(blockIdx.x);
     }
   }
-  pc.mark(22);
+  Sync sy{&mbar, &tbase, 0, P.status};
+  const uint32_t tm = tc_setup(sy);
+  for (int it = blockIdx.x; it < items; it += gridDim.x) {
+    const int nxt = it + gridDim.x;
+    SmemAlloc sa{reinterpret_cast<float*>(sm + 6 * kTileBytes), 0};
+    Ctx cx;
+    ctx_at(P, cx, it / P.nch, it % P.nch);
+    zero_tile(tMs);  // the last MMA of the previous chunk is done with it
+    if (tens) {      // fp32 phi rows, converted here (no TMA)
+      fill_rows_psi(P, cx, tPsi);
+      fill_keys_phi(P, cx, tPhi);
+    }
+    load_ctx_gates(P, sa, cx, kT);
+    float* sSv = sa.take(kR + 1);
+    float* sZv = sa.take(kR + 1);
+    float* zZv = sa.take(kR + 1);
+    const int n = cx.n, L = cx.L;
+    __syncthreads();  // gates visible, tMs zero
+    pc.mark(16);
+    if (wg == 0) {  // column j = row of tMs: cS of key j before each token i (tile zero-filled)
+      const int j = row;
+      fwd_column_z(P, cx, j, [&](int i, float cs, float, float) { st_bf(tMs, i, j, cs); });
+    } else if (wg == 1 && row < 32) {
+      fwd_scalars_warp(cx, sSv, sZv, zZv);  // state-path scalars before token i
+    }
+    tma_wait(ldA, P.status);
+    if (wg > 0) {
+      zero_rows_from(tPsi, L, 128, kT - 128);
+      loaders_sync();
+      phi_xform(P, tPsi, 128, kT - 128);
+      phi_xform(P, tPhi, 128, kT - 128);
+    }
+    pc.mark(17);
+    smem_to_tc();
+    if (tid == 0) {
+      mma_chain(tm, op(tPsi, kD, 0), op(tPhi, kD, 0), kD / 16, kR, false);          // A2 = Psi Phi^T
+      mma_chain(tm + 128, op(tPsi, kD, 0), op(tSin, kD, 0), kD / 16, kD, false);    // Psi S_in^T
+      mma_chain(tm + 256, op(tPsi, kD, 0), op(tZin, kD, 0), kD / 16, kD, false);    // Psi Z_in^T
+    }
+    ATLAS_MMA_WAIT_OR_LEAVE(sy, tm, 512);
+    if (tid == 0 && nxt < items) issue_A(nxt);  // Psi, Phi, S_in, Z_in are free
+    pc.mark(19);
+#pragma unroll
+    for (int h = 0; h < kCPW; ++h) {  // Ms = cS o A2 (row `row`, this warpgroup's columns)
+      const int c16 = wg * kCPW + h;
+      float a[16], m0[8], m1[8];
+      umma::tmem_ld16(lane_addr(tm, c16 * 16), a);
+      umma::tmem_ld_wait();
+      load_unit(tMs, row, 2 * c16, kR, m0);
+      load_unit(tMs, row, 2 * c16 + 1, kR, m1);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) { m0[i] *= a[i]; m1[i] *= a[8 + i]; }
+      store_unit(tMs, row, 2 * c16, kR, m0);
+      store_unit(tMs, row, 2 * c16 + 1, kR, m1);
+    }
+    pc.mark(20);
+    if (tid == 0) tma_wait(ldB, P.status);  // delta, read only by the MMA thread 0 issues
+    smem_to_tc();
+    if (tid == 0) mma_chain(tm + 384, op(tMs, kR, 0), op(tDl, kD, 1), 8, kD, false);
+    ATLAS_MMA_WAIT_OR_LEAVE(sy, tm, 512);
+    if (tid == 0 && nxt < items) issue_B(nxt);  // delta is free
+    pc.mark(21);
+    {
+      const int i = row;
+      const float ss = i < L ? sSv[i] : 0.f, sz = i < L ? sZv[i] : 0.f;
+#pragma unroll
+      for (int h = 0; h < kCPW; ++h) {
+        const int c16 = wg * kCPW + h;
+        float yi[16], ps[16], pz[16];
+        umma::tmem_ld16(lane_addr(tm, 384 + c16 * 16), yi);
+        umma::tmem_ld16(lane_addr(tm, 128 + c16 * 16), ps);
+        umma::tmem_ld16(lane_addr(tm, 256 + c16 * 16), pz);
+        umma::tmem_ld_wait();
+        if (i < L) {
+#pragma unroll
+          for (int k = 0; k < 16; ++k) yi[k] += ss * ps[k] + sz * pz[k];
+          st16bf(reinterpret_cast<__nv_bfloat16*>(P.y) + ((int64_t)n * P.T + cx.t0 + i) * P.dv + c16 * 16, yi);
+        }
+      }
+    }
+    pc.mark(22);
+    umma::fence_before();
+    __syncthreads();  // TMEM read and sSv / sZv used before the next chunk rewrites them
+    umma::fence_after();
+  }
   tc_teardown(tm);
 }
 
