@@ -11,10 +11,11 @@ from .ops import memory_recurrence, MemoryRecurrenceFn
 from ._lib import check_device_status
 from .scan import AssocScan, assoc_scan
 from .omega_store import omega_store_update
+from .affine_scan import affine_associative_scan
 from .rnn_memory import (RNNMemState, state_detach, PolynomialFeatureMap, MultiheadRMSNorm,
                          RNNMemoryCell, OmegaRNNMemoryCell, RNNMemory, OmegaRNNMemory)
 from .rnn_transformer import LMMBlock, LongTermMemoryModel, RNNMemoryTransformer
 
-__all__ = ["memory_recurrence", "MemoryRecurrenceFn", "check_device_status", "AssocScan", "assoc_scan", "omega_store_update", "RNNMemState", "state_detach",
+__all__ = ["memory_recurrence", "MemoryRecurrenceFn", "check_device_status", "AssocScan", "assoc_scan", "omega_store_update", "affine_associative_scan", "RNNMemState", "state_detach",
            "PolynomialFeatureMap", "MultiheadRMSNorm", "RNNMemoryCell", "OmegaRNNMemoryCell",
            "RNNMemory", "OmegaRNNMemory", "LMMBlock", "LongTermMemoryModel", "RNNMemoryTransformer"]

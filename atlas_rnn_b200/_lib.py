@@ -111,6 +111,10 @@ def lib():
         L.atlas_omega_store_forward.restype = ctypes.c_int
         L.atlas_omega_store_backward.argtypes = [_vp] * 18 + [i64, i64, i64, ci, ci, _vp]
         L.atlas_omega_store_backward.restype = ctypes.c_int
+        L.atlas_affine_scan_forward.argtypes = [_vp] * 4 + [i64, i64, ci, ci, ci, _vp]
+        L.atlas_affine_scan_forward.restype = ctypes.c_int
+        L.atlas_affine_scan_backward.argtypes = [_vp] * 7 + [i64, i64, ci, ci, ci, _vp]
+        L.atlas_affine_scan_backward.restype = ctypes.c_int
         L.atlas_mem_read_status.argtypes = [_vp, _vp]
         L.atlas_mem_read_status.restype = ctypes.c_int
         L.atlas_mem_selftest_wait_timeout.argtypes = [_vp, ctypes.c_int, _vp]

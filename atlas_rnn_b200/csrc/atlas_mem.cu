@@ -14,6 +14,7 @@
 #include "decode.cuh"
 #include "scan_op.cuh"
 #include "omega_store.cuh"
+#include "affine_scan.cuh"
 #include "carry.cuh"
 #include "dwconv.cuh"
 #include "headprep.cuh"
@@ -173,7 +174,8 @@ int ensure_attrs() {
                       (const void*)tc::k_fwd_scan_tc<1>, (const void*)tc::k_fwd_scan_tc<2>,
                       (const void*)tc::k_fwd_scan_tc<4>, (const void*)tc::k_bwd_scan_tc<1>,
                       (const void*)tc::k_bwd_scan_tc<2>, (const void*)tc::k_bwd_scan_tc<4>,
-                      (const void*)tc::k_fmap_fwd_tc, (const void*)tc::k_fmap_bwd_tc};
+                      (const void*)tc::k_fmap_fwd_tc, (const void*)tc::k_fmap_bwd_tc,
+                      (const void*)k_affine_scan_fwd, (const void*)k_affine_scan_bwd};
   for (const void* k : ks) {
     cudaFuncAttributes fa;
     if (cudaFuncGetAttributes(&fa, k) != cudaSuccess) return ATLAS_ERR_LAUNCH;
@@ -281,12 +283,12 @@ Params make_params(const AtlasMemShape* s, const Layout& L, const AtlasMemFwd* f
 enum KernelId {
   KID_FMAP_FWD, KID_FWD_CHUNK, KID_FWD_SCAN, KID_FWD_OUT, KID_BUF_OUT, KID_BWD_CHUNK, KID_BWD_SCAN,
   KID_BWD_GRADS, KID_BWD_BUFOUT, KID_BWD_FINAL, KID_BWD_DSREF, KID_FMAP_BWD, KID_FWD_CHUNK_TC, KID_FWD_OUT_TC, KID_FWD_BUF_Y,
-  KID_BWD_CHUNK_TC, KID_BWD_STATE_GATES_TC, KID_BWD_BUF_TC, KID_BWD_FINAL_TC, KID_BWD_DSREF_TC, KID_BWD_KEYS_TC, KID_SREF_TILE, KID_DECODE, KID_SCAN_OP_FWD, KID_SCAN_OP_BWD, KID_CARRY, KID_DWCONV_FWD, KID_DWCONV_BWD, KID_HEADPREP_FWD, KID_HEADPREP_BWD, KID_PROJ_TILES, KID_FMAP_FWD_TC, KID_FMAP_BWD_TC, KID_OMEGA_STORE_FWD, KID_OMEGA_STORE_BWD, KID_COUNT
+  KID_BWD_CHUNK_TC, KID_BWD_STATE_GATES_TC, KID_BWD_BUF_TC, KID_BWD_FINAL_TC, KID_BWD_DSREF_TC, KID_BWD_KEYS_TC, KID_SREF_TILE, KID_DECODE, KID_SCAN_OP_FWD, KID_SCAN_OP_BWD, KID_CARRY, KID_DWCONV_FWD, KID_DWCONV_BWD, KID_HEADPREP_FWD, KID_HEADPREP_BWD, KID_PROJ_TILES, KID_FMAP_FWD_TC, KID_FMAP_BWD_TC, KID_OMEGA_STORE_FWD, KID_OMEGA_STORE_BWD, KID_AFFINE_FWD, KID_AFFINE_BWD, KID_COUNT
 };
 const char* const kKernelNames[KID_COUNT] = {
   "k_fmap_tensor_fwd", "k_fwd_chunk", "k_fwd_scan", "k_fwd_out", "k_buf_out", "k_bwd_chunk", "k_bwd_scan",
   "k_bwd_grads", "k_bwd_bufout", "k_bwd_finalize", "k_bwd_dsref", "k_fmap_tensor_bwd", "k_fwd_chunk_tc", "k_fwd_out_tc", "k_fwd_buf_y",
-  "k_bwd_chunk_tc", "k_bwd_state_gates_tc", "k_bwd_buf_tc", "k_bwd_finalize_tc", "k_bwd_dsref_tc", "k_bwd_keys_tc", "k_sref_tile", "k_decode_step", "k_scan_op_fwd", "k_scan_op_bwd", "k_compose_carries", "k_dwconv3_fwd", "k_dwconv3_bwd", "k_head_prep_fwd", "k_head_prep_bwd", "k_proj_tiles", "k_fmap_fwd_tc", "k_fmap_bwd_tc", "k_omega_store_fwd", "k_omega_store_bwd"};
+  "k_bwd_chunk_tc", "k_bwd_state_gates_tc", "k_bwd_buf_tc", "k_bwd_finalize_tc", "k_bwd_dsref_tc", "k_bwd_keys_tc", "k_sref_tile", "k_decode_step", "k_scan_op_fwd", "k_scan_op_bwd", "k_compose_carries", "k_dwconv3_fwd", "k_dwconv3_bwd", "k_head_prep_fwd", "k_head_prep_bwd", "k_proj_tiles", "k_fmap_fwd_tc", "k_fmap_bwd_tc", "k_omega_store_fwd", "k_omega_store_bwd", "k_affine_scan_fwd", "k_affine_scan_bwd"};
 
 constexpr int kMaxTimed = 8192;
 struct Prof {
@@ -857,6 +859,42 @@ int atlas_omega_store_backward(const float* beta, const void* surprise, const fl
   const dim3 grid((unsigned)((D + kScanOpThreads - 1) / kScanOpThreads), (unsigned)B);
   if (dtype_io == ATLAS_F32) LAUNCH_T(KID_OMEGA_STORE_BWD, k_omega_store_bwd<float>, grid, kScanOpThreads, 0, st, A);
   else LAUNCH_T(KID_OMEGA_STORE_BWD, k_omega_store_bwd<__nv_bfloat16>, grid, kScanOpThreads, 0, st, A);
+  return ATLAS_OK;
+}
+
+namespace {
+int affine_check(const void* a, const void* b, int64_t N, int64_t T, int R, int D) {
+  if (!a || !b || N < 1 || T < 1 || R < 1 || D < 1) return ATLAS_ERR_INVALID_ARG;
+  if (R % 8 || D % 8 || R > kAffMaxD || D > kAffMaxD || N > 2147483647 || T > 2147483647)
+    return ATLAS_ERR_UNSUPPORTED;
+  return ATLAS_OK;
+}
+}  // namespace
+
+int atlas_affine_scan_forward(const float* A, const float* B, const float* prev, float* out, int64_t N, int64_t T,
+                              int R, int D, int remove_prev, void* stream) {
+  int v = affine_check(A, B, N, T, R, D);
+  if (v) return v;
+  if (!out) return ATLAS_ERR_INVALID_ARG;
+  if ((v = ensure_attrs())) return v;
+  const int off = (prev && !remove_prev) ? 1 : 0;
+  const size_t smem = (size_t)(D + R) * (D + 4) * sizeof(float);
+  LAUNCH_T(KID_AFFINE_FWD, k_affine_scan_fwd, dim3((unsigned)N), kAffThreads, smem, (cudaStream_t)stream, A, B,
+           prev, out, (int)T, R, D, off);
+  return ATLAS_OK;
+}
+
+int atlas_affine_scan_backward(const float* A, const float* prev, const float* out, const float* d_out, float* d_A,
+                               float* d_B, float* d_prev, int64_t N, int64_t T, int R, int D, int remove_prev,
+                               void* stream) {
+  int v = affine_check(A, out, N, T, R, D);
+  if (v) return v;
+  if (!d_out || !d_A || !d_B) return ATLAS_ERR_INVALID_ARG;
+  if ((v = ensure_attrs())) return v;
+  const int off = (prev && !remove_prev) ? 1 : 0;
+  const size_t smem = (size_t)(D + 2 * R) * (D + 4) * sizeof(float);
+  LAUNCH_T(KID_AFFINE_BWD, k_affine_scan_bwd, dim3((unsigned)N), kAffThreads, smem, (cudaStream_t)stream, A, prev,
+           out, d_out, d_A, d_B, prev ? d_prev : nullptr, (int)T, R, D, off);
   return ATLAS_OK;
 }
 

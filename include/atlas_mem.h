@@ -359,6 +359,22 @@ int atlas_scan_backward(const float* gates, const void* out, const float* prev, 
                         float* d_gates, void* d_inputs, float* d_prev, int64_t B, int64_t T, int64_t D,
                         int dtype_io, int remove_prev, void* stream);
 
+/* ---- right-affine matrix scan: the GPU counterpart of the reference's
+ * affine_associative_scan (atlas_pytorch/affine_scan.py:36-160; composition
+ * rule _assoc_compose_affine :7-33):
+ *   H_t = H_{t-1} A_t + B_t,  H_{-1} = prev (NULL = zeros),
+ * A [N,T,D,D], B [N,T,R,D], prev [N,R,D], all fp32. out [N,T+1,R,D] with
+ * prev first when prev is given and remove_prev is 0, else [N,T,R,D]
+ * (the reference's remove_prev=True keeps the T states). R and D multiples of
+ * 8 up to 128. The backward takes the forward's out and its gradient d_out
+ * (same layout) and writes d_A, d_B (required) and d_prev (when prev is
+ * given). */
+int atlas_affine_scan_forward(const float* A, const float* B, const float* prev, float* out, int64_t N,
+                              int64_t T, int R, int D, int remove_prev, void* stream);
+int atlas_affine_scan_backward(const float* A, const float* prev, const float* out, const float* d_out,
+                               float* d_A, float* d_B, float* d_prev, int64_t N, int64_t T, int R, int D,
+                               int remove_prev, void* stream);
+
 /* ---- legacy OmegaNeuralMemory per-parameter update (omega.py:262-315) ----
  * One fused pass over surprises s [B,T,D] (B = batch*heads, T = chunks, D =
  * the parameter's elements flattened), replacing the momentum assoc_scan

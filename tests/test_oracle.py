@@ -198,3 +198,19 @@ def test_legacy_omega_update_matches_sequential():
         outs.append(h)
     assert torch.allclose(upd, torch.stack(outs, 1)) and torch.allclose(m_last, m)
     assert torch.allclose(nb, torch.stack(hist[-(e - 1):], 1))
+
+
+# ---- right-affine matrix scan: the sequential restatement against the reference function's goldens ----
+@pytest.mark.parametrize("path", golden_files("affine_scan_"), ids=lambda p: p.split("/")[-1])
+def test_affine_scan_oracle_matches_reference(path):
+    from oracle.affine_scan_ref import affine_scan_sequential
+    z = load(path)
+    A = torch.tensor(z["A"]).requires_grad_(True)
+    B = torch.tensor(z["B"]).requires_grad_(True)
+    prev = torch.tensor(z["prev"]).requires_grad_(True) if "prev" in z else None
+    out = affine_scan_sequential(A, B, prev, bool(z["remove_prev"]))
+    assert rel_l2(out, z["out"]) < 1e-12
+    (out * torch.tensor(z["W"])).sum().backward()
+    assert rel_l2(A.grad, z["dA"]) < 1e-12 and rel_l2(B.grad, z["dB"]) < 1e-12
+    if prev is not None:
+        assert rel_l2(prev.grad, z["dprev"]) < 1e-12
