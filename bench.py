@@ -613,7 +613,8 @@ def config_dict(w, ws):
     tok_heads = w.N * w.T
     return {"workload": w.name, "B": w.B, "H": w.H, "T": w.T, "d_k": w.d_k, "d_phi": w.d_phi, "d_v": w.d_v,
             "window": w.window, "gate": w.gate, "fmap": f"{w.fmap_mode}:{w.fmap_degree}", "momentum": w.momentum,
-            "parallelism": (f"sequence-parallel x{ws} (T/{ws} per rank, NCCL carry exchange)" if seqpar and ws > 1
+            "parallelism": ("single GPU" if ws == 1 else
+                            f"sequence-parallel x{ws} (T/{ws} per rank, NCCL carry exchange)" if seqpar
                             else f"batch*head sharded x{ws}"),
             "l2": ("inputs exceed L2 (no flush needed)" if tok_heads * (2 * w.d_k + w.d_v) * w.dtype.itemsize > 126e6
                    else "inputs fit L2")}
