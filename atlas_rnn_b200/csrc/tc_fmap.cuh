@@ -68,7 +68,7 @@ __host__ __device__ __forceinline__ size_t fm_fwd_smem(int dk, int dphi) {
 // Backward: G Proj chunks per MMA (N = G dk <= 128), two B stages of G chunks, the d phi tile.
 __host__ __device__ __forceinline__ int fm_group(int dk) { return dk >= 48 ? 2 : 128 / dk; }
 __host__ __device__ __forceinline__ size_t fm_bwd_smem(int dk, int dphi) {
-  return 2 * (size_t)fm_group(dk) * fm_chunk_bytes(dk, dphi) + (size_t)kR * dphi * 2;
+  return 2 * (size_t)fm_group(dk) * fm_chunk_bytes(dk, dphi) + (size_t)kR * dphi * 2 + (size_t)kR * (dk + 8) * 2;
 }
 
 // phi of 256 tokens of one unit for keys (blockIdx.z = 0) or queries (1), out to
@@ -122,6 +122,26 @@ __global__ void __launch_bounds__(kFmT) k_fmap_fwd_tc(Params P) {
   const uint32_t tm = tbase;
   const uint32_t idesc = umma::make_idesc(128, dphi, 0, 1);
   const int cpr = dk / 8, units = kR * cpr;
+  // This thread's units of every feature chunk (the same for all chunks: 2 x 128 x cpr units over
+  // kFmT threads = cpr <= 8 each): its raw x values stay in registers, the tile offset and the row
+  // of the chunk's scalar x_{c-1} are fixed, so a chunk costs one shared load, a scale and a store per unit.
+  uint4 xv[8];
+  uint32_t aoff[8];
+  int xrow[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    xv[k] = make_uint4(0u, 0u, 0u, 0u);
+    aoff[k] = 0;
+    xrow[k] = 0;
+    if (k < cpr) {
+      const int u = tid + k * kFmT, h = u >= units, uu = u - h * units;
+      int r, cb;
+      unit_rc(uu, cpr, r, cb);
+      xrow[k] = (h * kR + r) * xl;
+      xv[k] = *reinterpret_cast<const uint4*>(xs + xrow[k] + cb * 8);
+      aoff[k] = (uint32_t)(h * a_bytes + 16 * uu);
+    }
+  }
   bool ok = true;
   for (int c = 0; c < nch; ++c) {
     const int sa = c & 1, sb = c % 3;
@@ -136,19 +156,22 @@ __global__ void __launch_bounds__(kFmT) k_fmap_fwd_tc(Params P) {
     }
     // feature chunk c of both halves: x itself (c = 0) or x_{c-1} * x
     unsigned char* A = As + sa * 2 * a_bytes;
-    for (int u = tid; u < 2 * units; u += kFmT) {
-      const int h = u >= units, uu = u - h * units;
-      int r, cb;
-      unit_rc(uu, cpr, r, cb);
-      const __nv_bfloat16* xr = xs + (h * kR + r) * xl;
-      float v[8];
-      unpack_unit(*reinterpret_cast<const uint4*>(xr + cb * 8), v);
-      if (c > 0) {
-        const float s = __bfloat162float(xr[c - 1]);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) v[i] *= s;
+    for (int k = 0; k < 8; ++k) {
+      if (k >= cpr) break;
+      if (c == 0) {
+        *reinterpret_cast<uint4*>(A + aoff[k]) = xv[k];
+      } else {
+        const float s = __bfloat162float(xs[xrow[k] + c - 1]);
+        const __nv_bfloat162* xh = reinterpret_cast<const __nv_bfloat162*>(&xv[k]);
+        __align__(16) __nv_bfloat162 o[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 a = __bfloat1622float2(xh[i]);
+          o[i] = __floats2bfloat162_rn(a.x * s, a.y * s);
+        }
+        *reinterpret_cast<uint4*>(A + aoff[k]) = *reinterpret_cast<uint4*>(o);
       }
-      *reinterpret_cast<uint4*>(A + h * a_bytes + 16 * uu) = pack_unit(v);
     }
     umma::fence_async_smem();
     umma::fence_before();
@@ -208,6 +231,9 @@ __global__ void __launch_bounds__(kFmT) k_fmap_bwd_tc(Params P) {
   const int cb_bytes = fm_chunk_bytes(dk, dphi), gb_bytes = G * cb_bytes;
   unsigned char* Bs = sm;                  // 2 stages of G Proj chunks (K-major: rows = G dk, K = dphi)
   unsigned char* Ag = sm + 2 * gb_bytes;   // d phi tile [128 x dphi] bf16
+  const int xl = fm_xh_stride(dk);
+  __nv_bfloat16* xsh = reinterpret_cast<__nv_bfloat16*>(Ag + (size_t)kR * dphi * 2);  // [128][dk + 8] raw x
+  constexpr uint32_t kDotCol = 256;       // TMEM columns 256 .. 256 + dk: the per-token dots
   __shared__ uint64_t bb[2], mb[2];
   __shared__ uint32_t tbase;
   // bytes of group g present in projb (the last group may hold fewer than G chunks)
@@ -220,7 +246,7 @@ __global__ void __launch_bounds__(kFmT) k_fmap_bwd_tc(Params P) {
     }
   }
   if (tid < 32) {
-    umma::tmem_alloc(&tbase, 256);
+    umma::tmem_alloc(&tbase, 512);
     umma::tmem_relinquish();
   }
   {  // d phi rows -> bf16 operand tile (rows past the unit's end are zero)
@@ -246,6 +272,7 @@ __global__ void __launch_bounds__(kFmT) k_fmap_bwd_tc(Params P) {
     for (int i = 0; i < 64; ++i) {
       x[i] = (i < dk && row < TT) ? ldio(src, ((int64_t)n * P.T + t0 + row) * dk + i, P.bf) : 0.f;
       dx[i] = 0.f;
+      if (wgp == 0 && i < dk) xsh[row * xl + i] = __float2bfloat16_rn(x[i]);
     }
   }
   umma::fence_async_smem();
@@ -283,9 +310,7 @@ __global__ void __launch_bounds__(kFmT) k_fmap_bwd_tc(Params P) {
     for (int i = 0; i < half; ++i) {
       const int j = wgp * half + i, c = g * G + j;  // chunk of this warpgroup
       if (c >= nch) break;
-      float xa = 0.f;
-#pragma unroll
-      for (int q = 0; q < 64; ++q) xa = (q == c - 1) ? x[q] : xa;
+      const float xa = c == 0 ? 0.f : __bfloat162float(xsh[row * xl + c - 1]);
       float dot = 0.f;
 #pragma unroll
       for (int q16 = 0; q16 < 4; ++q16) {
@@ -303,17 +328,28 @@ __global__ void __launch_bounds__(kFmT) k_fmap_bwd_tc(Params P) {
           }
         }
       }
-      if (c > 0) {
-#pragma unroll
-        for (int q = 0; q < 64; ++q) dx[q] += (q == c - 1) ? dot : 0.f;
-      }
+      if (c > 0) umma::tmem_st1(tm + lane + kDotCol + c - 1, dot);  // dx_{c-1} += dot, folded in at the end
     }
     umma::fence_before();
     __syncthreads();  // accumulator g & 1 is read: MMA g + 2 may overwrite it
   }
+  umma::tmem_st_wait();
+  umma::fence_before();
   if (__syncthreads_or(!ok)) {
     if (tid == 0 && P.status) atomicExch(P.status, kDevStatMmaTimeout);
   } else {
+    umma::fence_after();
+    if (wgp == 0) {  // the dx_a += <D_a, x> terms of both warpgroups, kept in TMEM columns kDotCol + a
+#pragma unroll
+      for (int q16 = 0; q16 < 4; ++q16) {
+        if (q16 * 16 >= dk) break;
+        float a[16];
+        umma::tmem_ld16(tm + lane + kDotCol + q16 * 16, a);
+        umma::tmem_ld_wait();
+#pragma unroll
+        for (int q = 0; q < 16; ++q) dx[q16 * 16 + q] += a[q];
+      }
+    }
     // sum the two warpgroups' dx copies through shared memory (the B ring is no longer read)
     float* red = reinterpret_cast<float*>(sm);
     if (wgp == 1) {
@@ -329,7 +365,7 @@ __global__ void __launch_bounds__(kFmT) k_fmap_bwd_tc(Params P) {
   }
   umma::fence_before();
   __syncthreads();
-  if (tid < 32) umma::tmem_dealloc(tm, 256);
+  if (tid < 32) umma::tmem_dealloc(tm, 512);
 }
 
 }  // namespace tc
