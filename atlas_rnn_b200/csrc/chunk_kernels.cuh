@@ -67,6 +67,48 @@ __device__ __forceinline__ void load_ctx_gates(const Params& P, SmemAlloc& sa, C
       cx.U[x] = ldio(P.gate, row0 * P.e + x, P.bf);
 }
 
+// Gates of one chunk held in registers by each of `nthreads` (>= 128) threads,
+// loaded one chunk ahead in the persistent kernels so the global loads overlap
+// the current chunk's work; gates_to_smem() then lays them out as load_ctx_gates does.
+struct GatePre {
+  float al, et, be, u, U[4];
+};
+__device__ __forceinline__ void gates_fetch(const Params& P, int n, int c, GatePre& g, int nthreads) {
+  Ctx cx;
+  ctx_at(P, cx, n, c);
+  const int i = threadIdx.x;
+  const int64_t row0 = (int64_t)n * P.T + cx.t0;
+  g.al = g.et = g.be = 0.f;
+  g.u = 1.f;
+  if (i < cx.L) {
+    g.al = ldio(P.decay, row0 + i, P.bf);
+    g.et = ldio(P.lr, row0 + i, P.bf);
+    g.be = P.mom ? ldio(P.beta, row0 + i, P.bf) : 0.f;
+  }
+  if (P.gmode == ATLAS_GATE_TOKEN && i < cx.K && cx.kp0 + i >= 0) g.u = ldio(P.gate, (int64_t)n * P.T + cx.kp0 + i, P.bf);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int x = i + k * nthreads;
+    g.U[k] = (P.gmode == ATLAS_GATE_WINDOW && x < cx.L * P.e) ? ldio(P.gate, row0 * P.e + x, P.bf) : 0.f;
+  }
+}
+__device__ __forceinline__ void gates_to_smem(const Params& P, SmemAlloc& sa, Ctx& cx, const GatePre& g,
+                                              int nthreads) {
+  cx.al = sa.take(P.C);
+  cx.et = sa.take(P.C);
+  cx.be = sa.take(P.C);
+  cx.u = sa.take(P.C + P.e);
+  cx.U = sa.take(P.C * P.e);
+  const int i = threadIdx.x;
+  if (i < cx.L) { cx.al[i] = g.al; cx.et[i] = g.et; cx.be[i] = g.be; }
+  if (P.gmode == ATLAS_GATE_TOKEN && i < cx.K) cx.u[i] = g.u;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int x = i + k * nthreads;
+    if (P.gmode == ATLAS_GATE_WINDOW && x < cx.L * P.e) cx.U[x] = g.U[k];
+  }
+}
+
 // Weight of key j in g of local token i (0 outside the window). TOKEN mode: the
 // per-token gate u_p (buffer entries are stored already gated, weight 1).
 __device__ __forceinline__ float wgt(const Params& P, const Ctx& cx, int i, int j) {

@@ -397,6 +397,8 @@ __global__ void __launch_bounds__(kT) k_fwd_out_tc(const __grid_constant__ Param
     }
   }
   Sync sy{&mbar, &tbase, 0, P.status};
+  GatePre gp;
+  if ((int)blockIdx.x < items) gates_fetch(P, blockIdx.x / P.nch, blockIdx.x % P.nch, gp, kT);
   const uint32_t tm = tc_setup(sy);
   for (int it = blockIdx.x; it < items; it += gridDim.x) {
     const int nxt = it + gridDim.x;
@@ -408,7 +410,8 @@ __global__ void __launch_bounds__(kT) k_fwd_out_tc(const __grid_constant__ Param
       fill_rows_psi(P, cx, tPsi);
       fill_keys_phi(P, cx, tPhi);
     }
-    load_ctx_gates(P, sa, cx, kT);
+    gates_to_smem(P, sa, cx, gp, kT);
+    if (nxt < items) gates_fetch(P, nxt / P.nch, nxt % P.nch, gp, kT);  // the next chunk's, in flight
     float* sSv = sa.take(kR + 1);
     float* sZv = sa.take(kR + 1);
     float* zZv = sa.take(kR + 1);
