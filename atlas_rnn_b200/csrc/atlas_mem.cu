@@ -464,7 +464,8 @@ int run_bwd_finish(const AtlasMemShape* s, const Params& P, cudaStream_t st) {
     const dim3 g(P.nch, P.N);
     // keys (d psi part I5, G, xf), the carried-buffer terms of chunk 0 (G columns, xf, d psi),
     // then the state side and the gate gradients (d psi completed)
-    LAUNCH_T(KID_BWD_KEYS_TC, tc::k_bwd_keys_tc, g, tc::kT, m.tc_b6, st, P);
+    LAUNCH_T(KID_BWD_KEYS_TC, tc::k_bwd_keys_tc, dim3((unsigned)std::min(P.nch * P.N, sm_count())), tc::kT,
+             m.tc_b6, st, P);  // persistent
     if (P.e > 1 && (P.buf || P.dbuf)) LAUNCH(KID_BWD_BUF_TC, tc::k_bwd_buf_tc, dim3(1, P.N), m.buf_b, st, P);
     LAUNCH_T(KID_BWD_STATE_GATES_TC, tc::k_bwd_state_gates_tc, g, tc::kT, m.tc_b4, st, P);
   } else {

@@ -169,27 +169,53 @@ __global__ void __launch_bounds__(kT) k_bwd_keys_tc(const __grid_constant__ Para
   SmemAlloc sa{reinterpret_cast<float*>(sm + 6 * kTileBytes), 0};
   __shared__ uint64_t mbar, lbar;
   __shared__ uint32_t tbase;
-  Ctx cx;
-  ctx_geom(P, cx);
-  const int64_t cid = chunk_id(P, cx);
-  const unsigned char* FS = P.adjb + cid * 2 * kTileBytes;
+  const int tid = threadIdx.x, e = P.e, row = row_of(), wg = wg_of();
+  const int items = P.N * P.nch;
+  const bool tens = P.fmode == ATLAS_FMAP_TENSOR;
   TmaBatch ld{&lbar, 0};
-  if (threadIdx.x == 0) tma_init(ld);
-  load_keys_phi(P, cx, tPhi, ld);
-  load_keys_delta(P, cx, tDl, ld);
-  load_tile(tFS, FS, ld);
-  load_tile(tFZ, FS + kTileBytes, ld);
-  if (threadIdx.x == 0) tma_commit(ld);
-  load_ctx(P, sa, cx, kT);
+  // thread 0: the first operand batch of item `it` (the adjoint tiles may go in earlier than the rows,
+  // still on the same barrier phase); `rows` also commits the batch
+  auto issue_adj = [&](int it) {
+    const unsigned char* Fa = P.adjb + (int64_t)it * 2 * kTileBytes;  // item = n nch + c = chunk id
+    tma_tile(tFS, Fa, ld.bar);
+    tma_tile(tFZ, Fa + kTileBytes, ld.bar);
+  };
+  auto issue_rows = [&](int it) {
+    Ctx g;
+    ctx_at(P, g, it / P.nch, it % P.nch);
+    if (!tens) tma_rows(&P.tm_k, tPhi, g.n, g.kp0, ld.bar);
+    tma_rows(&P.tm_dl, tDl, g.n, g.kp0, ld.bar);
+    tma_commit(ld);
+  };
+  if (tid == 0) {
+    tma_init(ld);
+    if ((int)blockIdx.x < items) {
+      issue_adj(blockIdx.x);
+      issue_rows(blockIdx.x);
+    }
+  }
+  GatePre gp;
+  if ((int)blockIdx.x < items) gates_fetch(P, blockIdx.x / P.nch, blockIdx.x % P.nch, gp, kT);
+  Sync sy{&mbar, &tbase, 0, P.status};
+  const uint32_t tm = tc_setup(sy);
+  // Persistent: each CTA walks chunks it = blockIdx.x, + gridDim.x, ... (chunk fastest); the next
+  // chunk's adjoint tiles load while this one's hand-offs are written, its key rows right after.
+  for (int it = blockIdx.x; it < items; it += gridDim.x) {
+  const int nxt = it + gridDim.x;
+  SmemAlloc sa{reinterpret_cast<float*>(sm + 6 * kTileBytes), 0};
+  Ctx cx;
+  ctx_at(P, cx, it / P.nch, it % P.nch);
+  const int64_t cid = chunk_id(P, cx);
+  if (tens) fill_keys_phi(P, cx, tPhi);
+  gates_to_smem(P, sa, cx, gp, kT);
+  if (nxt < items) gates_fetch(P, nxt / P.nch, nxt % P.nch, gp, kT);
   float* hS = sa.take(kR + 1);
   float* hZS = sa.take(kR + 1);
   float* hZZ = sa.take(kR + 1);
   float* part = sa.take(2 * kWG * kR);
-  const int n = cx.n, K = cx.K, L = cx.L, tid = threadIdx.x, e = P.e, row = row_of(), wg = wg_of();
-  Sync sy{&mbar, &tbase, 0, P.status};
-  const uint32_t tm = tc_setup(sy);
+  const int n = cx.n, K = cx.K, L = cx.L;
   zero_tile(tM3);
-  __syncthreads();  // gates of load_ctx visible, tM3 zero
+  __syncthreads();  // gates visible, tM3 zero
   pc.mark(0);
   if (wg == 0) {
     fwd_column_z(P, cx, row, [&](int i, float cs, float, float) { st_bf(tM3, i, row, cs); });
@@ -301,6 +327,7 @@ __global__ void __launch_bounds__(kT) k_bwd_keys_tc(const __grid_constant__ Para
     mma_chain(tm + 128, op(tM3, kR, 0), op(tPhi, kD, 1), 8, kD, false);  // I5 = M3 Phi
   }
   ATLAS_MMA_WAIT_OR_LEAVE(sy, tm, 512);
+  if (tid == 0 && nxt < items) issue_adj(nxt);  // F_S / F_Z tiles (Psi, dY now) are read by no one any more
   pc.mark(9);
   {
     const int r = row, p = cx.kp0 + r;
@@ -337,6 +364,12 @@ __global__ void __launch_bounds__(kT) k_bwd_keys_tc(const __grid_constant__ Para
     store_rows_from_tile(tM1, [&](int r) { return r < L ? P.dpsib + (base + cx.t0 + r) * P.dphi : nullptr; });
   }
   pc.mark(10);
+  umma::fence_async_smem();
+  umma::fence_before();
+  __syncthreads();  // the staged rows are written out; TMEM read
+  umma::fence_after();
+  if (tid == 0 && nxt < items) issue_rows(nxt);
+  }
   tc_teardown(tm);
 }
 
