@@ -212,7 +212,7 @@ def _fmap_tc_ok(d_k: int, d_phi: int) -> bool:
 
 def _split_phi_call(k, q, v, lr, decay, beta, gate, S_ref, S0, Z0, buf, proj, *, window, gate_mode, fmap_degree,
                     chunk):
-    """The tensor feature map with d_phi = H * 128 (256): phi(k), phi(q) on
+    """The tensor feature map with d_phi = H * 128 (benchmark config 4: 256): phi(k), phi(q) on
     the tensor cores, then the recurrence as H units of d_phi = 128 each. The state splits by
     columns, S = [S_1 | .. | S_H], and every part evolves with the same gates and the same
     delta_t = S_ref phi_t - v_t = sum_g S_ref,g phi_g,t - v_t, so part h is the d_phi = 128

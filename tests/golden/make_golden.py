@@ -57,7 +57,7 @@ def make_core(rm, name, B, H, T, d, e, gate_on, mom, mode, deg, nonzero, seed):
     q = q / q.norm(dim=-1, keepdim=True)
     k = k / k.norm(dim=-1, keepdim=True)
     v = v / v.norm(dim=-1, keepdim=True)
-    # gate distributions of BASELINE configs (alpha, eta, beta, u), reference layout [B, T, H]
+    # gate distributions of the benchmark configs (alpha, eta, beta, u), reference layout [B, T, H]
     lr = 0.1 * sg(0, 1, B, T, H, g=g)
     decay = sg(3, 0.5, B, T, H, g=g)
     beta = sg(1, 0.5, B, T, H, g=g) if mom else None

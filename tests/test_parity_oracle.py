@@ -118,13 +118,13 @@ def test_bf16_padded_tensor_core_path(native_lib, w):
 
 
 def test_config0_full(native_lib):
-    """BASELINE config 0 at full size (fp32)."""
+    """Benchmark config 0 at full size (fp32)."""
     run_case(CONFIGS[0], state_scale=0.0)
     run_case(CONFIGS[0], state_scale=0.1, seed=1)
 
 
 def test_config1_slice(native_lib):
-    """BASELINE config 1 (bf16, e=4, window gates, elementwise g=2) on a batch*head slice,
+    """Benchmark config 1 (bf16, e=4, window gates, elementwise g=2) on a batch*head slice,
     from a zero state (the benchmark's) and from a non-zero S0 / Z0 / omega buffer
     (scale 0.1, as the reference's tests use: test_rnn_all.py:469-470,551-553)."""
     run_case(shrink(CONFIGS[1], B=1, H=2, T=1024), state_scale=0.0)
@@ -162,7 +162,7 @@ def test_clamp_saturated(native_lib, w):
 
 
 def test_config4_slice(native_lib):
-    """BASELINE config 4 (tensor feature map 64 -> 256, e=16) on a small slice."""
+    """Benchmark config 4 (tensor feature map 64 -> 256, e=16) on a small slice."""
     run_case(shrink(CONFIGS[4], B=1, H=1, T=160), state_scale=0.1)
 
 
