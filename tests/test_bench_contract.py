@@ -37,3 +37,20 @@ def test_reference_arm_line():
 def test_reference_cuda_arm_refuses_other_shapes():
     d = run("--impl", "reference-cuda", "--config", "1", "--steps", "1", "--warmup", "3")
     assert d["impl"] == "reference-cuda" and "unavailable" in d
+
+
+def test_shard_workload_partitions_the_configuration():
+    """bench.py --gpus N: the long-context configuration splits its tokens over the ranks,
+    the others their batch (heads when the batch does not divide); the shards cover the job."""
+    sys.path.insert(0, ROOT)
+    import bench
+    from atlas_rnn_b200.workloads import CONFIGS
+    for ws in (1, 2, 4, 8):
+        w1 = bench.shard_workload(CONFIGS[1], ws)
+        assert w1.N * w1.T * ws == CONFIGS[1].N * CONFIGS[1].T and w1.T == CONFIGS[1].T
+        w2 = bench.shard_workload(CONFIGS[2], ws)
+        assert w2.T * ws == CONFIGS[2].T and w2.N == CONFIGS[2].N
+        w4 = bench.shard_workload(CONFIGS[4], ws)
+        assert w4.N * ws == CONFIGS[4].N
+    assert bench.config_dict(CONFIGS[2], 8)["parallelism"].startswith("sequence-parallel x8")
+    assert bench.config_dict(CONFIGS[1], 1)["parallelism"] == "single GPU"
