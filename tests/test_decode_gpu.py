@@ -78,3 +78,26 @@ def test_decode_chain_carries_state(native_lib, w):
         assert rel_l2(y.float(), ref["y"]) <= tol, (t, "y", rel_l2(y.float(), ref["y"]))
         assert rel_l2(S, ref["S_end"]) <= tol, (t, "S", rel_l2(S, ref["S_end"]))
         Sr, Zr, bufr = ref["S_end"], ref["Z_end"], ref["buf_out"]
+
+
+@pytest.mark.parametrize("w", [CASES[2], CASES[8]], ids=lambda w: w.name)
+def test_decode_step_clamp_saturated(native_lib, w):
+    """The clamp of S_end (rnn_memory.py:701) in the one-token kernel: |S0| of order 150 and alpha
+    close to 1, so most of S_T lies beyond +-100; against the oracle and the general kernels."""
+    tol = TOL_F32 if w.dtype == torch.float32 else TOL_BF16
+    inp = make_inputs(w, seed=5, device="cuda", state_scale=0.1)
+    inp["S0"] = (1500.0 * inp["S0"]).contiguous()
+    inp["decay"] = torch.full_like(inp["decay"], 0.9995)
+    g = torch.Generator().manual_seed(6)
+    S_ref = (0.1 * torch.randn(inp["S0"].shape, generator=g)).cuda()
+    with torch.no_grad():
+        out = call(inp, w, S_ref=S_ref)
+    gen = call(dict(inp, k=inp["k"].clone().requires_grad_(True)), w, S_ref=S_ref)
+    gm = "window" if w.gate == "window" else ("token" if w.gate == "token" else None)
+    ref, _ = oracle_run(inp, w.window, gm, w.fmap_mode, w.fmap_degree, grads=False, S_ref=S_ref)
+    assert (out[1].abs() >= 100).float().mean() > 0.3
+    for name, a, gg in zip(("y", "S_end", "Z_end", "buf_out"), out, gen):
+        if a is None:
+            continue
+        assert rel_l2(a.float(), ref[name]) <= tol, name
+        assert rel_l2(a.float(), gg.detach().float()) <= tol, name
