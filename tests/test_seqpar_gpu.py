@@ -13,13 +13,17 @@ from tests.helpers import TOL_BF16, TOL_F32, rel_l2
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("dtype,T,P,d", [(torch.float32, 200, 4, 32), (torch.float32, 97, 3, 16),
-                                         (torch.bfloat16, 8192, 4, 128)])
-def test_segments_match_full_call(native_lib, dtype, T, P, d):
+@pytest.mark.parametrize("dtype,T,P,d,saturate", [(torch.float32, 200, 4, 32, False), (torch.float32, 97, 3, 16, False),
+                                                  (torch.bfloat16, 8192, 4, 128, False),
+                                                  (torch.float32, 200, 4, 32, True)])
+def test_segments_match_full_call(native_lib, dtype, T, P, d, saturate):
     w = shrink(CONFIGS[2], B=1, H=2, T=T)
     from dataclasses import replace
     w = replace(w, d_k=d, d_phi=d, d_v=d, dtype=dtype)
     inp = make_inputs(w, seed=3, device="cuda", state_scale=0.1)
+    if saturate:  # the clamp of S_end active: alpha close to 1, |S0| of order 150 (S_ref = S0)
+        inp["S0"] = (1500.0 * inp["S0"]).contiguous()
+        inp["decay"] = torch.full_like(inp["decay"], 0.9995)
     tol = TOL_F32 if dtype == torch.float32 else TOL_BF16
     names = ("k", "q", "v", "lr", "decay", "beta")
     # full call with autograd
@@ -48,6 +52,8 @@ def test_segments_match_full_call(native_lib, dtype, T, P, d):
     ys = [s.forward_finish(*c)[0] for s, c in zip(segs, carries)]
     assert rel_l2(torch.cat(ys, 1).float(), y.float()) < tol
     assert rel_l2(S_T.clamp(-100, 100), S_end) < tol
+    if saturate:
+        assert (S_T.abs() > 100).float().mean() > 0.3
     assert rel_l2(Z_T, Z_end) < tol
     btr = [s.backward_local(inp["dy"][:, lo:hi].contiguous()) for s, (lo, hi) in zip(segs, bounds)]
     FS_end = dS_end * ((S_T >= -100) & (S_T <= 100))
